@@ -1,0 +1,205 @@
+/*
+ * bfvgpu.h -- C ABI of the B200 (sm_100a) BFV ciphertext-arithmetic library.
+ *
+ * Drop-in boundary for privacy-rag's GPU backends (IV1 = implementation_v1/ of the
+ * reference).  Each object below replaces one reference C++ backend class; the
+ * per-function comments name the member it stands in for.  SEAL types do not cross
+ * this boundary: ciphertexts, keys and polynomials are flat little-endian uint64
+ * arrays in the reference's own layouts ([2][k][n] ciphertexts, [digit][2][k+1][n]
+ * keys, [prime][n] polynomials), exactly what the reference adapters copy out of SEAL
+ * objects (e.g. IV1/experiments/matrix_gpu/adapter.cpp:27-31).
+ *
+ * Conventions
+ *  - Every function returns an int status: BFVGPU_OK (0) or a stable error code below.
+ *    No C++ exception crosses the ABI.  bfvgpu_last_error() gives a thread-local text.
+ *    Validation failures correspond to the reference's std::invalid_argument codes,
+ *    CUDA failures to its runtime_error("E_...: "+cudaGetErrorString) after release.
+ *  - Host pointers are caller-owned and only read/written during the call.
+ *  - close() functions are idempotent and never fail; they zero every sensitive device
+ *    buffer, synchronise, free it, and report the bytes in bfvgpu_cleanup, like the
+ *    reference's Cleanup{first_cuda_error, wiped, freed, closed}
+ *    (IV1/experiments/matrix_gpu/matrix.hpp:8).  release() frees the handle itself
+ *    (closing first if needed).
+ *  - One thread drives an object at a time (the reference's single session thread).
+ *  - There is no CPU fallback: without a compute-capability-10.x device every
+ *    constructor fails with BFVGPU_E_DEVICE.
+ */
+#ifndef BFVGPU_H
+#define BFVGPU_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum bfvgpu_status {
+  BFVGPU_OK = 0,
+  BFVGPU_E_ARGUMENT = 1,     /* null pointer / unsupported parameter value          */
+  BFVGPU_E_CONTEXT = 2,      /* E_NTT_CONTEXT, MATRIX_GPU_CONTEXT: wrong parameter set */
+  BFVGPU_E_SHAPE = 3,        /* MATRIX_GPU_SHAPE, E_SWITCH_SHAPE, E_NTT_SHAPE         */
+  BFVGPU_E_CANONICAL = 4,    /* E_NTT_CANONICAL_REQUIRED: residue >= its prime        */
+  BFVGPU_E_RING = 5,         /* MATRIX_GPU_RING: ring word >= 2^59                    */
+  BFVGPU_E_TARGET_COUNT = 6, /* MATRIX_GPU_TARGET_COUNT: 0 or > 512 targets           */
+  BFVGPU_E_TARGET_INDEX = 7, /* MATRIX_GPU_TARGET_INDEX: >= n or not increasing       */
+  BFVGPU_E_CLOSED = 8,       /* E_SWITCH_CLOSED, E_NTT_CLOSED, E_RESIDENT_CLOSED      */
+  BFVGPU_E_CUDA = 9,         /* a CUDA call failed; the object has been released      */
+  BFVGPU_E_DEVICE = 10,      /* no usable sm_100 device (RTX2060_REQUIRED analogue)   */
+  BFVGPU_E_STATE = 11,       /* E_PACK_PAIR_STATE, E_CLIENT_KEY_STATE, E_LOCAL_BINDING */
+  BFVGPU_E_BOUND = 12,       /* E_RESIDENT_WEIGHT_BOUND: |w| > 2^20                   */
+  BFVGPU_E_ELEMENT = 13,     /* Galois element even or >= 2n                          */
+  BFVGPU_E_ALLOC = 14        /* device allocation failed                              */
+};
+
+typedef struct bfvgpu_cleanup {
+  int32_t first_cuda_error; /* first CUDA error seen while releasing, 0 if none */
+  int32_t closed;           /* 1 once every device buffer is gone              */
+  uint64_t wiped;           /* sensitive bytes zeroed and synchronised          */
+  uint64_t freed;           /* sensitive bytes freed                            */
+} bfvgpu_cleanup;
+
+typedef struct bfvgpu_ctx bfvgpu_ctx;
+typedef struct bfvgpu_ntt bfvgpu_ntt;
+typedef struct bfvgpu_matrix bfvgpu_matrix;
+typedef struct bfvgpu_switch bfvgpu_switch;
+typedef struct bfvgpu_enc0 bfvgpu_enc0;
+typedef struct bfvgpu_token bfvgpu_token;
+
+/* ---- library ---------------------------------------------------------------------- */
+int32_t bfvgpu_version(void);
+const char *bfvgpu_error_name(int32_t code);
+const char *bfvgpu_last_error(void);
+/* Number of kernel launches this process has issued through the library. */
+uint64_t bfvgpu_launch_count(void);
+
+/* ---- parameters (IV1/native/src/bfv.cpp:91-137) ------------------------------------- */
+/* Prime chain for degree n with the given bit sizes, every prime = 1 mod 2n, found by a
+ * downward search from 2^bits; equal sizes are handed out smallest first (the rule that
+ * yields the locked ART-002 list).  Replaces seal::CoeffModulus::Create at bfv.cpp:95. */
+int32_t bfvgpu_find_primes(uint32_t n, const int32_t *bits, uint32_t count, uint64_t *out);
+
+/* Parameter context on one device: n = 2^logn (logn in {5,6,12,13,14}), data primes
+ * primes[0..data_primes), then special_primes (0 or 1) special prime, plaintext
+ * modulus t (a power of two or < 2^32).  Computes the NTT tables (minimal primitive
+ * 2n-th root, reference table layout), BFV scaling and CRT constants, and uploads them;
+ * device == -1 builds a host-only context (tables and constants, no device work).
+ * Replaces the SEALContext plus the per-backend table extraction
+ * (IV1/experiments/matrix_gpu/adapter.cpp:19-31, client_phase/seal_tables.cpp:22-33). */
+int32_t bfvgpu_ctx_create(uint32_t n, const uint64_t *primes, uint32_t data_primes,
+                          uint32_t special_primes, uint64_t plain_modulus, int32_t device,
+                          bfvgpu_ctx **out);
+/* The locked ART-002 profile: n = 16384, six 60-bit data primes + one special prime,
+ * t = 2^59 (bfv.cpp:91-105; IV1/artifacts/bfv_context.json). */
+int32_t bfvgpu_ctx_create_art002(int32_t device, bfvgpu_ctx **out);
+int32_t bfvgpu_ctx_destroy(bfvgpu_ctx *ctx);
+/* Host copies of prime `prime`'s tables: fwd/inv [n][2] {w, floor(w 2^64/q)} in the
+ * reference layout (fwd[brv(i)] = psi^i, inv[brv(i-1)+1] = psi^-i), invn [2]. */
+int32_t bfvgpu_ctx_tables(const bfvgpu_ctx *ctx, uint32_t prime, uint64_t *fwd, uint64_t *inv,
+                          uint64_t *invn);
+/* The 16 words of prime `prime`'s constant record: q, floor((2^128-1)/q) (low, high),
+ * n^-1 and its Shoup quotient, q_special^-1 and quotient, floor(q_special/2) mod q,
+ * floor(Q/t) mod q and quotient, then zeros.  Diagnostic; used by the CPU pre-checks. */
+int32_t bfvgpu_ctx_moduli(const bfvgpu_ctx *ctx, uint32_t prime, uint64_t *out);
+/* The context's CUDA stream (cudaStream_t) and device ordinal. */
+int32_t bfvgpu_ctx_stream(const bfvgpu_ctx *ctx, void **stream, int32_t *device);
+
+/* ---- device-resident entry points (batched; all pointers are device memory) ------------
+ * stream == NULL uses the context stream.  No validation of residue ranges. */
+/* In-place negacyclic NTT (inverse != 0: inverse) of [polys][n]; poly i is reduced by
+ * prime prime_offset + i % prime_count.  One call replaces the 14 `stage` launches of
+ * NttBatch::transform (IV1/native/gpu/client_phase/ntt.cu:152-157). */
+int32_t bfvgpu_ntt_device(bfvgpu_ctx *ctx, uint64_t *data, uint64_t polys, uint32_t prime_count,
+                          uint32_t prime_offset, int32_t inverse, void *stream);
+/* Galois automorphism + keyswitch of count ciphertexts [count][2][dk][n] with one key
+ * [dk][2][k][n]; scratch holds bfvgpu_keyswitch_scratch_words(ctx, count) words;
+ * out [count][2][dk][n].  Switch::apply for a whole batch (switch.cu:142-154). */
+uint64_t bfvgpu_keyswitch_scratch_words(const bfvgpu_ctx *ctx, uint64_t count);
+int32_t bfvgpu_keyswitch_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,
+                                const uint64_t *key, uint32_t galois_elt, uint64_t *scratch,
+                                uint64_t *out, void *stream);
+/* Lift + forward NTT of ring-59 weight blocks [blocks][n] -> [blocks][dk][n]. */
+int32_t bfvgpu_weights_ntt_device(bfvgpu_ctx *ctx, const uint64_t *ring, uint64_t blocks,
+                                  uint64_t *out, void *stream);
+/* out[g][c] = INTT(sum_b in[b][c] . w[g][b]) for g < groups, with the optional mask
+ * [groups][n] subtracted (Delta-scaled) from c0 and Enc(0) pre-moddown polys
+ * enc0_x [groups][2][k][n] added.  in [inputs][2][dk][n] NTT form, w [groups][inputs][dk][n]. */
+int32_t bfvgpu_matrix_groups_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_t inputs,
+                                    const uint64_t *w, uint64_t groups, const uint64_t *mask,
+                                    const uint64_t *enc0_x, uint64_t *out, void *stream);
+
+/* ---- NttBatch (IV1/native/gpu/client_phase/ntt.hpp:22-40) ------------------------------ */
+/* key_level != 0: all k primes, else the dk data primes; batches in [1, 19]. */
+int32_t bfvgpu_ntt_open(bfvgpu_ctx *ctx, int32_t key_level, uint64_t batches, bfvgpu_ntt **out);
+/* [batches][primes][n] canonical in, out; forward: natural -> bit-reversed order. */
+int32_t bfvgpu_ntt_transform(bfvgpu_ntt *h, const uint64_t *in, uint64_t *out, int32_t inverse);
+/* Secret key s [dk][n] in NTT form (data level); once per object. */
+int32_t bfvgpu_ntt_bind_client_key(bfvgpu_ntt *h, const uint64_t *sk_ntt);
+/* c1 [batches][dk][n] -> INTT(NTT(c1) . s) (ntt.cu:181-199). */
+int32_t bfvgpu_ntt_client_phase(bfvgpu_ntt *h, const uint64_t *in, uint64_t *out);
+int32_t bfvgpu_ntt_close(bfvgpu_ntt *h, bfvgpu_cleanup *cleanup);
+int32_t bfvgpu_ntt_release(bfvgpu_ntt *h);
+
+/* ---- Matrix (IV1/experiments/matrix_gpu/matrix.hpp:9-24) -------------------------------- */
+/* inputs in [1, 512] coefficient-form ciphertexts [inputs][2][dk][n]; validated
+ * canonical, uploaded and forward-transformed once (Matrix::Matrix, matrix.cu:81-87). */
+int32_t bfvgpu_matrix_open(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t inputs, bfvgpu_matrix **out);
+/* ring [inputs][n] ring-59 words -> out [2][dk][n] (Matrix::evaluate). */
+int32_t bfvgpu_matrix_evaluate(bfvgpu_matrix *m, const uint64_t *ring, uint64_t *out);
+/* As evaluate, but c0 is zero except at 1..512 strictly increasing targets
+ * (Matrix::evaluate_selective, matrix.cu:90-106). */
+int32_t bfvgpu_matrix_evaluate_selective(bfvgpu_matrix *m, const uint64_t *ring, const uint64_t *targets,
+                                         uint64_t count, uint64_t *out);
+/* Public key [2][k][n] (NTT form, key level) for the Enc(0) re-randomisation. */
+int32_t bfvgpu_matrix_bind_public_key(bfvgpu_matrix *m, const uint64_t *pk);
+/* Several output groups of BfvEngine::matrix's server loop in one call
+ * (bfv_matrix.inc:150-233): per group g, W = lift(ring[g]) [inputs][n], product, INTT,
+ * c0 -= Delta*mask[g] (mask nullable), + Enc(0) from samples[g] [3][k][n] (nullable;
+ * needs the public key), then c1 [g][dk][n] in full and the c0 residues at the group's
+ * targets ([g][dk][max_count], targets [g][max_count], counts[g] <= max_count <= 512);
+ * c0_crt (nullable) [g][max_count][dk] receives each target's CRT value in [0,Q) as dk
+ * little-endian 64-bit limbs (rns_coefficient, bfv.cpp:138-147). */
+int32_t bfvgpu_matrix_evaluate_groups(bfvgpu_matrix *m, uint64_t groups, const uint64_t *ring,
+                                      const uint64_t *targets, const uint32_t *counts, uint32_t max_count,
+                                      const uint64_t *mask, const uint64_t *samples, uint64_t *c1_out,
+                                      uint64_t *c0_targets, uint64_t *c0_crt);
+int32_t bfvgpu_matrix_device_bytes(const bfvgpu_matrix *m, uint64_t *bytes);
+int32_t bfvgpu_matrix_close(bfvgpu_matrix *m, bfvgpu_cleanup *cleanup);
+int32_t bfvgpu_matrix_release(bfvgpu_matrix *m);
+
+/* ---- Switch (IV1/experiments/keyswitch_full_gpu/switch.hpp:12-28) ----------------------- */
+/* key [dk][2][k][n] NTT form at the key level for Galois element `galois_elt` (odd, < 2n). */
+int32_t bfvgpu_switch_open(bfvgpu_ctx *ctx, const uint64_t *key, uint32_t galois_elt, bfvgpu_switch **out);
+/* Galois automorphism then keyswitch of one ciphertext [2][dk][n] (Switch::apply). */
+int32_t bfvgpu_switch_apply(bfvgpu_switch *s, const uint64_t *ct, uint64_t *out);
+/* The same for count ciphertexts [count][2][dk][n] in one transfer and launch. */
+int32_t bfvgpu_switch_apply_many(bfvgpu_switch *s, const uint64_t *cts, uint64_t count, uint64_t *out);
+/* Acyclic merge (Switch::packing_pair, switch.cu:155-185): s holds element 1, other
+ * holds 2^(level+1)+1, level < logn-5 ... out = sw1(L + X^(n>>(level+1)) R) + swg(...). */
+int32_t bfvgpu_switch_packing_pair(bfvgpu_switch *s, const uint64_t *left, const uint64_t *right,
+                                   bfvgpu_switch *other, uint32_t level, uint64_t *out);
+/* Device milliseconds of the last apply: upload, kernels, download (Switch::timing). */
+int32_t bfvgpu_switch_timing(const bfvgpu_switch *s, double *upload_ms, double *kernel_ms, double *download_ms);
+int32_t bfvgpu_switch_close(bfvgpu_switch *s, bfvgpu_cleanup *cleanup);
+int32_t bfvgpu_switch_release(bfvgpu_switch *s);
+
+/* ---- PublicZero (IV1/native/gpu/enc0/enc0.hpp:15-25) ------------------------------------ */
+int32_t bfvgpu_enc0_open(bfvgpu_ctx *ctx, const uint64_t *pk, bfvgpu_enc0 **out);
+/* samples [3][k][n] (ternary u, e0, e1 as canonical residues) -> Enc(0) [2][dk][n]. */
+int32_t bfvgpu_enc0_encrypt_from_samples(bfvgpu_enc0 *e, const uint64_t *samples, uint64_t *out);
+int32_t bfvgpu_enc0_close(bfvgpu_enc0 *e, bfvgpu_cleanup *cleanup);
+int32_t bfvgpu_enc0_release(bfvgpu_enc0 *e);
+
+/* ---- TokenWeights (IV1/experiments/resident_token_gpu/resident.hpp:23-48) --------------- */
+/* ART-002 only: cts [slots][19][2][dk][n] coefficient form, slots in [1,4]. */
+int32_t bfvgpu_token_open(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t slots, bfvgpu_token **out);
+/* ring [19][8192] ring-59 weights with |w| <= 2^20; local [slots] ring-59 local shares;
+ * out [slots][2][dk][n] (evaluate_finished + download). */
+int32_t bfvgpu_token_evaluate_finished(bfvgpu_token *t, const uint64_t *ring, const uint64_t *local,
+                                       uint64_t *out);
+int32_t bfvgpu_token_close(bfvgpu_token *t, bfvgpu_cleanup *cleanup);
+int32_t bfvgpu_token_release(bfvgpu_token *t);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BFVGPU_H */

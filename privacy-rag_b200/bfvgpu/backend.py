@@ -1,0 +1,368 @@
+"""Python mirror of privacy-rag's GPU backend classes over the bfvgpu C ABI.
+
+Each class keeps the reference class's name, member names, argument meaning and
+error behaviour (IV1 = implementation_v1/ of the reference):
+
+* ``NttBatch``      IV1/native/gpu/client_phase/ntt.hpp:22-40
+* ``Matrix``        IV1/experiments/matrix_gpu/matrix.hpp:9-24
+* ``Switch``        IV1/experiments/keyswitch_full_gpu/switch.hpp:12-28
+* ``PublicZero``    IV1/native/gpu/enc0/enc0.hpp:15-25
+* ``TokenWeights``  IV1/experiments/resident_token_gpu/resident.hpp:23-48
+
+SEAL objects become flat ``numpy.uint64`` arrays in the layouts the reference
+adapters copy out of them.  Validation failures raise ``BfvGpuInvalidArgument``
+(a ``ValueError``, the reference's ``std::invalid_argument``); CUDA failures raise
+``BfvGpuError`` after the object's device state has been released; ``close()``
+never raises and returns the cleanup record.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from ._lib import Cleanup, U32, U64, VP, check, lib, ptr, u64
+
+ART002_PRIMES = (
+    1152921504599080961, 1152921504600260609, 1152921504604979201,
+    1152921504605962241, 1152921504606584833, 1152921504606683137,
+    1152921504606748673,
+)
+
+
+def find_primes(n: int, bits: list[int]) -> list[int]:
+    """Prime chain = 1 mod 2n with the given bit sizes (bfvgpu_find_primes)."""
+    out = (U64 * len(bits))()
+    arr = (ctypes.c_int32 * len(bits))(*bits)
+    check(lib().bfvgpu_find_primes(n, arr, len(bits), out), "find_primes")
+    return [int(v) for v in out]
+
+
+def launch_count() -> int:
+    """Kernel launches this process issued through the library."""
+    return int(lib().bfvgpu_launch_count())
+
+
+class Context:
+    """Parameter context on one device (device=-1: host-only, tables and constants)."""
+
+    def __init__(self, n: int, primes, data_primes: int, special_primes: int = 1,
+                 plain_modulus: int = 1 << 59, device: int = 0):
+        self.n = int(n)
+        self.primes = [int(p) for p in primes]
+        self.data_primes = int(data_primes)
+        self.k = self.data_primes + int(special_primes)
+        self.t = int(plain_modulus)
+        self.device = int(device)
+        if len(self.primes) != self.k:
+            raise ValueError("E_BFVGPU_PRIME_COUNT")
+        arr = u64(self.primes)
+        h = VP()
+        check(lib().bfvgpu_ctx_create(self.n, ptr(arr), self.data_primes, int(special_primes), self.t,
+                                      self.device, ctypes.byref(h)), "Context")
+        self._h = h
+
+    @classmethod
+    def art002(cls, device: int = 0) -> "Context":
+        return cls(16384, ART002_PRIMES, 6, 1, 1 << 59, device)
+
+    @property
+    def handle(self):
+        return self._h
+
+    @property
+    def dk(self) -> int:
+        return self.data_primes
+
+    def tables(self, prime: int):
+        fwd = np.zeros((self.n, 2), dtype=np.uint64)
+        inv = np.zeros((self.n, 2), dtype=np.uint64)
+        invn = np.zeros(2, dtype=np.uint64)
+        check(lib().bfvgpu_ctx_tables(self._h, prime, ptr(fwd), ptr(inv), ptr(invn)), "tables")
+        return fwd, inv, invn
+
+    def moduli(self) -> np.ndarray:
+        out = np.zeros((self.k, 16), dtype=np.uint64)
+        for p in range(self.k):
+            check(lib().bfvgpu_ctx_moduli(self._h, p, ptr(out[p])), "moduli")
+        return out
+
+    def stream(self) -> int:
+        s = VP()
+        check(lib().bfvgpu_ctx_stream(self._h, ctypes.byref(s), None), "stream")
+        return s.value or 0
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().bfvgpu_ctx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- device-resident batched entry points (torch CUDA tensors or raw pointers) ----
+    @staticmethod
+    def _dptr(x) -> int:
+        if x is None:
+            return 0
+        if isinstance(x, int):
+            return x
+        return int(x.data_ptr())
+
+    def ntt_device(self, data, polys: int, prime_count: int, prime_offset: int = 0, inverse: bool = False,
+                   stream: int | None = None) -> None:
+        check(lib().bfvgpu_ntt_device(self._h, self._dptr(data), polys, prime_count, prime_offset,
+                                      int(bool(inverse)), stream), "ntt_device")
+
+    def keyswitch_scratch_words(self, count: int) -> int:
+        return int(lib().bfvgpu_keyswitch_scratch_words(self._h, count))
+
+    def keyswitch_device(self, cts, count: int, key, galois_elt: int, scratch, out, stream: int | None = None):
+        check(lib().bfvgpu_keyswitch_device(self._h, self._dptr(cts), count, self._dptr(key), galois_elt,
+                                            self._dptr(scratch), self._dptr(out), stream), "keyswitch_device")
+
+    def weights_ntt_device(self, ring, blocks: int, out, stream: int | None = None):
+        check(lib().bfvgpu_weights_ntt_device(self._h, self._dptr(ring), blocks, self._dptr(out), stream),
+              "weights_ntt_device")
+
+    def matrix_groups_device(self, inputs_ntt, inputs: int, weights_ntt, groups: int, out, mask=None,
+                             enc0_x=None, stream: int | None = None):
+        check(lib().bfvgpu_matrix_groups_device(self._h, self._dptr(inputs_ntt), inputs, self._dptr(weights_ntt),
+                                                groups, self._dptr(mask) or None, self._dptr(enc0_x) or None,
+                                                self._dptr(out), stream), "matrix_groups_device")
+
+
+class _Handle:
+    _close_fn = ""
+    _release_fn = ""
+
+    def __init__(self, ctx: Context):
+        self.ctx = ctx
+        self._h = None
+        self._cleanup = None
+
+    def close(self) -> dict:
+        """Wipe and free every sensitive device buffer; idempotent, never raises."""
+        c = Cleanup()
+        if self._h is not None:
+            getattr(lib(), self._close_fn)(self._h, ctypes.byref(c))
+            self._cleanup = c.as_dict()
+        return self._cleanup or {"first_cuda_error": 0, "closed": True, "wiped": 0, "freed": 0}
+
+    def __del__(self):
+        try:
+            if self._h is not None:
+                getattr(lib(), self._release_fn)(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+
+class NttBatch(_Handle):
+    """Batched canonical NTT/INTT and the client phase c1*s (layout [batch][prime][n])."""
+
+    _close_fn = "bfvgpu_ntt_close"
+    _release_fn = "bfvgpu_ntt_release"
+
+    def __init__(self, ctx: Context, key_level: bool, batches: int):
+        super().__init__(ctx)
+        self.primes = ctx.k if key_level else ctx.dk
+        self.batches = int(batches)
+        h = VP()
+        check(lib().bfvgpu_ntt_open(ctx.handle, int(bool(key_level)), self.batches, ctypes.byref(h)), "NttBatch")
+        self._h = h
+
+    def transform(self, data, inverse: bool) -> np.ndarray:
+        a = u64(data)
+        if a.size != self.batches * self.primes * self.ctx.n:
+            raise ValueError("E_NTT_SHAPE")
+        out = np.empty_like(a)
+        check(lib().bfvgpu_ntt_transform(self._h, ptr(a), ptr(out), int(bool(inverse))), "NttBatch.transform")
+        return out
+
+    def bind_client_key(self, ntt_key) -> None:
+        k = u64(ntt_key)
+        if k.size != self.ctx.dk * self.ctx.n:
+            raise ValueError("E_CLIENT_KEY_SHAPE")
+        check(lib().bfvgpu_ntt_bind_client_key(self._h, ptr(k)), "NttBatch.bind_client_key")
+
+    def client_phase(self, data) -> np.ndarray:
+        a = u64(data)
+        if a.size != self.batches * self.primes * self.ctx.n:
+            raise ValueError("E_NTT_SHAPE")
+        out = np.empty_like(a)
+        check(lib().bfvgpu_ntt_client_phase(self._h, ptr(a), ptr(out)), "NttBatch.client_phase")
+        return out
+
+
+class Matrix(_Handle):
+    """Coefficient-packed ct-pt product backend of BfvEngine::matrix."""
+
+    _close_fn = "bfvgpu_matrix_close"
+    _release_fn = "bfvgpu_matrix_release"
+
+    def __init__(self, ctx: Context, cts):
+        super().__init__(ctx)
+        a = u64(cts)
+        per = 2 * ctx.dk * ctx.n
+        if a.size == 0 or a.size % per:
+            raise ValueError("MATRIX_GPU_CONTEXT")
+        self.blocks = a.size // per
+        h = VP()
+        check(lib().bfvgpu_matrix_open(ctx.handle, ptr(a), self.blocks, ctypes.byref(h)), "Matrix")
+        self._h = h
+
+    def evaluate(self, ring) -> np.ndarray:
+        r = u64(ring)
+        if r.size != self.blocks * self.ctx.n:
+            raise ValueError("MATRIX_GPU_SHAPE")
+        out = np.zeros((2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
+        check(lib().bfvgpu_matrix_evaluate(self._h, ptr(r), ptr(out)), "Matrix.evaluate")
+        return out
+
+    def evaluate_selective(self, ring, targets) -> np.ndarray:
+        r = u64(ring)
+        t = u64(targets)
+        if r.size != self.blocks * self.ctx.n:
+            raise ValueError("MATRIX_GPU_SHAPE")
+        out = np.zeros((2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
+        check(lib().bfvgpu_matrix_evaluate_selective(self._h, ptr(r), ptr(t) if t.size else None, t.size,
+                                                      ptr(out)), "Matrix.evaluate_selective")
+        return out
+
+    def bind_public_key(self, pk) -> None:
+        p = u64(pk)
+        if p.size != 2 * self.ctx.k * self.ctx.n:
+            raise ValueError("E_BFV_KEY")
+        check(lib().bfvgpu_matrix_bind_public_key(self._h, ptr(p)), "Matrix.bind_public_key")
+
+    def evaluate_groups(self, ring, targets: list, mask=None, samples=None, crt: bool = False):
+        """Several output groups: ring [G][blocks][n]; targets: list of G increasing lists.
+        Returns (c1 [G][dk][n], c0 residues [G][dk][max], crt limbs [G][max][dk] or None)."""
+        r = u64(ring)
+        G = len(targets)
+        n, dk = self.ctx.n, self.ctx.dk
+        if r.size != G * self.blocks * n:
+            raise ValueError("MATRIX_GPU_SHAPE")
+        mx = max(1, max(len(t) for t in targets))
+        tg = np.zeros((G, mx), dtype=np.uint64)
+        counts = (U32 * G)()
+        for g, t in enumerate(targets):
+            tg[g, :len(t)] = t
+            counts[g] = len(t)
+        m = u64(mask) if mask is not None else None
+        s = u64(samples) if samples is not None else None
+        c1 = np.zeros((G, dk, n), dtype=np.uint64)
+        c0 = np.zeros((G, dk, mx), dtype=np.uint64)
+        cr = np.zeros((G, mx, dk), dtype=np.uint64) if crt else None
+        check(lib().bfvgpu_matrix_evaluate_groups(self._h, G, ptr(r), ptr(tg), counts, mx, ptr(m), ptr(s),
+                                                  ptr(c1), ptr(c0), ptr(cr)), "Matrix.evaluate_groups")
+        return c1, c0, cr
+
+    def device_bytes(self) -> int:
+        b = U64()
+        check(lib().bfvgpu_matrix_device_bytes(self._h, ctypes.byref(b)), "Matrix.device_bytes")
+        return int(b.value)
+
+
+class Switch(_Handle):
+    """Galois automorphism + alpha=1 special-prime keyswitch for one Galois element."""
+
+    _close_fn = "bfvgpu_switch_close"
+    _release_fn = "bfvgpu_switch_release"
+
+    def __init__(self, ctx: Context, key, element: int):
+        super().__init__(ctx)
+        k = u64(key)
+        if k.size != ctx.dk * 2 * ctx.k * ctx.n:
+            raise ValueError("E_NTT_CONTEXT")
+        self.element = int(element)
+        h = VP()
+        check(lib().bfvgpu_switch_open(ctx.handle, ptr(k), self.element, ctypes.byref(h)), "Switch")
+        self._h = h
+
+    def apply(self, ct) -> np.ndarray:
+        a = u64(ct)
+        if a.size != 2 * self.ctx.dk * self.ctx.n:
+            raise ValueError("E_SWITCH_CIPHERTEXT")
+        out = np.empty((2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
+        check(lib().bfvgpu_switch_apply(self._h, ptr(a), ptr(out)), "Switch.apply")
+        return out
+
+    def apply_many(self, cts) -> np.ndarray:
+        a = u64(cts)
+        per = 2 * self.ctx.dk * self.ctx.n
+        if a.size == 0 or a.size % per:
+            raise ValueError("E_SWITCH_CIPHERTEXT")
+        out = np.empty((a.size // per, 2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
+        check(lib().bfvgpu_switch_apply_many(self._h, ptr(a), a.size // per, ptr(out)), "Switch.apply_many")
+        return out
+
+    def packing_pair(self, left, right, difference: "Switch", level: int) -> np.ndarray:
+        L, R = u64(left), u64(right)
+        out = np.empty((2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
+        check(lib().bfvgpu_switch_packing_pair(self._h, ptr(L), ptr(R), difference._h, level, ptr(out)),
+              "Switch.packing_pair")
+        return out
+
+    def timing(self) -> dict:
+        a, b, c = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+        check(lib().bfvgpu_switch_timing(self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)), "timing")
+        return {"upload_ms": a.value, "kernel_ms": b.value, "download_ms": c.value}
+
+
+class PublicZero(_Handle):
+    """Enc(0) from explicit samples (u ternary, e0, e1) with a bound public key."""
+
+    _close_fn = "bfvgpu_enc0_close"
+    _release_fn = "bfvgpu_enc0_release"
+
+    def __init__(self, ctx: Context, pk):
+        super().__init__(ctx)
+        p = u64(pk)
+        if p.size != 2 * ctx.k * ctx.n:
+            raise ValueError("E_NTT_CONTEXT")
+        h = VP()
+        check(lib().bfvgpu_enc0_open(ctx.handle, ptr(p), ctypes.byref(h)), "PublicZero")
+        self._h = h
+
+    def encrypt_from_samples(self, samples) -> np.ndarray:
+        s = u64(samples)
+        if s.size != 3 * self.ctx.k * self.ctx.n:
+            raise ValueError("E_ENC0_SAMPLE_SHAPE")
+        out = np.empty((2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
+        check(lib().bfvgpu_enc0_encrypt_from_samples(self._h, ptr(s), ptr(out)), "PublicZero.encrypt_from_samples")
+        return out
+
+
+class TokenWeights(_Handle):
+    """Resident token-lookup product (ART-002): 19 input blocks per slot."""
+
+    _close_fn = "bfvgpu_token_close"
+    _release_fn = "bfvgpu_token_release"
+
+    def __init__(self, ctx: Context, cts):
+        super().__init__(ctx)
+        a = u64(cts)
+        per = 19 * 2 * ctx.dk * ctx.n
+        if a.size == 0 or a.size % per:
+            raise ValueError("E_GPU_TOKEN_CONTEXT_LAYOUT")
+        self.slots = a.size // per
+        h = VP()
+        check(lib().bfvgpu_token_open(ctx.handle, ptr(a), self.slots, ctypes.byref(h)), "TokenWeights")
+        self._h = h
+
+    def evaluate_finished(self, weights, local) -> np.ndarray:
+        w = u64(weights)
+        loc = u64(local)
+        if w.size != 19 * 8192:
+            raise ValueError("E_RESIDENT_WEIGHT_SHAPE")
+        if loc.size != self.slots:
+            raise ValueError("E_RESIDENT_LOCAL_SHAPE")
+        out = np.empty((self.slots, 2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
+        check(lib().bfvgpu_token_evaluate_finished(self._h, ptr(w), ptr(loc), ptr(out)),
+              "TokenWeights.evaluate_finished")
+        return out

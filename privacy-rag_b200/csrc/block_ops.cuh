@@ -1,0 +1,333 @@
+// Per-thread-block bodies of the BFV kernels, written against an executor (ntt_core.cuh)
+// so the same code runs as a CUDA thread block (BlockExec) and, for the CPU pre-checks
+// in tests/emu, as a host loop over the block's work units (HostExec).  The __global__
+// wrappers in kernels.cu only pick the block index and shared memory.
+//
+// Reference behaviour restated here (IV1 = implementation_v1/):
+//   op_lift_ntt ...... `lift` + forward stages (IV1/experiments/matrix_gpu/matrix.cu:48-51, :96)
+//   op_mac_intt ...... `product` + inverse stages (matrix.cu:59-63, :96) with the sub_plain
+//                      mask (IV1/native/src/bfv_matrix.inc:215-219) and Enc(0) add (:220-227)
+//   op_ks_main ....... apply_galois (IV1/experiments/keyswitch_full_gpu/seal_adapter.cpp:50),
+//                      `decompose`, forward stages, `product`, inverse stages (switch.cu:92-102)
+//   op_ks_moddown .... `moddown` (switch.cu:103-111)
+//   op_enc0_x ........ PublicZero::evaluate up to noise_add (IV1/native/gpu/enc0/enc0.cu:74-80, :129-134)
+//   op_client_phase .. NTT, `client_dyadic`, INTT (IV1/native/gpu/client_phase/ntt.cu:96-98, :186-194)
+//   op_token_* ....... `lift`, `accumulate`, inverse stages, `add_shift`
+//                      (IV1/experiments/resident_token_gpu/resident.cu:71-107)
+//   crt_target ....... rns_coefficient (IV1/native/src/bfv.cpp:138-147) in fixed-width limbs
+#pragma once
+#include "ntt_core.cuh"
+
+namespace bfvgpu {
+
+// Divide-and-round by the special prime q_s (last prime) of one coefficient:
+// (x_p - ((x_s + floor(q_s/2)) mod q_s mod q_p - floor(q_s/2) mod q_p)) * q_s^-1 mod q_p.
+BFV_HD uint64_t moddown_elem(uint64_t xv, uint64_t xs, const Modulus& mp, const Modulus& ms) {
+  const uint64_t last = add_mod(xs, ms.q >> 1, ms.q);
+  const uint64_t lastp = reduce64(last, mp);
+  const uint64_t corr = sub_mod(lastp, mp.half_special_mod, mp.q);
+  return shoup(sub_mod(xv, corr, mp.q), mp.inv_special, mp.inv_special_q, mp.q);
+}
+
+struct ProtectArgs {
+  const uint64_t* mask;    // [groups][n] ring-59 words, or null
+  const uint64_t* enc0_x;  // [groups][2][k][n] pre-moddown Enc(0) polys, or null
+  uint64_t q_mod_t, upper_half, t;
+  int tlog;
+};
+
+// ---- batched transform: block = one poly -----------------------------------------------
+template <int LOGN, class Ex>
+BFV_HD void op_ntt(const Ex& ex, uint64_t* s, uint64_t blk, bool inverse, uint64_t* data, uint32_t prime_count,
+                   uint32_t prime_offset, const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv) {
+  const uint32_t p = prime_offset + (uint32_t)(blk % prime_count);
+  const Modulus m = mods[p];
+  uint64_t* a = data + (blk << LOGN);
+  auto ld = [a](int i) { return a[i]; };
+  auto st = [a](int i, uint64_t v) { a[i] = v; };
+  if (inverse)
+    ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+  else
+    ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+}
+
+// ---- weight lift + NTT: block = (weight block b, data prime p) --------------------------
+template <int LOGN, class Ex>
+BFV_HD void op_lift_ntt(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* ring, uint64_t* out, uint32_t dk,
+                        const Modulus* mods, const ulonglong2* fwd) {
+  const uint64_t b = blk / dk;
+  const uint32_t p = (uint32_t)(blk % dk);
+  const Modulus m = mods[p];
+  const uint64_t* r = ring + (b << LOGN);
+  uint64_t* o = out + ((b * dk + p) << LOGN);
+  const uint64_t adjust = m.q - (uint64_t(1) << 59);
+  auto ld = [r, adjust](int i) {
+    const uint64_t v = r[i];
+    return v + (adjust & (uint64_t(0) - (v >> 58)));
+  };
+  auto st = [o](int i, uint64_t v) { o[i] = v; };
+  ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+}
+
+// ---- product over input blocks + INTT (+ mask, + Enc(0)): block = (group g, c, p) -------
+template <int LOGN, class Ex>
+BFV_HD void op_mac_intt(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* in, const uint64_t* w, uint64_t* out,
+                        uint32_t inputs, uint32_t k, uint32_t dk, const Modulus* mods, const ulonglong2* inv,
+                        const ProtectArgs& prot) {
+  constexpr uint64_t N = uint64_t(1) << LOGN;
+  const uint64_t g = blk / (2 * dk);
+  const uint32_t cp = (uint32_t)(blk % (2 * dk)), c = cp / dk, p = cp % dk;
+  const Modulus m = mods[p];
+  const uint64_t* in_cp = in + (uint64_t)cp * N;
+  const uint64_t in_stride = 2 * (uint64_t)dk * N;
+  const uint64_t* w_gp = w + ((g * inputs) * dk + p) * N;
+  const uint64_t w_stride = (uint64_t)dk * N;
+  auto ld = [=](int i) {
+    Acc128 acc;
+    for (uint32_t b = 0; b < inputs; ++b) {
+      acc.mac(in_cp[b * in_stride + i], w_gp[b * w_stride + i]);
+      if ((b & 127u) == 127u) acc.fold(m);
+    }
+    return acc.reduce(m);
+  };
+  uint64_t* o = out + ((g * 2 + c) * dk + p) * N;
+  const uint64_t* x = prot.enc0_x ? prot.enc0_x + g * 2 * k * N : nullptr;
+  const uint64_t* mask = (prot.mask && c == 0) ? prot.mask + g * N : nullptr;
+  const Modulus* ms = mods + (k - 1);
+  const ProtectArgs pa = prot;
+  auto st = [=](int i, uint64_t v) {
+    if (x) {
+      const uint64_t xv = x[((uint64_t)c * k + p) * N + i];
+      const uint64_t xs = x[((uint64_t)c * k + k - 1) * N + i];
+      v = add_mod(v, moddown_elem(xv, xs, m, *ms), m.q);
+    }
+    if (mask) v = sub_mod(v, scale_plain_coeff(mask[i], pa.q_mod_t, pa.upper_half, pa.t, pa.tlog, m), m.q);
+    o[i] = v;
+  };
+  ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+}
+
+// ---- Galois automorphism + keyswitch main part: block = (ciphertext, key-level prime p) --
+// For each digit j (data prime j of c1) the coefficient-domain digit is built in
+// natural order from the UNPERMUTED c1, pre-negated where the automorphism will negate
+// it, so that the mod-q_p automorphism applied afterwards as an NTT-slot permutation
+// yields exactly the reference's digit: sigma(c1)_j with its "q_j - x" negation, then
+// reduced into q_p.  acc [ct][2][k][n] receives INTT(sum_j digit_j . key_j).
+template <int LOGN, class Ex>
+BFV_HD void op_ks_main(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* cts, const uint64_t* key,
+                       uint64_t* acc, uint32_t elt, uint32_t k, uint32_t dk, const Modulus* mods, const uint64_t* qjp,
+                       const ulonglong2* fwd, const ulonglong2* inv) {
+  constexpr int N = 1 << LOGN;
+  const uint64_t ct = blk / k;
+  const uint32_t p = (uint32_t)(blk % k);
+  const Modulus m = mods[p];
+  const uint64_t* c1 = cts + (ct * 2 * dk + dk) * (uint64_t)N;
+  uint64_t* acc0 = acc + ((ct * 2 + 0) * k + p) * (uint64_t)N;
+  uint64_t* acc1 = acc + ((ct * 2 + 1) * k + p) * (uint64_t)N;
+  const uint32_t mask2n = 2u * N - 1u;
+  for (uint32_t j = 0; j < dk; ++j) {
+    const uint64_t* src = c1 + (uint64_t)j * N;
+    const uint64_t adj = qjp[j * k + p];
+    const bool reduce = mods[j].q > m.q;
+    auto ld = [=](int i) {
+      const uint64_t x = src[i];
+      uint64_t y = reduce ? reduce64(x, m) : x;
+      const bool neg = (((uint32_t)i * elt) & mask2n) >= (uint32_t)N;
+      if (neg && x) y = sub_mod(y, adj, m.q);
+      return y;
+    };
+    auto st = [s](int i, uint64_t v) { s[spad(i)] = v; };
+    ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+    const uint64_t* k0 = key + ((uint64_t)(j * 2 + 0) * k + p) * N;
+    const uint64_t* k1 = key + ((uint64_t)(j * 2 + 1) * k + p) * N;
+    ex.run(N, [&](int i) {
+      const uint64_t v = s[spad(galois_slot(i, elt, LOGN))];
+      const uint64_t a = mul_mod(v, k0[i], m), b = mul_mod(v, k1[i], m);
+      if (j == 0) {
+        acc0[i] = a;
+        acc1[i] = b;
+      } else {
+        acc0[i] = add_mod(acc0[i], a, m.q);
+        acc1[i] = add_mod(acc1[i], b, m.q);
+      }
+    });
+    ex.sync();
+  }
+  for (int c = 0; c < 2; ++c) {
+    uint64_t* a = c ? acc1 : acc0;
+    auto ld = [a](int i) { return a[i]; };
+    auto st = [a](int i, uint64_t v) { a[i] = v; };
+    ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+  }
+}
+
+// out_c[p] = moddown(acc_c)[p] (+ sigma(c0)[p] for c = 0).  Block (ct, data prime p);
+// the c0 limb is staged unpadded in shared memory so the automorphism is a gather there.
+template <int LOGN, class Ex>
+BFV_HD void op_ks_moddown(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* acc, const uint64_t* cts,
+                          uint64_t* out, uint32_t ginv, uint32_t k, uint32_t dk, const Modulus* mods) {
+  constexpr int N = 1 << LOGN;
+  const uint64_t ct = blk / dk;
+  const uint32_t p = (uint32_t)(blk % dk);
+  const Modulus m = mods[p], ms = mods[k - 1];
+  const uint64_t* c0 = cts + (ct * 2 * dk + p) * (uint64_t)N;
+  ex.run(N, [&](int i) { s[i] = c0[i]; });
+  ex.sync();
+  const uint32_t mask2n = 2u * N - 1u;
+  ex.run(N, [&](int i) {
+    const uint32_t src = ((uint32_t)i * ginv) & mask2n;
+    const uint64_t w = src < (uint32_t)N ? s[src] : neg_mod(s[src - N], m.q);
+    for (int c = 0; c < 2; ++c) {
+      const uint64_t* a = acc + ((ct * 2 + c) * k) * (uint64_t)N;
+      uint64_t v = moddown_elem(a[(uint64_t)p * N + i], a[(uint64_t)(k - 1) * N + i], m, ms);
+      if (c == 0) v = add_mod(v, w, m.q);
+      out[((ct * 2 + c) * dk + p) * (uint64_t)N + i] = v;
+    }
+  });
+  ex.sync();
+}
+
+// ---- Enc(0) pre-moddown polys: block = (group, key-level prime p) ------------------------
+template <int LOGN, class Ex>
+BFV_HD void op_enc0_x(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* samples, const uint64_t* pk,
+                      uint64_t* u_ntt, uint64_t* x, uint32_t k, const Modulus* mods, const ulonglong2* fwd,
+                      const ulonglong2* inv) {
+  constexpr uint64_t N = uint64_t(1) << LOGN;
+  const uint64_t g = blk / k;
+  const uint32_t p = (uint32_t)(blk % k);
+  const Modulus m = mods[p];
+  const uint64_t* u = samples + (g * 3 * k + p) * N;
+  uint64_t* U = u_ntt + (g * k + p) * N;
+  {
+    auto ld = [u](int i) { return u[i]; };
+    auto st = [U](int i, uint64_t v) { U[i] = v; };
+    ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+  }
+  for (uint32_t c = 0; c < 2; ++c) {
+    const uint64_t* pkc = pk + ((uint64_t)c * k + p) * N;
+    const uint64_t* e = samples + ((g * 3 + 1 + c) * k + p) * N;
+    uint64_t* xo = x + ((g * 2 + c) * k + p) * N;
+    auto ld = [=](int i) { return mul_mod(U[i], pkc[i], m); };
+    auto st = [=](int i, uint64_t v) { xo[i] = add_mod(v, e[i], m.q); };
+    ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+  }
+}
+
+// ---- client phase: block = (batch b, data prime p) -----------------------------------------
+template <int LOGN, class Ex>
+BFV_HD void op_client_phase(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* data, const uint64_t* sk, uint32_t dk,
+                            const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv) {
+  constexpr uint64_t N = uint64_t(1) << LOGN;
+  const uint64_t b = blk / dk;
+  const uint32_t p = (uint32_t)(blk % dk);
+  const Modulus m = mods[p];
+  uint64_t* a = data + (b * dk + p) * N;
+  const uint64_t* key = sk + (uint64_t)p * N;
+  {
+    auto ld = [a](int i) { return a[i]; };
+    auto st = [s](int i, uint64_t v) { s[spad(i)] = v; };
+    ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+  }
+  {
+    auto ld = [=](int i) { return mul_mod(s[spad(i)], key[i], m); };
+    auto st = [a](int i, uint64_t v) { a[i] = v; };
+    ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+  }
+}
+
+// ---- resident token product (n = 16384: 19 blocks of 8192 weights) -------------------------
+constexpr int kTokenBlocks = 19, kTokenWidth = 8192;
+
+template <int LOGN, class Ex>
+BFV_HD void op_token_lift_ntt(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* ring, uint64_t* w, uint32_t dk,
+                              const Modulus* mods, const ulonglong2* fwd) {
+  constexpr uint64_t N = uint64_t(1) << LOGN;
+  const uint32_t b = (uint32_t)(blk / dk), p = (uint32_t)(blk % dk);
+  const Modulus m = mods[p];
+  const uint64_t* r = ring + (uint64_t)b * kTokenWidth;
+  uint64_t* o = w + ((uint64_t)b * dk + p) * N;
+  const uint64_t adjust = m.q - (uint64_t(1) << 59);
+  auto ld = [=](int i) {
+    if (i >= kTokenWidth) return uint64_t(0);
+    const uint64_t v = r[kTokenWidth - 1 - i];
+    return v + (adjust & (uint64_t(0) - (v >> 58)));
+  };
+  auto st = [o](int i, uint64_t v) { o[i] = v; };
+  ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+}
+
+template <int LOGN, class Ex>
+BFV_HD void op_token_mac_intt(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* in, const uint64_t* w,
+                              const uint64_t* scaled, uint64_t* out, uint32_t slots, uint32_t dk, const Modulus* mods,
+                              const ulonglong2* inv) {
+  constexpr uint64_t N = uint64_t(1) << LOGN;
+  const uint32_t sl = (uint32_t)(blk / (2 * dk)), cp = (uint32_t)(blk % (2 * dk)), c = cp / dk, p = cp % dk;
+  const Modulus m = mods[p];
+  const uint64_t words = (uint64_t)slots * 2 * dk * N;
+  const uint64_t* inb = in + ((uint64_t)sl * 2 * dk + cp) * N;
+  const uint64_t* wp = w + (uint64_t)p * N;
+  auto ld = [=](int i) {
+    Acc128 acc;
+    for (int b = 0; b < kTokenBlocks; ++b) acc.mac(inb[b * words + i], wp[(uint64_t)b * dk * N + i]);
+    return acc.reduce(m);
+  };
+  uint64_t* o = out + ((uint64_t)sl * 2 * dk + cp) * N;
+  const uint64_t add = scaled[(uint64_t)sl * dk + p];
+  auto st = [=](int j, uint64_t v) {
+    if (c == 0 && j == kTokenWidth - 1) v = add_mod(v, add, m.q);
+    const uint32_t dest = ((uint32_t)j + 2u * (uint32_t)N - (kTokenWidth - 1)) & (2u * (uint32_t)N - 1u);
+    o[dest & (N - 1)] = dest >= N ? neg_mod(v, m.q) : v;
+  };
+  ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+}
+
+// ---- CRT of one target's dk residues to dk little-endian 64-bit limbs in [0, Q) ------------
+// sum_j (a_j (Q/q_j)^-1 mod q_j) (Q/q_j) < dk*Q, then Q is subtracted while the sum >= Q.
+BFV_HD void crt_target(const uint64_t* res, uint32_t dk, const Modulus* mods, const uint64_t* crt_part,
+                       const uint64_t* crt_inv, const uint64_t* crt_q, uint64_t* limbs) {
+  uint64_t acc[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  for (uint32_t j = 0; j < dk; ++j) {
+    const uint64_t y = shoup(res[j], crt_inv[2 * j], crt_inv[2 * j + 1], mods[j].q);
+    uint64_t carry = 0;
+    for (uint32_t l = 0; l < dk; ++l) {
+      const uint64_t plo = y * crt_part[j * dk + l], phi = mulhi64(y, crt_part[j * dk + l]);
+      const uint64_t s1 = acc[l] + plo;
+      const uint64_t c1 = s1 < plo;
+      const uint64_t s2 = s1 + carry;
+      const uint64_t c2 = s2 < s1;
+      acc[l] = s2;
+      carry = phi + c1 + c2;
+    }
+    for (uint32_t l = dk; l < 9 && carry; ++l) {
+      const uint64_t s1 = acc[l] + carry;
+      carry = s1 < carry;
+      acc[l] = s1;
+    }
+  }
+  for (uint32_t iter = 0; iter <= dk; ++iter) {
+    bool ge = acc[dk] != 0;
+    if (!ge) {
+      ge = true;
+      for (int l = (int)dk - 1; l >= 0; --l) {
+        if (acc[l] != crt_q[l]) {
+          ge = acc[l] > crt_q[l];
+          break;
+        }
+      }
+    }
+    if (!ge) break;
+    uint64_t borrow = 0;
+    for (uint32_t l = 0; l <= dk; ++l) {
+      const uint64_t ql = l < dk ? crt_q[l] : 0;
+      const uint64_t d1 = acc[l] - ql;
+      const uint64_t b1 = acc[l] < ql;
+      const uint64_t d2 = d1 - borrow;
+      const uint64_t b2 = d1 < borrow;
+      acc[l] = d2;
+      borrow = b1 | b2;
+    }
+  }
+  for (uint32_t l = 0; l < dk; ++l) limbs[l] = acc[l];
+}
+
+}  // namespace bfvgpu

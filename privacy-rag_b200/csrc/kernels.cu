@@ -1,0 +1,363 @@
+// BFV ciphertext-arithmetic kernels for sm_100a.
+//
+// Every transform-bearing kernel runs one RNS limb per thread block with the limb
+// resident in shared memory (ntt_core.cuh); the reference's separate elementwise
+// kernels (lift, product, decompose, moddown, gather, add_shift) become prologues
+// and epilogues of those transforms, so each limb crosses HBM once per kernel.
+//
+// Reference kernels restated (IV1 = implementation_v1/):
+//   k_ntt ............. `stage` (matrix.cu:52-58; switch.cu:47-58; ntt.cu:83-94; enc0.cu:45-56)
+//   k_lift_ntt ........ `lift` + forward stages (matrix.cu:48-51, :96)
+//   k_mac_intt ........ `product` + inverse stages (matrix.cu:59-63, :96), with the
+//                       sub_plain mask (bfv_matrix.inc:215-219) and the Enc(0) add
+//                       (bfv_matrix.inc:220-227) fused into the epilogue
+//   k_gather_targets .. `gather_c0` (matrix.cu:66-69) + rns_coefficient (bfv.cpp:138-147)
+//   k_ks_main ......... CPU apply_galois (keyswitch seal_adapter.cpp:50) + `decompose`,
+//                       forward stages, `product`, inverse stages (switch.cu:92-102, :146-149)
+//   k_ks_moddown ...... `moddown` (switch.cu:103-111) with the permuted c0 add
+//   k_enc0_x/k_moddown  PublicZero::evaluate (enc0.cu:74-89, :125-140)
+//   k_client_phase .... client_phase (ntt.cu:96-98, :181-199)
+//   k_token_* ......... TokenWeights::evaluate_device (resident.cu:71-107, :200-221)
+//   k_packing_prepare . packing_prepare (switch.cu:78-87)
+#include <cuda_runtime.h>
+
+#include "kernels.cuh"
+#include "block_ops.cuh"
+
+namespace bfvgpu {
+
+template <int LOGN>
+constexpr int threads_for() {
+  return ((1 << LOGN) / 16) < 512 ? ((1 << LOGN) / 16) : 512;
+}
+template <int LOGN>
+constexpr size_t smem_bytes() {
+  return (size_t)SmemWords<LOGN>::value * sizeof(uint64_t);
+}
+
+// ---------------------------------------------------------------------------------
+// transform-bearing kernels: one block per limb, bodies in block_ops.cuh
+// ---------------------------------------------------------------------------------
+template <int LOGN, bool INV>
+__global__ void __launch_bounds__(threads_for<LOGN>())
+    k_ntt(uint64_t* data, uint32_t prime_count, uint32_t prime_offset, const Modulus* mods, const ulonglong2* fwd,
+          const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_ntt<LOGN>(BlockExec{}, smem, blockIdx.x, INV, data, prime_count, prime_offset, mods, fwd, inv);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>())
+    k_lift_ntt(const uint64_t* ring, uint64_t* out, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
+  extern __shared__ uint64_t smem[];
+  op_lift_ntt<LOGN>(BlockExec{}, smem, blockIdx.x, ring, out, dk, mods, fwd);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>())
+    k_mac_intt(const uint64_t* in, const uint64_t* w, uint64_t* out, uint32_t inputs, uint32_t k, uint32_t dk,
+               const Modulus* mods, const ulonglong2* inv, ProtectArgs prot) {
+  extern __shared__ uint64_t smem[];
+  op_mac_intt<LOGN>(BlockExec{}, smem, blockIdx.x, in, w, out, inputs, k, dk, mods, inv, prot);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>())
+    k_ks_main(const uint64_t* cts, const uint64_t* key, uint64_t* acc, uint32_t elt, uint32_t k, uint32_t dk,
+              const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_ks_main<LOGN>(BlockExec{}, smem, blockIdx.x, cts, key, acc, elt, k, dk, mods, qjp, fwd, inv);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>())
+    k_ks_moddown(const uint64_t* acc, const uint64_t* cts, uint64_t* out, uint32_t ginv, uint32_t k, uint32_t dk,
+                 const Modulus* mods) {
+  extern __shared__ uint64_t smem[];
+  op_ks_moddown<LOGN>(BlockExec{}, smem, blockIdx.x, acc, cts, out, ginv, k, dk, mods);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>())
+    k_enc0_x(const uint64_t* samples, const uint64_t* pk, uint64_t* u_ntt, uint64_t* x, uint32_t k,
+             const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_enc0_x<LOGN>(BlockExec{}, smem, blockIdx.x, samples, pk, u_ntt, x, k, mods, fwd, inv);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>())
+    k_client_phase(uint64_t* data, const uint64_t* sk, uint32_t dk, const Modulus* mods, const ulonglong2* fwd,
+                   const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_client_phase<LOGN>(BlockExec{}, smem, blockIdx.x, data, sk, dk, mods, fwd, inv);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>())
+    k_token_lift_ntt(const uint64_t* ring, uint64_t* w, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
+  extern __shared__ uint64_t smem[];
+  op_token_lift_ntt<LOGN>(BlockExec{}, smem, blockIdx.x, ring, w, dk, mods, fwd);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>())
+    k_token_mac_intt(const uint64_t* in, const uint64_t* w, const uint64_t* scaled, uint64_t* out, uint32_t slots,
+                     uint32_t dk, const Modulus* mods, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_token_mac_intt<LOGN>(BlockExec{}, smem, blockIdx.x, in, w, scaled, out, slots, dk, mods, inv);
+}
+
+// c0 target gather (+ CRT): thread = (group, target)
+__global__ void k_gather_targets(const uint64_t* out, const uint64_t* targets, const uint32_t* counts,
+                                 uint32_t max_count, uint32_t dk, int logn, const Modulus* mods,
+                                 const uint64_t* crt_part, const uint64_t* crt_inv, const uint64_t* crt_q,
+                                 uint64_t* selected, uint64_t* crt) {
+  const uint64_t g = blockIdx.y;
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= counts[g]) return;
+  const uint64_t N = uint64_t(1) << logn;
+  const uint64_t idx = targets[g * max_count + i];
+  uint64_t res[8];
+  for (uint32_t p = 0; p < dk; ++p) {
+    res[p] = out[((g * 2) * dk + p) * N + idx];
+    selected[(g * dk + p) * max_count + i] = res[p];
+  }
+  if (crt) crt_target(res, dk, mods, crt_part, crt_inv, crt_q, crt + (g * max_count + i) * dk);
+}
+
+__global__ void k_moddown(const uint64_t* x, uint64_t* out, uint64_t groups, uint32_t k, uint32_t dk, int logn,
+                          const Modulus* mods) {
+  const uint64_t N = uint64_t(1) << logn;
+  const uint64_t total = groups * 2 * dk * N;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t i = e & (N - 1);
+    const uint64_t row = e >> logn;  // (g*2 + c)*dk + p
+    const uint32_t p = (uint32_t)(row % dk);
+    const uint64_t gc = row / dk;
+    const uint64_t* xr = x + gc * k * N;
+    out[e] = moddown_elem(xr[(uint64_t)p * N + i], xr[(uint64_t)(k - 1) * N + i], mods[p], mods[k - 1]);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// small elementwise kernels
+// ---------------------------------------------------------------------------------
+__global__ void k_packing_prepare(const uint64_t* left, const uint64_t* right, uint64_t* sum, uint64_t* diff,
+                                  uint32_t dk, int logn, uint32_t shift, const Modulus* mods) {
+  const uint64_t N = uint64_t(1) << logn;
+  const uint64_t total = 2 * (uint64_t)dk * N;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t j = e & (N - 1), base = e - j;
+    const uint64_t q = mods[(e >> logn) % dk].q;
+    const uint64_t src = (j + N - shift) & (N - 1);
+    uint64_t v = right[base + src];
+    if (j < shift) v = neg_mod(v, q);
+    sum[e] = add_mod(left[e], v, q);
+    diff[e] = sub_mod(left[e], v, q);
+  }
+}
+
+__global__ void k_add(uint64_t* a, const uint64_t* b, uint64_t polys, uint32_t dk, int logn, const Modulus* mods) {
+  const uint64_t total = polys << logn;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x)
+    a[e] = add_mod(a[e], b[e], mods[(e >> logn) % dk].q);
+}
+
+__global__ void k_check_canonical(const uint64_t* data, uint64_t polys, uint32_t count, uint32_t offset, int logn,
+                                  const Modulus* mods, uint32_t* bad) {
+  const uint64_t total = polys << logn;
+  uint32_t found = 0;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x)
+    found |= data[e] >= mods[offset + (e >> logn) % count].q;
+  if (__any_sync(0xffffffffu, found) && (threadIdx.x & 31) == 0) atomicOr(bad, 1u);
+}
+
+// ---------------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------------
+bool logn_supported(int logn) { return logn == 5 || logn == 6 || (logn >= 12 && logn <= 14); }
+
+#define BFV_DISPATCH(LOGN_VAR, ...)                      \
+  switch (LOGN_VAR) {                                     \
+    case 5: { constexpr int L_ = 5; __VA_ARGS__; } break;   \
+    case 6: { constexpr int L_ = 6; __VA_ARGS__; } break;   \
+    case 12: { constexpr int L_ = 12; __VA_ARGS__; } break; \
+    case 13: { constexpr int L_ = 13; __VA_ARGS__; } break; \
+    case 14: { constexpr int L_ = 14; __VA_ARGS__; } break; \
+    default: return cudaErrorInvalidValue;                \
+  }
+
+template <class K>
+static cudaError_t allow_smem(K kernel, size_t bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+template <int L>
+static cudaError_t configure_for() {
+  const size_t s = smem_bytes<L>();
+  cudaError_t e = cudaSuccess;
+  auto chk = [&](cudaError_t r) { if (e == cudaSuccess) e = r; };
+  chk(allow_smem(k_ntt<L, false>, s));
+  chk(allow_smem(k_ntt<L, true>, s));
+  chk(allow_smem(k_lift_ntt<L>, s));
+  chk(allow_smem(k_mac_intt<L>, s));
+  chk(allow_smem(k_ks_main<L>, s));
+  chk(allow_smem(k_ks_moddown<L>, (size_t(1) << L) * 8));
+  chk(allow_smem(k_enc0_x<L>, s));
+  chk(allow_smem(k_client_phase<L>, s));
+  if constexpr (L == 14) {
+    chk(allow_smem(k_token_lift_ntt<L>, s));
+    chk(allow_smem(k_token_mac_intt<L>, s));
+  }
+  return e;
+}
+
+cudaError_t configure_kernels(int logn) {
+  BFV_DISPATCH(logn, return configure_for<L_>());
+  return cudaSuccess;
+}
+
+static unsigned elementwise_blocks(uint64_t total) {
+  uint64_t b = (total + 255) / 256;
+  const uint64_t cap = 148ull * 16;
+  return (unsigned)(b < cap ? (b ? b : 1) : cap);
+}
+
+cudaError_t launch_ntt(const DevParams& P, uint64_t* data, uint64_t polys, uint32_t prime_count,
+                       uint32_t prime_offset, bool inverse, cudaStream_t st) {
+  if (!polys) return cudaSuccess;
+  BFV_DISPATCH(P.logn, {
+    if (inverse)
+      k_ntt<L_, true><<<(unsigned)polys, threads_for<L_>(), smem_bytes<L_>(), st>>>(data, prime_count, prime_offset,
+                                                                                 P.mod, P.fwd, P.inv);
+    else
+      k_ntt<L_, false><<<(unsigned)polys, threads_for<L_>(), smem_bytes<L_>(), st>>>(data, prime_count, prime_offset,
+                                                                                  P.mod, P.fwd, P.inv);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lift_ntt(const DevParams& P, const uint64_t* ring, uint64_t* out, uint64_t blocks,
+                            cudaStream_t st) {
+  if (!blocks) return cudaSuccess;
+  BFV_DISPATCH(P.logn, {
+    k_lift_ntt<L_><<<(unsigned)(blocks * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(ring, out, P.dk, P.mod,
+                                                                                            P.fwd);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mac_intt(const DevParams& P, const uint64_t* in, const uint64_t* w, uint64_t* out,
+                            uint64_t inputs, uint64_t groups, const Protect& prot, cudaStream_t st) {
+  if (!groups) return cudaSuccess;
+  ProtectArgs a{prot.mask, prot.enc0_x, P.q_mod_t, P.upper_half, P.t, P.tlog};
+  BFV_DISPATCH(P.logn, {
+    k_mac_intt<L_><<<(unsigned)(groups * 2 * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(
+        in, w, out, (uint32_t)inputs, P.k, P.dk, P.mod, P.inv, a);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_targets(const DevParams& P, const uint64_t* out, const uint64_t* targets,
+                                  const uint32_t* counts, uint32_t max_count, uint64_t groups, uint64_t* selected,
+                                  uint64_t* crt, cudaStream_t st) {
+  if (!groups || !max_count) return cudaSuccess;
+  if (P.dk > 8) return cudaErrorInvalidValue;
+  dim3 grid((max_count + 127) / 128, (unsigned)groups);
+  k_gather_targets<<<grid, 128, 0, st>>>(out, targets, counts, max_count, P.dk, P.logn, P.mod, P.crt_part,
+                                         P.crt_inv, P.crt_q, selected, crt);
+  return cudaGetLastError();
+}
+
+static uint32_t inverse_mod_2n(uint32_t g, uint32_t two_n) {
+  // g odd; the units mod 2^m have exponent dividing 2^(m-1) = n, so g^(n-1) = g^-1.
+  uint64_t r = 1, b = g % two_n, e = two_n / 2 - 1;
+  while (e) {
+    if (e & 1) r = (r * b) % two_n;
+    b = (b * b) % two_n;
+    e >>= 1;
+  }
+  return (uint32_t)r;
+}
+
+cudaError_t launch_keyswitch(const DevParams& P, const uint64_t* cts, const uint64_t* key, uint32_t elt,
+                             uint64_t count, uint64_t* acc, uint64_t* out, cudaStream_t st) {
+  if (!count) return cudaSuccess;
+  if (P.k != P.dk + 1) return cudaErrorInvalidValue;
+  const uint32_t ginv = inverse_mod_2n(elt, 2 * P.n);
+  BFV_DISPATCH(P.logn, {
+    k_ks_main<L_><<<(unsigned)(count * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(cts, key, acc, elt, P.k,
+                                                                                        P.dk, P.mod, P.qjp, P.fwd,
+                                                                                        P.inv);
+    k_ks_moddown<L_><<<(unsigned)(count * P.dk), threads_for<L_>(), (size_t(1) << L_) * 8, st>>>(acc, cts, out, ginv,
+                                                                                                 P.k, P.dk, P.mod);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_enc0_x(const DevParams& P, const uint64_t* samples, const uint64_t* pk, uint64_t* u_ntt,
+                          uint64_t* x, uint64_t groups, cudaStream_t st) {
+  if (!groups) return cudaSuccess;
+  if (P.k != P.dk + 1) return cudaErrorInvalidValue;
+  BFV_DISPATCH(P.logn, {
+    k_enc0_x<L_><<<(unsigned)(groups * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(samples, pk, u_ntt, x, P.k,
+                                                                                       P.mod, P.fwd, P.inv);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moddown(const DevParams& P, const uint64_t* x, uint64_t* out, uint64_t groups, cudaStream_t st) {
+  if (!groups) return cudaSuccess;
+  if (P.k != P.dk + 1) return cudaErrorInvalidValue;
+  const uint64_t total = groups * 2 * P.dk * P.n;
+  k_moddown<<<elementwise_blocks(total), 256, 0, st>>>(x, out, groups, P.k, P.dk, P.logn, P.mod);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_client_phase(const DevParams& P, uint64_t* data, const uint64_t* sk, uint64_t batches,
+                                cudaStream_t st) {
+  if (!batches) return cudaSuccess;
+  BFV_DISPATCH(P.logn, {
+    k_client_phase<L_><<<(unsigned)(batches * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(data, sk, P.dk,
+                                                                                               P.mod, P.fwd, P.inv);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_check_canonical(const DevParams& P, const uint64_t* data, uint64_t polys, uint32_t prime_count,
+                                   uint32_t prime_offset, uint32_t* bad, cudaStream_t st) {
+  if (!polys) return cudaSuccess;
+  k_check_canonical<<<elementwise_blocks(polys << P.logn), 256, 0, st>>>(data, polys, prime_count, prime_offset,
+                                                                         P.logn, P.mod, bad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_token_evaluate(const DevParams& P, const uint64_t* inputs, uint64_t slots, const uint64_t* ring,
+                                  const uint64_t* scaled, uint64_t* wscratch, uint64_t* acc, uint64_t* out,
+                                  cudaStream_t st) {
+  (void)acc;
+  if (P.logn != 14) return cudaErrorInvalidValue;
+  constexpr int L_ = 14;
+  k_token_lift_ntt<L_><<<kTokenBlocks * P.dk, threads_for<L_>(), smem_bytes<L_>(), st>>>(ring, wscratch, P.dk, P.mod,
+                                                                                        P.fwd);
+  k_token_mac_intt<L_><<<(unsigned)(slots * 2 * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(
+      inputs, wscratch, scaled, out, (uint32_t)slots, P.dk, P.mod, P.inv);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_packing_prepare(const DevParams& P, const uint64_t* left, const uint64_t* right, uint64_t* sum,
+                                   uint64_t* diff, unsigned level, cudaStream_t st) {
+  const uint64_t total = 2 * (uint64_t)P.dk * P.n;
+  k_packing_prepare<<<elementwise_blocks(total), 256, 0, st>>>(left, right, sum, diff, P.dk, P.logn,
+                                                              P.n >> (level + 1), P.mod);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint64_t polys, cudaStream_t st) {
+  if (!polys) return cudaSuccess;
+  k_add<<<elementwise_blocks(polys << P.logn), 256, 0, st>>>(a, b, polys, P.dk, P.logn, P.mod);
+  return cudaGetLastError();
+}
+
+}  // namespace bfvgpu

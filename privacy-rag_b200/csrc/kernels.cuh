@@ -1,0 +1,103 @@
+// Internal launch API of the BFV kernels (device pointers, one CUDA stream).
+// The C ABI in bfvgpu.cu builds the reference-shaped objects on top of these.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "arith.cuh"
+
+namespace bfvgpu {
+
+// Device view of a parameter context.
+struct DevParams {
+  int logn = 0;
+  uint32_t n = 0;
+  uint32_t k = 0;   // primes held (data + special)
+  uint32_t dk = 0;  // data primes
+  uint64_t t = 0;
+  int tlog = 0;     // log2 t when t is a power of two, else 0
+  uint64_t q_mod_t = 0, upper_half = 0;
+  const Modulus* mod = nullptr;       // [k]
+  const ulonglong2* fwd = nullptr;    // [k][n]
+  const ulonglong2* inv = nullptr;    // [k][n]
+  const uint64_t* qjp = nullptr;      // [dk][k]: q_j mod q_p
+  const uint64_t* crt_part = nullptr; // [dk][dk] limbs of Q/q_j
+  const uint64_t* crt_inv = nullptr;  // [dk][2] Shoup pair of (Q/q_j)^-1 mod q_j
+  const uint64_t* crt_q = nullptr;    // [dk] limbs of Q
+};
+
+// Smallest and largest supported log2(n).
+constexpr int kMinLogN = 5;
+constexpr int kMaxLogN = 14;
+bool logn_supported(int logn);
+
+// Opt the kernels into large dynamic shared memory on the current device.
+cudaError_t configure_kernels(int logn);
+
+// In-place batched transform of [polys][n]; poly i uses prime offset + i % count.
+cudaError_t launch_ntt(const DevParams& P, uint64_t* data, uint64_t polys, uint32_t prime_count,
+                       uint32_t prime_offset, bool inverse, cudaStream_t st);
+
+// Centred lift of ring-59 words [blocks][n] into each data prime and forward NTT:
+// out [blocks][dk][n].
+cudaError_t launch_lift_ntt(const DevParams& P, const uint64_t* ring, uint64_t* out, uint64_t blocks,
+                            cudaStream_t st);
+
+// Optional epilogue of the ct-pt product: plaintext mask (c0 -= Delta-scaled mask)
+// and Enc(0) re-randomisation from pre-moddown key-level polys x [2][k][n].
+struct Protect {
+  const uint64_t* mask = nullptr;      // [groups][n] ring-59 words, or null
+  const uint64_t* enc0_x = nullptr;    // [groups][2][k][n], or null
+};
+
+// out[g][c][p] = INTT( sum_b in[b][c][p] . w[g][b][p] )  (+ protect epilogue)
+// in [inputs][2][dk][n] NTT form; w [groups][inputs][dk][n] NTT form.
+cudaError_t launch_mac_intt(const DevParams& P, const uint64_t* in, const uint64_t* w, uint64_t* out,
+                            uint64_t inputs, uint64_t groups, const Protect& prot, cudaStream_t st);
+
+// selected[g][p][i] = c0[g][p][targets[g*max + i]] for i < counts[g]; if crt != null,
+// crt[g][i][dk] = the CRT of the dk residues as dk 64-bit limbs (little endian).
+cudaError_t launch_gather_targets(const DevParams& P, const uint64_t* out /*[groups][2][dk][n]*/,
+                                  const uint64_t* targets, const uint32_t* counts, uint32_t max_count,
+                                  uint64_t groups, uint64_t* selected, uint64_t* crt, cudaStream_t st);
+
+// Galois automorphism g then keyswitch of `count` ciphertexts [count][2][dk][n] with
+// key [dk][2][k][n] (NTT form).  acc is scratch [count][2][k][n]; out [count][2][dk][n].
+cudaError_t launch_keyswitch(const DevParams& P, const uint64_t* cts, const uint64_t* key, uint32_t elt,
+                             uint64_t count, uint64_t* acc, uint64_t* out, cudaStream_t st);
+
+// Enc(0) pre-moddown polys: x [groups][2][k][n] = INTT(NTT(u) . pk_c) + e_c with
+// samples [groups][3][k][n]; scratch u_ntt [groups][k][n].
+cudaError_t launch_enc0_x(const DevParams& P, const uint64_t* samples, const uint64_t* pk, uint64_t* u_ntt,
+                          uint64_t* x, uint64_t groups, cudaStream_t st);
+
+// Divide-and-round by the special prime: x [groups][2][k][n] -> out [groups][2][dk][n].
+cudaError_t launch_moddown(const DevParams& P, const uint64_t* x, uint64_t* out, uint64_t groups,
+                           cudaStream_t st);
+
+// c1 . s for each data prime: data [batches][dk][n] in place, sk [dk][n] NTT form.
+cudaError_t launch_client_phase(const DevParams& P, uint64_t* data, const uint64_t* sk, uint64_t batches,
+                                cudaStream_t st);
+
+// Checks canonical residues of [polys][n] (prime offset + i % count); sets *bad to 1
+// if any word is >= its prime.
+cudaError_t launch_check_canonical(const DevParams& P, const uint64_t* data, uint64_t polys,
+                                   uint32_t prime_count, uint32_t prime_offset, uint32_t* bad,
+                                   cudaStream_t st);
+
+// Resident token product (TokenWeights::evaluate_device): inputs [19][slots][2][dk][n]
+// NTT form, ring [19][8192] weights, scaled [slots][dk]; weight scratch [19][dk][n];
+// out [slots][2][dk][n] after add_shift.
+cudaError_t launch_token_evaluate(const DevParams& P, const uint64_t* inputs, uint64_t slots,
+                                  const uint64_t* ring, const uint64_t* scaled, uint64_t* wscratch,
+                                  uint64_t* acc, uint64_t* out, cudaStream_t st);
+
+// Acyclic packing merge prologue (Switch::packing_prepare): sum = L + X^s R and
+// diff = sigma_g(L - X^s R), g = 2^(level+1)+1, for [2][dk][n] ciphertexts.
+cudaError_t launch_packing_prepare(const DevParams& P, const uint64_t* left, const uint64_t* right,
+                                   uint64_t* sum, uint64_t* diff, unsigned level, cudaStream_t st);
+// a += b on [polys][n] data-prime polys.
+cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint64_t polys, cudaStream_t st);
+
+}  // namespace bfvgpu

@@ -1,0 +1,242 @@
+// Shared-memory-resident negacyclic NTT / inverse NTT of one RNS limb per thread block.
+//
+// Transform definition (the reference's stage kernels, IV1/experiments/matrix_gpu/
+// matrix.cu:52-58 and :79, and every other `stage` copy):
+//   forward  natural -> bit-reversed, Cooley-Tukey level l has gap n>>(l+1) and uses
+//            twiddle table entry 2^l + group;
+//   inverse  bit-reversed -> natural, Gentleman-Sande level l has gap 2^l and uses
+//            entry n-(n>>l)+1+group; the result is scaled by n^-1.
+// Tables hold {w, floor(w 2^64/q)} pairs (ulonglong2) in that layout.
+//
+// B200 schedule: instead of one global-memory launch per level (14 launches for
+// n = 16384 in the reference), one thread block keeps the whole limb in shared memory
+// (padded one word per 16 to spread 64-bit accesses over the 32 banks) and runs the
+// log2(n) levels as 3 or 4 passes of radix-16 / radix-8 butterfly units held in
+// registers.  The first pass reads through a loader functor (global memory, with any
+// fused prologue: lift, Galois pre-negation, digit reduction, multiply-accumulate) and
+// the last pass writes through a storer functor (fused epilogue).  Values stay lazy
+// (forward in [0,4q), inverse in [0,2q)) between levels and are made canonical once.
+//
+// Every pass is written as a per-unit function driven by an executor, so the exact
+// index arithmetic also runs on the host (tests/emu) against the CPU oracle.
+#pragma once
+#include "arith.cuh"
+
+#if !defined(__CUDACC__)
+struct ulonglong2 {
+  unsigned long long x, y;
+};
+#endif
+
+namespace bfvgpu {
+
+// Padded shared-memory word index: one spare word after every 16.
+BFV_HD int spad(int i) { return i + (i >> 4); }
+template <int LOGN>
+struct SmemWords {
+  static constexpr int value = (1 << LOGN) + ((1 << LOGN) >> 4);
+};
+
+// Pass schedule: radix-16 passes first, then radix-8 (forward); reversed for inverse.
+template <int LOGN>
+struct Schedule {
+  static constexpr int passes = LOGN <= 4 ? 1 : (LOGN == 5 ? 2 : (LOGN + 3) / 4);
+  static constexpr int fours = LOGN <= 4 ? 0 : (LOGN == 5 ? 0 : LOGN - 3 * passes);
+  // radix (log2) of forward pass p
+  static constexpr int fwd_r(int p) {
+    return LOGN <= 4 ? LOGN : (LOGN == 5 ? (p == 0 ? 3 : 2) : (p < fours ? 4 : 3));
+  }
+  static constexpr int fwd_level(int p) {
+    int l = 0;
+    for (int i = 0; i < p; ++i) l += fwd_r(i);
+    return l;
+  }
+  static constexpr int inv_r(int p) { return fwd_r(passes - 1 - p); }
+  static constexpr int inv_level(int p) {
+    int l = 0;
+    for (int i = 0; i < p; ++i) l += inv_r(i);
+    return l;
+  }
+};
+
+BFV_HD uint64_t reduce_4q(uint64_t v, uint64_t q) {
+  const uint64_t two_q = 2 * q;
+  if (v >= two_q) v -= two_q;
+  if (v >= q) v -= q;
+  return v;
+}
+
+// One radix-2^R Cooley-Tukey unit of forward pass starting at level L.
+template <int LOGN, int R, bool FIRST, bool LAST, class Ld, class St>
+BFV_HD void fwd_unit(uint64_t* s, int u, int L, const ulonglong2* tw, uint64_t q, const Ld& ld,
+                     const St& st) {
+  constexpr int K = 1 << R;
+  const int shift = LOGN - L - R;  // smallest gap of the pass is 2^shift
+  const int o = u & ((1 << shift) - 1);
+  const int gl = u >> shift;
+  const int base = (gl << (LOGN - L)) + o;
+  uint64_t x[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int idx = base + (k << shift);
+    if constexpr (FIRST)
+      x[k] = ld(idx);
+    else
+      x[k] = s[spad(idx)];
+  }
+  const uint64_t two_q = 2 * q;
+#pragma unroll
+  for (int t = 0; t < R; ++t) {
+    const int hs = R - t - 1;  // half = 2^hs pairs per twiddle group
+    ulonglong2 w = tw[(1 << (L + t)) + (gl << t)];
+#pragma unroll
+    for (int pr = 0; pr < K / 2; ++pr) {
+      const int j = pr >> hs, kk = pr & ((1 << hs) - 1);
+      const int k = (j << (hs + 1)) + kk;
+      if (kk == 0 && j > 0) w = tw[(1 << (L + t)) + (gl << t) + j];
+      uint64_t a = x[k];
+      if (a >= two_q) a -= two_q;
+      const uint64_t b = shoup_lazy(x[k + (1 << hs)], w.x, w.y, q);
+      x[k] = a + b;
+      x[k + (1 << hs)] = a + two_q - b;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int idx = base + (k << shift);
+    if constexpr (LAST)
+      st(idx, reduce_4q(x[k], q));
+    else
+      s[spad(idx)] = x[k];
+  }
+}
+
+// One radix-2^R Gentleman-Sande unit of inverse pass starting at level L.
+template <int LOGN, int R, bool FIRST, bool LAST, class Ld, class St>
+BFV_HD void inv_unit(uint64_t* s, int u, int L, const ulonglong2* tw, uint64_t q, uint64_t invn,
+                     uint64_t invn_q, const Ld& ld, const St& st) {
+  constexpr int K = 1 << R;
+  constexpr int N = 1 << LOGN;
+  const int o = u & ((1 << L) - 1);
+  const int gg = u >> L;
+  const int base = (gg << (L + R)) + o;
+  uint64_t x[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int idx = base + (k << L);
+    if constexpr (FIRST)
+      x[k] = ld(idx);
+    else
+      x[k] = s[spad(idx)];
+  }
+  const uint64_t two_q = 2 * q;
+#pragma unroll
+  for (int t = 0; t < R; ++t) {
+    const int l = L + t;
+    const int root0 = N - (N >> l) + 1 + (gg << (R - t - 1));
+    ulonglong2 w = tw[root0];
+#pragma unroll
+    for (int pr = 0; pr < K / 2; ++pr) {
+      const int j = pr >> t, kk = pr & ((1 << t) - 1);
+      const int k = (j << (t + 1)) + kk;
+      if (kk == 0 && j > 0) w = tw[root0 + j];
+      const uint64_t a = x[k], b = x[k + (1 << t)];
+      uint64_t sum = a + b;
+      if (sum >= two_q) sum -= two_q;
+      x[k] = sum;
+      x[k + (1 << t)] = shoup_lazy(a + two_q - b, w.x, w.y, q);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int idx = base + (k << L);
+    if constexpr (LAST)
+      st(idx, shoup(x[k], invn, invn_q, q));
+    else
+      s[spad(idx)] = x[k];
+  }
+}
+
+// Executors: device (threads of one block + __syncthreads) and host (all units in turn).
+#if defined(__CUDACC__)
+struct BlockExec {
+  template <class F>
+  __device__ __forceinline__ void run(int units, F&& f) const {
+    for (int u = threadIdx.x; u < units; u += blockDim.x) f(u);
+  }
+  __device__ __forceinline__ void sync() const { __syncthreads(); }
+};
+#endif
+struct HostExec {
+  template <class F>
+  void run(int units, F&& f) const {
+    for (int u = 0; u < units; ++u) f(u);
+  }
+  void sync() const {}
+};
+
+template <int LOGN, int P, class Ex, class Ld, class St>
+BFV_HD void fwd_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t q, const Ld& ld,
+                       const St& st) {
+  using S = Schedule<LOGN>;
+  if constexpr (P < S::passes) {
+    constexpr int R = S::fwd_r(P);
+    constexpr int L = S::fwd_level(P);
+    constexpr bool first = P == 0, last = P == S::passes - 1;
+    ex.run(1 << (LOGN - R), [&](int u) { fwd_unit<LOGN, R, first, last>(s, u, L, tw, q, ld, st); });
+    ex.sync();
+    fwd_passes<LOGN, P + 1>(ex, s, tw, q, ld, st);
+  }
+}
+
+template <int LOGN, int P, class Ex, class Ld, class St>
+BFV_HD void inv_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t q, uint64_t invn,
+                       uint64_t invn_q, const Ld& ld, const St& st) {
+  using S = Schedule<LOGN>;
+  if constexpr (P < S::passes) {
+    constexpr int R = S::inv_r(P);
+    constexpr int L = S::inv_level(P);
+    constexpr bool first = P == 0, last = P == S::passes - 1;
+    ex.run(1 << (LOGN - R),
+           [&](int u) { inv_unit<LOGN, R, first, last>(s, u, L, tw, q, invn, invn_q, ld, st); });
+    ex.sync();
+    inv_passes<LOGN, P + 1>(ex, s, tw, q, invn, invn_q, ld, st);
+  }
+}
+
+// Forward NTT of one limb: ld(i) gives input coefficient i (< 4q), st(i, v) receives
+// canonical NTT slot i.  Ends with a block-wide barrier.
+template <int LOGN, class Ex, class Ld, class St>
+BFV_HD void ntt_forward(const Ex& ex, uint64_t* s, const ulonglong2* tw, const Modulus& m, const Ld& ld,
+                        const St& st) {
+  fwd_passes<LOGN, 0>(ex, s, tw, m.q, ld, st);
+}
+
+// Inverse NTT of one limb: ld(i) gives NTT slot i (< 2q), st(i, v) receives canonical
+// coefficient i.  Ends with a block-wide barrier.
+template <int LOGN, class Ex, class Ld, class St>
+BFV_HD void ntt_inverse(const Ex& ex, uint64_t* s, const ulonglong2* tw, const Modulus& m, const Ld& ld,
+                        const St& st) {
+  inv_passes<LOGN, 0>(ex, s, tw, m.q, m.invn, m.invn_q, ld, st);
+}
+
+// Bit reversal of an index of LOGN bits.
+BFV_HD int bit_reverse(int x, int logn) {
+#if defined(__CUDA_ARCH__)
+  return (int)(__brev((unsigned)x) >> (32 - logn));
+#else
+  unsigned r = 0;
+  for (int i = 0; i < logn; ++i) r |= ((unsigned)(x >> i) & 1u) << (logn - 1 - i);
+  return (int)r;
+#endif
+}
+
+// NTT-slot permutation of the Galois automorphism X -> X^g: with slot i holding the
+// evaluation at psi^(2 brv(i)+1), NTT(sigma_g a)[i] = NTT(a)[galois_slot(i)].
+BFV_HD int galois_slot(int i, uint32_t g, int logn) {
+  const uint32_t two_n_mask = (2u << logn) - 1u;
+  const uint32_t e = ((2u * (uint32_t)bit_reverse(i, logn) + 1u) * g) & two_n_mask;
+  return bit_reverse((int)(e >> 1), logn);
+}
+
+}  // namespace bfvgpu

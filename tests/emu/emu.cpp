@@ -1,0 +1,154 @@
+// Host emulation of the CUDA kernel bodies (TEST INFRASTRUCTURE).
+//
+// Compiles privacy-rag_b200/csrc/block_ops.cuh with the host compiler and runs every
+// thread block's work units in turn (HostExec), so the exact index arithmetic, pass
+// schedule, prologues and epilogues of the kernels are checked against the CPU oracle
+// without a GPU, and before any of them is launched on one.  Constants (the 16-word
+// per-prime records and the twiddle tables) come from the product library's host-only
+// context, so they are the same values the kernels receive.
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "block_ops.cuh"
+
+using namespace bfvgpu;
+
+namespace {
+struct Tabs {
+  std::vector<Modulus> mods;
+  const ulonglong2* fwd;
+  const ulonglong2* inv;
+};
+Tabs tabs(uint32_t k, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv) {
+  Tabs t;
+  t.mods.resize(k);
+  std::memcpy(t.mods.data(), mods16, k * sizeof(Modulus));
+  t.fwd = reinterpret_cast<const ulonglong2*>(fwd);
+  t.inv = reinterpret_cast<const ulonglong2*>(inv);
+  return t;
+}
+uint32_t inv_mod_2n(uint32_t g, uint32_t two_n) {
+  uint64_t r = 1, b = g % two_n, e = two_n / 2 - 1;
+  while (e) {
+    if (e & 1) r = (r * b) % two_n;
+    b = (b * b) % two_n;
+    e >>= 1;
+  }
+  return (uint32_t)r;
+}
+}  // namespace
+
+#define EMU_DISPATCH(LOGN_VAR, ...)                        \
+  switch (LOGN_VAR) {                                      \
+    case 5: { constexpr int L_ = 5; __VA_ARGS__; } break;   \
+    case 6: { constexpr int L_ = 6; __VA_ARGS__; } break;   \
+    case 12: { constexpr int L_ = 12; __VA_ARGS__; } break; \
+    case 13: { constexpr int L_ = 13; __VA_ARGS__; } break; \
+    case 14: { constexpr int L_ = 14; __VA_ARGS__; } break; \
+    default: return -1;                                    \
+  }
+
+extern "C" {
+
+int emu_ntt(int logn, uint32_t k, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv, uint64_t* data,
+            uint64_t polys, uint32_t prime_count, uint32_t prime_offset, int inverse) {
+  Tabs T = tabs(k, mods16, fwd, inv);
+  EMU_DISPATCH(logn, {
+    std::vector<uint64_t> s(SmemWords<L_>::value);
+    for (uint64_t b = 0; b < polys; ++b)
+      op_ntt<L_>(HostExec{}, s.data(), b, inverse != 0, data, prime_count, prime_offset, T.mods.data(), T.fwd, T.inv);
+  });
+  return 0;
+}
+
+// cts [count][2][dk][n], key [dk][2][k][n] -> out [count][2][dk][n]
+int emu_keyswitch(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv,
+                  const uint64_t* cts, uint64_t count, const uint64_t* key, uint32_t elt, uint64_t* out) {
+  Tabs T = tabs(k, mods16, fwd, inv);
+  const uint64_t n = 1ull << logn;
+  std::vector<uint64_t> qjp((size_t)dk * k);
+  for (uint32_t j = 0; j < dk; ++j)
+    for (uint32_t p = 0; p < k; ++p) qjp[j * k + p] = T.mods[j].q % T.mods[p].q;
+  std::vector<uint64_t> acc(count * 2 * k * n);
+  const uint32_t ginv = inv_mod_2n(elt, 2 * (uint32_t)n);
+  EMU_DISPATCH(logn, {
+    std::vector<uint64_t> s(SmemWords<L_>::value);
+    for (uint64_t b = 0; b < count * k; ++b)
+      op_ks_main<L_>(HostExec{}, s.data(), b, cts, key, acc.data(), elt, k, dk, T.mods.data(), qjp.data(), T.fwd,
+                     T.inv);
+    std::vector<uint64_t> s2(n);
+    for (uint64_t b = 0; b < count * dk; ++b)
+      op_ks_moddown<L_>(HostExec{}, s2.data(), b, acc.data(), cts, out, ginv, k, dk, T.mods.data());
+  });
+  return 0;
+}
+
+// Full protected matrix evaluation for `groups` groups:
+// cts [inputs][2][dk][n] coefficient form; ring [groups][inputs][n]; mask [groups][n]
+// or null; samples [groups][3][k][n] or null (pk [2][k][n]); out [groups][2][dk][n].
+int emu_matrix(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv,
+               const uint64_t* cts, uint64_t inputs, const uint64_t* ring, uint64_t groups, const uint64_t* mask,
+               const uint64_t* samples, const uint64_t* pk, uint64_t q_mod_t, uint64_t upper_half, uint64_t t,
+               int tlog, uint64_t* out) {
+  Tabs T = tabs(k, mods16, fwd, inv);
+  const uint64_t n = 1ull << logn;
+  std::vector<uint64_t> in(cts, cts + inputs * 2 * dk * n);
+  std::vector<uint64_t> w(groups * inputs * dk * n);
+  std::vector<uint64_t> u_ntt(groups * k * n), x(groups * 2 * k * n);
+  EMU_DISPATCH(logn, {
+    std::vector<uint64_t> s(SmemWords<L_>::value);
+    for (uint64_t b = 0; b < inputs * 2 * dk; ++b)
+      op_ntt<L_>(HostExec{}, s.data(), b, false, in.data(), dk, 0, T.mods.data(), T.fwd, T.inv);
+    for (uint64_t b = 0; b < groups * inputs * dk; ++b)
+      op_lift_ntt<L_>(HostExec{}, s.data(), b, ring, w.data(), dk, T.mods.data(), T.fwd);
+    ProtectArgs prot{mask, nullptr, q_mod_t, upper_half, t, tlog};
+    if (samples) {
+      for (uint64_t b = 0; b < groups * k; ++b)
+        op_enc0_x<L_>(HostExec{}, s.data(), b, samples, pk, u_ntt.data(), x.data(), k, T.mods.data(), T.fwd, T.inv);
+      prot.enc0_x = x.data();
+    }
+    for (uint64_t b = 0; b < groups * 2 * dk; ++b)
+      op_mac_intt<L_>(HostExec{}, s.data(), b, in.data(), w.data(), out, (uint32_t)inputs, k, dk, T.mods.data(),
+                      T.inv, prot);
+  });
+  return 0;
+}
+
+// data [batches][dk][n] in place, sk [dk][n] NTT form.
+int emu_client_phase(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd,
+                     const uint64_t* inv, uint64_t* data, const uint64_t* sk, uint64_t batches) {
+  Tabs T = tabs(k, mods16, fwd, inv);
+  EMU_DISPATCH(logn, {
+    std::vector<uint64_t> s(SmemWords<L_>::value);
+    for (uint64_t b = 0; b < batches * dk; ++b)
+      op_client_phase<L_>(HostExec{}, s.data(), b, data, sk, dk, T.mods.data(), T.fwd, T.inv);
+  });
+  return 0;
+}
+
+// res [count][dk] residues -> limbs [count][dk]; CRT constants from the caller.
+int emu_crt(uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* res, uint64_t count,
+            const uint64_t* part, const uint64_t* cinv, const uint64_t* qlimbs, uint64_t* limbs) {
+  std::vector<Modulus> mods(k);
+  std::memcpy(mods.data(), mods16, k * sizeof(Modulus));
+  for (uint64_t i = 0; i < count; ++i) crt_target(res + i * dk, dk, mods.data(), part, cinv, qlimbs, limbs + i * dk);
+  return 0;
+}
+
+// Token product: cts_ntt [19][slots][2][dk][n] NTT form, ring [19][8192], scaled [slots][dk].
+int emu_token(uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv,
+              const uint64_t* cts_ntt, uint64_t slots, const uint64_t* ring, const uint64_t* scaled, uint64_t* out) {
+  Tabs T = tabs(k, mods16, fwd, inv);
+  constexpr int L_ = 14;
+  const uint64_t n = 1ull << L_;
+  std::vector<uint64_t> w(19 * dk * n), s(SmemWords<L_>::value);
+  for (uint64_t b = 0; b < 19 * dk; ++b)
+    op_token_lift_ntt<L_>(HostExec{}, s.data(), b, ring, w.data(), dk, T.mods.data(), T.fwd);
+  for (uint64_t b = 0; b < slots * 2 * dk; ++b)
+    op_token_mac_intt<L_>(HostExec{}, s.data(), b, cts_ntt, w.data(), scaled, out, (uint32_t)slots, dk,
+                          T.mods.data(), T.inv);
+  return 0;
+}
+
+}  // extern "C"
