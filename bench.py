@@ -1,0 +1,390 @@
+"""Benchmark of the B200 BFV hot path (one JSON line on rank 0).
+
+Headline (BASELINE.json metric, config 2): Galois automorphism + keyswitch of 256
+seeded random ciphertexts by rotations r = 1..128 (Galois element 3^r mod 2n), n = 8192,
+four ~50-bit ciphertext primes + one 60-bit special prime, t = 65537, dnum = 4 (alpha = 1).
+One step = all 32,768 keyswitches.  Secondary (config 1): NTT round trips of
+64 ciphertexts x 2 polys x 3 limbs at n = 4096.
+
+  value  keyswitches/s with inputs resident in HBM (device entry point)
+  e2e    the same through the reference-facing object API (bfvgpu.Switch.apply_many,
+         host buffers, pinned), H2D of each batch and D2H of every result inside the
+         timed region -- the reference's Switch::apply contract
+  cpu_baseline  the CPU oracle (restatement of the reference's algorithm) on the host
+         cores, a bounded sample
+
+Multi-GPU (torchrun): one rank per GPU, each runs the full config-2 workload on its
+own seeded inputs (independent ciphertexts, no data-path collective): weak scaling;
+value = all ranks' keyswitches / max-over-ranks time.
+
+`--impl reference` times the reference algorithm's CPU implementation (the oracle;
+the SEAL-based original cannot be built here) on all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "privacy-rag_b200")
+
+N2 = 8192
+BITS2 = [50, 50, 50, 50, 60]
+T2 = 65537
+CTS = 256
+ROTATIONS = 128
+ALG_BYTES_PER_KS = 2 * 4 * N2 * 8 * 2 + (4 * 2 * 5 * N2 * 8) // CTS  # ct in + ct out + key/256
+N1 = 4096
+BITS1 = [36, 36, 37]
+NTT_POLYS = 384  # 64 cts x 2 polys x 3 limbs
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def env_rank():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(
+        os.environ.get("LOCAL_RANK", "0"))
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, device: int):
+        self.device = device
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        def run():
+            q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", "-i", str(self.device), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                         timeout=5).stdout.strip()
+                    if out:
+                        self.rows.append([x.strip() for x in out.split(",")])
+                except Exception:
+                    return
+                self._stop.wait(0.2)
+
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit())
+        mx = max((float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 4 + i and "Active" in r[4 + i]
+                          and "Not" not in r[4 + i]})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def galois_elements(n: int, rotations: int):
+    return [pow(3, r, 2 * n) for r in range(1, rotations + 1)]
+
+
+def cpu_count() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_keyswitch_sample(seconds: float = 12.0):
+    """Oracle keyswitch on all host cores until ~`seconds` of wall time are spent."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    primes = O.coeff_modulus(N2, BITS2)
+    oc = O.Ctx(N2, primes, data_k=4, t=T2)
+    cores = cpu_count()
+    cts = oc.uniform(101, cores * 2 * 4).reshape(cores, 2, 4, N2)
+    key = oc.uniform(102, 4 * 2 * 5, prime_count=5).reshape(4, 2, 5, N2)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        oc.keyswitch_many(cts, key, [3], threads=cores)
+        done += cores
+    dt = time.perf_counter() - t0
+    return done / dt, cores, f"{done} keyswitches (n=8192, 4+1 primes) on {cores} threads in {dt:.1f}s"
+
+
+def cpu_ntt_sample(seconds: float = 4.0):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    primes = O.coeff_modulus(N1, BITS1)
+    oc = O.Ctx(N1, primes, data_k=3, t=T2)
+    cores = cpu_count()
+    data = oc.uniform(103, NTT_POLYS)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        f = oc.ntt(data, prime_count=3, threads=cores)
+        oc.ntt(f, prime_count=3, inverse=True, threads=cores)
+        done += 2 * NTT_POLYS
+    dt = time.perf_counter() - t0
+    return done / dt, cores
+
+
+# ----------------------------------------------------------------------------------------------
+def run_reference(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return 0
+    cores = cpu_count()
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    primes = O.coeff_modulus(N2, BITS2)
+    oc = O.Ctx(N2, primes, data_k=4, t=T2)
+    cts = oc.uniform(201, cores * 2 * 4).reshape(cores, 2, 4, N2)
+    key = oc.uniform(202, 4 * 2 * 5, prime_count=5).reshape(4, 2, 5, N2)
+    for _ in range(args.warmup):
+        oc.keyswitch_many(cts[:1], key, [3], threads=1)
+    times = []
+    for s in range(args.steps):
+        t0 = time.perf_counter()
+        oc.keyswitch_many(cts, key, [pow(3, s + 1, 2 * N2)], threads=cores)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = cores * args.steps / total
+    line = {
+        "metric": "keyswitches/s (n=8192, 4x50-bit + 60-bit special prime, dnum=4, Galois rotation)",
+        "value": value, "unit": "keyswitches/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+        "config": {"workload": "config2 keyswitch sample: one keyswitch per host thread per step",
+                   "n": N2, "primes_bits": BITS2, "t": T2, "dnum": 4},
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "keyswitches/s", "cores": cores, "kind": "port",
+                         "sample": f"{cores} keyswitches per step x {args.steps} steps (CPU oracle restatement; "
+                                   "SEAL 4.1.2 is not buildable here)"},
+        "e2e": {"value": value, "unit": "keyswitches/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    sys.path.insert(0, PKG)
+    import build as B
+    if not os.path.exists(B.LIB):
+        B.build()
+    import bfvgpu
+
+    primes2 = bfvgpu.find_primes(N2, BITS2)
+    ctx = bfvgpu.Context(N2, primes2, 4, 1, T2, device=local)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1234 + rank)
+
+    def uniform(shape, primes_cycle):
+        """Residues uniform in [0, q) per limb, generated on the device."""
+        flat = torch.randint(0, 2 ** 62, shape, dtype=torch.int64, device="cuda", generator=g)
+        q = torch.tensor(primes_cycle, dtype=torch.int64, device="cuda")
+        nlimb = shape[-2]
+        return torch.remainder(flat, q[torch.arange(nlimb, device="cuda") % len(primes_cycle)].view(
+            *([1] * (len(shape) - 2)), nlimb, 1))
+
+    cts = uniform((CTS, 2, 4, N2), primes2[:4]).contiguous()
+    keys = uniform((ROTATIONS, 4 * 2, 5, N2), primes2).contiguous()  # [r][digit*2+c][p][n]
+    elts = galois_elements(N2, ROTATIONS)
+    scratch = torch.empty(ctx.keyswitch_scratch_words(CTS), dtype=torch.int64, device="cuda")
+    out = torch.empty_like(cts)
+    torch.cuda.synchronize()
+
+    def step(ev_pairs=None):
+        for r in range(ROTATIONS):
+            if ev_pairs is not None:
+                ev_pairs[r][0].record(stream)
+            ctx.keyswitch_device(cts, CTS, keys[r], elts[r], scratch, out, stream=ctx.stream())
+            if ev_pairs is not None:
+                ev_pairs[r][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(ROTATIONS)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = bfvgpu.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    per_launch = []
+    with Clocks(local) as clk:
+        start.record(stream)
+        for s in range(args.steps):
+            step(ev if s == args.steps - 1 else None)
+        end.record(stream)
+        torch.cuda.synchronize()
+    launches = bfvgpu.launch_count() - launches0
+    elapsed = start.elapsed_time(end) / 1e3
+    per_launch = [a.elapsed_time(b) / 1e3 for a, b in ev]
+    if dist:
+        t = torch.tensor([elapsed], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    total_ks = CTS * ROTATIONS * args.steps * world
+    value = total_ks / elapsed
+    ms_per_step = 1e3 * elapsed / args.steps
+
+    # ---- roofline of the dominant launch pair (k_ks_main + k_ks_moddown per rotation) ----
+    import json as _json
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = _json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    peak_kind = "measured" if "hbm_gbs" in peaks else "fallback"
+    avg_launch = sum(per_launch) / len(per_launch)
+    alg_bytes_launch = ALG_BYTES_PER_KS * CTS
+    achieved = alg_bytes_launch / avg_launch / 1e9
+
+    # ---- secondary: NTT round trips (config 1) ----
+    primes1 = bfvgpu.find_primes(N1, BITS1)
+    ctx1 = bfvgpu.Context(N1, primes1, 3, 0, T2, device=local)
+    s1 = torch.cuda.ExternalStream(ctx1.stream())
+    reps = 200
+    ntt_data = uniform((NTT_POLYS // 3, 3, N1), primes1).contiguous()
+    big = [ntt_data.clone() for _ in range(4)]  # 4 x 12.6 MB rotating buffers
+    for _ in range(5):
+        for b in big:
+            ctx1.ntt_device(b, NTT_POLYS, 3, 0, False, stream=ctx1.stream())
+            ctx1.ntt_device(b, NTT_POLYS, 3, 0, True, stream=ctx1.stream())
+    torch.cuda.synchronize()
+    a, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s1)
+    for i in range(reps):
+        bb = big[i % 4]
+        ctx1.ntt_device(bb, NTT_POLYS, 3, 0, False, stream=ctx1.stream())
+        ctx1.ntt_device(bb, NTT_POLYS, 3, 0, True, stream=ctx1.stream())
+    b2.record(s1)
+    torch.cuda.synchronize()
+    ntt_dt = a.elapsed_time(b2) / 1e3
+    ntts_per_s = reps * 2 * NTT_POLYS / ntt_dt
+    ntt_launch_s = ntt_dt / (2 * reps)
+    ntt_bytes = NTT_POLYS * N1 * 8 * 2
+    ntt_ok = bool(torch.equal(big[0], ntt_data))
+
+    # ---- e2e through the object API with pinned host buffers ----
+    key_host = [keys[r].cpu().numpy().view(np.uint64) for r in range(ROTATIONS)]
+    switches = [bfvgpu.Switch(ctx, key_host[r], elts[r]) for r in range(ROTATIONS)]
+    host_in = torch.empty((CTS, 2, 4, N2), dtype=torch.int64, pin_memory=True)
+    host_in.copy_(cts.cpu())
+    hin = host_in.numpy().view(np.uint64)
+    host_out = torch.empty((CTS, 2, 4, N2), dtype=torch.int64, pin_memory=True).numpy().view(np.uint64)
+    lib = bfvgpu.lib()
+    from bfvgpu._lib import ptr
+
+    def e2e_step():
+        for r in range(ROTATIONS):
+            rc = lib.bfvgpu_switch_apply_many(switches[r]._h, ptr(hin), CTS, ptr(host_out))
+            if rc:
+                raise RuntimeError(lib.bfvgpu_last_error().decode())
+
+    e2e_step()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e2e_dt = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_dt], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_dt = float(t.item())
+    e2e_value = CTS * ROTATIONS * args.e2e_steps * world / e2e_dt
+    # parity spot check of the last e2e result against the device path
+    ctx.keyswitch_device(cts, CTS, keys[ROTATIONS - 1], elts[ROTATIONS - 1], scratch, out, stream=ctx.stream())
+    torch.cuda.synchronize()
+    e2e_match = bool(np.array_equal(out[:4].cpu().numpy().view(np.uint64), host_out[:4]))
+    for sw in switches:
+        sw.close()
+
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return 0
+
+    cpu = None
+    if not args.no_cpu:
+        v, cores, sample = cpu_keyswitch_sample()
+        nv, _ = cpu_ntt_sample()
+        cpu = {"value": v, "unit": "keyswitches/s", "cores": cores, "kind": "port", "sample": sample,
+               "ntt_value": nv, "ntt_unit": "NTTs/s"}
+
+    line = {
+        "metric": "keyswitches/s (n=8192, 4x50-bit + 60-bit special prime, dnum=4, Galois rotation)",
+        "value": value, "unit": "keyswitches/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u64", "data": "synthetic",
+        "config": {"workload": "config2: 256 random cts x rotations 1..128 (g = 3^r mod 2n), seeded random "
+                               "NTT-form keys", "n": N2, "primes_bits": BITS2, "t": T2, "dnum": 4,
+                   "cts": CTS, "rotations": ROTATIONS, "parallelism": f"replicas x{world} (weak)",
+                   "l2": "inputs+keys 448 MB > 126 MB L2; every rotation re-reads all cts"},
+        "e2e": {"value": e2e_value, "unit": "keyswitches/s", "api": "bfvgpu.Switch.apply_many (C ABI, pinned host)",
+                "h2d_bytes_per_step": CTS * 2 * 4 * N2 * 8 * ROTATIONS,
+                "d2h_bytes_per_step": CTS * 2 * 4 * N2 * 8 * ROTATIONS, "steps": args.e2e_steps,
+                "matches_device_path": e2e_match},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "traffic": None, "peak_source": peak_kind,
+                     "kernel": "keyswitch launch pair k_ks_main+k_ks_moddown (256 cts)",
+                     "alg_bytes_per_launch": alg_bytes_launch, "avg_launch_ms": avg_launch * 1e3,
+                     "note": "integer-pipe bound: 30 NTTs of n=8192 per keyswitch"},
+        "secondary": {"ntt": {"value": ntts_per_s, "unit": "NTTs/s",
+                              "config": "config1: n=4096, primes 36/36/37-bit, 384 limb-polys fwd+inv",
+                              "avg_launch_ms": ntt_launch_s * 1e3,
+                              "achieved_gbs": ntt_bytes / ntt_launch_s / 1e9,
+                              "frac_hbm": ntt_bytes / ntt_launch_s / 1e9 / hbm_peak,
+                              "round_trip_identity": ntt_ok}},
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -981,12 +981,16 @@ int32_t bfvgpu_switch_open(bfvgpu_ctx* ctx, const uint64_t* key, uint32_t elt, b
   });
 }
 
+// Ciphertexts per launch of Switch::apply_many; bounds an object's working set to
+// kSwitchChunk * (2 ct + scratch) words (64 cts at n = 8192, 4+1 primes: 106 MB).
+constexpr uint64_t kSwitchChunk = 64;
+
 static void switch_reserve(bfvgpu_switch* s, uint64_t count) {
+  if (count > kSwitchChunk) count = kSwitchChunk;
   if (count <= s->cap) return;
   const Context& c = *s->h.ctx;
   const uint64_t ctw = 2ull * c.dk * c.n;
   s->in = s->h.grow(s->in, count * ctw);
-  s->right = s->h.grow(s->right, count * ctw);
   s->out = s->h.grow(s->out, count * ctw);
   s->acc = s->h.grow(s->acc, count * 2 * c.k * c.n);
   s->cap = count;
@@ -1001,23 +1005,30 @@ int32_t bfvgpu_switch_apply_many(bfvgpu_switch* s, const uint64_t* cts, uint64_t
     DeviceScope scope(c.device);
     s->h.run([&] {
       switch_reserve(s, count);
-      const uint64_t words = count * 2 * c.dk * c.n;
-      cuda_check(cudaEventRecord(s->ev[0], c.stream), "event");
-      s->h.h2d(s->in, cts, words);
-      cuda_check(cudaEventRecord(s->ev[1], c.stream), "event");
-      cuda_check(launch_keyswitch(c.P, s->in, s->key, s->elt, count, s->acc, s->out, c.stream), "keyswitch");
-      count_launch(2);
-      cuda_check(cudaEventRecord(s->ev[2], c.stream), "event");
-      s->h.d2h(out, s->out, words);
-      cuda_check(cudaEventRecord(s->ev[3], c.stream), "event");
-      s->h.sync();
-      float a = 0, b = 0, d = 0;
-      cudaEventElapsedTime(&a, s->ev[0], s->ev[1]);
-      cudaEventElapsedTime(&b, s->ev[1], s->ev[2]);
-      cudaEventElapsedTime(&d, s->ev[2], s->ev[3]);
-      s->upload_ms = a;
-      s->kernel_ms = b;
-      s->download_ms = d;
+      const uint64_t ctw = 2ull * c.dk * c.n;
+      double up = 0, ker = 0, down = 0;
+      for (uint64_t first = 0; first < count; first += s->cap) {
+        const uint64_t m = count - first < s->cap ? count - first : s->cap;
+        cuda_check(cudaEventRecord(s->ev[0], c.stream), "event");
+        s->h.h2d(s->in, cts + first * ctw, m * ctw);
+        cuda_check(cudaEventRecord(s->ev[1], c.stream), "event");
+        cuda_check(launch_keyswitch(c.P, s->in, s->key, s->elt, m, s->acc, s->out, c.stream), "keyswitch");
+        count_launch(2);
+        cuda_check(cudaEventRecord(s->ev[2], c.stream), "event");
+        s->h.d2h(out + first * ctw, s->out, m * ctw);
+        cuda_check(cudaEventRecord(s->ev[3], c.stream), "event");
+        s->h.sync();
+        float a = 0, b = 0, d = 0;
+        cudaEventElapsedTime(&a, s->ev[0], s->ev[1]);
+        cudaEventElapsedTime(&b, s->ev[1], s->ev[2]);
+        cudaEventElapsedTime(&d, s->ev[2], s->ev[3]);
+        up += a;
+        ker += b;
+        down += d;
+      }
+      s->upload_ms = up;
+      s->kernel_ms = ker;
+      s->download_ms = down;
     });
   });
 }
@@ -1041,6 +1052,7 @@ int32_t bfvgpu_switch_packing_pair(bfvgpu_switch* s, const uint64_t* left, const
       switch_reserve(s, 1);
       switch_reserve(other, 1);
       const uint64_t words = 2ull * c.dk * c.n;
+      if (!s->right) s->right = s->h.alloc(words);
       s->h.h2d(s->in, left, words);
       s->h.h2d(s->right, right, words);
       // sum -> s->out (temporarily), diff -> other->in

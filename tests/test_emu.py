@@ -1,0 +1,166 @@
+"""CPU pre-check of the CUDA kernel bodies (no GPU).
+
+tests/emu/libemu.so compiles privacy-rag_b200/csrc/block_ops.cuh with the host compiler
+and runs each thread block's work units in turn, with the constants and twiddle tables
+of the product library's host-only context.  Every kernel's pass schedule, index
+arithmetic, prologue and epilogue is compared bit for bit with the CPU oracle at the
+sizes the kernels are instantiated for (n = 32, 64, 4096, 8192, 16384).
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import pytest
+
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "emu"))
+import emu_api  # noqa: E402
+
+p = emu_api.p
+
+SETS = {
+    5: (lambda O: O.ART002_PRIMES, 6, 1 << 59),
+    6: (lambda O: O.ART002_PRIMES, 6, 1 << 59),
+    12: (lambda O: O.coeff_modulus(4096, [36, 36, 37]), 3, 65537),
+    13: (lambda O: O.coeff_modulus(8192, [50, 50, 50, 50, 60]), 4, 65537),
+    14: (lambda O: O.ART002_PRIMES, 6, 1 << 59),
+}
+
+
+def make(bfv, oracle, logn):
+    primes_fn, dk, t = SETS[logn]
+    primes = primes_fn(oracle)
+    n = 1 << logn
+    hc = bfv.Context(n, primes, dk, len(primes) - dk, t, device=-1)
+    oc = oracle.Ctx(n, primes, data_k=dk, t=t)
+    mods = np.ascontiguousarray(hc.moduli())
+    fwd = np.ascontiguousarray(np.stack([hc.tables(i)[0] for i in range(hc.k)]))
+    inv = np.ascontiguousarray(np.stack([hc.tables(i)[1] for i in range(hc.k)]))
+    return hc, oc, mods, fwd, inv
+
+
+@pytest.fixture(scope="module")
+def E(emu):
+    return emu_api.bind(emu)
+
+
+@pytest.mark.parametrize("logn", [5, 6, 12, 13, 14])
+def test_tables_match_oracle(bfv, oracle, logn):
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+    ofwd, oinv, oinvn = oc.tables()
+    assert np.array_equal(fwd, ofwd) and np.array_equal(inv, oinv)
+    assert np.array_equal(mods[:, 3:5], oinvn)
+    for i, q in enumerate(oc.primes):
+        r = ((1 << 128) - 1) // q
+        assert int(mods[i, 0]) == q and int(mods[i, 1]) == r & ((1 << 64) - 1) and int(mods[i, 2]) == r >> 64
+    for i in range(oc.data_k):
+        assert int(mods[i, 8]) == oc.delta[i]
+
+
+@pytest.mark.parametrize("logn", [5, 6, 12, 13, 14])
+def test_ntt_kernel_body(bfv, oracle, E, logn):
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+    k = hc.k
+    data = oc.uniform(logn, 2 * k, prime_count=k)
+    n = 1 << logn
+    data[0, :13] = 0
+    data[1, :13] = oc.primes[1] - 1
+    got = data.copy()
+    assert E.emu_ntt(logn, k, p(mods), p(fwd), p(inv), p(got), data.shape[0], k, 0, 0) == 0
+    assert np.array_equal(got, oc.ntt(data, prime_count=k))
+    back = got.copy()
+    E.emu_ntt(logn, k, p(mods), p(fwd), p(inv), p(back), data.shape[0], k, 0, 1)
+    assert np.array_equal(back, data)
+    # prime offset / count selection (polys on primes 1..k-1 only)
+    if k > 2:
+        sub = data[: k - 1].copy()
+        E.emu_ntt(logn, k, p(mods), p(fwd), p(inv), p(sub), k - 1, k - 1, 1, 0)
+        exp = np.stack([oc.ntt_one(data[i], 1 + i) for i in range(k - 1)])
+        assert np.array_equal(sub, exp)
+
+
+@pytest.mark.parametrize("logn,elts", [(5, [1, 3, 63]), (6, [5, 127, 9]), (13, [3, 2 ** 13 + 1, 16383]),
+                                       (14, [1, 3, 1025])])
+def test_keyswitch_kernel_body(bfv, oracle, E, logn, elts):
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+    k, dk, n = hc.k, hc.dk, 1 << logn
+    count = 2
+    cts = oc.uniform(100 + logn, count * 2 * dk, prime_count=dk).reshape(count, 2, dk, n)
+    cts[0, 1, :, ::5] = 0  # zero digits: the automorphism must keep them zero
+    key = oc.uniform(200 + logn, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n)
+    for elt in elts:
+        out = np.zeros_like(cts)
+        E.emu_keyswitch(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), count, p(key), elt, p(out))
+        for c in range(count):
+            assert np.array_equal(out[c], oc.keyswitch(cts[c], key, elt)), (logn, elt, c)
+
+
+@pytest.mark.parametrize("logn", [6, 14])
+def test_matrix_mask_enc0_kernel_bodies(bfv, oracle, E, logn):
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+    k, dk, n = hc.k, hc.dk, 1 << logn
+    tb = oracle.TestBfv(oc, seed=logn)
+    rng = np.random.default_rng(logn)
+    I, G = 3, 2
+    cts = np.stack([tb.encrypt(rng.integers(0, 1 << 59, size=n, dtype=np.uint64)) for _ in range(I)])
+    ring = rng.integers(0, 1 << 59, size=(G, I, n), dtype=np.uint64)
+    ring[0, 0, :4] = [(1 << 59) - 1, 1 << 58, (1 << 58) - 1, 0]
+    mask = rng.integers(0, 1 << 59, size=(G, n), dtype=np.uint64)
+    samples = np.stack([tb.samples() for _ in range(G)])
+    out = np.zeros((G, 2, dk, n), dtype=np.uint64)
+    E.emu_matrix(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), I, p(ring), G, p(mask), p(samples), p(tb.pk),
+                 oc.q_mod_t, oc.upper_half, 1 << 59, 59, p(out))
+    cn = oc.matrix_open(cts)
+    for g in range(G):
+        e = oc.matrix_evaluate(cn, ring[g])
+        e[0] = oc.sub_plain(e[0], mask[g])
+        e = oc.add(e, oc.enc0(samples[g], tb.pk))
+        assert np.array_equal(out[g], e), g
+    # unprotected product
+    out2 = np.zeros((1, 2, dk, n), dtype=np.uint64)
+    E.emu_matrix(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), I, p(ring[0]), 1, None, None, None,
+                 oc.q_mod_t, oc.upper_half, 1 << 59, 59, p(out2))
+    assert np.array_equal(out2[0], oc.matrix_evaluate(cn, ring[0]))
+
+
+def test_client_phase_kernel_body(bfv, oracle, E):
+    hc, oc, mods, fwd, inv = make(bfv, oracle, 14)
+    tb = oracle.TestBfv(oc, seed=2)
+    c1 = oc.uniform(5, 2 * 6).reshape(2, 6, oc.n)
+    got = c1.copy()
+    E.emu_client_phase(14, 7, 6, p(mods), p(fwd), p(inv), p(got), p(tb.sk_data_ntt()), 2)
+    for b in range(2):
+        assert np.array_equal(got[b], oc.client_phase(c1[b], tb.sk_data_ntt()))
+
+
+def test_crt_body(bfv, oracle, E):
+    primes = oracle.ART002_PRIMES[:6]
+    Q = 1
+    for q in primes:
+        Q *= q
+    vals = [0, 1, Q - 1, Q // 2, 2 ** 359, 12345678901234567890123456789 ** 3 % Q]
+    res = np.array([[v % q for q in primes] for v in vals], dtype=np.uint64)
+    hc = bfv.Context(64, oracle.ART002_PRIMES, 6, 1, 1 << 59, device=-1)
+    mods = np.ascontiguousarray(hc.moduli())
+    part = np.array([[((Q // q) >> (64 * l)) & ((1 << 64) - 1) for l in range(6)] for q in primes], dtype=np.uint64)
+    cinv = np.array([[pow(Q // q % q, -1, q), (pow(Q // q % q, -1, q) << 64) // q] for q in primes], dtype=np.uint64)
+    ql = np.array([(Q >> (64 * l)) & ((1 << 64) - 1) for l in range(6)], dtype=np.uint64)
+    limbs = np.zeros_like(res)
+    E.emu_crt(7, 6, p(mods), p(res), len(vals), p(part), p(cinv), p(ql), p(limbs))
+    for i, v in enumerate(vals):
+        assert sum(int(limbs[i, l]) << (64 * l) for l in range(6)) == v
+
+
+def test_token_kernel_bodies(bfv, oracle, E):
+    hc, oc, mods, fwd, inv = make(bfv, oracle, 14)
+    rng = np.random.default_rng(8)
+    slots = 1
+    cts = oc.uniform(77, 19 * slots * 2 * 6).reshape(19, slots, 2, 6, oc.n)
+    cts_ntt = oc.ntt(cts.reshape(-1, oc.n), prime_count=6).reshape(cts.shape)
+    bound = 1 << 20
+    ring = (rng.integers(-bound, bound + 1, size=19 * 8192) & ((1 << 59) - 1)).astype(np.uint64)
+    scaled = np.array([oc.scale_plain(int(rng.integers(0, 1 << 59)))], dtype=np.uint64)
+    out = np.zeros((slots, 2, 6, oc.n), dtype=np.uint64)
+    E.emu_token(7, 6, p(mods), p(fwd), p(inv), p(cts_ntt), slots, p(ring), p(scaled), p(out))
+    assert np.array_equal(out, oc.token_evaluate(cts_ntt, slots, ring, scaled))

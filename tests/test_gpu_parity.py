@@ -1,0 +1,336 @@
+"""GPU parity: the CUDA path through the C ABI against the CPU oracle, bit for bit.
+
+Sizes are the BASELINE parameter sets (config 1: n=4096, 3 primes of 36/36/37 bits;
+config 2: n=8192, 4 x 50-bit + one 60-bit special prime; ART-002: n=16384, 6+1 x 60-bit)
+with batch sizes the oracle finishes in seconds.  Boundary residues follow
+IV1/experiments/resident_token_gpu/check_resident.cpp:98 (j%13 in {0,1,2} -> 0, q-1, 1)
+and the keyswitch plaintext patterns follow keyswitch_full_gpu/check_switch.cpp:80.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CFG1 = dict(n=4096, bits=[36, 36, 37], dk=3, special=0, t=65537)
+CFG2 = dict(n=8192, bits=[50, 50, 50, 50, 60], dk=4, special=1, t=65537)
+
+
+@pytest.fixture(scope="module")
+def gpu(bfv):
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return bfv
+
+
+def _contexts(bfv, oracle, cfg):
+    primes = oracle.coeff_modulus(cfg["n"], cfg["bits"])
+    hc = bfv.Context(cfg["n"], primes, cfg["dk"], cfg["special"], cfg["t"], device=0)
+    oc = oracle.Ctx(cfg["n"], primes, data_k=cfg["dk"], t=cfg["t"])
+    return hc, oc
+
+
+@pytest.fixture(scope="module")
+def art(gpu, oracle):
+    return gpu.Context.art002(0), oracle.art002()
+
+
+@pytest.fixture(scope="module")
+def cfg1(gpu, oracle):
+    return _contexts(gpu, oracle, CFG1)
+
+
+@pytest.fixture(scope="module")
+def cfg2(gpu, oracle):
+    return _contexts(gpu, oracle, CFG2)
+
+
+def boundary(a: np.ndarray, q) -> np.ndarray:
+    """check_resident.cpp:98 pattern on [polys][n] with prime of poly i = q[i % len(q)]."""
+    a = a.copy()
+    n = a.shape[-1]
+    j = np.arange(n)
+    flat = a.reshape(-1, n)
+    for i in range(flat.shape[0]):
+        qi = q[i % len(q)]
+        flat[i, j % 13 == 0] = 0
+        flat[i, j % 13 == 1] = qi - 1
+        flat[i, j % 13 == 2] = 1
+    return a
+
+
+# ---- NTT -----------------------------------------------------------------------------------
+def test_ntt_batch_config1_forward_inverse(cfg1):
+    hc, oc = cfg1
+    batches = 19
+    data = boundary(oc.uniform(1, batches * 3), oc.primes).reshape(batches, 3, hc.n)
+    nb = __import__("bfvgpu").NttBatch(hc, key_level=False, batches=batches)
+    fwd = nb.transform(data, inverse=False)
+    assert np.array_equal(fwd, oc.ntt(data, prime_count=3))
+    back = nb.transform(fwd, inverse=True)
+    assert np.array_equal(back, data)
+    c = nb.close()
+    assert c["closed"] and c["wiped"] == c["freed"] == data.nbytes
+    assert nb.close() == c  # idempotent
+
+
+def test_ntt_device_config1_full_batch(cfg1):
+    """The BASELINE config-1 batch: 64 ciphertexts x 2 polys x 3 limbs, in place."""
+    import torch
+    hc, oc = cfg1
+    data = boundary(oc.uniform(2, 384), oc.primes)
+    d = torch.from_numpy(data.view(np.int64)).cuda()
+    torch.cuda.synchronize()
+    hc.ntt_device(d, 384, 3, 0, inverse=False)
+    torch.cuda.synchronize()
+    got = d.cpu().numpy().view(np.uint64)
+    assert np.array_equal(got, oc.ntt(data, prime_count=3, threads=8))
+    hc.ntt_device(d, 384, 3, 0, inverse=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(d.cpu().numpy().view(np.uint64), data)
+
+
+def test_ntt_art002_key_level(art):
+    hc, oc = art
+    data = boundary(oc.uniform(3, 2 * 7, prime_count=7), oc.primes).reshape(2, 7, hc.n)
+    nb = __import__("bfvgpu").NttBatch(hc, key_level=True, batches=2)
+    fwd = nb.transform(data, inverse=False)
+    assert np.array_equal(fwd, oc.ntt(data, prime_count=7))
+    assert np.array_equal(nb.transform(fwd, inverse=True), data)
+
+
+def test_ntt_rejects_non_canonical(art):
+    import bfvgpu
+    hc, oc = art
+    nb = bfvgpu.NttBatch(hc, key_level=False, batches=1)
+    bad = np.zeros((1, 6, hc.n), dtype=np.uint64)
+    bad[0, 2, 5] = oc.primes[2]
+    with pytest.raises(bfvgpu.BfvGpuInvalidArgument) as e:
+        nb.transform(bad, inverse=False)
+    assert e.value.name == "BFVGPU_E_CANONICAL"
+    nb.close()
+    with pytest.raises(bfvgpu.BfvGpuError):
+        nb.transform(np.zeros((1, 6, hc.n), dtype=np.uint64), inverse=False)
+
+
+# ---- keyswitch ----------------------------------------------------------------------------
+def _ks_case(hc, oc, oracle, seed, elts, patterns=True):
+    import bfvgpu
+    tb = oracle.TestBfv(oc, seed=seed)
+    n = oc.n
+    plains = []
+    if patterns:
+        plains.append(np.zeros(n, dtype=np.uint64))
+        p1 = np.zeros(n, dtype=np.uint64)
+        p1[n - 1] = oc.t - 1
+        plains.append(p1)
+        plains.append(((np.arange(n, dtype=np.uint64) * 7919 + 123456) % np.uint64(oc.t)).astype(np.uint64))
+    cts = np.stack([tb.encrypt(p) for p in plains])
+    for elt in elts:
+        key = tb.galois_key(elt)
+        sw = bfvgpu.Switch(hc, key, elt)
+        got = sw.apply_many(cts)
+        for i in range(cts.shape[0]):
+            exp = oc.keyswitch(cts[i], key, elt)
+            assert np.array_equal(got[i], exp), (elt, i)
+        # single-ct entry point, and decryption of the switched ciphertext
+        one = sw.apply(cts[2])
+        assert np.array_equal(one, got[2])
+        dec = tb.decrypt(one)
+        m = [int(v) for v in plains[2]]
+        exp_plain = [0] * n
+        for j in range(n):
+            d = (j * elt) % (2 * n)
+            if d >= n:
+                exp_plain[d - n] = (-m[j]) % oc.t
+            else:
+                exp_plain[d] = m[j]
+        assert dec == exp_plain
+        c = sw.close()
+        assert c["closed"] and c["first_cuda_error"] == 0 and c["wiped"] == c["freed"] > 0
+
+
+def test_keyswitch_config2(cfg2, oracle):
+    hc, oc = cfg2
+    _ks_case(hc, oc, oracle, 11, [3, 3 ** 7 % (2 * oc.n), 2 * oc.n - 1])
+
+
+def test_keyswitch_art002_acyclic_elements(art, oracle):
+    hc, oc = art
+    # acyclic packing elements of bfv_acyclic_pack.hpp:30: 1 and 2^(l+1)+1 for l in 0..8
+    _ks_case(hc, oc, oracle, 12, [1, 3, 2 ** 9 + 1])
+
+
+def test_keyswitch_random_residues_with_zero_digits(cfg2, oracle):
+    """Uniform residues (no decryption structure) incl. zero coefficients in c1, which
+    exercise the zero branch of the automorphism's negation."""
+    import bfvgpu
+    hc, oc = cfg2
+    cts = oc.uniform(21, 4 * 2 * 4).reshape(4, 2, 4, oc.n)
+    cts[0, 1, :, ::7] = 0
+    key = oc.uniform(22, 4 * 2 * 5, prime_count=5).reshape(4, 2, 5, oc.n)
+    for elt in (5, 25, 2 * oc.n - 3):
+        sw = bfvgpu.Switch(hc, key, elt)
+        got = sw.apply_many(cts)
+        exp = oc.keyswitch_many(cts, key, [elt], threads=8)[0]
+        assert np.array_equal(got, exp)
+        sw.close()
+
+
+def test_keyswitch_device_batch(cfg2):
+    """Device-resident batched entry point agrees with the host-buffer object."""
+    import torch
+    import bfvgpu
+    hc, oc = cfg2
+    cts = oc.uniform(31, 8 * 2 * 4).reshape(8, 2, 4, oc.n)
+    key = oc.uniform(32, 4 * 2 * 5, prime_count=5).reshape(4, 2, 5, oc.n)
+    elt = 3 ** 5 % (2 * oc.n)
+    d_cts = torch.from_numpy(cts.view(np.int64)).cuda()
+    d_key = torch.from_numpy(key.view(np.int64)).cuda()
+    scratch = torch.empty(hc.keyswitch_scratch_words(8), dtype=torch.int64, device="cuda")
+    out = torch.empty_like(d_cts)
+    torch.cuda.synchronize()
+    hc.keyswitch_device(d_cts, 8, d_key, elt, scratch, out)
+    torch.cuda.synchronize()
+    sw = bfvgpu.Switch(hc, key, elt)
+    assert np.array_equal(out.cpu().numpy().view(np.uint64), sw.apply_many(cts))
+
+
+def test_packing_pair(art, oracle):
+    import bfvgpu
+    hc, oc = art
+    tb = oracle.TestBfv(oc, seed=41)
+    level = 2
+    g = (1 << (level + 1)) + 1
+    k1 = tb.galois_key(1)
+    kg = tb.galois_key(g)
+    rng = np.random.default_rng(3)
+    L = tb.encrypt(rng.integers(0, 1 << 20, size=oc.n, dtype=np.uint64))
+    R = tb.encrypt(rng.integers(0, 1 << 20, size=oc.n, dtype=np.uint64))
+    s1 = bfvgpu.Switch(hc, k1, 1)
+    sg = bfvgpu.Switch(hc, kg, g)
+    got = s1.packing_pair(L, R, sg, level)
+    assert np.array_equal(got, oc.packing_pair(L, R, k1, kg, level))
+    with pytest.raises(bfvgpu.BfvGpuError):
+        sg.packing_pair(L, R, s1, level)  # wrong element order -> E_PACK_PAIR_STATE
+
+
+# ---- Enc(0), client phase ---------------------------------------------------------------------
+def test_enc0(art, oracle):
+    import bfvgpu
+    hc, oc = art
+    tb = oracle.TestBfv(oc, seed=51)
+    pz = bfvgpu.PublicZero(hc, tb.pk)
+    for _ in range(2):
+        s = tb.samples()
+        got = pz.encrypt_from_samples(s)
+        assert np.array_equal(got, oc.enc0(s, tb.pk))
+        assert all(v == 0 for v in tb.decrypt(got)[:64])
+    c = pz.close()
+    assert c["closed"] and c["wiped"] == c["freed"]
+
+
+def test_client_phase(art, oracle):
+    import bfvgpu
+    hc, oc = art
+    tb = oracle.TestBfv(oc, seed=61)
+    nb = bfvgpu.NttBatch(hc, key_level=False, batches=3)
+    nb.bind_client_key(tb.sk_data_ntt())
+    c1 = oc.uniform(62, 3 * 6).reshape(3, 6, oc.n)
+    got = nb.client_phase(c1)
+    for b in range(3):
+        assert np.array_equal(got[b], oc.client_phase(c1[b], tb.sk_data_ntt()))
+    with pytest.raises(bfvgpu.BfvGpuError):
+        nb.bind_client_key(tb.sk_data_ntt())  # E_CLIENT_KEY_STATE
+
+
+# ---- matrix -----------------------------------------------------------------------------------
+def test_matrix_evaluate_and_selective(art, oracle):
+    import bfvgpu
+    hc, oc = art
+    tb = oracle.TestBfv(oc, seed=71)
+    rng = np.random.default_rng(72)
+    I = 4
+    cts = np.stack([tb.encrypt(rng.integers(0, 1 << 59, size=oc.n, dtype=np.uint64)) for _ in range(I)])
+    m = bfvgpu.Matrix(hc, cts)
+    ring = rng.integers(0, 1 << 59, size=(I, oc.n), dtype=np.uint64)
+    ring[0, :4] = [(1 << 59) - 1, 1 << 58, (1 << 58) - 1, 0]
+    cn = oc.matrix_open(cts, threads=8)
+    full = m.evaluate(ring)
+    assert np.array_equal(full, oc.matrix_evaluate(cn, ring, threads=8))
+    targets = [3, 100, 8191, 16383]
+    sel = m.evaluate_selective(ring, targets)
+    assert np.array_equal(sel, oc.matrix_evaluate(cn, ring, targets=targets, threads=8))
+    for bad in ([], [5, 5], [16384], list(range(513))):
+        with pytest.raises(bfvgpu.BfvGpuInvalidArgument):
+            m.evaluate_selective(ring, bad)
+    bad_ring = ring.copy()
+    bad_ring[1, 7] = 1 << 59
+    with pytest.raises(bfvgpu.BfvGpuInvalidArgument) as e:
+        m.evaluate(bad_ring)
+    assert e.value.name == "BFVGPU_E_RING"
+    c = m.close()
+    assert c["closed"] and c["wiped"] == c["freed"] and c["first_cuda_error"] == 0
+    assert m.close() == c
+    with pytest.raises(bfvgpu.BfvGpuInvalidArgument):
+        m.evaluate(ring)  # closed: MATRIX_GPU_SHAPE like the reference
+
+
+def test_matrix_groups_mask_enc0_crt(art, oracle):
+    import bfvgpu
+    hc, oc = art
+    tb = oracle.TestBfv(oc, seed=81)
+    rng = np.random.default_rng(82)
+    I, G = 3, 3
+    cts = np.stack([tb.encrypt(rng.integers(0, 1 << 59, size=oc.n, dtype=np.uint64)) for _ in range(I)])
+    m = bfvgpu.Matrix(hc, cts)
+    m.bind_public_key(tb.pk)
+    ring = rng.integers(0, 1 << 59, size=(G, I, oc.n), dtype=np.uint64)
+    mask = rng.integers(0, 1 << 59, size=(G, oc.n), dtype=np.uint64)
+    samples = np.stack([tb.samples() for _ in range(G)])
+    targets = [[0, 5, 16383], list(range(7, 7 + 512 * 31, 31)), [9]]
+    c1, c0, crt = m.evaluate_groups(ring, targets, mask=mask, samples=samples, crt=True)
+    cn = oc.matrix_open(cts, threads=8)
+    for g in range(G):
+        e = oc.matrix_evaluate(cn, ring[g], threads=8)
+        e[0] = oc.sub_plain(e[0], mask[g])
+        e = oc.add(e, oc.enc0(samples[g], tb.pk))
+        assert np.array_equal(c1[g], e[1])
+        for i, t in enumerate(targets[g]):
+            assert np.array_equal(c0[g, :, i], e[0][:, t])
+            v = sum(int(crt[g, i, l]) << (64 * l) for l in range(6))
+            assert v == oracle.crt(e[0][:, t], oc.primes[:6])
+
+
+# ---- resident token ----------------------------------------------------------------------------
+def test_token_weights(art, oracle):
+    import bfvgpu
+    hc, oc = art
+    rng = np.random.default_rng(91)
+    slots = 1
+    cts = oc.uniform(92, slots * 19 * 2 * 6).reshape(slots, 19, 2, 6, oc.n)
+    cts = boundary(cts.reshape(-1, oc.n), oc.primes[:6]).reshape(cts.shape)
+    tw = bfvgpu.TokenWeights(hc, cts)
+    bound = 1 << 20
+    for case in range(2):
+        if case == 0:
+            vals = np.array([0, 1, -1, bound, -bound, bound - 1, -(bound - 1)], dtype=np.int64)
+            ring = (vals[np.arange(19 * 8192) % 7] & ((1 << 59) - 1)).astype(np.uint64)
+        else:
+            ring = (rng.integers(-bound, bound + 1, size=19 * 8192) & ((1 << 59) - 1)).astype(np.uint64)
+        local = rng.integers(0, 1 << 59, size=slots, dtype=np.uint64)
+        got = tw.evaluate_finished(ring, local)
+        inputs_ntt = np.stack([oc.ntt(cts[s].reshape(-1, oc.n), prime_count=6).reshape(19, 2, 6, oc.n)
+                               for s in range(slots)], axis=1)  # [19][slots][2][6][n]
+        scaled = np.array([oc.scale_plain(int(v)) for v in local], dtype=np.uint64)
+        exp = oc.token_evaluate(inputs_ntt, slots, ring, scaled)
+        assert np.array_equal(got, exp), case
+    bad = np.zeros(19 * 8192, dtype=np.uint64)
+    bad[0] = bound + 1
+    with pytest.raises(bfvgpu.BfvGpuInvalidArgument) as e:
+        tw.evaluate_finished(bad, np.zeros(slots, dtype=np.uint64))
+    assert e.value.name == "BFVGPU_E_BOUND"
+    c = tw.close()
+    assert c["closed"] and c["wiped"] == c["freed"]
