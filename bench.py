@@ -194,7 +194,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=2, help="0 skips the e2e leg")
+    ap.add_argument("--rotations", type=int, default=ROTATIONS, help="rotations per step (profiling cases)")
+    ap.add_argument("--ntt-reps", type=int, default=200)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -228,14 +230,15 @@ def main():
             *([1] * (len(shape) - 2)), nlimb, 1))
 
     cts = uniform((CTS, 2, 4, N2), primes2[:4]).contiguous()
-    keys = uniform((ROTATIONS, 4 * 2, 5, N2), primes2).contiguous()  # [r][digit*2+c][p][n]
-    elts = galois_elements(N2, ROTATIONS)
+    rotations = args.rotations
+    keys = uniform((rotations, 4 * 2, 5, N2), primes2).contiguous()  # [r][digit*2+c][p][n]
+    elts = galois_elements(N2, rotations)
     scratch = torch.empty(ctx.keyswitch_scratch_words(CTS), dtype=torch.int64, device="cuda")
     out = torch.empty_like(cts)
     torch.cuda.synchronize()
 
     def step(ev_pairs=None):
-        for r in range(ROTATIONS):
+        for r in range(rotations):
             if ev_pairs is not None:
                 ev_pairs[r][0].record(stream)
             ctx.keyswitch_device(cts, CTS, keys[r], elts[r], scratch, out, stream=ctx.stream())
@@ -245,7 +248,7 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(ROTATIONS)]
+    ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(rotations)]
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -265,7 +268,7 @@ def main():
         t = torch.tensor([elapsed], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed = float(t.item())
-    total_ks = CTS * ROTATIONS * args.steps * world
+    total_ks = CTS * rotations * args.steps * world
     value = total_ks / elapsed
     ms_per_step = 1e3 * elapsed / args.steps
 
@@ -283,7 +286,7 @@ def main():
     primes1 = bfvgpu.find_primes(N1, BITS1)
     ctx1 = bfvgpu.Context(N1, primes1, 3, 0, T2, device=local)
     s1 = torch.cuda.ExternalStream(ctx1.stream())
-    reps = 200
+    reps = max(1, args.ntt_reps)
     ntt_data = uniform((NTT_POLYS // 3, 3, N1), primes1).contiguous()
     big = [ntt_data.clone() for _ in range(4)]  # 4 x 12.6 MB rotating buffers
     for _ in range(5):
@@ -305,40 +308,42 @@ def main():
     ntt_bytes = NTT_POLYS * N1 * 8 * 2
     ntt_ok = bool(torch.equal(big[0], ntt_data))
 
-    # ---- e2e through the object API with pinned host buffers ----
-    key_host = [keys[r].cpu().numpy().view(np.uint64) for r in range(ROTATIONS)]
-    switches = [bfvgpu.Switch(ctx, key_host[r], elts[r]) for r in range(ROTATIONS)]
-    host_in = torch.empty((CTS, 2, 4, N2), dtype=torch.int64, pin_memory=True)
-    host_in.copy_(cts.cpu())
-    hin = host_in.numpy().view(np.uint64)
-    host_out = torch.empty((CTS, 2, 4, N2), dtype=torch.int64, pin_memory=True).numpy().view(np.uint64)
-    lib = bfvgpu.lib()
-    from bfvgpu._lib import ptr
+    e2e_value, e2e_match = None, None
+    if args.e2e_steps > 0:
+        # ---- e2e through the object API with pinned host buffers ----
+        key_host = [keys[r].cpu().numpy().view(np.uint64) for r in range(rotations)]
+        switches = [bfvgpu.Switch(ctx, key_host[r], elts[r]) for r in range(rotations)]
+        host_in = torch.empty((CTS, 2, 4, N2), dtype=torch.int64, pin_memory=True)
+        host_in.copy_(cts.cpu())
+        hin = host_in.numpy().view(np.uint64)
+        host_out = torch.empty((CTS, 2, 4, N2), dtype=torch.int64, pin_memory=True).numpy().view(np.uint64)
+        lib = bfvgpu.lib()
+        from bfvgpu._lib import ptr
 
-    def e2e_step():
-        for r in range(ROTATIONS):
-            rc = lib.bfvgpu_switch_apply_many(switches[r]._h, ptr(hin), CTS, ptr(host_out))
-            if rc:
-                raise RuntimeError(lib.bfvgpu_last_error().decode())
+        def e2e_step():
+            for r in range(rotations):
+                rc = lib.bfvgpu_switch_apply_many(switches[r]._h, ptr(hin), CTS, ptr(host_out))
+                if rc:
+                    raise RuntimeError(lib.bfvgpu_last_error().decode())
 
-    e2e_step()
-    if dist:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
         e2e_step()
-    e2e_dt = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_dt], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_dt = float(t.item())
-    e2e_value = CTS * ROTATIONS * args.e2e_steps * world / e2e_dt
-    # parity spot check of the last e2e result against the device path
-    ctx.keyswitch_device(cts, CTS, keys[ROTATIONS - 1], elts[ROTATIONS - 1], scratch, out, stream=ctx.stream())
-    torch.cuda.synchronize()
-    e2e_match = bool(np.array_equal(out[:4].cpu().numpy().view(np.uint64), host_out[:4]))
-    for sw in switches:
-        sw.close()
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e2e_dt = time.perf_counter() - t0
+        if dist:
+            t = torch.tensor([e2e_dt], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_dt = float(t.item())
+        e2e_value = CTS * rotations * args.e2e_steps * world / e2e_dt
+        # parity spot check of the last e2e result against the device path
+        ctx.keyswitch_device(cts, CTS, keys[rotations - 1], elts[rotations - 1], scratch, out, stream=ctx.stream())
+        torch.cuda.synchronize()
+        e2e_match = bool(np.array_equal(out[:4].cpu().numpy().view(np.uint64), host_out[:4]))
+        for sw in switches:
+            sw.close()
 
     if rank != 0:
         if dist:
@@ -359,11 +364,11 @@ def main():
         "dtype": "u64", "data": "synthetic",
         "config": {"workload": "config2: 256 random cts x rotations 1..128 (g = 3^r mod 2n), seeded random "
                                "NTT-form keys", "n": N2, "primes_bits": BITS2, "t": T2, "dnum": 4,
-                   "cts": CTS, "rotations": ROTATIONS, "parallelism": f"replicas x{world} (weak)",
+                   "cts": CTS, "rotations": rotations, "parallelism": f"replicas x{world} (weak)",
                    "l2": "inputs+keys 448 MB > 126 MB L2; every rotation re-reads all cts"},
         "e2e": {"value": e2e_value, "unit": "keyswitches/s", "api": "bfvgpu.Switch.apply_many (C ABI, pinned host)",
-                "h2d_bytes_per_step": CTS * 2 * 4 * N2 * 8 * ROTATIONS,
-                "d2h_bytes_per_step": CTS * 2 * 4 * N2 * 8 * ROTATIONS, "steps": args.e2e_steps,
+                "h2d_bytes_per_step": CTS * 2 * 4 * N2 * 8 * rotations,
+                "d2h_bytes_per_step": CTS * 2 * 4 * N2 * 8 * rotations, "steps": args.e2e_steps,
                 "matches_device_path": e2e_match},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
