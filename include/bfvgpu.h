@@ -117,6 +117,20 @@ uint64_t bfvgpu_keyswitch_scratch_words(const bfvgpu_ctx *ctx, uint64_t count);
 int32_t bfvgpu_keyswitch_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,
                                 const uint64_t *key, uint32_t galois_elt, uint64_t *scratch,
                                 uint64_t *out, void *stream);
+/* The same keyswitch as bfvgpu_keyswitch_device, for callers that cannot allocate
+ * device memory when they need it (a worker whose device footprint is fixed and
+ * audited at session start, or code that must not take cudaMalloc's implicit device
+ * synchronisation).  No counterpart in the reference.  It allocates nothing: the
+ * scratch is a fixed 8 MiB array in the library's device image, which every GPU that
+ * loads the library holds until exit.  Limit: count * 2 * k * n * 8 bytes <= 8 MiB
+ * (12 ciphertexts at n = 8192 with 4+1 primes, 4 at ART-002); larger counts fail with
+ * BFVGPU_E_SHAPE.  The first call for a device looks the array's address up with that
+ * device current, so make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race; it keeps the last call's contents (nothing in it
+ * needs to start at zero). */
+int32_t bfvgpu_keyswitch_device_noalloc(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,
+                                        const uint64_t *key, uint32_t galois_elt, uint64_t *out,
+                                        void *stream);
 /* Lift + forward NTT of ring-59 weight blocks [blocks][n] -> [blocks][dk][n]. */
 int32_t bfvgpu_weights_ntt_device(bfvgpu_ctx *ctx, const uint64_t *ring, uint64_t blocks,
                                   uint64_t *out, void *stream);

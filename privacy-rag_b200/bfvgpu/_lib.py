@@ -69,6 +69,7 @@ _SIGNATURES = {
     "bfvgpu_ntt_device": (I32, [VP, VP, U64, U32, U32, I32, VP]),
     "bfvgpu_keyswitch_scratch_words": (U64, [VP, U64]),
     "bfvgpu_keyswitch_device": (I32, [VP, VP, U64, VP, U32, VP, VP, VP]),
+    "bfvgpu_keyswitch_device_noalloc": (I32, [VP, VP, U64, VP, U32, VP, VP]),
     "bfvgpu_weights_ntt_device": (I32, [VP, VP, U64, VP, VP]),
     "bfvgpu_matrix_groups_device": (I32, [VP, VP, U64, VP, U64, VP, VP, VP, VP]),
     "bfvgpu_ntt_open": (I32, [VP, I32, U64, ctypes.POINTER(VP)]),

@@ -14,8 +14,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "lib", "libbfvgpu.so")
-SOURCES = ["kernels.cu", "bfvgpu.cu"]
-HEADERS = ["arith.cuh", "ntt_core.cuh", "block_ops.cuh", "kernels.cuh"]
+SOURCES = ["kernels.cu", "bfvgpu.cu", "noalloc.cu"]
+HEADERS = ["arith.cuh", "ntt_core.cuh", "block_ops.cuh", "kernels.cuh", "ctx_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

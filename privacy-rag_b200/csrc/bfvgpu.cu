@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "bfvgpu.h"
+#include "ctx_internal.h"
 #include "kernels.cuh"
 
 using u128 = unsigned __int128;
@@ -1242,3 +1243,15 @@ int32_t bfvgpu_token_release(bfvgpu_token* t) {
 }
 
 }  // extern "C"
+
+// ---- library-internal hooks (ctx_internal.h) ---------------------------------------------
+namespace bfvgpu {
+const DevParams* internal_params(const bfvgpu_ctx* ctx, int* device, cudaStream_t* stream) {
+  if (!ctx) return nullptr;
+  if (device) *device = ctx->c.device;
+  if (stream) *stream = ctx->c.stream;
+  return &ctx->c.P;
+}
+void internal_set_error(const std::string& what) { g_last_error = what; }
+void internal_count_launch(uint64_t n) { count_launch(n); }
+}  // namespace bfvgpu
