@@ -20,6 +20,10 @@
 
 namespace bfvgpu {
 
+// Largest radix (log2) of the register butterfly units: radix-8 passes keep a unit in
+// ~16 registers, which lets 2-3 blocks share an SM (measured fastest on B200).
+constexpr int kMaxRadix = 3;
+
 // Divide-and-round by the special prime q_s (last prime) of one coefficient:
 // (x_p - ((x_s + floor(q_s/2)) mod q_s mod q_p - floor(q_s/2) mod q_p)) * q_s^-1 mod q_p.
 BFV_HD uint64_t moddown_elem(uint64_t xv, uint64_t xs, const Modulus& mp, const Modulus& ms) {
@@ -46,9 +50,9 @@ BFV_HD void op_ntt(const Ex& ex, uint64_t* s, uint64_t blk, bool inverse, uint64
   auto ld = [a](int i) { return a[i]; };
   auto st = [a](int i, uint64_t v) { a[i] = v; };
   if (inverse)
-    ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+    ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
   else
-    ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+    ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
 }
 
 // ---- weight lift + NTT: block = (weight block b, data prime p) --------------------------
@@ -66,7 +70,7 @@ BFV_HD void op_lift_ntt(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t*
     return v + (adjust & (uint64_t(0) - (v >> 58)));
   };
   auto st = [o](int i, uint64_t v) { o[i] = v; };
-  ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+  ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
 }
 
 // ---- product over input blocks + INTT (+ mask, + Enc(0)): block = (group g, c, p) -------
@@ -104,7 +108,7 @@ BFV_HD void op_mac_intt(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t*
     if (mask) v = sub_mod(v, scale_plain_coeff(mask[i], pa.q_mod_t, pa.upper_half, pa.t, pa.tlog, m), m.q);
     o[i] = v;
   };
-  ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+  ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
 }
 
 // ---- Galois automorphism + keyswitch main part: block = (ciphertext, key-level prime p) --
@@ -137,7 +141,7 @@ BFV_HD void op_ks_main(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* 
       return y;
     };
     auto st = [s](int i, uint64_t v) { s[spad(i)] = v; };
-    ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+    ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
     const uint64_t* k0 = key + ((uint64_t)(j * 2 + 0) * k + p) * N;
     const uint64_t* k1 = key + ((uint64_t)(j * 2 + 1) * k + p) * N;
     ex.run(N, [&](int i) {
@@ -157,7 +161,7 @@ BFV_HD void op_ks_main(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* 
     uint64_t* a = c ? acc1 : acc0;
     auto ld = [a](int i) { return a[i]; };
     auto st = [a](int i, uint64_t v) { a[i] = v; };
-    ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+    ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
   }
 }
 
@@ -201,7 +205,7 @@ BFV_HD void op_enc0_x(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* s
   {
     auto ld = [u](int i) { return u[i]; };
     auto st = [U](int i, uint64_t v) { U[i] = v; };
-    ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+    ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
   }
   for (uint32_t c = 0; c < 2; ++c) {
     const uint64_t* pkc = pk + ((uint64_t)c * k + p) * N;
@@ -209,7 +213,7 @@ BFV_HD void op_enc0_x(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* s
     uint64_t* xo = x + ((g * 2 + c) * k + p) * N;
     auto ld = [=](int i) { return mul_mod(U[i], pkc[i], m); };
     auto st = [=](int i, uint64_t v) { xo[i] = add_mod(v, e[i], m.q); };
-    ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+    ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
   }
 }
 
@@ -226,12 +230,12 @@ BFV_HD void op_client_phase(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* d
   {
     auto ld = [a](int i) { return a[i]; };
     auto st = [s](int i, uint64_t v) { s[spad(i)] = v; };
-    ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+    ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
   }
   {
     auto ld = [=](int i) { return mul_mod(s[spad(i)], key[i], m); };
     auto st = [a](int i, uint64_t v) { a[i] = v; };
-    ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+    ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
   }
 }
 
@@ -253,7 +257,7 @@ BFV_HD void op_token_lift_ntt(const Ex& ex, uint64_t* s, uint64_t blk, const uin
     return v + (adjust & (uint64_t(0) - (v >> 58)));
   };
   auto st = [o](int i, uint64_t v) { o[i] = v; };
-  ntt_forward<LOGN>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+  ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
 }
 
 template <int LOGN, class Ex>
@@ -278,7 +282,7 @@ BFV_HD void op_token_mac_intt(const Ex& ex, uint64_t* s, uint64_t blk, const uin
     const uint32_t dest = ((uint32_t)j + 2u * (uint32_t)N - (kTokenWidth - 1)) & (2u * (uint32_t)N - 1u);
     o[dest & (N - 1)] = dest >= N ? neg_mod(v, m.q) : v;
   };
-  ntt_inverse<LOGN>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+  ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
 }
 
 // ---- CRT of one target's dk residues to dk little-endian 64-bit limbs in [0, Q) ------------

@@ -26,9 +26,16 @@
 
 namespace bfvgpu {
 
+// Block shape per degree, from a sweep of radix x blocks/SM x block size on B200:
+// n <= 8192: 256 threads, 3 blocks per SM (<= 80 registers); n = 16384: 512 threads,
+// one block per SM (136 KiB of shared memory).  Small test degrees use n/16 threads.
 template <int LOGN>
 constexpr int threads_for() {
-  return ((1 << LOGN) / 16) < 512 ? ((1 << LOGN) / 16) : 512;
+  return LOGN >= 14 ? 512 : (((1 << LOGN) / 16) < 256 ? ((1 << LOGN) / 16) : 256);
+}
+template <int LOGN>
+constexpr int blocks_per_sm() {
+  return LOGN >= 14 ? 1 : 3;
 }
 template <int LOGN>
 constexpr size_t smem_bytes() {
@@ -39,7 +46,7 @@ constexpr size_t smem_bytes() {
 // transform-bearing kernels: one block per limb, bodies in block_ops.cuh
 // ---------------------------------------------------------------------------------
 template <int LOGN, bool INV>
-__global__ void __launch_bounds__(threads_for<LOGN>())
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_ntt(uint64_t* data, uint32_t prime_count, uint32_t prime_offset, const Modulus* mods, const ulonglong2* fwd,
           const ulonglong2* inv) {
   extern __shared__ uint64_t smem[];
@@ -47,14 +54,14 @@ __global__ void __launch_bounds__(threads_for<LOGN>())
 }
 
 template <int LOGN>
-__global__ void __launch_bounds__(threads_for<LOGN>())
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_lift_ntt(const uint64_t* ring, uint64_t* out, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
   extern __shared__ uint64_t smem[];
   op_lift_ntt<LOGN>(BlockExec{}, smem, blockIdx.x, ring, out, dk, mods, fwd);
 }
 
 template <int LOGN>
-__global__ void __launch_bounds__(threads_for<LOGN>())
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_mac_intt(const uint64_t* in, const uint64_t* w, uint64_t* out, uint32_t inputs, uint32_t k, uint32_t dk,
                const Modulus* mods, const ulonglong2* inv, ProtectArgs prot) {
   extern __shared__ uint64_t smem[];
@@ -62,7 +69,7 @@ __global__ void __launch_bounds__(threads_for<LOGN>())
 }
 
 template <int LOGN>
-__global__ void __launch_bounds__(threads_for<LOGN>())
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_ks_main(const uint64_t* cts, const uint64_t* key, uint64_t* acc, uint32_t elt, uint32_t k, uint32_t dk,
               const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv) {
   extern __shared__ uint64_t smem[];
@@ -70,7 +77,7 @@ __global__ void __launch_bounds__(threads_for<LOGN>())
 }
 
 template <int LOGN>
-__global__ void __launch_bounds__(threads_for<LOGN>())
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_ks_moddown(const uint64_t* acc, const uint64_t* cts, uint64_t* out, uint32_t ginv, uint32_t k, uint32_t dk,
                  const Modulus* mods) {
   extern __shared__ uint64_t smem[];
@@ -78,7 +85,7 @@ __global__ void __launch_bounds__(threads_for<LOGN>())
 }
 
 template <int LOGN>
-__global__ void __launch_bounds__(threads_for<LOGN>())
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_enc0_x(const uint64_t* samples, const uint64_t* pk, uint64_t* u_ntt, uint64_t* x, uint32_t k,
              const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv) {
   extern __shared__ uint64_t smem[];
@@ -86,7 +93,7 @@ __global__ void __launch_bounds__(threads_for<LOGN>())
 }
 
 template <int LOGN>
-__global__ void __launch_bounds__(threads_for<LOGN>())
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_client_phase(uint64_t* data, const uint64_t* sk, uint32_t dk, const Modulus* mods, const ulonglong2* fwd,
                    const ulonglong2* inv) {
   extern __shared__ uint64_t smem[];
@@ -94,14 +101,14 @@ __global__ void __launch_bounds__(threads_for<LOGN>())
 }
 
 template <int LOGN>
-__global__ void __launch_bounds__(threads_for<LOGN>())
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_token_lift_ntt(const uint64_t* ring, uint64_t* w, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
   extern __shared__ uint64_t smem[];
   op_token_lift_ntt<LOGN>(BlockExec{}, smem, blockIdx.x, ring, w, dk, mods, fwd);
 }
 
 template <int LOGN>
-__global__ void __launch_bounds__(threads_for<LOGN>())
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_token_mac_intt(const uint64_t* in, const uint64_t* w, const uint64_t* scaled, uint64_t* out, uint32_t slots,
                      uint32_t dk, const Modulus* mods, const ulonglong2* inv) {
   extern __shared__ uint64_t smem[];

@@ -37,15 +37,15 @@ struct SmemWords {
   static constexpr int value = (1 << LOGN) + ((1 << LOGN) >> 4);
 };
 
-// Pass schedule: radix-16 passes first, then radix-8 (forward); reversed for inverse.
-template <int LOGN>
+// Pass schedule: ceil(LOGN / MAXR) passes, the larger radices first (forward) and
+// reversed for the inverse.  MAXR = 4 gives radix-16/8 passes, MAXR = 3 radix-8/4.
+template <int LOGN, int MAXR = 4>
 struct Schedule {
-  static constexpr int passes = LOGN <= 4 ? 1 : (LOGN == 5 ? 2 : (LOGN + 3) / 4);
-  static constexpr int fours = LOGN <= 4 ? 0 : (LOGN == 5 ? 0 : LOGN - 3 * passes);
+  static constexpr int passes = LOGN <= MAXR ? 1 : (LOGN + MAXR - 1) / MAXR;
+  static constexpr int base = LOGN / passes;
+  static constexpr int extra = LOGN % passes;  // passes with radix base + 1
   // radix (log2) of forward pass p
-  static constexpr int fwd_r(int p) {
-    return LOGN <= 4 ? LOGN : (LOGN == 5 ? (p == 0 ? 3 : 2) : (p < fours ? 4 : 3));
-  }
+  static constexpr int fwd_r(int p) { return p < extra ? base + 1 : base; }
   static constexpr int fwd_level(int p) {
     int l = 0;
     for (int i = 0; i < p; ++i) l += fwd_r(i);
@@ -175,24 +175,24 @@ struct HostExec {
   void sync() const {}
 };
 
-template <int LOGN, int P, class Ex, class Ld, class St>
+template <int LOGN, int MAXR, int P, class Ex, class Ld, class St>
 BFV_HD void fwd_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t q, const Ld& ld,
                        const St& st) {
-  using S = Schedule<LOGN>;
+  using S = Schedule<LOGN, MAXR>;
   if constexpr (P < S::passes) {
     constexpr int R = S::fwd_r(P);
     constexpr int L = S::fwd_level(P);
     constexpr bool first = P == 0, last = P == S::passes - 1;
     ex.run(1 << (LOGN - R), [&](int u) { fwd_unit<LOGN, R, first, last>(s, u, L, tw, q, ld, st); });
     ex.sync();
-    fwd_passes<LOGN, P + 1>(ex, s, tw, q, ld, st);
+    fwd_passes<LOGN, MAXR, P + 1>(ex, s, tw, q, ld, st);
   }
 }
 
-template <int LOGN, int P, class Ex, class Ld, class St>
+template <int LOGN, int MAXR, int P, class Ex, class Ld, class St>
 BFV_HD void inv_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t q, uint64_t invn,
                        uint64_t invn_q, const Ld& ld, const St& st) {
-  using S = Schedule<LOGN>;
+  using S = Schedule<LOGN, MAXR>;
   if constexpr (P < S::passes) {
     constexpr int R = S::inv_r(P);
     constexpr int L = S::inv_level(P);
@@ -200,24 +200,25 @@ BFV_HD void inv_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t
     ex.run(1 << (LOGN - R),
            [&](int u) { inv_unit<LOGN, R, first, last>(s, u, L, tw, q, invn, invn_q, ld, st); });
     ex.sync();
-    inv_passes<LOGN, P + 1>(ex, s, tw, q, invn, invn_q, ld, st);
+    inv_passes<LOGN, MAXR, P + 1>(ex, s, tw, q, invn, invn_q, ld, st);
   }
 }
 
 // Forward NTT of one limb: ld(i) gives input coefficient i (< 4q), st(i, v) receives
-// canonical NTT slot i.  Ends with a block-wide barrier.
-template <int LOGN, class Ex, class Ld, class St>
+// canonical NTT slot i.  Ends with a block-wide barrier.  The block needs at most
+// n >> MAXR threads' worth of units per pass (any block size up to that works).
+template <int LOGN, int MAXR = 4, class Ex, class Ld, class St>
 BFV_HD void ntt_forward(const Ex& ex, uint64_t* s, const ulonglong2* tw, const Modulus& m, const Ld& ld,
                         const St& st) {
-  fwd_passes<LOGN, 0>(ex, s, tw, m.q, ld, st);
+  fwd_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, ld, st);
 }
 
 // Inverse NTT of one limb: ld(i) gives NTT slot i (< 2q), st(i, v) receives canonical
 // coefficient i.  Ends with a block-wide barrier.
-template <int LOGN, class Ex, class Ld, class St>
+template <int LOGN, int MAXR = 4, class Ex, class Ld, class St>
 BFV_HD void ntt_inverse(const Ex& ex, uint64_t* s, const ulonglong2* tw, const Modulus& m, const Ld& ld,
                         const St& st) {
-  inv_passes<LOGN, 0>(ex, s, tw, m.q, m.invn, m.invn_q, ld, st);
+  inv_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, m.invn, m.invn_q, ld, st);
 }
 
 // Bit reversal of an index of LOGN bits.
