@@ -117,6 +117,27 @@ uint64_t bfvgpu_keyswitch_scratch_words(const bfvgpu_ctx *ctx, uint64_t count);
 int32_t bfvgpu_keyswitch_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,
                                 const uint64_t *key, uint32_t galois_elt, uint64_t *scratch,
                                 uint64_t *out, void *stream);
+/* Hoisted multi-rotation keyswitch: the same outputs as bfvgpu_keyswitch_device for
+ * every (key, ciphertext) pair, when many Galois elements are applied to one batch.
+ *  1. prepare (once per key): prepared [bfvgpu_keyswitch_prepared_words] = the key with
+ *     its NTT slots permuted for galois_elt plus the element's negation correction;
+ *  2. hoist (once per ciphertext batch): hoisted [bfvgpu_keyswitch_hoist_words(count)] =
+ *     the NTT of every c1 digit reduced into every key-level prime, and a flag per
+ *     ciphertext whose c1 holds a zero word (those take an exact per-element path);
+ *  3. rotate (per element): out [count][2][dk][n] from hoisted + prepared; scratch holds
+ *     count * 2 * k * n words.  galois_elt must be the element the key was prepared for.
+ * Per element this runs 2k inverse NTTs per ciphertext instead of dk*k forward + 2k
+ * inverse (switch.cu:146-149 runs both per apply). */
+uint64_t bfvgpu_keyswitch_prepared_words(const bfvgpu_ctx *ctx);
+uint64_t bfvgpu_keyswitch_hoist_words(const bfvgpu_ctx *ctx, uint64_t count);
+int32_t bfvgpu_keyswitch_prepare_device(bfvgpu_ctx *ctx, const uint64_t *key, uint32_t galois_elt,
+                                        uint64_t *prepared, void *stream);
+int32_t bfvgpu_keyswitch_hoist_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,
+                                      uint64_t *hoisted, void *stream);
+int32_t bfvgpu_keyswitch_rotate_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,
+                                       const uint64_t *hoisted, const uint64_t *prepared,
+                                       uint32_t galois_elt, uint64_t *scratch, uint64_t *out,
+                                       void *stream);
 /* The same keyswitch as bfvgpu_keyswitch_device, for callers that cannot allocate
  * device memory when they need it (a worker whose device footprint is fixed and
  * audited at session start, or code that must not take cudaMalloc's implicit device

@@ -70,6 +70,11 @@ _SIGNATURES = {
     "bfvgpu_keyswitch_scratch_words": (U64, [VP, U64]),
     "bfvgpu_keyswitch_device": (I32, [VP, VP, U64, VP, U32, VP, VP, VP]),
     "bfvgpu_keyswitch_device_noalloc": (I32, [VP, VP, U64, VP, U32, VP, VP]),
+    "bfvgpu_keyswitch_prepared_words": (U64, [VP]),
+    "bfvgpu_keyswitch_hoist_words": (U64, [VP, U64]),
+    "bfvgpu_keyswitch_prepare_device": (I32, [VP, VP, U32, VP, VP]),
+    "bfvgpu_keyswitch_hoist_device": (I32, [VP, VP, U64, VP, VP]),
+    "bfvgpu_keyswitch_rotate_device": (I32, [VP, VP, U64, VP, VP, U32, VP, VP, VP]),
     "bfvgpu_weights_ntt_device": (I32, [VP, VP, U64, VP, VP]),
     "bfvgpu_matrix_groups_device": (I32, [VP, VP, U64, VP, U64, VP, VP, VP, VP]),
     "bfvgpu_ntt_open": (I32, [VP, I32, U64, ctypes.POINTER(VP)]),

@@ -124,6 +124,26 @@ class Context:
         check(lib().bfvgpu_keyswitch_device(self._h, self._dptr(cts), count, self._dptr(key), galois_elt,
                                             self._dptr(scratch), self._dptr(out), stream), "keyswitch_device")
 
+    def keyswitch_prepared_words(self) -> int:
+        return int(lib().bfvgpu_keyswitch_prepared_words(self._h))
+
+    def keyswitch_hoist_words(self, count: int) -> int:
+        return int(lib().bfvgpu_keyswitch_hoist_words(self._h, count))
+
+    def keyswitch_prepare_device(self, key, galois_elt: int, prepared, stream: int | None = None):
+        check(lib().bfvgpu_keyswitch_prepare_device(self._h, self._dptr(key), galois_elt, self._dptr(prepared),
+                                                    stream), "keyswitch_prepare_device")
+
+    def keyswitch_hoist_device(self, cts, count: int, hoisted, stream: int | None = None):
+        check(lib().bfvgpu_keyswitch_hoist_device(self._h, self._dptr(cts), count, self._dptr(hoisted), stream),
+              "keyswitch_hoist_device")
+
+    def keyswitch_rotate_device(self, cts, count: int, hoisted, prepared, galois_elt: int, scratch, out,
+                                stream: int | None = None):
+        check(lib().bfvgpu_keyswitch_rotate_device(self._h, self._dptr(cts), count, self._dptr(hoisted),
+                                                   self._dptr(prepared), galois_elt, self._dptr(scratch),
+                                                   self._dptr(out), stream), "keyswitch_rotate_device")
+
     def weights_ntt_device(self, ring, blocks: int, out, stream: int | None = None):
         check(lib().bfvgpu_weights_ntt_device(self._h, self._dptr(ring), blocks, self._dptr(out), stream),
               "weights_ntt_device")

@@ -630,6 +630,58 @@ int32_t bfvgpu_keyswitch_device(bfvgpu_ctx* ctx, const uint64_t* cts, uint64_t c
   });
 }
 
+uint64_t bfvgpu_keyswitch_prepared_words(const bfvgpu_ctx* ctx) {
+  return ctx ? (2ull * ctx->c.dk + 2) * ctx->c.k * ctx->c.n : 0;
+}
+
+uint64_t bfvgpu_keyswitch_hoist_words(const bfvgpu_ctx* ctx, uint64_t count) {
+  return ctx ? count * ctx->c.dk * ctx->c.k * ctx->c.n + (count + 1) / 2 : 0;
+}
+
+int32_t bfvgpu_keyswitch_prepare_device(bfvgpu_ctx* ctx, const uint64_t* key, uint32_t galois_elt,
+                                        uint64_t* prepared, void* stream) {
+  return guard([&] {
+    if (!ctx || !key || !prepared) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    if (!(galois_elt & 1) || galois_elt >= 2 * ctx->c.n) fail(BFVGPU_E_ELEMENT, "E_BFVGPU_GALOIS_ELEMENT");
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    cuda_check(launch_ks_keyprep(ctx->c.P, key, galois_elt, prepared, pick(ctx, stream)), "keyprep");
+    count_launch();
+  });
+}
+
+int32_t bfvgpu_keyswitch_hoist_device(bfvgpu_ctx* ctx, const uint64_t* cts, uint64_t count, uint64_t* hoisted,
+                                      void* stream) {
+  return guard([&] {
+    if (!ctx || !cts || !hoisted || !count) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    uint32_t* zflag = (uint32_t*)(hoisted + count * ctx->c.dk * ctx->c.k * ctx->c.n);
+    cuda_check(launch_ks_hoist(ctx->c.P, cts, count, hoisted, zflag, pick(ctx, stream)), "hoist");
+    count_launch();
+  });
+}
+
+int32_t bfvgpu_keyswitch_rotate_device(bfvgpu_ctx* ctx, const uint64_t* cts, uint64_t count, const uint64_t* hoisted,
+                                       const uint64_t* prepared, uint32_t galois_elt, uint64_t* scratch,
+                                       uint64_t* out, void* stream) {
+  return guard([&] {
+    if (!ctx || !cts || !hoisted || !prepared || !scratch || !out || !count)
+      fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    if (!(galois_elt & 1) || galois_elt >= 2 * ctx->c.n) fail(BFVGPU_E_ELEMENT, "E_BFVGPU_GALOIS_ELEMENT");
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    const uint32_t* zflag = (const uint32_t*)(hoisted + count * ctx->c.dk * ctx->c.k * ctx->c.n);
+    cuda_check(launch_ks_rotate(ctx->c.P, cts, count, hoisted, zflag, prepared, galois_elt, scratch, out,
+                                pick(ctx, stream)),
+               "rotate");
+    count_launch(2);
+  });
+}
+
 int32_t bfvgpu_weights_ntt_device(bfvgpu_ctx* ctx, const uint64_t* ring, uint64_t blocks, uint64_t* out,
                                   void* stream) {
   return guard([&] {

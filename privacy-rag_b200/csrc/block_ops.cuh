@@ -191,6 +191,156 @@ BFV_HD void op_ks_moddown(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_
   ex.sync();
 }
 
+// ---- hoisted rotations: many Galois elements over one ciphertext batch -------------------
+// With slot(i) the NTT-slot permutation of X -> X^g, the reference's keyswitch product
+// acc_c[i] = sum_j NTT(digit_j)[i] key_j[c][i] is acc_c[i] = A_c[slot(i)] where
+//   A_c[s] = sum_j NTT(b_j)[s] Kt_j[c][s],   Kt_j[c][s] = key_j[c][slot^-1(s)]
+// and b_j is the pre-negated digit of op_ks_main.  Without zero coefficients in c1,
+// NTT(b_j) = Y_j - (q_j mod q_p) W with Y_j = NTT(c1_j mod q_p) (independent of g) and
+// W = NTT(neg_g) (neg_g[s] = 1 where X -> X^g negates coefficient s), so
+//   A_c[s] = sum_j Y_j[s] Kt_j[c][s] - Ct_c[s],   Ct_c[s] = W[s] sum_j (q_j mod q_p) Kt_j[c][s].
+// INTT(A_c permuted by slot) = sigma_g(INTT(A_c)), and divide-and-round by the odd special
+// prime commutes with sigma_g, so the output is sigma_g(moddown(INTT(A_c)) + [c=0] c0):
+// the automorphism becomes one coefficient permutation at the very end.
+
+// Y [ct][dk][k][n]: hoisted digit transforms; zflag[ct] set if c1 has a zero coefficient.
+template <int LOGN, class Ex>
+BFV_HD void op_ks_hoist(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* cts, uint64_t* Y, uint32_t* zflag,
+                        uint32_t k, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
+  constexpr uint64_t N = uint64_t(1) << LOGN;
+  const uint64_t ct = blk / ((uint64_t)dk * k);
+  const uint32_t j = (uint32_t)((blk / k) % dk), p = (uint32_t)(blk % k);
+  const Modulus m = mods[p];
+  const uint64_t* src = cts + (ct * 2 * dk + dk + j) * N;
+  uint64_t* y = Y + ((ct * dk + j) * k + p) * N;
+  const bool reduce = mods[j].q > m.q;
+  uint32_t zero = 0;
+  auto ld = [&](int i) {
+    const uint64_t x = src[i];
+    zero |= (x == 0);
+    return reduce ? reduce64(x, m) : x;
+  };
+  auto st = [y](int i, uint64_t v) { y[i] = v; };
+  ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+  if (zero && p == 0) {
+#if defined(__CUDA_ARCH__)
+    atomicOr(zflag + ct, 1u);
+#else
+    zflag[ct] = 1;
+#endif
+  }
+}
+
+// Prepared key for element g: Kt [dk][2][k][n] then Ct [2][k][n].  Block = prime p.
+template <int LOGN, class Ex>
+BFV_HD void op_ks_keyprep(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* key, uint64_t* prepared,
+                          uint32_t elt, uint32_t ginv, uint32_t k, uint32_t dk, const Modulus* mods,
+                          const uint64_t* qjp, const ulonglong2* fwd) {
+  constexpr int N = 1 << LOGN;
+  const uint32_t p = (uint32_t)blk;
+  const Modulus m = mods[p];
+  const uint32_t mask2n = 2u * N - 1u;
+  auto ld = [=](int i) { return (uint64_t)((((uint32_t)i * elt) & mask2n) >= (uint32_t)N ? 1 : 0); };
+  auto st = [s](int i, uint64_t v) { s[spad(i)] = v; };
+  ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+  uint64_t* Kt = prepared;
+  uint64_t* Ct = prepared + (uint64_t)dk * 2 * k * N;
+  ex.run(N, [&](int sl) {
+    const int from = galois_slot(sl, ginv, LOGN);
+    for (uint32_t c = 0; c < 2; ++c) {
+      uint64_t sum = 0;
+      for (uint32_t j = 0; j < dk; ++j) {
+        const uint64_t v = key[((uint64_t)(j * 2 + c) * k + p) * N + from];
+        Kt[((uint64_t)(j * 2 + c) * k + p) * N + sl] = v;
+        sum = add_mod(sum, mul_mod(v, qjp[j * k + p], m), m.q);
+      }
+      Ct[((uint64_t)c * k + p) * N + sl] = mul_mod(sum, s[spad(sl)], m);
+    }
+  });
+  ex.sync();
+}
+
+// One rotation for block (ct, c, p): x [ct][2][k][n] = INTT(A_c).  Ciphertexts flagged in
+// zflag take the exact path: A_c accumulated from fresh pre-negated digit transforms in
+// x itself, then transformed in place.
+template <int LOGN, class Ex>
+BFV_HD void op_ks_rotate(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* cts, const uint64_t* Y,
+                         const uint32_t* zflag, const uint64_t* prepared, uint64_t* x, uint32_t elt, uint32_t k,
+                         uint32_t dk, const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd,
+                         const ulonglong2* inv) {
+  constexpr int N = 1 << LOGN;
+  const uint64_t ct = blk / (2 * k);
+  const uint32_t cp = (uint32_t)(blk % (2 * k)), c = cp / k, p = cp % k;
+  const Modulus m = mods[p];
+  const uint64_t* Kt = prepared + ((uint64_t)c * k + p) * N;  // digit j at + j*2*k*N
+  const uint64_t kstride = 2ull * k * N;
+  const uint64_t* Ct = prepared + (uint64_t)dk * 2 * k * N + ((uint64_t)c * k + p) * N;
+  uint64_t* xo = x + ((ct * 2 + c) * k + p) * (uint64_t)N;
+  auto st = [xo](int i, uint64_t v) { xo[i] = v; };
+  if (!zflag[ct]) {
+    const uint64_t* y = Y + (ct * dk * k + p) * (uint64_t)N;  // digit j at + j*k*N
+    const uint64_t ystride = (uint64_t)k * N;
+    auto ld = [=](int i) {
+      Acc128 acc;
+      for (uint32_t j = 0; j < dk; ++j) acc.mac(y[j * ystride + i], Kt[j * kstride + i]);
+      return sub_mod(acc.reduce(m), Ct[i], m.q);
+    };
+    ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+    return;
+  }
+  const uint64_t* c1 = cts + (ct * 2 * dk + dk) * (uint64_t)N;
+  const uint32_t mask2n = 2u * N - 1u;
+  for (uint32_t j = 0; j < dk; ++j) {
+    const uint64_t* src = c1 + (uint64_t)j * N;
+    const uint64_t adj = qjp[j * k + p];
+    const bool reduce = mods[j].q > m.q;
+    auto ldj = [=](int i) {
+      const uint64_t xv = src[i];
+      uint64_t y = reduce ? reduce64(xv, m) : xv;
+      if (xv && (((uint32_t)i * elt) & mask2n) >= (uint32_t)N) y = sub_mod(y, adj, m.q);
+      return y;
+    };
+    auto stj = [s](int i, uint64_t v) { s[spad(i)] = v; };
+    ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ldj, stj);
+    const uint64_t* kj = Kt + j * kstride;
+    ex.run(N, [&](int i) {
+      const uint64_t v = mul_mod(s[spad(i)], kj[i], m);
+      xo[i] = j ? add_mod(xo[i], v, m.q) : v;
+    });
+    ex.sync();
+  }
+  auto ldx = [xo](int i) { return xo[i]; };
+  ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ldx, st);
+}
+
+// out [ct][2][dk][n] = sigma_g(moddown(x_c) + [c=0] c0).  Block (ct, data prime p); the
+// pre-permutation limb is staged unpadded in shared memory and gathered per output.
+template <int LOGN, class Ex>
+BFV_HD void op_ks_finish(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* x, const uint64_t* cts,
+                         uint64_t* out, uint32_t ginv, uint32_t k, uint32_t dk, const Modulus* mods) {
+  constexpr int N = 1 << LOGN;
+  const uint64_t ct = blk / dk;
+  const uint32_t p = (uint32_t)(blk % dk);
+  const Modulus m = mods[p], ms = mods[k - 1];
+  const uint32_t mask2n = 2u * N - 1u;
+  for (uint32_t c = 0; c < 2; ++c) {
+    const uint64_t* xc = x + (ct * 2 + c) * k * (uint64_t)N;
+    const uint64_t* c0 = cts + (ct * 2 * dk + p) * (uint64_t)N;
+    ex.run(N, [&](int i) {
+      uint64_t v = moddown_elem(xc[(uint64_t)p * N + i], xc[(uint64_t)(k - 1) * N + i], m, ms);
+      if (c == 0) v = add_mod(v, c0[i], m.q);
+      s[i] = v;
+    });
+    ex.sync();
+    uint64_t* o = out + ((ct * 2 + c) * dk + p) * (uint64_t)N;
+    ex.run(N, [&](int i) {
+      const uint32_t src = ((uint32_t)i * ginv) & mask2n;
+      o[i] = src < (uint32_t)N ? s[src] : neg_mod(s[src - N], m.q);
+    });
+    ex.sync();
+  }
+}
+
 // ---- Enc(0) pre-moddown polys: block = (group, key-level prime p) ------------------------
 template <int LOGN, class Ex>
 BFV_HD void op_enc0_x(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* samples, const uint64_t* pk,

@@ -115,6 +115,39 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
   op_token_mac_intt<LOGN>(BlockExec{}, smem, blockIdx.x, in, w, scaled, out, slots, dk, mods, inv);
 }
 
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_ks_hoist(const uint64_t* cts, uint64_t* Y, uint32_t* zflag, uint32_t k, uint32_t dk, const Modulus* mods,
+               const ulonglong2* fwd) {
+  extern __shared__ uint64_t smem[];
+  op_ks_hoist<LOGN>(BlockExec{}, smem, blockIdx.x, cts, Y, zflag, k, dk, mods, fwd);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_ks_keyprep(const uint64_t* key, uint64_t* prepared, uint32_t elt, uint32_t ginv, uint32_t k, uint32_t dk,
+                 const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd) {
+  extern __shared__ uint64_t smem[];
+  op_ks_keyprep<LOGN>(BlockExec{}, smem, blockIdx.x, key, prepared, elt, ginv, k, dk, mods, qjp, fwd);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_ks_rotate(const uint64_t* cts, const uint64_t* Y, const uint32_t* zflag, const uint64_t* prepared, uint64_t* x,
+                uint32_t elt, uint32_t k, uint32_t dk, const Modulus* mods, const uint64_t* qjp,
+                const ulonglong2* fwd, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_ks_rotate<LOGN>(BlockExec{}, smem, blockIdx.x, cts, Y, zflag, prepared, x, elt, k, dk, mods, qjp, fwd, inv);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_ks_finish(const uint64_t* x, const uint64_t* cts, uint64_t* out, uint32_t ginv, uint32_t k, uint32_t dk,
+                const Modulus* mods) {
+  extern __shared__ uint64_t smem[];
+  op_ks_finish<LOGN>(BlockExec{}, smem, blockIdx.x, x, cts, out, ginv, k, dk, mods);
+}
+
 // c0 target gather (+ CRT): thread = (group, target)
 __global__ void k_gather_targets(const uint64_t* out, const uint64_t* targets, const uint32_t* counts,
                                  uint32_t max_count, uint32_t dk, int logn, const Modulus* mods,
@@ -212,6 +245,10 @@ static cudaError_t configure_for() {
   chk(allow_smem(k_ks_main<L>, s));
   chk(allow_smem(k_ks_moddown<L>, (size_t(1) << L) * 8));
   chk(allow_smem(k_enc0_x<L>, s));
+  chk(allow_smem(k_ks_hoist<L>, s));
+  chk(allow_smem(k_ks_keyprep<L>, s));
+  chk(allow_smem(k_ks_rotate<L>, s));
+  chk(allow_smem(k_ks_finish<L>, (size_t(1) << L) * 8));
   chk(allow_smem(k_client_phase<L>, s));
   if constexpr (L == 14) {
     chk(allow_smem(k_token_lift_ntt<L>, s));
@@ -299,6 +336,45 @@ cudaError_t launch_keyswitch(const DevParams& P, const uint64_t* cts, const uint
                                                                                         P.inv);
     k_ks_moddown<L_><<<(unsigned)(count * P.dk), threads_for<L_>(), (size_t(1) << L_) * 8, st>>>(acc, cts, out, ginv,
                                                                                                  P.k, P.dk, P.mod);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ks_hoist(const DevParams& P, const uint64_t* cts, uint64_t count, uint64_t* Y, uint32_t* zflag,
+                            cudaStream_t st) {
+  if (!count) return cudaSuccess;
+  if (P.k != P.dk + 1) return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(zflag, 0, count * sizeof(uint32_t), st);
+  if (e != cudaSuccess) return e;
+  BFV_DISPATCH(P.logn, {
+    k_ks_hoist<L_><<<(unsigned)(count * P.dk * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(cts, Y, zflag, P.k,
+                                                                                               P.dk, P.mod, P.fwd);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ks_keyprep(const DevParams& P, const uint64_t* key, uint32_t elt, uint64_t* prepared,
+                              cudaStream_t st) {
+  if (P.k != P.dk + 1) return cudaErrorInvalidValue;
+  const uint32_t ginv = inverse_mod_2n(elt, 2 * P.n);
+  BFV_DISPATCH(P.logn, {
+    k_ks_keyprep<L_><<<P.k, threads_for<L_>(), smem_bytes<L_>(), st>>>(key, prepared, elt, ginv, P.k, P.dk, P.mod,
+                                                                      P.qjp, P.fwd);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ks_rotate(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
+                             const uint32_t* zflag, const uint64_t* prepared, uint32_t elt, uint64_t* x, uint64_t* out,
+                             cudaStream_t st) {
+  if (!count) return cudaSuccess;
+  if (P.k != P.dk + 1) return cudaErrorInvalidValue;
+  const uint32_t ginv = inverse_mod_2n(elt, 2 * P.n);
+  BFV_DISPATCH(P.logn, {
+    k_ks_rotate<L_><<<(unsigned)(count * 2 * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(
+        cts, Y, zflag, prepared, x, elt, P.k, P.dk, P.mod, P.qjp, P.fwd, P.inv);
+    k_ks_finish<L_><<<(unsigned)(count * P.dk), threads_for<L_>(), (size_t(1) << L_) * 8, st>>>(x, cts, out, ginv,
+                                                                                               P.k, P.dk, P.mod);
   });
   return cudaGetLastError();
 }

@@ -67,6 +67,19 @@ cudaError_t launch_gather_targets(const DevParams& P, const uint64_t* out /*[gro
 cudaError_t launch_keyswitch(const DevParams& P, const uint64_t* cts, const uint64_t* key, uint32_t elt,
                              uint64_t count, uint64_t* acc, uint64_t* out, cudaStream_t st);
 
+// Hoisted multi-rotation keyswitch (see op_ks_hoist / op_ks_rotate):
+//  hoist:   Y [count][dk][k][n] = NTT(c1_j mod q_p); zflag [count] = c1 has a zero word
+//  keyprep: prepared [(dk*2 + 2)*k][n] = permuted key and correction for element elt
+//  rotate:  out [count][2][dk][n] = Galois(elt) + keyswitch of every ciphertext, x is
+//           scratch [count][2][k][n]
+cudaError_t launch_ks_hoist(const DevParams& P, const uint64_t* cts, uint64_t count, uint64_t* Y, uint32_t* zflag,
+                            cudaStream_t st);
+cudaError_t launch_ks_keyprep(const DevParams& P, const uint64_t* key, uint32_t elt, uint64_t* prepared,
+                              cudaStream_t st);
+cudaError_t launch_ks_rotate(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
+                             const uint32_t* zflag, const uint64_t* prepared, uint32_t elt, uint64_t* x, uint64_t* out,
+                             cudaStream_t st);
+
 // Enc(0) pre-moddown polys: x [groups][2][k][n] = INTT(NTT(u) . pk_c) + e_c with
 // samples [groups][3][k][n]; scratch u_ntt [groups][k][n].
 cudaError_t launch_enc0_x(const DevParams& P, const uint64_t* samples, const uint64_t* pk, uint64_t* u_ntt,
@@ -93,8 +106,9 @@ cudaError_t launch_token_evaluate(const DevParams& P, const uint64_t* inputs, ui
                                   const uint64_t* ring, const uint64_t* scaled, uint64_t* wscratch,
                                   uint64_t* acc, uint64_t* out, cudaStream_t st);
 
-// Acyclic packing merge prologue (Switch::packing_prepare): sum = L + X^s R and
-// diff = sigma_g(L - X^s R), g = 2^(level+1)+1, for [2][dk][n] ciphertexts.
+// Acyclic packing merge prologue (Switch::packing_prepare without its permutation, which
+// the keyswitch of the difference applies): sum = L + X^s R, diff = L - X^s R for
+// [2][dk][n] ciphertexts, s = n >> (level+1).
 cudaError_t launch_packing_prepare(const DevParams& P, const uint64_t* left, const uint64_t* right,
                                    uint64_t* sum, uint64_t* diff, unsigned level, cudaStream_t st);
 // a += b on [polys][n] data-prime polys.

@@ -84,6 +84,36 @@ int emu_keyswitch(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, con
   return 0;
 }
 
+// Hoisted path: hoist, key preparation, rotate + finish for one element.
+int emu_keyswitch_hoisted(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd,
+                          const uint64_t* inv, const uint64_t* cts, uint64_t count, const uint64_t* key, uint32_t elt,
+                          uint64_t* out, uint32_t* zflag_out) {
+  Tabs T = tabs(k, mods16, fwd, inv);
+  const uint64_t n = 1ull << logn;
+  std::vector<uint64_t> qjp((size_t)dk * k);
+  for (uint32_t j = 0; j < dk; ++j)
+    for (uint32_t p = 0; p < k; ++p) qjp[j * k + p] = T.mods[j].q % T.mods[p].q;
+  std::vector<uint64_t> Y(count * dk * k * n), prepared((2ull * dk + 2) * k * n), x(count * 2 * k * n);
+  std::vector<uint32_t> zflag(count, 0);
+  const uint32_t ginv = inv_mod_2n(elt, 2 * (uint32_t)n);
+  EMU_DISPATCH(logn, {
+    std::vector<uint64_t> s(SmemWords<L_>::value);
+    for (uint64_t b = 0; b < count * dk * k; ++b)
+      op_ks_hoist<L_>(HostExec{}, s.data(), b, cts, Y.data(), zflag.data(), k, dk, T.mods.data(), T.fwd);
+    for (uint64_t b = 0; b < k; ++b)
+      op_ks_keyprep<L_>(HostExec{}, s.data(), b, key, prepared.data(), elt, ginv, k, dk, T.mods.data(), qjp.data(),
+                        T.fwd);
+    for (uint64_t b = 0; b < count * 2 * k; ++b)
+      op_ks_rotate<L_>(HostExec{}, s.data(), b, cts, Y.data(), zflag.data(), prepared.data(), x.data(), elt, k, dk,
+                       T.mods.data(), qjp.data(), T.fwd, T.inv);
+    std::vector<uint64_t> s2(n);
+    for (uint64_t b = 0; b < count * dk; ++b)
+      op_ks_finish<L_>(HostExec{}, s2.data(), b, x.data(), cts, out, ginv, k, dk, T.mods.data());
+  });
+  for (uint64_t i = 0; i < count; ++i) zflag_out[i] = zflag[i];
+  return 0;
+}
+
 // Full protected matrix evaluation for `groups` groups:
 // cts [inputs][2][dk][n] coefficient form; ring [groups][inputs][n]; mask [groups][n]
 // or null; samples [groups][3][k][n] or null (pk [2][k][n]); out [groups][2][dk][n].

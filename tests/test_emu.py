@@ -96,6 +96,27 @@ def test_keyswitch_kernel_body(bfv, oracle, E, logn, elts):
             assert np.array_equal(out[c], oc.keyswitch(cts[c], key, elt)), (logn, elt, c)
 
 
+@pytest.mark.parametrize("logn,elts", [(5, [1, 3, 63]), (6, [5, 127, 9]), (13, [3, 2 ** 13 + 1, 16383]),
+                                       (14, [3, 1025])])
+def test_hoisted_keyswitch_kernel_bodies(bfv, oracle, E, logn, elts):
+    """Hoist + key preparation + rotate + finish equals the reference keyswitch; the
+    ciphertext with zero c1 words is flagged and takes the exact path."""
+    import ctypes
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+    k, dk, n = hc.k, hc.dk, 1 << logn
+    count = 3
+    cts = oc.uniform(300 + logn, count * 2 * dk, prime_count=dk).reshape(count, 2, dk, n)
+    cts[1, 1, 2, ::3] = 0
+    key = oc.uniform(400 + logn, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n)
+    for elt in elts:
+        out = np.zeros_like(cts)
+        flags = (ctypes.c_uint32 * count)()
+        E.emu_keyswitch_hoisted(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), count, p(key), elt, p(out), flags)
+        assert list(flags) == [0, 1, 0]
+        for c in range(count):
+            assert np.array_equal(out[c], oc.keyswitch(cts[c], key, elt)), (logn, elt, c)
+
+
 @pytest.mark.parametrize("logn", [6, 14])
 def test_matrix_mask_enc0_kernel_bodies(bfv, oracle, E, logn):
     hc, oc, mods, fwd, inv = make(bfv, oracle, logn)

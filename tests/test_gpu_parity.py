@@ -198,6 +198,39 @@ def test_keyswitch_device_batch(cfg2):
     assert np.array_equal(out.cpu().numpy().view(np.uint64), sw.apply_many(cts))
 
 
+@pytest.mark.parametrize("which", ["cfg2", "art"])
+def test_keyswitch_hoisted_device(which, request, oracle):
+    """Hoist once, prepare one key per element, rotate: every output equals the oracle's
+    reference keyswitch; a ciphertext with zero c1 words takes the exact path."""
+    import torch
+    hc, oc = request.getfixturevalue(which)
+    n, k, dk = oc.n, oc.k, oc.data_k
+    count = 5 if which == "cfg2" else 2
+    cts = oc.uniform(51, count * 2 * dk).reshape(count, 2, dk, n)
+    cts[1, 1, 0, ::9] = 0
+    elts = [3, pow(3, 11, 2 * n), 2 * n - 1] if which == "cfg2" else [1, 2 ** 9 + 1]
+    d_cts = torch.from_numpy(cts.view(np.int64)).cuda()
+    hoisted = torch.empty(hc.keyswitch_hoist_words(count), dtype=torch.int64, device="cuda")
+    prepared = torch.empty(hc.keyswitch_prepared_words(), dtype=torch.int64, device="cuda")
+    scratch = torch.empty(hc.keyswitch_scratch_words(count), dtype=torch.int64, device="cuda")
+    out = torch.empty_like(d_cts)
+    out_plain = torch.empty_like(d_cts)
+    torch.cuda.synchronize()
+    hc.keyswitch_hoist_device(d_cts, count, hoisted)
+    for i, elt in enumerate(elts):
+        key = oc.uniform(60 + i, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n)
+        d_key = torch.from_numpy(key.view(np.int64)).cuda()
+        torch.cuda.synchronize()
+        hc.keyswitch_prepare_device(d_key, elt, prepared)
+        hc.keyswitch_rotate_device(d_cts, count, hoisted, prepared, elt, scratch, out)
+        hc.keyswitch_device(d_cts, count, d_key, elt, scratch, out_plain)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy().view(np.uint64)
+        assert np.array_equal(got, out_plain.cpu().numpy().view(np.uint64)), elt
+        exp = oc.keyswitch_many(cts, key, [elt], threads=8)[0]
+        assert np.array_equal(got, exp), elt
+
+
 def test_packing_pair(art, oracle):
     import bfvgpu
     hc, oc = art
