@@ -119,8 +119,10 @@ int32_t bfvgpu_keyswitch_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t c
                                 uint64_t *out, void *stream);
 /* Hoisted multi-rotation keyswitch: the same outputs as bfvgpu_keyswitch_device for
  * every (key, ciphertext) pair, when many Galois elements are applied to one batch.
- *  1. prepare (once per key): prepared [bfvgpu_keyswitch_prepared_words] = the key with
- *     its NTT slots permuted for galois_elt plus the element's negation correction;
+ *  1. prepare (once per key, any number of keys per call): keys [count][dk][2][k][n]
+ *     (device), galois_elts [count] (host); prepared [count][bfvgpu_keyswitch_prepared_words]
+ *     = each key with its NTT slots permuted for its element plus the element's negation
+ *     correction;
  *  2. hoist (once per ciphertext batch): hoisted [bfvgpu_keyswitch_hoist_words(count)] =
  *     the NTT of every c1 digit reduced into every key-level prime, and a flag per
  *     ciphertext whose c1 holds a zero word (those take an exact per-element path);
@@ -130,8 +132,8 @@ int32_t bfvgpu_keyswitch_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t c
  * inverse (switch.cu:146-149 runs both per apply). */
 uint64_t bfvgpu_keyswitch_prepared_words(const bfvgpu_ctx *ctx);
 uint64_t bfvgpu_keyswitch_hoist_words(const bfvgpu_ctx *ctx, uint64_t count);
-int32_t bfvgpu_keyswitch_prepare_device(bfvgpu_ctx *ctx, const uint64_t *key, uint32_t galois_elt,
-                                        uint64_t *prepared, void *stream);
+int32_t bfvgpu_keyswitch_prepare_device(bfvgpu_ctx *ctx, const uint64_t *keys, const uint32_t *galois_elts,
+                                        uint64_t count, uint64_t *prepared, void *stream);
 int32_t bfvgpu_keyswitch_hoist_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,
                                       uint64_t *hoisted, void *stream);
 int32_t bfvgpu_keyswitch_rotate_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,

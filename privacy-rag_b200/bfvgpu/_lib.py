@@ -72,7 +72,7 @@ _SIGNATURES = {
     "bfvgpu_keyswitch_device_noalloc": (I32, [VP, VP, U64, VP, U32, VP, VP]),
     "bfvgpu_keyswitch_prepared_words": (U64, [VP]),
     "bfvgpu_keyswitch_hoist_words": (U64, [VP, U64]),
-    "bfvgpu_keyswitch_prepare_device": (I32, [VP, VP, U32, VP, VP]),
+    "bfvgpu_keyswitch_prepare_device": (I32, [VP, VP, U32P, U64, VP, VP]),
     "bfvgpu_keyswitch_hoist_device": (I32, [VP, VP, U64, VP, VP]),
     "bfvgpu_keyswitch_rotate_device": (I32, [VP, VP, U64, VP, VP, U32, VP, VP, VP]),
     "bfvgpu_weights_ntt_device": (I32, [VP, VP, U64, VP, VP]),

@@ -130,8 +130,12 @@ class Context:
     def keyswitch_hoist_words(self, count: int) -> int:
         return int(lib().bfvgpu_keyswitch_hoist_words(self._h, count))
 
-    def keyswitch_prepare_device(self, key, galois_elt: int, prepared, stream: int | None = None):
-        check(lib().bfvgpu_keyswitch_prepare_device(self._h, self._dptr(key), galois_elt, self._dptr(prepared),
+    def keyswitch_prepare_device(self, keys, galois_elts, prepared, stream: int | None = None):
+        """keys [count][dk][2][k][n] (device) for the Galois elements galois_elts (ints)
+        -> prepared [count][keyswitch_prepared_words()] (device)."""
+        elts = [int(e) for e in (galois_elts if hasattr(galois_elts, "__len__") else [galois_elts])]
+        arr = (U32 * len(elts))(*elts)
+        check(lib().bfvgpu_keyswitch_prepare_device(self._h, self._dptr(keys), arr, len(elts), self._dptr(prepared),
                                                     stream), "keyswitch_prepare_device")
 
     def keyswitch_hoist_device(self, cts, count: int, hoisted, stream: int | None = None):

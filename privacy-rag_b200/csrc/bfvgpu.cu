@@ -638,16 +638,17 @@ uint64_t bfvgpu_keyswitch_hoist_words(const bfvgpu_ctx* ctx, uint64_t count) {
   return ctx ? count * ctx->c.dk * ctx->c.k * ctx->c.n + (count + 1) / 2 : 0;
 }
 
-int32_t bfvgpu_keyswitch_prepare_device(bfvgpu_ctx* ctx, const uint64_t* key, uint32_t galois_elt,
-                                        uint64_t* prepared, void* stream) {
+int32_t bfvgpu_keyswitch_prepare_device(bfvgpu_ctx* ctx, const uint64_t* keys, const uint32_t* galois_elts,
+                                        uint64_t count, uint64_t* prepared, void* stream) {
   return guard([&] {
-    if (!ctx || !key || !prepared) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (!ctx || !keys || !galois_elts || !prepared || !count) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
     if (ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
-    if (!(galois_elt & 1) || galois_elt >= 2 * ctx->c.n) fail(BFVGPU_E_ELEMENT, "E_BFVGPU_GALOIS_ELEMENT");
+    for (uint64_t r = 0; r < count; ++r)
+      if (!(galois_elts[r] & 1) || galois_elts[r] >= 2 * ctx->c.n) fail(BFVGPU_E_ELEMENT, "E_BFVGPU_GALOIS_ELEMENT");
     require_device(ctx->c);
     DeviceScope scope(ctx->c.device);
-    cuda_check(launch_ks_keyprep(ctx->c.P, key, galois_elt, prepared, pick(ctx, stream)), "keyprep");
-    count_launch();
+    cuda_check(launch_ks_keyprep(ctx->c.P, keys, galois_elts, count, prepared, pick(ctx, stream)), "keyprep");
+    count_launch(2 * ((count + 255) / 256));
   });
 }
 

@@ -141,7 +141,7 @@ BFV_HD void op_ks_main(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* 
       return y;
     };
     auto st = [s](int i, uint64_t v) { s[spad(i)] = v; };
-    ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+    ntt_forward<LOGN, kMaxRadix, false>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
     const uint64_t* k0 = key + ((uint64_t)(j * 2 + 0) * k + p) * N;
     const uint64_t* k1 = key + ((uint64_t)(j * 2 + 1) * k + p) * N;
     ex.run(N, [&](int i) {
@@ -231,33 +231,47 @@ BFV_HD void op_ks_hoist(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t*
   }
 }
 
-// Prepared key for element g: Kt [dk][2][k][n] then Ct [2][k][n].  Block = prime p.
+// Key preparation for a batch of keys, in two kernels.  The prepared layout of key r is
+// Kt [dk][2][k][n] then Ct [2][k][n] (prepared_words = (2*dk + 2)*k*n).
+// (1) block (r, p): W = NTT_p(neg_g) written to Ct[c = 0][p] of key r.
 template <int LOGN, class Ex>
-BFV_HD void op_ks_keyprep(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* key, uint64_t* prepared,
-                          uint32_t elt, uint32_t ginv, uint32_t k, uint32_t dk, const Modulus* mods,
-                          const uint64_t* qjp, const ulonglong2* fwd) {
+BFV_HD void op_ks_negntt(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* prepared, uint64_t prepared_words,
+                         const uint32_t* elts, uint32_t k, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
   constexpr int N = 1 << LOGN;
-  const uint32_t p = (uint32_t)blk;
+  const uint64_t r = blk / k;
+  const uint32_t p = (uint32_t)(blk % k);
   const Modulus m = mods[p];
-  const uint32_t mask2n = 2u * N - 1u;
+  const uint32_t elt = elts[r], mask2n = 2u * N - 1u;
+  uint64_t* w = prepared + r * prepared_words + (uint64_t)dk * 2 * k * N + (uint64_t)p * N;
   auto ld = [=](int i) { return (uint64_t)((((uint32_t)i * elt) & mask2n) >= (uint32_t)N ? 1 : 0); };
-  auto st = [s](int i, uint64_t v) { s[spad(i)] = v; };
+  auto st = [w](int i, uint64_t v) { w[i] = v; };
   ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
-  uint64_t* Kt = prepared;
-  uint64_t* Ct = prepared + (uint64_t)dk * 2 * k * N;
-  ex.run(N, [&](int sl) {
-    const int from = galois_slot(sl, ginv, LOGN);
-    for (uint32_t c = 0; c < 2; ++c) {
-      uint64_t sum = 0;
-      for (uint32_t j = 0; j < dk; ++j) {
-        const uint64_t v = key[((uint64_t)(j * 2 + c) * k + p) * N + from];
-        Kt[((uint64_t)(j * 2 + c) * k + p) * N + sl] = v;
-        sum = add_mod(sum, mul_mod(v, qjp[j * k + p], m), m.q);
-      }
-      Ct[((uint64_t)c * k + p) * N + sl] = mul_mod(sum, s[spad(sl)], m);
+}
+
+// (2) one (key r, prime p, slot s) per work item: Kt_j[c][p][s] = key_j[c][p][slot^-1(s)],
+// Ct[c][p][s] = W[s] * sum_j (q_j mod q_p) Kt_j[c][p][s].
+BFV_HD void ks_keyperm_item(uint64_t item, const uint64_t* keys, uint64_t* prepared, uint64_t prepared_words,
+                            const uint32_t* ginvs, int logn, uint32_t k, uint32_t dk, const Modulus* mods,
+                            const uint64_t* qjp) {
+  const uint64_t N = uint64_t(1) << logn;
+  const uint64_t r = item / (k * N);
+  const uint32_t p = (uint32_t)((item >> logn) % k);
+  const int sl = (int)(item & (N - 1));
+  const Modulus& m = mods[p];
+  const uint64_t* key = keys + r * (uint64_t)dk * 2 * k * N;
+  uint64_t* Kt = prepared + r * prepared_words;
+  uint64_t* Ct = Kt + (uint64_t)dk * 2 * k * N;
+  const int from = galois_slot(sl, ginvs[r], logn);
+  const uint64_t w = Ct[(uint64_t)p * N + sl];  // NTT(neg_g), overwritten below
+  for (uint32_t c = 0; c < 2; ++c) {
+    uint64_t sum = 0;
+    for (uint32_t j = 0; j < dk; ++j) {
+      const uint64_t v = key[((uint64_t)(j * 2 + c) * k + p) * N + from];
+      Kt[((uint64_t)(j * 2 + c) * k + p) * N + sl] = v;
+      sum = add_mod(sum, mul_mod(v, qjp[j * k + p], m), m.q);
     }
-  });
-  ex.sync();
+    Ct[((uint64_t)c * k + p) * N + sl] = mul_mod(sum, w, m);
+  }
 }
 
 // One rotation for block (ct, c, p): x [ct][2][k][n] = INTT(A_c).  Ciphertexts flagged in
@@ -301,7 +315,7 @@ BFV_HD void op_ks_rotate(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t
       return y;
     };
     auto stj = [s](int i, uint64_t v) { s[spad(i)] = v; };
-    ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ldj, stj);
+    ntt_forward<LOGN, kMaxRadix, false>(ex, s, fwd + ((size_t)p << LOGN), m, ldj, stj);
     const uint64_t* kj = Kt + j * kstride;
     ex.run(N, [&](int i) {
       const uint64_t v = mul_mod(s[spad(i)], kj[i], m);
@@ -380,7 +394,7 @@ BFV_HD void op_client_phase(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* d
   {
     auto ld = [a](int i) { return a[i]; };
     auto st = [s](int i, uint64_t v) { s[spad(i)] = v; };
-    ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+    ntt_forward<LOGN, kMaxRadix, false>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
   }
   {
     auto ld = [=](int i) { return mul_mod(s[spad(i)], key[i], m); };

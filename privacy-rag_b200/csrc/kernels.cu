@@ -123,12 +123,26 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
   op_ks_hoist<LOGN>(BlockExec{}, smem, blockIdx.x, cts, Y, zflag, k, dk, mods, fwd);
 }
 
+// Galois elements of up to kKeyBatch keys and their inverses mod 2n, passed by value.
+constexpr int kKeyBatch = 256;
+struct EltBatch {
+  uint32_t elt[kKeyBatch];
+  uint32_t ginv[kKeyBatch];
+};
+
 template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
-    k_ks_keyprep(const uint64_t* key, uint64_t* prepared, uint32_t elt, uint32_t ginv, uint32_t k, uint32_t dk,
-                 const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd) {
+    k_ks_negntt(uint64_t* prepared, uint64_t prepared_words, EltBatch eb, uint32_t k, uint32_t dk,
+                const Modulus* mods, const ulonglong2* fwd) {
   extern __shared__ uint64_t smem[];
-  op_ks_keyprep<LOGN>(BlockExec{}, smem, blockIdx.x, key, prepared, elt, ginv, k, dk, mods, qjp, fwd);
+  op_ks_negntt<LOGN>(BlockExec{}, smem, blockIdx.x, prepared, prepared_words, eb.elt, k, dk, mods, fwd);
+}
+
+__global__ void k_ks_keyperm(const uint64_t* keys, uint64_t* prepared, uint64_t prepared_words, EltBatch eb,
+                             uint64_t items, int logn, uint32_t k, uint32_t dk, const Modulus* mods,
+                             const uint64_t* qjp) {
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < items; e += (uint64_t)gridDim.x * blockDim.x)
+    ks_keyperm_item(e, keys, prepared, prepared_words, eb.ginv, logn, k, dk, mods, qjp);
 }
 
 template <int LOGN>
@@ -246,7 +260,7 @@ static cudaError_t configure_for() {
   chk(allow_smem(k_ks_moddown<L>, (size_t(1) << L) * 8));
   chk(allow_smem(k_enc0_x<L>, s));
   chk(allow_smem(k_ks_hoist<L>, s));
-  chk(allow_smem(k_ks_keyprep<L>, s));
+  chk(allow_smem(k_ks_negntt<L>, s));
   chk(allow_smem(k_ks_rotate<L>, s));
   chk(allow_smem(k_ks_finish<L>, (size_t(1) << L) * 8));
   chk(allow_smem(k_client_phase<L>, s));
@@ -353,14 +367,27 @@ cudaError_t launch_ks_hoist(const DevParams& P, const uint64_t* cts, uint64_t co
   return cudaGetLastError();
 }
 
-cudaError_t launch_ks_keyprep(const DevParams& P, const uint64_t* key, uint32_t elt, uint64_t* prepared,
-                              cudaStream_t st) {
+cudaError_t launch_ks_keyprep(const DevParams& P, const uint64_t* keys, const uint32_t* elts, uint64_t count,
+                              uint64_t* prepared, cudaStream_t st) {
   if (P.k != P.dk + 1) return cudaErrorInvalidValue;
-  const uint32_t ginv = inverse_mod_2n(elt, 2 * P.n);
-  BFV_DISPATCH(P.logn, {
-    k_ks_keyprep<L_><<<P.k, threads_for<L_>(), smem_bytes<L_>(), st>>>(key, prepared, elt, ginv, P.k, P.dk, P.mod,
-                                                                      P.qjp, P.fwd);
-  });
+  const uint64_t pw = (2ull * P.dk + 2) * P.k * P.n;
+  const uint64_t kw = 2ull * P.dk * P.k * P.n;
+  for (uint64_t first = 0; first < count; first += kKeyBatch) {
+    const uint64_t m = count - first < (uint64_t)kKeyBatch ? count - first : (uint64_t)kKeyBatch;
+    EltBatch eb{};
+    for (uint64_t r = 0; r < m; ++r) {
+      eb.elt[r] = elts[first + r];
+      eb.ginv[r] = inverse_mod_2n(elts[first + r], 2 * P.n);
+    }
+    uint64_t* pr = prepared + first * pw;
+    BFV_DISPATCH(P.logn, {
+      k_ks_negntt<L_><<<(unsigned)(m * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(pr, pw, eb, P.k, P.dk, P.mod,
+                                                                                        P.fwd);
+    });
+    const uint64_t items = m * P.k * P.n;
+    k_ks_keyperm<<<elementwise_blocks(items), 256, 0, st>>>(keys + first * kw, pr, pw, eb, items, P.logn, P.k, P.dk,
+                                                           P.mod, P.qjp);
+  }
   return cudaGetLastError();
 }
 

@@ -69,13 +69,14 @@ cudaError_t launch_keyswitch(const DevParams& P, const uint64_t* cts, const uint
 
 // Hoisted multi-rotation keyswitch (see op_ks_hoist / op_ks_rotate):
 //  hoist:   Y [count][dk][k][n] = NTT(c1_j mod q_p); zflag [count] = c1 has a zero word
-//  keyprep: prepared [(dk*2 + 2)*k][n] = permuted key and correction for element elt
+//  keyprep: prepared [count][(dk*2 + 2)*k][n] = permuted keys and corrections for count
+//           keys [count][dk][2][k][n] and Galois elements elts (host array)
 //  rotate:  out [count][2][dk][n] = Galois(elt) + keyswitch of every ciphertext, x is
 //           scratch [count][2][k][n]
 cudaError_t launch_ks_hoist(const DevParams& P, const uint64_t* cts, uint64_t count, uint64_t* Y, uint32_t* zflag,
                             cudaStream_t st);
-cudaError_t launch_ks_keyprep(const DevParams& P, const uint64_t* key, uint32_t elt, uint64_t* prepared,
-                              cudaStream_t st);
+cudaError_t launch_ks_keyprep(const DevParams& P, const uint64_t* keys, const uint32_t* elts, uint64_t count,
+                              uint64_t* prepared, cudaStream_t st);
 cudaError_t launch_ks_rotate(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
                              const uint32_t* zflag, const uint64_t* prepared, uint32_t elt, uint64_t* x, uint64_t* out,
                              cudaStream_t st);

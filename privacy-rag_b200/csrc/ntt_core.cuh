@@ -207,18 +207,40 @@ BFV_HD void inv_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t
 // Forward NTT of one limb: ld(i) gives input coefficient i (< 4q), st(i, v) receives
 // canonical NTT slot i.  Ends with a block-wide barrier.  The block needs at most
 // n >> MAXR threads' worth of units per pass (any block size up to that works).
-template <int LOGN, int MAXR = 4, class Ex, class Ld, class St>
+// The first forward pass reads each unit's words n/2^R apart, so consecutive threads
+// read consecutive words.  Its last pass writes 2^R contiguous words per thread; with
+// STAGE_OUT the results go to shared memory first and st(i, v) is called in index order
+// (consecutive threads, consecutive i), which coalesces global stores.  Storers that
+// write shared memory themselves pass STAGE_OUT = false.
+template <int LOGN, int MAXR = 4, bool STAGE_OUT = true, class Ex, class Ld, class St>
 BFV_HD void ntt_forward(const Ex& ex, uint64_t* s, const ulonglong2* tw, const Modulus& m, const Ld& ld,
                         const St& st) {
-  fwd_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, ld, st);
+  if constexpr (STAGE_OUT) {
+    auto to_smem = [s](int i, uint64_t v) { s[spad(i)] = v; };
+    fwd_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, ld, to_smem);
+    ex.run(1 << LOGN, [&](int i) { st(i, s[spad(i)]); });
+    ex.sync();
+  } else {
+    fwd_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, ld, st);
+  }
 }
 
 // Inverse NTT of one limb: ld(i) gives NTT slot i (< 2q), st(i, v) receives canonical
-// coefficient i.  Ends with a block-wide barrier.
-template <int LOGN, int MAXR = 4, class Ex, class Ld, class St>
+// coefficient i.  Ends with a block-wide barrier.  Its first pass reads 2^R contiguous
+// words per thread; with STAGE_IN, ld(i) is called in index order into shared memory
+// first (coalesced global loads, and each word of a fused prologue computed once).
+// Loaders that read shared memory themselves pass STAGE_IN = false.
+template <int LOGN, int MAXR = 4, bool STAGE_IN = true, class Ex, class Ld, class St>
 BFV_HD void ntt_inverse(const Ex& ex, uint64_t* s, const ulonglong2* tw, const Modulus& m, const Ld& ld,
                         const St& st) {
-  inv_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, m.invn, m.invn_q, ld, st);
+  if constexpr (STAGE_IN) {
+    ex.run(1 << LOGN, [&](int i) { s[spad(i)] = ld(i); });
+    ex.sync();
+    auto from_smem = [s](int i) { return s[spad(i)]; };
+    inv_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, m.invn, m.invn_q, from_smem, st);
+  } else {
+    inv_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, m.invn, m.invn_q, ld, st);
+  }
 }
 
 // Bit reversal of an index of LOGN bits.

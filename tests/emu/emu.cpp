@@ -100,9 +100,11 @@ int emu_keyswitch_hoisted(int logn, uint32_t k, uint32_t dk, const uint64_t* mod
     std::vector<uint64_t> s(SmemWords<L_>::value);
     for (uint64_t b = 0; b < count * dk * k; ++b)
       op_ks_hoist<L_>(HostExec{}, s.data(), b, cts, Y.data(), zflag.data(), k, dk, T.mods.data(), T.fwd);
+    const uint64_t pw = prepared.size();
     for (uint64_t b = 0; b < k; ++b)
-      op_ks_keyprep<L_>(HostExec{}, s.data(), b, key, prepared.data(), elt, ginv, k, dk, T.mods.data(), qjp.data(),
-                        T.fwd);
+      op_ks_negntt<L_>(HostExec{}, s.data(), b, prepared.data(), pw, &elt, k, dk, T.mods.data(), T.fwd);
+    for (uint64_t item = 0; item < k * n; ++item)
+      ks_keyperm_item(item, key, prepared.data(), pw, &ginv, L_, k, dk, T.mods.data(), qjp.data());
     for (uint64_t b = 0; b < count * 2 * k; ++b)
       op_ks_rotate<L_>(HostExec{}, s.data(), b, cts, Y.data(), zflag.data(), prepared.data(), x.data(), elt, k, dk,
                        T.mods.data(), qjp.data(), T.fwd, T.inv);
