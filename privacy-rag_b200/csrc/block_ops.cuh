@@ -274,23 +274,19 @@ BFV_HD void ks_keyperm_item(uint64_t item, const uint64_t* keys, uint64_t* prepa
   }
 }
 
-// One rotation for block (ct, c, p): x [ct][2][k][n] = INTT(A_c).  Ciphertexts flagged in
+// One rotation for (ct, c, p): st(i, v) receives INTT(A_c)[i].  Ciphertexts flagged in
 // zflag take the exact path: A_c accumulated from fresh pre-negated digit transforms in
-// x itself, then transformed in place.
-template <int LOGN, class Ex>
-BFV_HD void op_ks_rotate(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* cts, const uint64_t* Y,
-                         const uint32_t* zflag, const uint64_t* prepared, uint64_t* x, uint32_t elt, uint32_t k,
-                         uint32_t dk, const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd,
-                         const ulonglong2* inv) {
+// the global scratch x [ct][2][k][n], then transformed.
+template <int LOGN, class Ex, class St>
+BFV_HD void op_ks_rotate_into(const Ex& ex, uint64_t* s, uint64_t ct, uint32_t c, uint32_t p, const uint64_t* cts,
+                              const uint64_t* Y, const uint32_t* zflag, const uint64_t* prepared, uint64_t* x,
+                              uint32_t elt, uint32_t k, uint32_t dk, const Modulus* mods, const uint64_t* qjp,
+                              const ulonglong2* fwd, const ulonglong2* inv, const St& st) {
   constexpr int N = 1 << LOGN;
-  const uint64_t ct = blk / (2 * k);
-  const uint32_t cp = (uint32_t)(blk % (2 * k)), c = cp / k, p = cp % k;
   const Modulus m = mods[p];
   const uint64_t* Kt = prepared + ((uint64_t)c * k + p) * N;  // digit j at + j*2*k*N
   const uint64_t kstride = 2ull * k * N;
   const uint64_t* Ct = prepared + (uint64_t)dk * 2 * k * N + ((uint64_t)c * k + p) * N;
-  uint64_t* xo = x + ((ct * 2 + c) * k + p) * (uint64_t)N;
-  auto st = [xo](int i, uint64_t v) { xo[i] = v; };
   if (!zflag[ct]) {
     const uint64_t* y = Y + (ct * dk * k + p) * (uint64_t)N;  // digit j at + j*k*N
     const uint64_t ystride = (uint64_t)k * N;
@@ -302,6 +298,7 @@ BFV_HD void op_ks_rotate(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t
     ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
     return;
   }
+  uint64_t* xo = x + ((ct * 2 + c) * k + p) * (uint64_t)N;
   const uint64_t* c1 = cts + (ct * 2 * dk + dk) * (uint64_t)N;
   const uint32_t mask2n = 2u * N - 1u;
   for (uint32_t j = 0; j < dk; ++j) {
@@ -325,6 +322,19 @@ BFV_HD void op_ks_rotate(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t
   }
   auto ldx = [xo](int i) { return xo[i]; };
   ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ldx, st);
+}
+
+// Block (ct, c, p): x [ct][2][k][n] = INTT(A_c); op_ks_finish completes the keyswitch.
+template <int LOGN, class Ex>
+BFV_HD void op_ks_rotate(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* cts, const uint64_t* Y,
+                         const uint32_t* zflag, const uint64_t* prepared, uint64_t* x, uint32_t elt, uint32_t k,
+                         uint32_t dk, const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd,
+                         const ulonglong2* inv) {
+  const uint64_t ct = blk / (2 * k);
+  const uint32_t cp = (uint32_t)(blk % (2 * k)), c = cp / k, p = cp % k;
+  uint64_t* xo = x + ((ct * 2 + c) * k + p) * ((uint64_t)1 << LOGN);
+  auto st = [xo](int i, uint64_t v) { xo[i] = v; };
+  op_ks_rotate_into<LOGN>(ex, s, ct, c, p, cts, Y, zflag, prepared, x, elt, k, dk, mods, qjp, fwd, inv, st);
 }
 
 // out [ct][2][dk][n] = sigma_g(moddown(x_c) + [c=0] c0).  Block (ct, data prime p); the
