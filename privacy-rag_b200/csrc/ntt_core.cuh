@@ -32,6 +32,20 @@ namespace bfvgpu {
 
 // Padded shared-memory word index: one spare word after every 16.
 BFV_HD int spad(int i) { return i + (i >> 4); }
+
+// Padded index of base + off for the words of one butterfly unit.  A unit's words are
+// base + k*stride with (base mod 16) + (k*stride mod 16) < 16 (base mod 16 < stride when
+// stride < 16, and k*stride is a multiple of 16 otherwise), so the pad of base + off is
+// pad(base) + pad(off): one compile-time offset per word.  The host build checks the
+// identity on every access.
+BFV_HD int spad_unit(int base, int sbase, int off) {
+#if !defined(__CUDA_ARCH__)
+  if (spad(base + off) != sbase + off + (off >> 4)) __builtin_trap();
+#else
+  (void)base;
+#endif
+  return sbase + off + (off >> 4);
+}
 template <int LOGN>
 struct SmemWords {
   static constexpr int value = (1 << LOGN) + ((1 << LOGN) >> 4);
@@ -75,6 +89,7 @@ BFV_HD void fwd_unit(uint64_t* s, int u, int L, const ulonglong2* tw, uint64_t q
   const int o = u & ((1 << shift) - 1);
   const int gl = u >> shift;
   const int base = (gl << (LOGN - L)) + o;
+  const int sbase = spad(base);
   uint64_t x[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
@@ -82,7 +97,7 @@ BFV_HD void fwd_unit(uint64_t* s, int u, int L, const ulonglong2* tw, uint64_t q
     if constexpr (FIRST)
       x[k] = ld(idx);
     else
-      x[k] = s[spad(idx)];
+      x[k] = s[spad_unit(base, sbase, k << shift)];
   }
   const uint64_t two_q = 2 * q;
 #pragma unroll
@@ -107,7 +122,7 @@ BFV_HD void fwd_unit(uint64_t* s, int u, int L, const ulonglong2* tw, uint64_t q
     if constexpr (LAST)
       st(idx, reduce_4q(x[k], q));
     else
-      s[spad(idx)] = x[k];
+      s[spad_unit(base, sbase, k << shift)] = x[k];
   }
 }
 
@@ -120,6 +135,7 @@ BFV_HD void inv_unit(uint64_t* s, int u, int L, const ulonglong2* tw, uint64_t q
   const int o = u & ((1 << L) - 1);
   const int gg = u >> L;
   const int base = (gg << (L + R)) + o;
+  const int sbase = spad(base);
   uint64_t x[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
@@ -127,7 +143,7 @@ BFV_HD void inv_unit(uint64_t* s, int u, int L, const ulonglong2* tw, uint64_t q
     if constexpr (FIRST)
       x[k] = ld(idx);
     else
-      x[k] = s[spad(idx)];
+      x[k] = s[spad_unit(base, sbase, k << L)];
   }
   const uint64_t two_q = 2 * q;
 #pragma unroll
@@ -153,7 +169,7 @@ BFV_HD void inv_unit(uint64_t* s, int u, int L, const ulonglong2* tw, uint64_t q
     if constexpr (LAST)
       st(idx, shoup(x[k], invn, invn_q, q));
     else
-      s[spad(idx)] = x[k];
+      s[spad_unit(base, sbase, k << L)] = x[k];
   }
 }
 
