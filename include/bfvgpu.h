@@ -164,6 +164,19 @@ int32_t bfvgpu_matrix_groups_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_
                                     const uint64_t *w, uint64_t groups, const uint64_t *mask,
                                     const uint64_t *enc0_x, uint64_t *out, void *stream);
 
+/* Enc(0) polynomials before the divide-and-round, for the matrix epilogue: samples
+ * [groups][3][k][n] (ternary u, e0, e1), pk [2][k][n] NTT form; u_scratch [groups][k][n];
+ * x_out [groups][2][k][n] = INTT(NTT(u) . pk_c) + e_c (enc0.cu:125-134).  Pass x_out as
+ * enc0_x of bfvgpu_matrix_groups_device. */
+int32_t bfvgpu_enc0_device(bfvgpu_ctx *ctx, const uint64_t *samples, const uint64_t *pk, uint64_t groups,
+                           uint64_t *u_scratch, uint64_t *x_out, void *stream);
+/* c0 residues at each group's targets (gather_c0, matrix.cu:66-69) and optionally their
+ * CRT values: out [groups][2][dk][n]; targets [groups][max_count], counts [groups];
+ * selected [groups][dk][max_count]; crt (nullable) [groups][max_count][dk] limbs. */
+int32_t bfvgpu_gather_targets_device(bfvgpu_ctx *ctx, const uint64_t *out, uint64_t groups,
+                                     const uint64_t *targets, const uint32_t *counts, uint32_t max_count,
+                                     uint64_t *selected, uint64_t *crt, void *stream);
+
 /* ---- NttBatch (IV1/native/gpu/client_phase/ntt.hpp:22-40) ------------------------------ */
 /* key_level != 0: all k primes, else the dk data primes; batches in [1, 19]. */
 int32_t bfvgpu_ntt_open(bfvgpu_ctx *ctx, int32_t key_level, uint64_t batches, bfvgpu_ntt **out);
@@ -223,6 +236,10 @@ int32_t bfvgpu_switch_release(bfvgpu_switch *s);
 int32_t bfvgpu_enc0_open(bfvgpu_ctx *ctx, const uint64_t *pk, bfvgpu_enc0 **out);
 /* samples [3][k][n] (ternary u, e0, e1 as canonical residues) -> Enc(0) [2][dk][n]. */
 int32_t bfvgpu_enc0_encrypt_from_samples(bfvgpu_enc0 *e, const uint64_t *samples, uint64_t *out);
+/* Public-key encryption of a plaintext (the client's input blocks, bfv_matrix.inc:31-49):
+ * Enc(0) from samples, then c0 += Delta-scaled plain[i] for i < count (plain < t). */
+int32_t bfvgpu_enc0_encrypt_plain(bfvgpu_enc0 *e, const uint64_t *samples, const uint64_t *plain,
+                                  uint64_t count, uint64_t *out);
 int32_t bfvgpu_enc0_close(bfvgpu_enc0 *e, bfvgpu_cleanup *cleanup);
 int32_t bfvgpu_enc0_release(bfvgpu_enc0 *e);
 

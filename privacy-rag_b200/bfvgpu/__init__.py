@@ -9,3 +9,4 @@ from .backend import (ART002_PRIMES, Context, Matrix, NttBatch, PublicZero, Swit
                       TokenWeights, find_primes, launch_count)
 from .layout import (MatrixPacking, matrix_packing, matrix_packing_qk_reverse64,  # noqa: F401
                      pack_inputs, pack_weights, packed_bfv_rows_per_ciphertext, targets)
+from . import engine  # noqa: F401,E402

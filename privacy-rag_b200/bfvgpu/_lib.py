@@ -77,6 +77,8 @@ _SIGNATURES = {
     "bfvgpu_keyswitch_rotate_device": (I32, [VP, VP, U64, VP, VP, U32, VP, VP, VP]),
     "bfvgpu_weights_ntt_device": (I32, [VP, VP, U64, VP, VP]),
     "bfvgpu_matrix_groups_device": (I32, [VP, VP, U64, VP, U64, VP, VP, VP, VP]),
+    "bfvgpu_enc0_device": (I32, [VP, VP, VP, U64, VP, VP, VP]),
+    "bfvgpu_gather_targets_device": (I32, [VP, VP, U64, VP, VP, U32, VP, VP, VP]),
     "bfvgpu_ntt_open": (I32, [VP, I32, U64, ctypes.POINTER(VP)]),
     "bfvgpu_ntt_transform": (I32, [VP, U64P, U64P, I32]),
     "bfvgpu_ntt_bind_client_key": (I32, [VP, U64P]),
@@ -101,6 +103,7 @@ _SIGNATURES = {
     "bfvgpu_switch_release": (I32, [VP]),
     "bfvgpu_enc0_open": (I32, [VP, U64P, ctypes.POINTER(VP)]),
     "bfvgpu_enc0_encrypt_from_samples": (I32, [VP, U64P, U64P]),
+    "bfvgpu_enc0_encrypt_plain": (I32, [VP, U64P, U64P, U64, U64P]),
     "bfvgpu_enc0_close": (I32, [VP, ctypes.POINTER(Cleanup)]),
     "bfvgpu_enc0_release": (I32, [VP]),
     "bfvgpu_token_open": (I32, [VP, U64P, U64, ctypes.POINTER(VP)]),

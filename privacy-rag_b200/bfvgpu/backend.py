@@ -152,6 +152,16 @@ class Context:
         check(lib().bfvgpu_weights_ntt_device(self._h, self._dptr(ring), blocks, self._dptr(out), stream),
               "weights_ntt_device")
 
+    def enc0_device(self, samples, pk, groups: int, u_scratch, x_out, stream: int | None = None):
+        check(lib().bfvgpu_enc0_device(self._h, self._dptr(samples), self._dptr(pk), groups, self._dptr(u_scratch),
+                                       self._dptr(x_out), stream), "enc0_device")
+
+    def gather_targets_device(self, out, groups: int, targets, counts, max_count: int, selected, crt=None,
+                              stream: int | None = None):
+        check(lib().bfvgpu_gather_targets_device(self._h, self._dptr(out), groups, self._dptr(targets),
+                                                 self._dptr(counts), max_count, self._dptr(selected),
+                                                 self._dptr(crt) or None, stream), "gather_targets_device")
+
     def matrix_groups_device(self, inputs_ntt, inputs: int, weights_ntt, groups: int, out, mask=None,
                              enc0_x=None, stream: int | None = None):
         check(lib().bfvgpu_matrix_groups_device(self._h, self._dptr(inputs_ntt), inputs, self._dptr(weights_ntt),
@@ -359,6 +369,16 @@ class PublicZero(_Handle):
             raise ValueError("E_ENC0_SAMPLE_SHAPE")
         out = np.empty((2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
         check(lib().bfvgpu_enc0_encrypt_from_samples(self._h, ptr(s), ptr(out)), "PublicZero.encrypt_from_samples")
+        return out
+
+    def encrypt(self, samples, plain) -> np.ndarray:
+        """Enc(0) from samples plus the Delta-scaled plaintext (coefficients < t)."""
+        s = u64(samples)
+        p = u64(plain).ravel()
+        if s.size != 3 * self.ctx.k * self.ctx.n:
+            raise ValueError("E_ENC0_SAMPLE_SHAPE")
+        out = np.empty((2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
+        check(lib().bfvgpu_enc0_encrypt_plain(self._h, ptr(s), ptr(p), p.size, ptr(out)), "PublicZero.encrypt")
         return out
 
 

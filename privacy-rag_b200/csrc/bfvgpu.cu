@@ -482,7 +482,7 @@ struct bfvgpu_switch {
 
 struct bfvgpu_enc0 {
   Holder h;
-  uint64_t *pk = nullptr, *samples = nullptr, *u_ntt = nullptr, *x = nullptr, *out = nullptr;
+  uint64_t *pk = nullptr, *samples = nullptr, *u_ntt = nullptr, *x = nullptr, *out = nullptr, *plain = nullptr;
 };
 
 struct bfvgpu_token {
@@ -704,6 +704,32 @@ int32_t bfvgpu_matrix_groups_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_
     DeviceScope scope(ctx->c.device);
     Protect prot{mask, enc0_x};
     cuda_check(launch_mac_intt(ctx->c.P, in, w, out, inputs, groups, prot, pick(ctx, stream)), "mac_intt");
+    count_launch();
+  });
+}
+
+int32_t bfvgpu_enc0_device(bfvgpu_ctx* ctx, const uint64_t* samples, const uint64_t* pk, uint64_t groups,
+                           uint64_t* u_scratch, uint64_t* x_out, void* stream) {
+  return guard([&] {
+    if (!ctx || !samples || !pk || !u_scratch || !x_out) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    cuda_check(launch_enc0_x(ctx->c.P, samples, pk, u_scratch, x_out, groups, pick(ctx, stream)), "enc0");
+    count_launch();
+  });
+}
+
+int32_t bfvgpu_gather_targets_device(bfvgpu_ctx* ctx, const uint64_t* out, uint64_t groups, const uint64_t* targets,
+                                     const uint32_t* counts, uint32_t max_count, uint64_t* selected, uint64_t* crt,
+                                     void* stream) {
+  return guard([&] {
+    if (!ctx || !out || !targets || !counts || !selected) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (max_count == 0 || max_count > 512) fail(BFVGPU_E_TARGET_COUNT, "MATRIX_GPU_TARGET_COUNT");
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    cuda_check(launch_gather_targets(ctx->c.P, out, targets, counts, max_count, groups, selected, crt, pick(ctx, stream)),
+               "gather");
     count_launch();
   });
 }
@@ -1206,6 +1232,37 @@ int32_t bfvgpu_enc0_encrypt_from_samples(bfvgpu_enc0* e, const uint64_t* samples
     });
   });
 }
+int32_t bfvgpu_enc0_encrypt_plain(bfvgpu_enc0* e, const uint64_t* samples, const uint64_t* plain, uint64_t count,
+                                  uint64_t* out) {
+  return guard([&] {
+    if (!e || !samples || !out || (!plain && count)) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    e->h.check_open("E_SWITCH_CLOSED");
+    const Context& c = *e->h.ctx;
+    if (count == 0 || count > c.n) fail(BFVGPU_E_SHAPE, "E_BFV_PACKED_SHAPE");
+    for (uint64_t i = 0; i < count; ++i)
+      if (plain[i] >= c.t) fail(BFVGPU_E_RING, "E_BFV_INPUT_PLAIN");
+    check_canonical_host(c, samples, 3 * c.k, c.k, 0);
+    DeviceScope scope(c.device);
+    e->h.run([&] {
+      const uint64_t n = c.n, k = c.k, dk = c.dk;
+      if (!e->plain) e->plain = e->h.alloc(n);
+      e->h.h2d(e->samples, samples, 3 * k * n);
+      e->h.h2d(e->plain, plain, count);
+      cuda_check(launch_enc0_x(c.P, e->samples, e->pk, e->u_ntt, e->x, 1, c.stream), "enc0");
+      cuda_check(launch_moddown(c.P, e->x, e->out, 1, c.stream), "moddown");
+      cuda_check(launch_add_plain(c.P, e->out, e->plain, count, c.stream), "add_plain");
+      count_launch(3);
+      e->h.d2h(out, e->out, 2 * dk * n);
+      cuda_check(cudaMemsetAsync(e->samples, 0, 3 * k * n * 8, c.stream), "wipe");
+      cuda_check(cudaMemsetAsync(e->u_ntt, 0, k * n * 8, c.stream), "wipe");
+      cuda_check(cudaMemsetAsync(e->x, 0, 2 * k * n * 8, c.stream), "wipe");
+      cuda_check(cudaMemsetAsync(e->out, 0, 2 * dk * n * 8, c.stream), "wipe");
+      cuda_check(cudaMemsetAsync(e->plain, 0, n * 8, c.stream), "wipe");
+      e->h.sync();
+    });
+  });
+}
+
 int32_t bfvgpu_enc0_close(bfvgpu_enc0* e, bfvgpu_cleanup* cleanup) {
   if (!e) return BFVGPU_E_ARGUMENT;
   const bfvgpu_cleanup c = e->h.release();

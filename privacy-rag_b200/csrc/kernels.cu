@@ -212,6 +212,20 @@ __global__ void k_packing_prepare(const uint64_t* left, const uint64_t* right, u
   }
 }
 
+// c0 [dk][n] += Delta-scaled plaintext coefficient (add_plain with the scaling variant),
+// for coefficients i < count (bfv_matrix.inc:40-46: encrypt_zero then add_plain_inplace).
+__global__ void k_add_plain(uint64_t* c0, const uint64_t* plain, uint64_t count, uint32_t dk, int logn,
+                            const Modulus* mods, uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
+  const uint64_t total = (uint64_t)dk * count;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t p = (uint32_t)(e / count);
+    const uint64_t i = e % count;
+    const Modulus& m = mods[p];
+    uint64_t* a = c0 + ((uint64_t)p << logn) + i;
+    *a = add_mod(*a, scale_plain_coeff(plain[i], q_mod_t, upper_half, t, tlog, m), m.q);
+  }
+}
+
 __global__ void k_add(uint64_t* a, const uint64_t* b, uint64_t polys, uint32_t dk, int logn, const Modulus* mods) {
   const uint64_t total = polys << logn;
   for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x)
@@ -461,6 +475,14 @@ cudaError_t launch_packing_prepare(const DevParams& P, const uint64_t* left, con
   const uint64_t total = 2 * (uint64_t)P.dk * P.n;
   k_packing_prepare<<<elementwise_blocks(total), 256, 0, st>>>(left, right, sum, diff, P.dk, P.logn,
                                                               P.n >> (level + 1), P.mod);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add_plain(const DevParams& P, uint64_t* c0, const uint64_t* plain, uint64_t count,
+                             cudaStream_t st) {
+  if (!count) return cudaSuccess;
+  k_add_plain<<<elementwise_blocks(count * P.dk), 256, 0, st>>>(c0, plain, count, P.dk, P.logn, P.mod, P.q_mod_t,
+                                                               P.upper_half, P.t, P.tlog);
   return cudaGetLastError();
 }
 

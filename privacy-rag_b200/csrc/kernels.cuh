@@ -112,6 +112,9 @@ cudaError_t launch_token_evaluate(const DevParams& P, const uint64_t* inputs, ui
 // [2][dk][n] ciphertexts, s = n >> (level+1).
 cudaError_t launch_packing_prepare(const DevParams& P, const uint64_t* left, const uint64_t* right,
                                    uint64_t* sum, uint64_t* diff, unsigned level, cudaStream_t st);
+// c0 [dk][n] += Delta * plain[i] (scaling variant) for i < count, plain < t.
+cudaError_t launch_add_plain(const DevParams& P, uint64_t* c0, const uint64_t* plain, uint64_t count,
+                             cudaStream_t st);
 // a += b on [polys][n] data-prime polys.
 cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint64_t polys, cudaStream_t st);
 
