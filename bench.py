@@ -148,6 +148,74 @@ def cpu_ntt_sample(seconds: float = 4.0):
 
 
 # ----------------------------------------------------------------------------------------------
+def run_layer_legs(torch, bfvgpu, device, args):
+    """Config 3: q_proj 2048x1024 for one token (B = 1); config 4: the four linear calls of
+    one Qwen3-0.6B-shaped layer for a 128-token prefill (8 tiles of B = 16).  ART-002
+    parameters (the reference's protocol); int8 weights uniform in [-127, 127] (seed 4),
+    client ciphertexts and Enc(0)/mask randomness synthetic and resident in HBM.  Each
+    step transforms the layer's weights once and runs every tile."""
+    from bfvgpu import layer as L
+    ctx = bfvgpu.Context.art002(device)
+    n, k, dk = ctx.n, ctx.k, ctx.dk
+    sp = ctx.stream()
+    stream = torch.cuda.ExternalStream(sp)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4)
+    q = torch.tensor(ctx.primes, dtype=torch.int64, device="cuda")
+
+    def residues(shape, nprimes):
+        raw = torch.randint(0, 2 ** 62, shape, dtype=torch.int64, device="cuda", generator=g)
+        return torch.remainder(raw, q[:nprimes].view(*([1] * (len(shape) - 2)), nprimes, 1))
+
+    def small(shape, lo, hi):
+        v = torch.randint(lo, hi + 1, shape, dtype=torch.int64, device="cuda", generator=g)
+        return torch.remainder(v.unsqueeze(-2), q.view(k, 1))
+
+    pk = residues((2, k, n), k)
+    out = {}
+    for label, projections, batch, tiles in (("config3", (("q_proj", 1024, 2048),), 1, 1),
+                                             ("config4", L.QWEN3_06B_LAYER, 16, args.layer_tiles)):
+        srv = L.LayerServer(torch, ctx, pk, projections, batch)
+        rings, cts, masks, samples = {}, {}, {}, {}
+        for p in srv.proj:
+            w = torch.randint(-127, 128, (p.outputs, p.inner), dtype=torch.int64, device="cuda", generator=g)
+            rings[p.name] = L.pack_weights_device(torch, w, p, n)
+            cts[p.name] = residues((p.inputs, 2, dk, n), dk)
+            masks[p.name] = torch.randint(0, 2 ** 59, (p.groups, n), dtype=torch.int64, device="cuda", generator=g)
+            samples[p.name] = torch.cat([small((p.groups, 1, n), -1, 1), small((p.groups, 2, n), -5, 5)], dim=1)
+        torch.cuda.synchronize()
+
+        def step():
+            srv.prepare_weights(rings, stream=sp)
+            for _ in range(tiles):
+                for p in srv.proj:
+                    srv.run_projection(p, cts[p.name], masks[p.name], samples[p.name], stream=sp)
+
+        step()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 3 if label == "config3" else 1
+        a.record(stream)
+        for _ in range(reps):
+            step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        weight_ntts = sum(p.groups * p.inputs * dk for p in srv.proj)
+        out[label] = {"ms": ms, "unit": "ms per layer (all tiles)" if label == "config4" else "ms per matvec",
+                      "tiles": tiles, "batch": batch,
+                      "calls": [{"name": p.name, "K": p.inner, "O": p.outputs, "d": p.d, "cap": p.cap,
+                                 "inputs": p.inputs, "groups": p.groups} for p in srv.proj],
+                      "weight_ntts_per_step": weight_ntts,
+                      "mac_modmuls_per_step": tiles * sum(p.groups * p.inputs * 2 * dk * n for p in srv.proj),
+                      "note": "ART-002 (n=16384, 6+1 x 60-bit, t=2^59); weights transformed once per layer"}
+        del srv, rings, cts, masks, samples
+        torch.cuda.empty_cache()
+    ctx.close()
+    return out
+
+
+# ----------------------------------------------------------------------------------------------
 def run_reference(args):
     rank, world, _ = env_rank()
     if rank != 0:
@@ -197,6 +265,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2, help="0 skips the e2e leg")
     ap.add_argument("--rotations", type=int, default=ROTATIONS, help="rotations per step (profiling cases)")
     ap.add_argument("--ntt-reps", type=int, default=200)
+    ap.add_argument("--layer", type=int, default=1, help="0 skips the config-3/4 legs")
+    ap.add_argument("--layer-tiles", type=int, default=8, help="16-token tiles in the config-4 leg")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -311,6 +381,9 @@ def main():
     alg_bytes_launch = ALG_BYTES_PER_KS * CTS
     achieved = alg_bytes_launch / avg_launch / 1e9
 
+    # ---- secondary: ct-pt matvec (config 3) and one decoder layer (config 4), ART-002 ----
+    layer_res = run_layer_legs(torch, bfvgpu, local, args) if args.layer else None
+
     # ---- secondary: NTT round trips (config 1) ----
     primes1 = bfvgpu.find_primes(N1, BITS1)
     ctx1 = bfvgpu.Context(N1, primes1, 3, 0, T2, device=local)
@@ -409,6 +482,8 @@ def main():
                                               "path": "bfvgpu_keyswitch_device (no hoisting, Switch::apply)",
                                               "avg_launch_ms": 1e3 * sum(plain_per) / len(plain_per),
                                               "matches_hoisted": plain_match},
+                      "matvec_config3": layer_res and layer_res["config3"],
+                      "layer_config4": layer_res and layer_res["config4"],
                       "ntt": {"value": ntts_per_s, "unit": "NTTs/s",
                               "config": "config1: n=4096, primes 36/36/37-bit, 384 limb-polys fwd+inv",
                               "avg_launch_ms": ntt_launch_s * 1e3,

@@ -1,0 +1,117 @@
+"""Device-resident server pipeline for the linear layers of one decoder layer.
+
+``Transformer::layer_from_shares`` (IV1/compute/model.hpp:173-238) runs four
+``private_matrix`` calls per 16-token tile -- q/k/v joint, o, gate/up joint, down
+(``project_joint_many`` / ``project_many``, model.hpp:66-126) -- each packed by
+``matrix_packing(B, K, O)``.  This module runs the server side of those calls with every
+buffer resident in HBM: the layer's weights are packed into ring polynomials on the
+device and transformed once per layer (the reference transforms them again in every
+call, bfv_matrix.inc:186-193), then each tile's inputs are transformed once and every
+output group runs through the fused product / INTT / mask / Enc(0) kernel, followed by
+the target gather with CRT.  Torch provides device memory; all arithmetic is the
+library's kernels.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+from .backend import Context
+from .layout import MASK59, matrix_packing
+
+QWEN3_06B_LAYER = (("qkv", 1024, 4096), ("o", 2048, 1024), ("gate_up", 1024, 6144), ("down", 3072, 1024))
+
+
+@dataclass(frozen=True)
+class Projection:
+    name: str
+    inner: int        # K
+    outputs: int      # O
+    batch: int        # B
+    d: int
+    cap: int
+    inputs: int       # I: input ciphertexts
+    groups: int       # G: returned ciphertexts
+
+    @property
+    def stride(self) -> int:
+        return 2 * self.d - 1
+
+
+def plan(name: str, batch: int, inner: int, outputs: int) -> Projection:
+    p = matrix_packing(batch, inner, outputs)
+    groups = (outputs + p.columns - 1) // p.columns
+    # one tile of 512/B columns holds whole groups for these shapes (cap divides 512/B)
+    return Projection(name, inner, outputs, batch, p.reduction, p.columns, p.inputs, groups)
+
+
+def pack_weights_device(torch, w_ring, pr: Projection, n: int):
+    """w_ring: int64 [O][K] ring-59 words (device) -> ring polys [G][I][n] (device):
+    row o of group g, column j of block b at coefficient o*B*(2d-1)+d-1-j."""
+    G, I, cap, d = pr.groups, pr.inputs, pr.cap, pr.d
+    O_pad, K_pad = G * cap, I * d
+    w = torch.zeros((O_pad, K_pad), dtype=torch.int64, device=w_ring.device)
+    w[: pr.outputs, : pr.inner] = w_ring & MASK59
+    w = w.view(G, cap, I, d).permute(0, 2, 1, 3).reshape(G, I, cap * d)
+    o = torch.arange(cap, device=w_ring.device).view(cap, 1)
+    j = torch.arange(d, device=w_ring.device).view(1, d)
+    pos = (o * pr.batch * pr.stride + d - 1 - j).reshape(-1)
+    ring = torch.zeros((G, I, n), dtype=torch.int64, device=w_ring.device)
+    ring[:, :, pos] = w
+    return ring
+
+
+def targets_device(torch, pr: Projection, device):
+    """[G][cap*B] target coefficients and [G] counts (int64 / int32 tensors)."""
+    cnt = [min(pr.cap, pr.outputs - g * pr.cap) * pr.batch for g in range(pr.groups)]
+    mx = pr.cap * pr.batch
+    idx = torch.arange(mx, device=device)
+    tg = (idx * pr.stride + pr.d - 1).repeat(pr.groups, 1).contiguous()  # (o*B+b)*(2d-1)+d-1
+    counts = torch.tensor(cnt, dtype=torch.int32, device=device)
+    return tg, counts, mx
+
+
+class LayerServer:
+    """Server-side linear protocol of one layer on one device (ART-002 context)."""
+
+    def __init__(self, torch, ctx: Context, pk_device, projections=QWEN3_06B_LAYER, batch: int = 16):
+        self.torch = torch
+        self.ctx = ctx
+        self.pk = pk_device
+        self.proj = [plan(nm, batch, k, o) for nm, k, o in projections]
+        self.batch = batch
+        t, n, dk, k = torch, ctx.n, ctx.dk, ctx.k
+        dev = pk_device.device
+        maxg = max(p.groups for p in self.proj)
+        self.w_ntt = {}
+        self.u = t.empty((maxg, k, n), dtype=t.int64, device=dev)
+        self.x = t.empty((maxg, 2, k, n), dtype=t.int64, device=dev)
+        self.out = t.empty((maxg, 2, dk, n), dtype=t.int64, device=dev)
+        self.targets = {p.name: targets_device(t, p, dev) for p in self.proj}
+        mx = max(v[2] for v in self.targets.values())
+        self.selected = t.empty((maxg, dk, mx), dtype=t.int64, device=dev)
+        self.crt = t.empty((maxg, mx, dk), dtype=t.int64, device=dev)
+
+    def prepare_weights(self, ring_by_name: dict, stream=None) -> None:
+        """Lift + NTT every weight block of the layer once (reused by all tiles)."""
+        for p in self.proj:
+            ring = ring_by_name[p.name]
+            w = self.w_ntt.get(p.name)
+            if w is None:
+                w = self.torch.empty((p.groups, p.inputs, self.ctx.dk, self.ctx.n), dtype=self.torch.int64,
+                                     device=ring.device)
+                self.w_ntt[p.name] = w
+            self.ctx.weights_ntt_device(ring, p.groups * p.inputs, w, stream=stream)
+
+    def run_projection(self, p: Projection, cts, masks, samples, stream=None):
+        """One private_matrix call of one tile: cts [I][2][dk][n] client ciphertexts in
+        coefficient form (transformed in place), masks [G][n], samples [G][3][k][n].
+        Leaves c1 in self.out[:G, 1] and the targets' c0 residues / CRT limbs in
+        self.selected / self.crt."""
+        ctx = self.ctx
+        I, G = p.inputs, p.groups
+        inp = cts
+        ctx.ntt_device(inp, I * 2 * ctx.dk, ctx.dk, 0, False, stream=stream)
+        ctx.enc0_device(samples, self.pk, G, self.u, self.x, stream=stream)
+        ctx.matrix_groups_device(inp, I, self.w_ntt[p.name], G, self.out, mask=masks, enc0_x=self.x, stream=stream)
+        tg, counts, mx = self.targets[p.name]
+        ctx.gather_targets_device(self.out, G, tg, counts, mx, self.selected, self.crt, stream=stream)
