@@ -175,40 +175,51 @@ def run_layer_legs(torch, bfvgpu, device, args):
     out = {}
     for label, projections, batch, tiles in (("config3", (("q_proj", 1024, 2048),), 1, 1),
                                              ("config4", L.QWEN3_06B_LAYER, 16, args.layer_tiles)):
-        srv = L.LayerServer(torch, ctx, pk, projections, batch)
+        srv = L.LayerServer(torch, ctx, pk, projections, batch, tiles)
         rings, cts, masks, samples = {}, {}, {}, {}
         for p in srv.proj:
             w = torch.randint(-127, 128, (p.outputs, p.inner), dtype=torch.int64, device="cuda", generator=g)
             rings[p.name] = L.pack_weights_device(torch, w, p, n)
-            cts[p.name] = residues((p.inputs, 2, dk, n), dk)
-            masks[p.name] = torch.randint(0, 2 ** 59, (p.groups, n), dtype=torch.int64, device="cuda", generator=g)
-            samples[p.name] = torch.cat([small((p.groups, 1, n), -1, 1), small((p.groups, 2, n), -5, 5)], dim=1)
+            cts[p.name] = residues((tiles, p.inputs, 2, dk, n), dk)
+            masks[p.name] = torch.randint(0, 2 ** 59, (tiles, p.groups, n), dtype=torch.int64, device="cuda",
+                                          generator=g)
+            samples[p.name] = torch.cat([small((tiles, p.groups, 1, n), -1, 1),
+                                         small((tiles, p.groups, 2, n), -5, 5)], dim=2)
         torch.cuda.synchronize()
 
-        def step():
+        def step(ev=None):
             srv.prepare_weights(rings, stream=sp)
-            for _ in range(tiles):
-                for p in srv.proj:
-                    srv.run_projection(p, cts[p.name], masks[p.name], samples[p.name], stream=sp)
+            if ev:
+                ev[1].record(stream)
+            for i, p in enumerate(srv.proj):
+                srv.run_projection(p, cts[p.name], masks[p.name], samples[p.name], stream=sp)
+                if ev:
+                    ev[2 + i].record(stream)
 
         step()
         torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 3 if label == "config3" else 1
-        a.record(stream)
-        for _ in range(reps):
-            step()
-        b.record(stream)
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2 + len(srv.proj))] for _ in range(reps)]
+        for r in range(reps):
+            evs[r][0].record(stream)
+            step(evs[r])
         torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / reps
+        ms = sum(e[0].elapsed_time(e[-1]) for e in evs) / reps
+        w_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / reps
+        per = [sum(e[1 + i].elapsed_time(e[2 + i]) for e in evs) / reps for i in range(len(srv.proj))]
         weight_ntts = sum(p.groups * p.inputs * dk for p in srv.proj)
+        mac = tiles * sum(p.groups * p.inputs * 2 * dk * n for p in srv.proj)
         out[label] = {"ms": ms, "unit": "ms per layer (all tiles)" if label == "config4" else "ms per matvec",
+                      "ms_weights_ntt": w_ms, "ms_with_cached_weights": ms - w_ms,
+                      "ms_per_call": {p.name: per[i] for i, p in enumerate(srv.proj)},
                       "tiles": tiles, "batch": batch,
                       "calls": [{"name": p.name, "K": p.inner, "O": p.outputs, "d": p.d, "cap": p.cap,
                                  "inputs": p.inputs, "groups": p.groups} for p in srv.proj],
                       "weight_ntts_per_step": weight_ntts,
-                      "mac_modmuls_per_step": tiles * sum(p.groups * p.inputs * 2 * dk * n for p in srv.proj),
-                      "note": "ART-002 (n=16384, 6+1 x 60-bit, t=2^59); weights transformed once per layer"}
+                      "mac_modmuls_per_step": mac,
+                      "mac_weight_bytes_per_step": weight_ntts * n * 8,
+                      "note": "ART-002 (n=16384, 6+1 x 60-bit, t=2^59); weights transformed once per layer "
+                              "and read once by the multi-tile product"}
         del srv, rings, cts, masks, samples
         torch.cuda.empty_cache()
     ctx.close()

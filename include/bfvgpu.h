@@ -164,6 +164,24 @@ int32_t bfvgpu_matrix_groups_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_
                                     const uint64_t *w, uint64_t groups, const uint64_t *mask,
                                     const uint64_t *enc0_x, uint64_t *out, void *stream);
 
+/* Words of device scratch bfvgpu_matrix_tiles_device needs: 0 without Enc(0), else
+ * tiles * groups * (k + 2) * n. */
+uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx *ctx, uint64_t tiles, uint64_t groups,
+                                           int32_t enc0);
+/* Server product of `tiles` token tiles that share one weight matrix (the four calls per
+ * tile of Transformer::layer_from_shares, model.hpp:173-238, batched over tiles; per tile
+ * and group the result is Matrix::evaluate of matrix.cu:90-106 plus the mask and Enc(0) of
+ * bfv_matrix.inc:215-227):
+ *   out[t][g][c] = INTT(sum_b in[t][b][c] . w[g][b]) + Enc(0)[t][g] - [c=0] Delta masks[t][g]
+ * in [tiles][inputs][2][dk][n] NTT form, w [groups][inputs][dk][n] NTT form, masks
+ * [tiles][groups][n] ring-59 words or NULL, samples [tiles][groups][3][k][n] or NULL (then
+ * pk and scratch may be NULL), pk [2][k][n] NTT form, out [tiles][groups][2][dk][n].  Each
+ * weight word is read once for all tiles. */
+int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_t tiles, uint64_t inputs,
+                                   const uint64_t *w, uint64_t groups, const uint64_t *masks,
+                                   const uint64_t *samples, const uint64_t *pk, uint64_t *scratch,
+                                   uint64_t *out, void *stream);
+
 /* Enc(0) polynomials before the divide-and-round, for the matrix epilogue: samples
  * [groups][3][k][n] (ternary u, e0, e1), pk [2][k][n] NTT form; u_scratch [groups][k][n];
  * x_out [groups][2][k][n] = INTT(NTT(u) . pk_c) + e_c (enc0.cu:125-134).  Pass x_out as

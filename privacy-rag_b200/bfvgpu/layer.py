@@ -7,9 +7,9 @@
 buffer resident in HBM: the layer's weights are packed into ring polynomials on the
 device and transformed once per layer (the reference transforms them again in every
 call, bfv_matrix.inc:186-193), then each tile's inputs are transformed once and every
-output group runs through the fused product / INTT / mask / Enc(0) kernel, followed by
-the target gather with CRT.  Torch provides device memory; all arithmetic is the
-library's kernels.
+projection runs as one multi-tile product (each NTT-form weight word read once for all
+tiles), the INTT with the mask and Enc(0) folded in, and the target gather with CRT.
+Torch provides device memory; all arithmetic is the library's kernels.
 """
 from __future__ import annotations
 
@@ -60,36 +60,39 @@ def pack_weights_device(torch, w_ring, pr: Projection, n: int):
     return ring
 
 
-def targets_device(torch, pr: Projection, device):
-    """[G][cap*B] target coefficients and [G] counts (int64 / int32 tensors)."""
-    cnt = [min(pr.cap, pr.outputs - g * pr.cap) * pr.batch for g in range(pr.groups)]
+def targets_device(torch, pr: Projection, device, tiles: int = 1):
+    """[tiles*G][cap*B] target coefficients and [tiles*G] counts (int64 / int32 tensors)."""
+    cnt = [min(pr.cap, pr.outputs - g * pr.cap) * pr.batch for g in range(pr.groups)] * tiles
     mx = pr.cap * pr.batch
     idx = torch.arange(mx, device=device)
-    tg = (idx * pr.stride + pr.d - 1).repeat(pr.groups, 1).contiguous()  # (o*B+b)*(2d-1)+d-1
+    tg = (idx * pr.stride + pr.d - 1).repeat(tiles * pr.groups, 1).contiguous()  # (o*B+b)*(2d-1)+d-1
     counts = torch.tensor(cnt, dtype=torch.int32, device=device)
     return tg, counts, mx
 
 
 class LayerServer:
-    """Server-side linear protocol of one layer on one device (ART-002 context)."""
+    """Server-side linear protocol of one layer on one device (ART-002 context), for
+    `tiles` token tiles at a time: the tiles of a prefill share every weight matrix, so
+    each projection runs as one multi-tile product that reads the NTT-form weights once."""
 
-    def __init__(self, torch, ctx: Context, pk_device, projections=QWEN3_06B_LAYER, batch: int = 16):
+    def __init__(self, torch, ctx: Context, pk_device, projections=QWEN3_06B_LAYER, batch: int = 16,
+                 tiles: int = 1):
         self.torch = torch
         self.ctx = ctx
         self.pk = pk_device
         self.proj = [plan(nm, batch, k, o) for nm, k, o in projections]
         self.batch = batch
-        t, n, dk, k = torch, ctx.n, ctx.dk, ctx.k
+        self.tiles = tiles
+        t, n, dk = torch, ctx.n, ctx.dk
         dev = pk_device.device
         maxg = max(p.groups for p in self.proj)
         self.w_ntt = {}
-        self.u = t.empty((maxg, k, n), dtype=t.int64, device=dev)
-        self.x = t.empty((maxg, 2, k, n), dtype=t.int64, device=dev)
-        self.out = t.empty((maxg, 2, dk, n), dtype=t.int64, device=dev)
-        self.targets = {p.name: targets_device(t, p, dev) for p in self.proj}
+        self.scratch = t.empty(max(1, ctx.matrix_tiles_scratch_words(tiles, maxg)), dtype=t.int64, device=dev)
+        self.out = t.empty(tiles * maxg * 2 * dk * n, dtype=t.int64, device=dev)
+        self.targets = {p.name: targets_device(t, p, dev, tiles) for p in self.proj}
         mx = max(v[2] for v in self.targets.values())
-        self.selected = t.empty((maxg, dk, mx), dtype=t.int64, device=dev)
-        self.crt = t.empty((maxg, mx, dk), dtype=t.int64, device=dev)
+        self.selected = t.empty((tiles * maxg, dk, mx), dtype=t.int64, device=dev)
+        self.crt = t.empty((tiles * maxg, mx, dk), dtype=t.int64, device=dev)
 
     def prepare_weights(self, ring_by_name: dict, stream=None) -> None:
         """Lift + NTT every weight block of the layer once (reused by all tiles)."""
@@ -102,16 +105,20 @@ class LayerServer:
                 self.w_ntt[p.name] = w
             self.ctx.weights_ntt_device(ring, p.groups * p.inputs, w, stream=stream)
 
+    def output(self, p: Projection):
+        """[tiles][G][2][dk][n] view of the last run of projection p."""
+        n, dk = self.ctx.n, self.ctx.dk
+        return self.out[: self.tiles * p.groups * 2 * dk * n].view(self.tiles, p.groups, 2, dk, n)
+
     def run_projection(self, p: Projection, cts, masks, samples, stream=None):
-        """One private_matrix call of one tile: cts [I][2][dk][n] client ciphertexts in
-        coefficient form (transformed in place), masks [G][n], samples [G][3][k][n].
-        Leaves c1 in self.out[:G, 1] and the targets' c0 residues / CRT limbs in
-        self.selected / self.crt."""
+        """One private_matrix call for every tile: cts [tiles][I][2][dk][n] client
+        ciphertexts in coefficient form (transformed in place), masks [tiles][G][n], samples
+        [tiles][G][3][k][n].  Leaves the re-randomised results in output(p) (c1 goes to the
+        client) and the targets' c0 residues / CRT limbs in self.selected / self.crt."""
         ctx = self.ctx
-        I, G = p.inputs, p.groups
-        inp = cts
-        ctx.ntt_device(inp, I * 2 * ctx.dk, ctx.dk, 0, False, stream=stream)
-        ctx.enc0_device(samples, self.pk, G, self.u, self.x, stream=stream)
-        ctx.matrix_groups_device(inp, I, self.w_ntt[p.name], G, self.out, mask=masks, enc0_x=self.x, stream=stream)
+        I, G, T = p.inputs, p.groups, self.tiles
+        ctx.ntt_device(cts, T * I * 2 * ctx.dk, ctx.dk, 0, False, stream=stream)
+        ctx.matrix_tiles_device(cts, T, I, self.w_ntt[p.name], G, self.out, masks=masks, samples=samples,
+                                pk=self.pk, scratch=self.scratch, stream=stream)
         tg, counts, mx = self.targets[p.name]
-        ctx.gather_targets_device(self.out, G, tg, counts, mx, self.selected, self.crt, stream=stream)
+        ctx.gather_targets_device(self.out, T * G, tg, counts, mx, self.selected, self.crt, stream=stream)

@@ -708,6 +708,37 @@ int32_t bfvgpu_matrix_groups_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_
   });
 }
 
+uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx* ctx, uint64_t tiles, uint64_t groups, int32_t enc0) {
+  if (!ctx || !enc0) return 0;
+  return tiles * groups * (ctx->c.k + 2) * (uint64_t)ctx->c.n;
+}
+
+int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t tiles, uint64_t inputs,
+                                   const uint64_t* w, uint64_t groups, const uint64_t* masks, const uint64_t* samples,
+                                   const uint64_t* pk, uint64_t* scratch, uint64_t* out, void* stream) {
+  return guard([&] {
+    if (!ctx || !in || !w || !out || !inputs) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (samples && (!pk || !scratch)) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (samples && ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    const uint64_t items = tiles * groups;
+    uint64_t* U = samples ? scratch : nullptr;
+    uint64_t* xs = samples ? scratch + items * ctx->c.k * (uint64_t)ctx->c.n : nullptr;
+    cudaStream_t st = pick(ctx, stream);
+    // out doubles as the product accumulator: each INTT block reads its whole limb
+    // before writing it back.
+    cuda_check(launch_mac_tiles(ctx->c.P, in, tiles, inputs, w, groups, out, st), "mac_tiles");
+    count_launch(mac_tiles_launches(tiles));
+    if (samples) {
+      cuda_check(launch_enc0_prep(ctx->c.P, samples, pk, items, U, xs, st), "enc0_prep");
+      count_launch();
+    }
+    cuda_check(launch_intt_protect(ctx->c.P, out, items, U, pk, xs, samples, masks, out, st), "intt_protect");
+    count_launch();
+  });
+}
+
 int32_t bfvgpu_enc0_device(bfvgpu_ctx* ctx, const uint64_t* samples, const uint64_t* pk, uint64_t groups,
                            uint64_t* u_scratch, uint64_t* x_out, void* stream) {
   return guard([&] {

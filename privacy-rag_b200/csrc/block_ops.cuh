@@ -391,6 +391,104 @@ BFV_HD void op_enc0_x(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* s
   }
 }
 
+// ---- multi-tile product and folded Enc(0) (the layer pipeline) -----------------------------
+// For T tiles that share one weight matrix, the product of group g is a per-coefficient
+// contraction acc[t][c] = sum_b in[t][b][c] . W[g][b]; each weight word is read once and
+// used for all 2T accumulators.  One work item = (group g, data prime p, coefficient z).
+template <int T>
+BFV_HD void mac_tiles_item(uint64_t g, uint32_t p, uint32_t z, const uint64_t* in, const uint64_t* W,
+                           uint64_t* acc_out, uint32_t inputs, uint64_t groups, uint32_t dk, int logn,
+                           const Modulus& m) {
+  const uint64_t N = uint64_t(1) << logn;
+  const uint64_t cstride = (uint64_t)dk * N;             // c -> c+1 inside one input
+  const uint64_t bstride = 2 * cstride;                  // b -> b+1
+  const uint64_t tstride = (uint64_t)inputs * bstride;   // t -> t+1
+  const uint64_t* ip = in + (uint64_t)p * N + z;
+  const uint64_t* wp = W + (g * inputs * dk + p) * N + z;
+  Acc128 acc[2 * T];
+  for (uint32_t b = 0; b < inputs; ++b) {
+    const uint64_t w = wp[(uint64_t)b * cstride];
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      acc[2 * t].mac(ip[t * tstride + b * bstride], w);
+      acc[2 * t + 1].mac(ip[t * tstride + b * bstride + cstride], w);
+    }
+    if ((b & 127u) == 127u) {
+#pragma unroll
+      for (int i = 0; i < 2 * T; ++i) acc[i].fold(m);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < T; ++t)
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+      acc_out[(((uint64_t)t * groups + g) * 2 + c) * cstride + (uint64_t)p * N + z] = acc[2 * t + c].reduce(m);
+}
+
+// Enc(0) preparation for item e (a tile-group pair): block (e, key-level prime p) stores
+// U[e][p] = NTT(u); the special-prime block also produces the special-prime coefficients
+// xs[e][c] = INTT(U . pk_c) + e_c that the divide-and-round needs.
+template <int LOGN, class Ex>
+BFV_HD void op_enc0_prep(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* samples, const uint64_t* pk,
+                         uint64_t* U, uint64_t* xs, uint32_t k, const Modulus* mods, const ulonglong2* fwd,
+                         const ulonglong2* inv) {
+  constexpr uint64_t N = uint64_t(1) << LOGN;
+  const uint64_t e = blk / k;
+  const uint32_t p = (uint32_t)(blk % k);
+  const Modulus m = mods[p];
+  const uint64_t* u = samples + (e * 3 * k + p) * N;
+  uint64_t* Up = U + (e * k + p) * N;
+  {
+    auto ld = [u](int i) { return u[i]; };
+    auto st = [Up](int i, uint64_t v) { Up[i] = v; };
+    ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+  }
+  if (p != k - 1) return;
+  for (uint32_t c = 0; c < 2; ++c) {
+    const uint64_t* pkc = pk + ((uint64_t)c * k + p) * N;
+    const uint64_t* ec = samples + ((e * 3 + 1 + c) * k + p) * N;
+    uint64_t* xo = xs + (e * 2 + c) * N;
+    auto ld = [=](int i) { return mul_mod(Up[i], pkc[i], m); };
+    auto st = [=](int i, uint64_t v) { xo[i] = add_mod(v, ec[i], m.q); };
+    ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+  }
+}
+
+// INTT of the accumulated product with the Enc(0) and mask epilogue, block (e, c, p):
+//   out = INTT(acc + U_p . pk_c,p . q_s^-1) + (e_c,p - corr(xs_c)) . q_s^-1  [- Delta mask]
+// which equals INTT(acc) + moddown(INTT(U . pk_c) + e_c) - Delta mask exactly, because
+// moddown_p(x) = (x_p - corr(x_s)) q_s^-1 is linear in x_p.
+template <int LOGN, class Ex>
+BFV_HD void op_intt_protect(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* acc, uint64_t* out,
+                            const uint64_t* U, const uint64_t* pk, const uint64_t* xs, const uint64_t* samples,
+                            const uint64_t* mask, uint32_t k, uint32_t dk, const Modulus* mods,
+                            const ulonglong2* inv, uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
+  constexpr uint64_t N = uint64_t(1) << LOGN;
+  const uint64_t e = blk / (2 * dk);
+  const uint32_t cp = (uint32_t)(blk % (2 * dk)), c = cp / dk, p = cp % dk;
+  const Modulus m = mods[p];
+  const uint64_t* a = acc + (e * 2 * dk + cp) * N;
+  uint64_t* o = out + (e * 2 * dk + cp) * N;
+  const bool enc0 = U != nullptr;
+  const uint64_t* Up = enc0 ? U + (e * k + p) * N : nullptr;
+  const uint64_t* pkc = enc0 ? pk + ((uint64_t)c * k + p) * N : nullptr;
+  const uint64_t* xsc = enc0 ? xs + (e * 2 + c) * N : nullptr;
+  const uint64_t* ec = enc0 ? samples + ((e * 3 + 1 + c) * k + p) * N : nullptr;
+  const uint64_t* mk = (mask && c == 0) ? mask + e * N : nullptr;
+  const Modulus* ms = mods + (k - 1);
+  auto ld = [=](int i) {
+    uint64_t v = a[i];
+    if (enc0) v = add_mod(v, shoup(mul_mod(Up[i], pkc[i], m), m.inv_special, m.inv_special_q, m.q), m.q);
+    return v;
+  };
+  auto st = [=](int i, uint64_t v) {
+    if (enc0) v = add_mod(v, moddown_elem(ec[i], xsc[i], m, *ms), m.q);
+    if (mk) v = sub_mod(v, scale_plain_coeff(mk[i], q_mod_t, upper_half, t, tlog, m), m.q);
+    o[i] = v;
+  };
+  ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
+}
+
 // ---- client phase: block = (batch b, data prime p) -----------------------------------------
 template <int LOGN, class Ex>
 BFV_HD void op_client_phase(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* data, const uint64_t* sk, uint32_t dk,

@@ -123,6 +123,40 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
   op_ks_hoist<LOGN>(BlockExec{}, smem, blockIdx.x, cts, Y, zflag, k, dk, mods, fwd);
 }
 
+// ---- layer pipeline: multi-tile product, Enc(0) preparation, INTT with epilogue -------
+// Block = 256 coefficients of one (data prime, group); consecutive blocks walk the groups
+// of one coefficient chunk, so the chunk's inputs (all tiles and blocks) stay in L2 while
+// every weight word is streamed from HBM once.
+template <int T>
+__global__ void __launch_bounds__(256) k_mac_tiles(const uint64_t* in, const uint64_t* w, uint64_t* acc,
+                                                   uint32_t inputs, uint32_t groups, uint32_t dk, int logn,
+                                                   uint32_t zchunks, const Modulus* mods) {
+  const uint32_t g = blockIdx.x % groups;
+  const uint32_t r = blockIdx.x / groups;
+  const uint32_t p = r / zchunks, zc = r % zchunks;
+  const uint32_t z = zc * blockDim.x + threadIdx.x;
+  const Modulus m = mods[p];
+  mac_tiles_item<T>(g, p, z, in, w, acc, inputs, groups, dk, logn, m);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_enc0_prep(const uint64_t* samples, const uint64_t* pk, uint64_t* U, uint64_t* xs, uint32_t k,
+                const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_enc0_prep<LOGN>(BlockExec{}, smem, blockIdx.x, samples, pk, U, xs, k, mods, fwd, inv);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_intt_protect(const uint64_t* acc, uint64_t* out, const uint64_t* U, const uint64_t* pk, const uint64_t* xs,
+                   const uint64_t* samples, const uint64_t* mask, uint32_t k, uint32_t dk, const Modulus* mods,
+                   const ulonglong2* inv, uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
+  extern __shared__ uint64_t smem[];
+  op_intt_protect<LOGN>(BlockExec{}, smem, blockIdx.x, acc, out, U, pk, xs, samples, mask, k, dk, mods, inv, q_mod_t,
+                        upper_half, t, tlog);
+}
+
 // Galois elements of up to kKeyBatch keys and their inverses mod 2n, passed by value.
 constexpr int kKeyBatch = 256;
 struct EltBatch {
@@ -278,6 +312,8 @@ static cudaError_t configure_for() {
   chk(allow_smem(k_ks_rotate<L>, s));
   chk(allow_smem(k_ks_finish<L>, (size_t(1) << L) * 8));
   chk(allow_smem(k_client_phase<L>, s));
+  chk(allow_smem(k_enc0_prep<L>, s));
+  chk(allow_smem(k_intt_protect<L>, s));
   if constexpr (L == 14) {
     chk(allow_smem(k_token_lift_ntt<L>, s));
     chk(allow_smem(k_token_mac_intt<L>, s));
@@ -489,6 +525,65 @@ cudaError_t launch_add_plain(const DevParams& P, uint64_t* c0, const uint64_t* p
 cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint64_t polys, cudaStream_t st) {
   if (!polys) return cudaSuccess;
   k_add<<<elementwise_blocks(polys << P.logn), 256, 0, st>>>(a, b, polys, P.dk, P.logn, P.mod);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t tiles, uint64_t inputs,
+                             const uint64_t* w, uint64_t groups, uint64_t* acc, cudaStream_t st) {
+  if (!tiles || !groups) return cudaSuccess;
+  const uint32_t threads = P.n < 256 ? P.n : 256;
+  const uint32_t zchunks = P.n / threads;
+  const uint64_t blocks = (uint64_t)P.dk * zchunks * groups;
+  if (blocks > 0x7fffffffull || inputs > 0xffffffffull || groups > 0xffffffffull) return cudaErrorInvalidValue;
+  const uint64_t in_tile = inputs * 2 * P.dk * (uint64_t)P.n, acc_tile = groups * 2 * P.dk * (uint64_t)P.n;
+  uint64_t t0 = 0;
+  while (t0 < tiles) {
+    const uint64_t left = tiles - t0;
+    const int T = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
+    const uint64_t* ip = in + t0 * in_tile;
+    uint64_t* ap = acc + t0 * acc_tile;
+    switch (T) {
+      case 8: k_mac_tiles<8><<<(unsigned)blocks, threads, 0, st>>>(ip, w, ap, (uint32_t)inputs, (uint32_t)groups, P.dk, P.logn, zchunks, P.mod); break;
+      case 4: k_mac_tiles<4><<<(unsigned)blocks, threads, 0, st>>>(ip, w, ap, (uint32_t)inputs, (uint32_t)groups, P.dk, P.logn, zchunks, P.mod); break;
+      case 2: k_mac_tiles<2><<<(unsigned)blocks, threads, 0, st>>>(ip, w, ap, (uint32_t)inputs, (uint32_t)groups, P.dk, P.logn, zchunks, P.mod); break;
+      default: k_mac_tiles<1><<<(unsigned)blocks, threads, 0, st>>>(ip, w, ap, (uint32_t)inputs, (uint32_t)groups, P.dk, P.logn, zchunks, P.mod); break;
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    t0 += T;
+  }
+  return cudaSuccess;
+}
+
+uint64_t mac_tiles_launches(uint64_t tiles) {
+  uint64_t c = 0;
+  while (tiles) {
+    tiles -= tiles >= 8 ? 8 : tiles >= 4 ? 4 : tiles >= 2 ? 2 : 1;
+    ++c;
+  }
+  return c;
+}
+
+cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const uint64_t* pk, uint64_t items,
+                             uint64_t* U, uint64_t* xs, cudaStream_t st) {
+  if (!items) return cudaSuccess;
+  if (items * P.k > 0x7fffffffull) return cudaErrorInvalidValue;
+  BFV_DISPATCH(P.logn, {
+    k_enc0_prep<L_><<<(unsigned)(items * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(samples, pk, U, xs, P.k,
+                                                                                         P.mod, P.fwd, P.inv);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_intt_protect(const DevParams& P, const uint64_t* acc, uint64_t items, const uint64_t* U,
+                                const uint64_t* pk, const uint64_t* xs, const uint64_t* samples, const uint64_t* mask,
+                                uint64_t* out, cudaStream_t st) {
+  if (!items) return cudaSuccess;
+  if (items * 2 * P.dk > 0x7fffffffull) return cudaErrorInvalidValue;
+  BFV_DISPATCH(P.logn, {
+    k_intt_protect<L_><<<(unsigned)(items * 2 * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(
+        acc, out, U, pk, xs, samples, mask, P.k, P.dk, P.mod, P.inv, P.q_mod_t, P.upper_half, P.t, P.tlog);
+  });
   return cudaGetLastError();
 }
 

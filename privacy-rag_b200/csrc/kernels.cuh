@@ -118,4 +118,22 @@ cudaError_t launch_add_plain(const DevParams& P, uint64_t* c0, const uint64_t* p
 // a += b on [polys][n] data-prime polys.
 cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint64_t polys, cudaStream_t st);
 
+// Layer pipeline over T tiles that share one weight matrix (E = T * groups items, item
+// e = t * groups + g):
+//  mac_tiles:    acc [T][G][2][dk][n] = sum_b in[t][b][c] . w[g][b]; in [T][I][2][dk][n] and
+//                w [G][I][dk][n] NTT form.  Tiles run in launches of 8/4/2/1
+//                (mac_tiles_launches counts them).
+//  enc0_prep:    U [E][k][n] = NTT(u); xs [E][2][n] = special-prime coefficients of
+//                INTT(U . pk_c) + e_c; samples [E][3][k][n].
+//  intt_protect: out [E][2][dk][n] = INTT(acc) + Enc(0) (if U) - Delta mask (if mask
+//                [E][n]), the Enc(0) data-prime part folded into the transform's input.
+cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t tiles, uint64_t inputs,
+                             const uint64_t* w, uint64_t groups, uint64_t* acc, cudaStream_t st);
+uint64_t mac_tiles_launches(uint64_t tiles);
+cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const uint64_t* pk, uint64_t items,
+                             uint64_t* U, uint64_t* xs, cudaStream_t st);
+cudaError_t launch_intt_protect(const DevParams& P, const uint64_t* acc, uint64_t items, const uint64_t* U,
+                                const uint64_t* pk, const uint64_t* xs, const uint64_t* samples, const uint64_t* mask,
+                                uint64_t* out, cudaStream_t st);
+
 }  // namespace bfvgpu

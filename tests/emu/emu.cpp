@@ -147,6 +147,54 @@ int emu_matrix(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const 
   return 0;
 }
 
+// Layer pipeline over T tiles: cts [T][I][2][dk][n] coefficient form, ring [G][I][n],
+// masks [T][G][n] or null, samples [T][G][3][k][n] or null (pk [2][k][n]);
+// out [T][G][2][dk][n].  Tiles are taken in chunks of 8/4/2/1 as the launcher does, and
+// out doubles as the product accumulator as on the device.
+int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd,
+                     const uint64_t* inv, const uint64_t* cts, uint64_t tiles, uint64_t inputs, const uint64_t* ring,
+                     uint64_t groups, const uint64_t* masks, const uint64_t* samples, const uint64_t* pk,
+                     uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog, uint64_t* out) {
+  Tabs T = tabs(k, mods16, fwd, inv);
+  const uint64_t n = 1ull << logn;
+  const uint64_t items = tiles * groups;
+  std::vector<uint64_t> in(cts, cts + tiles * inputs * 2 * dk * n);
+  std::vector<uint64_t> w(groups * inputs * dk * n);
+  std::vector<uint64_t> U(items * k * n), xs(items * 2 * n);
+  EMU_DISPATCH(logn, {
+    std::vector<uint64_t> s(SmemWords<L_>::value);
+    for (uint64_t b = 0; b < tiles * inputs * 2 * dk; ++b)
+      op_ntt<L_>(HostExec{}, s.data(), b, false, in.data(), dk, 0, T.mods.data(), T.fwd, T.inv);
+    for (uint64_t b = 0; b < groups * inputs * dk; ++b)
+      op_lift_ntt<L_>(HostExec{}, s.data(), b, ring, w.data(), dk, T.mods.data(), T.fwd);
+    const uint64_t in_tile = inputs * 2 * dk * n, acc_tile = groups * 2 * dk * n;
+    for (uint64_t t0 = 0; t0 < tiles;) {
+      const uint64_t left = tiles - t0;
+      const int TT = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
+      for (uint64_t g = 0; g < groups; ++g)
+        for (uint32_t p = 0; p < dk; ++p)
+          for (uint32_t z = 0; z < n; ++z) {
+            const uint64_t* ip = in.data() + t0 * in_tile;
+            uint64_t* ap = out + t0 * acc_tile;
+            switch (TT) {
+              case 8: mac_tiles_item<8>(g, p, z, ip, w.data(), ap, (uint32_t)inputs, groups, dk, L_, T.mods[p]); break;
+              case 4: mac_tiles_item<4>(g, p, z, ip, w.data(), ap, (uint32_t)inputs, groups, dk, L_, T.mods[p]); break;
+              case 2: mac_tiles_item<2>(g, p, z, ip, w.data(), ap, (uint32_t)inputs, groups, dk, L_, T.mods[p]); break;
+              default: mac_tiles_item<1>(g, p, z, ip, w.data(), ap, (uint32_t)inputs, groups, dk, L_, T.mods[p]); break;
+            }
+          }
+      t0 += TT;
+    }
+    if (samples)
+      for (uint64_t b = 0; b < items * k; ++b)
+        op_enc0_prep<L_>(HostExec{}, s.data(), b, samples, pk, U.data(), xs.data(), k, T.mods.data(), T.fwd, T.inv);
+    for (uint64_t b = 0; b < items * 2 * dk; ++b)
+      op_intt_protect<L_>(HostExec{}, s.data(), b, out, out, samples ? U.data() : nullptr, pk, xs.data(), samples,
+                          masks, k, dk, T.mods.data(), T.inv, q_mod_t, upper_half, t, tlog);
+  });
+  return 0;
+}
+
 // data [batches][dk][n] in place, sk [dk][n] NTT form.
 int emu_client_phase(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd,
                      const uint64_t* inv, uint64_t* data, const uint64_t* sk, uint64_t batches) {

@@ -145,6 +145,38 @@ def test_matrix_mask_enc0_kernel_bodies(bfv, oracle, E, logn):
     assert np.array_equal(out2[0], oc.matrix_evaluate(cn, ring[0]))
 
 
+@pytest.mark.parametrize("tiles", [1, 3, 8])
+def test_matrix_tiles_kernel_bodies(bfv, oracle, E, tiles):
+    """Layer pipeline (multi-tile product, Enc(0) prep, INTT with folded Enc(0) and mask)
+    against the oracle's per-tile matrix evaluation + sub_plain + Enc(0) add."""
+    logn = 5
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+    k, dk, n = hc.k, hc.dk, 1 << logn
+    tb = oracle.TestBfv(oc, seed=40 + tiles)
+    rng = np.random.default_rng(tiles)
+    I, G = 3, 2
+    cts = np.stack([np.stack([tb.encrypt(rng.integers(0, 1 << 59, size=n, dtype=np.uint64)) for _ in range(I)])
+                    for _ in range(tiles)])
+    ring = rng.integers(0, 1 << 59, size=(G, I, n), dtype=np.uint64)
+    ring[0, 0, :4] = [(1 << 59) - 1, 1 << 58, (1 << 58) - 1, 0]
+    masks = rng.integers(0, 1 << 59, size=(tiles, G, n), dtype=np.uint64)
+    samples = np.stack([np.stack([tb.samples() for _ in range(G)]) for _ in range(tiles)])
+    out = np.zeros((tiles, G, 2, dk, n), dtype=np.uint64)
+    E.emu_matrix_tiles(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), tiles, I, p(ring), G, p(masks), p(samples),
+                       p(tb.pk), oc.q_mod_t, oc.upper_half, 1 << 59, 59, p(out))
+    plain = np.zeros_like(out)
+    E.emu_matrix_tiles(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), tiles, I, p(ring), G, None, None, None,
+                       oc.q_mod_t, oc.upper_half, 1 << 59, 59, p(plain))
+    for t in range(tiles):
+        cn = oc.matrix_open(cts[t])
+        for g in range(G):
+            e = oc.matrix_evaluate(cn, ring[g])
+            assert np.array_equal(plain[t, g], e), (t, g)
+            e[0] = oc.sub_plain(e[0], masks[t, g])
+            e = oc.add(e, oc.enc0(samples[t, g], tb.pk))
+            assert np.array_equal(out[t, g], e), (t, g)
+
+
 def test_client_phase_kernel_body(bfv, oracle, E):
     hc, oc, mods, fwd, inv = make(bfv, oracle, 14)
     tb = oracle.TestBfv(oc, seed=2)

@@ -337,6 +337,45 @@ def test_matrix_groups_mask_enc0_crt(art, oracle):
             assert v == oracle.crt(e[0][:, t], oc.primes[:6])
 
 
+@pytest.mark.parametrize("tiles", [3, 9])
+def test_matrix_tiles_device(art, oracle, tiles):
+    """Layer pipeline through bfvgpu_matrix_tiles_device (tiles in launches of 8/2/1) against
+    the oracle's per-tile evaluate + sub_plain + Enc(0); also without mask and Enc(0)."""
+    import torch
+    hc, oc = art
+    n, k, dk = oc.n, oc.k, oc.data_k
+    tb = oracle.TestBfv(oc, seed=90 + tiles)
+    rng = np.random.default_rng(tiles)
+    I, G = 2, 2
+    cts = np.stack([np.stack([tb.encrypt(rng.integers(0, 1 << 59, size=n, dtype=np.uint64)) for _ in range(I)])
+                    for _ in range(tiles)])
+    ring = rng.integers(0, 1 << 59, size=(G, I, n), dtype=np.uint64)
+    ring[0, 0, :4] = [(1 << 59) - 1, 1 << 58, (1 << 58) - 1, 0]
+    masks = rng.integers(0, 1 << 59, size=(tiles, G, n), dtype=np.uint64)
+    samples = np.stack([np.stack([tb.samples() for _ in range(G)]) for _ in range(tiles)])
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int64)).cuda()
+    d_in, d_ring, d_masks, d_samples, d_pk = dev(cts), dev(ring), dev(masks), dev(samples), dev(tb.pk)
+    w = torch.empty((G, I, dk, n), dtype=torch.int64, device="cuda")
+    scratch = torch.empty(hc.matrix_tiles_scratch_words(tiles, G), dtype=torch.int64, device="cuda")
+    out = torch.empty((tiles, G, 2, dk, n), dtype=torch.int64, device="cuda")
+    plain = torch.empty_like(out)
+    torch.cuda.synchronize()
+    hc.ntt_device(d_in, tiles * I * 2 * dk, dk)
+    hc.weights_ntt_device(d_ring, G * I, w)
+    hc.matrix_tiles_device(d_in, tiles, I, w, G, out, masks=d_masks, samples=d_samples, pk=d_pk, scratch=scratch)
+    hc.matrix_tiles_device(d_in, tiles, I, w, G, plain)
+    torch.cuda.synchronize()
+    got, got_plain = out.cpu().numpy().view(np.uint64), plain.cpu().numpy().view(np.uint64)
+    for t in range(tiles):
+        cn = oc.matrix_open(cts[t], threads=8)
+        for g in range(G):
+            e = oc.matrix_evaluate(cn, ring[g], threads=8)
+            assert np.array_equal(got_plain[t, g], e), (t, g)
+            e[0] = oc.sub_plain(e[0], masks[t, g])
+            e = oc.add(e, oc.enc0(samples[t, g], tb.pk))
+            assert np.array_equal(got[t, g], e), (t, g)
+
+
 # ---- resident token ----------------------------------------------------------------------------
 def test_token_weights(art, oracle):
     import bfvgpu

@@ -123,3 +123,54 @@ def test_public_shape_rejections(bfv):
                                            ((1, 8), 1, 40, 20, False), ((1, 19 * 8192 + 1), 1, 12, 12, True)]:
         with pytest.raises(engine.ProtocolShapeError):
             engine.validate(shape, outputs, fx, fw, linear=linear)
+
+
+def test_layer_server_tiles_decrypt(bfv, oracle, setup):
+    """LayerServer (multi-tile product, folded Enc(0), mask, target gather with CRT) on two
+    small projections and three token tiles: every target decrypts to sum_j x.w minus the
+    mask at that coefficient (mod 2^59), and the gathered c0 residues and CRT limbs are the
+    output ciphertext's own."""
+    import torch
+    from bfvgpu import layer as L
+    from bfvgpu.layout import MASK59, pack_inputs
+    hc, oc, tb = setup
+    n, k, dk = oc.n, oc.k, oc.data_k
+    tiles, batch = 3, 2
+    rng = np.random.default_rng(77)
+    pk = torch.from_numpy(tb.pk.view(np.int64)).cuda()
+    srv = L.LayerServer(torch, hc, pk, (("a", 300, 200), ("b", 130, 600)), batch, tiles)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int64)).cuda()
+    rings, w_int = {}, {}
+    for p in srv.proj:
+        w_int[p.name] = rng.integers(-127, 128, size=(p.outputs, p.inner))
+        rings[p.name] = L.pack_weights_device(torch, dev(w_int[p.name].astype(np.int64).astype(np.uint64)), p, n)
+    srv.prepare_weights(rings)
+    for p in srv.proj:
+        x = rng.integers(0, 1 << 59, size=(tiles, batch, p.inner), dtype=np.uint64)
+        cts = np.stack([np.stack([tb.encrypt(poly) for poly in pack_inputs(x[t], p.d, p.inputs, n)])
+                        for t in range(tiles)])
+        masks = rng.integers(0, 1 << 59, size=(tiles, p.groups, n), dtype=np.uint64)
+        samples = np.stack([np.stack([tb.samples() for _ in range(p.groups)]) for _ in range(tiles)])
+        srv.run_projection(p, dev(cts), dev(masks), dev(samples))
+        torch.cuda.synchronize()
+        out = srv.output(p).cpu().numpy().view(np.uint64)
+        tg, counts, mx = srv.targets[p.name]
+        tg, counts = tg.cpu().numpy(), counts.cpu().numpy()
+        sel = srv.selected.cpu().numpy().view(np.uint64)
+        crt = srv.crt.cpu().numpy().view(np.uint64)
+        w_u = w_int[p.name].astype(np.int64).astype(np.uint64) & np.uint64(MASK59)
+        for t in range(tiles):
+            for g in range(p.groups):
+                e = t * p.groups + g
+                u = oc.client_phase(out[t, g, 1], tb.sk_data_ntt())
+                for i in range(counts[e]):
+                    z = int(tg[e, i])
+                    o, b = divmod(i, batch)
+                    row = g * p.cap + o
+                    expect = (int((x[t, b].astype(object) * w_u[row].astype(object)).sum()) - int(masks[t, g, z])) \
+                        % (1 << 59)
+                    res = [(int(out[t, g, 0, q, z]) + int(u[q, z])) % oc.primes[q] for q in range(dk)]
+                    assert oracle.decode(oracle.crt(res, oc.primes[:dk]), oc.Q) == expect, (p.name, t, g, i)
+                    assert np.array_equal(sel[e, :, i], out[t, g, 0, :, z])
+                    v = sum(int(crt[e, i, l]) << (64 * l) for l in range(dk))
+                    assert v == oracle.crt(out[t, g, 0, :, z], oc.primes[:dk])
