@@ -173,8 +173,11 @@ def run_layer_legs(torch, bfvgpu, device, args):
 
     pk = residues((2, k, n), k)
     out = {}
-    for label, projections, batch, tiles in (("config3", (("q_proj", 1024, 2048),), 1, 1),
-                                             ("config4", L.QWEN3_06B_LAYER, 16, args.layer_tiles)):
+    legs = (("config3", (("q_proj", 1024, 2048),), 1, 1), ("config4", L.QWEN3_06B_LAYER, 16, args.layer_tiles))
+    if getattr(args, "layer_shape", None):
+        kk, oo = (int(v) for v in args.layer_shape.split(","))
+        legs = (("probe", (("probe", kk, oo),), 16, args.layer_tiles),)
+    for label, projections, batch, tiles in legs:
         srv = L.LayerServer(torch, ctx, pk, projections, batch, tiles)
         rings, cts, masks, samples = {}, {}, {}, {}
         for p in srv.proj:
@@ -209,7 +212,7 @@ def run_layer_legs(torch, bfvgpu, device, args):
         per = [sum(e[1 + i].elapsed_time(e[2 + i]) for e in evs) / reps for i in range(len(srv.proj))]
         weight_ntts = sum(p.groups * p.inputs * dk for p in srv.proj)
         mac = tiles * sum(p.groups * p.inputs * 2 * dk * n for p in srv.proj)
-        out[label] = {"ms": ms, "unit": "ms per layer (all tiles)" if label == "config4" else "ms per matvec",
+        out[label] = {"ms": ms, "unit": "ms per matvec" if label == "config3" else "ms per layer (all tiles)",
                       "ms_weights_ntt": w_ms, "ms_with_cached_weights": ms - w_ms,
                       "ms_per_call": {p.name: per[i] for i, p in enumerate(srv.proj)},
                       "tiles": tiles, "batch": batch,
@@ -278,6 +281,10 @@ def main():
     ap.add_argument("--ntt-reps", type=int, default=200)
     ap.add_argument("--layer", type=int, default=1, help="0 skips the config-3/4 legs")
     ap.add_argument("--layer-tiles", type=int, default=8, help="16-token tiles in the config-4 leg")
+    ap.add_argument("--layer-only", action="store_true", help="run only the config-3/4 legs (profiling)")
+    ap.add_argument("--layer-shape", default=None,
+                    help="K,O: with --layer-only, one B=16 projection of this shape instead of config 3/4 "
+                         "(small profiling case)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -295,6 +302,10 @@ def main():
     if not os.path.exists(B.LIB):
         B.build()
     import bfvgpu
+
+    if args.layer_only:
+        print(json.dumps({"layer_legs": run_layer_legs(torch, bfvgpu, local, args)}), flush=True)
+        return 0
 
     primes2 = bfvgpu.find_primes(N2, BITS2)
     ctx = bfvgpu.Context(N2, primes2, 4, 1, T2, device=local)

@@ -168,12 +168,17 @@ int32_t bfvgpu_matrix_groups_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_
  * tiles * groups * (k + 2) * n. */
 uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx *ctx, uint64_t tiles, uint64_t groups,
                                            int32_t enc0);
+/* Forward NTT, in place, of `count` client ciphertexts [count][2][dk][n] (coefficient
+ * form) into the operand form of bfvgpu_matrix_tiles_device: every canonical NTT slot v
+ * is stored as ((v >> 30) << 32) | (v mod 2^30).  Needs data primes < 2^60 and n >= 32. */
+int32_t bfvgpu_matrix_tiles_inputs_device(bfvgpu_ctx *ctx, uint64_t *cts, uint64_t count, void *stream);
 /* Server product of `tiles` token tiles that share one weight matrix (the four calls per
  * tile of Transformer::layer_from_shares, model.hpp:173-238, batched over tiles; per tile
  * and group the result is Matrix::evaluate of matrix.cu:90-106 plus the mask and Enc(0) of
  * bfv_matrix.inc:215-227):
  *   out[t][g][c] = INTT(sum_b in[t][b][c] . w[g][b]) + Enc(0)[t][g] - [c=0] Delta masks[t][g]
- * in [tiles][inputs][2][dk][n] NTT form, w [groups][inputs][dk][n] NTT form, masks
+ * in [tiles][inputs][2][dk][n] from bfvgpu_matrix_tiles_inputs_device, w
+ * [groups][inputs][dk][n] NTT form (bfvgpu_weights_ntt_device), masks
  * [tiles][groups][n] ring-59 words or NULL, samples [tiles][groups][3][k][n] or NULL (then
  * pk and scratch may be NULL), pk [2][k][n] NTT form, out [tiles][groups][2][dk][n].  Each
  * weight word is read once for all tiles. */

@@ -168,13 +168,20 @@ class Context:
                                                 groups, self._dptr(mask) or None, self._dptr(enc0_x) or None,
                                                 self._dptr(out), stream), "matrix_groups_device")
 
+    def matrix_tiles_inputs_device(self, cts, count: int, stream: int | None = None):
+        """Transform client ciphertexts [count][2][dk][n] in place into the operand form of
+        matrix_tiles_device (NTT slots with their 30-bit halves split)."""
+        check(lib().bfvgpu_matrix_tiles_inputs_device(self._h, self._dptr(cts), count, stream),
+              "matrix_tiles_inputs_device")
+
     def matrix_tiles_scratch_words(self, tiles: int, groups: int, enc0: bool = True) -> int:
         return int(lib().bfvgpu_matrix_tiles_scratch_words(self._h, tiles, groups, int(bool(enc0))))
 
     def matrix_tiles_device(self, inputs_ntt, tiles: int, inputs: int, weights_ntt, groups: int, out, masks=None,
                             samples=None, pk=None, scratch=None, stream: int | None = None):
-        """out [tiles][groups][2][dk][n] = product of each tile's NTT-form inputs
-        [tiles][inputs][2][dk][n] with the shared weights [groups][inputs][dk][n], plus
+        """out [tiles][groups][2][dk][n] = product of each tile's inputs [tiles][inputs][2][dk][n]
+        (from matrix_tiles_inputs_device) with the shared NTT-form weights
+        [groups][inputs][dk][n], plus
         Enc(0) from samples [tiles][groups][3][k][n] and minus the Delta-scaled masks."""
         check(lib().bfvgpu_matrix_tiles_device(self._h, self._dptr(inputs_ntt), tiles, inputs,
                                                self._dptr(weights_ntt), groups, self._dptr(masks) or None,

@@ -110,6 +110,13 @@ class LayerServer:
         n, dk = self.ctx.n, self.ctx.dk
         return self.out[: self.tiles * p.groups * 2 * dk * n].view(self.tiles, p.groups, 2, dk, n)
 
+    def gathered(self, p: Projection):
+        """Views of the last run of projection p: target c0 residues [tiles*G][dk][cap*B] and
+        their CRT limbs [tiles*G][cap*B][dk] (entries past a group's count are unset)."""
+        e, dk, mx = self.tiles * p.groups, self.ctx.dk, self.targets[p.name][2]
+        return (self.selected.view(-1)[: e * dk * mx].view(e, dk, mx),
+                self.crt.view(-1)[: e * mx * dk].view(e, mx, dk))
+
     def run_projection(self, p: Projection, cts, masks, samples, stream=None):
         """One private_matrix call for every tile: cts [tiles][I][2][dk][n] client
         ciphertexts in coefficient form (transformed in place), masks [tiles][G][n], samples
@@ -117,7 +124,7 @@ class LayerServer:
         client) and the targets' c0 residues / CRT limbs in self.selected / self.crt."""
         ctx = self.ctx
         I, G, T = p.inputs, p.groups, self.tiles
-        ctx.ntt_device(cts, T * I * 2 * ctx.dk, ctx.dk, 0, False, stream=stream)
+        ctx.matrix_tiles_inputs_device(cts, T * I, stream=stream)
         ctx.matrix_tiles_device(cts, T, I, self.w_ntt[p.name], G, self.out, masks=masks, samples=samples,
                                 pk=self.pk, scratch=self.scratch, stream=stream)
         tg, counts, mx = self.targets[p.name]

@@ -713,11 +713,29 @@ uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx* ctx, uint64_t tiles
   return tiles * groups * (ctx->c.k + 2) * (uint64_t)ctx->c.n;
 }
 
+static void require_product_ring(const Context& c) {
+  if (c.n < 32) fail(BFVGPU_E_RING, "E_BFVGPU_PRODUCT_RING");
+  for (uint32_t p = 0; p < c.dk; ++p)
+    if (c.q[p] >> 60) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_PRODUCT_PRIME");
+}
+
+int32_t bfvgpu_matrix_tiles_inputs_device(bfvgpu_ctx* ctx, uint64_t* cts, uint64_t count, void* stream) {
+  return guard([&] {
+    if (!ctx || !cts) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    require_product_ring(ctx->c);
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    cuda_check(launch_ntt_split(ctx->c.P, cts, count * 2 * ctx->c.dk, pick(ctx, stream)), "ntt_split");
+    count_launch();
+  });
+}
+
 int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t tiles, uint64_t inputs,
                                    const uint64_t* w, uint64_t groups, const uint64_t* masks, const uint64_t* samples,
                                    const uint64_t* pk, uint64_t* scratch, uint64_t* out, void* stream) {
   return guard([&] {
     if (!ctx || !in || !w || !out || !inputs) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    require_product_ring(ctx->c);
     if (samples && (!pk || !scratch)) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
     if (samples && ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
     require_device(ctx->c);

@@ -393,36 +393,141 @@ BFV_HD void op_enc0_x(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* s
 
 // ---- multi-tile product and folded Enc(0) (the layer pipeline) -----------------------------
 // For T tiles that share one weight matrix, the product of group g is a per-coefficient
-// contraction acc[t][c] = sum_b in[t][b][c] . W[g][b]; each weight word is read once and
-// used for all 2T accumulators.  One work item = (group g, data prime p, coefficient z).
-template <int T>
-BFV_HD void mac_tiles_item(uint64_t g, uint32_t p, uint32_t z, const uint64_t* in, const uint64_t* W,
-                           uint64_t* acc_out, uint32_t inputs, uint64_t groups, uint32_t dk, int logn,
-                           const Modulus& m) {
+// contraction acc[t][c] = sum_b in[t][b][c] . W[g][b] over residues < 2^60.  Each product
+// is taken over 30-bit halves (a = a1 2^30 + a0, w = w1 2^30 + w0): four 32x32->64-bit
+// multiply-adds into three 64-bit sums, folded exactly into a 128-bit sum every 8 terms.
+// The inputs are stored with their halves pre-split (split30) by the transform that
+// produces them.
+constexpr uint64_t kMask30 = (uint64_t(1) << 30) - 1;
+BFV_HD uint64_t split30(uint64_t v) { return ((v >> 30) << 32) | (v & kMask30); }
+BFV_HD uint64_t join30(uint64_t s) { return ((s >> 32) << 30) | (s & 0xffffffffull); }
+
+struct Mac30 {
+  uint64_t s0 = 0, s1 = 0, s2 = 0;
+  // a in split form, w0/w1 < 2^30.  At most 8 calls between folds: s1 gains < 2^61 per call.
+  BFV_HD void mac(uint64_t a, uint32_t w0, uint32_t w1) {
+    const uint32_t a0 = (uint32_t)a, a1 = (uint32_t)(a >> 32);
+#ifdef __CUDA_ARCH__
+    // one fused 32x32+64 multiply-add each
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(s0) : "r"(a0), "r"(w0));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(s1) : "r"(a0), "r"(w1));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(s1) : "r"(a1), "r"(w0));
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(s2) : "r"(a1), "r"(w1));
+#else
+    s0 += (uint64_t)a0 * w0;
+    s1 += (uint64_t)a0 * w1;
+    s1 += (uint64_t)a1 * w0;
+    s2 += (uint64_t)a1 * w1;
+#endif
+  }
+  // A += s0 + s1 2^30 + s2 2^60, then clear.
+  BFV_HD void fold(Acc128& A) {
+    uint64_t lo = s0 + (s1 << 30);
+    uint64_t hi = (s1 >> 34) + (lo < s0);
+    const uint64_t t = s2 << 60;
+    lo += t;
+    hi += (s2 >> 4) + (lo < t);
+    A.lo += lo;
+    A.hi += hi + (A.lo < lo);
+    s0 = s1 = s2 = 0;
+  }
+};
+
+// Block of the product kernel: 16 warps x 32 coefficient lanes of one data prime p; warp w
+// takes tiles [h*TH, h*TH+TH) (h = w % H) of group g0 + w / H, so GB = 16 / H groups share
+// the block's staged inputs.  Input blocks are staged 8 at a time (one Mac30 fold each):
+// shared memory holds in [T][8][2][32] (split form) then W [GB][8][32], double-buffered.
+template <int T, int TH>
+struct MacShape {
+  static constexpr int kWarps = 16, kThreads = 32 * kWarps, kBc = 8;
+  static constexpr int H = T / TH, GB = kWarps / H;
+  static constexpr int kInWords = T * kBc * 2 * 32, kWWords = GB * kBc * 32;
+  static constexpr int kBufWords = kInWords + kWWords;
+  static constexpr int kSegs = kBufWords / 2;  // 16-byte staging segments per chunk
+  static_assert(T % TH == 0 && kWarps % H == 0, "tile split");
+};
+
+// Staging segment seg (two coefficients) of the chunk starting at input block b0: its
+// shared-memory word offset and its global source, or null where the segment is zero
+// (input block past `inputs`, or group past `groups`).
+template <int T, int TH>
+BFV_HD const uint64_t* mac_stage_src(int seg, uint32_t b0, const uint64_t* in, const uint64_t* w, uint32_t inputs,
+                                     uint32_t groups, uint32_t g0, uint32_t p, uint32_t z0, uint32_t dk, int logn,
+                                     int* dst) {
+  using S = MacShape<T, TH>;
   const uint64_t N = uint64_t(1) << logn;
-  const uint64_t cstride = (uint64_t)dk * N;             // c -> c+1 inside one input
-  const uint64_t bstride = 2 * cstride;                  // b -> b+1
-  const uint64_t tstride = (uint64_t)inputs * bstride;   // t -> t+1
-  const uint64_t* ip = in + (uint64_t)p * N + z;
-  const uint64_t* wp = W + (g * inputs * dk + p) * N + z;
-  Acc128 acc[2 * T];
-  for (uint32_t b = 0; b < inputs; ++b) {
-    const uint64_t w = wp[(uint64_t)b * cstride];
+  if (seg < S::kInWords / 2) {
+    const int row = seg >> 4, sg = seg & 15;
+    const int c = row & 1, bb = (row >> 1) % S::kBc, t = (row >> 1) / S::kBc;
+    *dst = row * 32 + 2 * sg;
+    const uint32_t b = b0 + bb;
+    if (b >= inputs) return nullptr;
+    return in + (((uint64_t)t * inputs + b) * 2 + c) * dk * N + (uint64_t)p * N + z0 + 2 * sg;
+  }
+  const int sw = seg - S::kInWords / 2;
+  const int row = sw >> 4, sg = sw & 15;
+  const int bb = row % S::kBc, gl = row / S::kBc;
+  *dst = S::kInWords + row * 32 + 2 * sg;
+  const uint32_t b = b0 + bb, g = g0 + gl;
+  if (b >= inputs || g >= groups) return nullptr;
+  return w + (((uint64_t)g * inputs + b) * dk + p) * N + z0 + 2 * sg;
+}
+
+// One staged chunk for thread (warp, lane); chunk index k (every 32 chunks the 128-bit sums
+// are reduced so that any number of input blocks stays exact).
+template <int T, int TH>
+BFV_HD void mac_chunk(const uint64_t* buf, int warp, int lane, Mac30 (&acc)[TH][2], Acc128 (&A)[TH][2],
+                      const Modulus& m, uint32_t k) {
+  using S = MacShape<T, TH>;
+  const int h = warp % S::H, gl = warp / S::H;
+  const uint64_t* sw = buf + S::kInWords + gl * S::kBc * 32 + lane;
+  const uint64_t* si = buf + h * TH * S::kBc * 2 * 32 + lane;
 #pragma unroll
-    for (int t = 0; t < T; ++t) {
-      acc[2 * t].mac(ip[t * tstride + b * bstride], w);
-      acc[2 * t + 1].mac(ip[t * tstride + b * bstride + cstride], w);
-    }
-    if ((b & 127u) == 127u) {
+  for (int bb = 0; bb < S::kBc; ++bb) {
+    const uint64_t wv = sw[bb * 32];
+    const uint32_t w0 = (uint32_t)(wv & kMask30), w1 = (uint32_t)(wv >> 30);
 #pragma unroll
-      for (int i = 0; i < 2 * T; ++i) acc[i].fold(m);
-    }
+    for (int tt = 0; tt < TH; ++tt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) acc[tt][c].mac(si[((tt * S::kBc + bb) * 2 + c) * 32], w0, w1);
   }
 #pragma unroll
-  for (int t = 0; t < T; ++t)
+  for (int tt = 0; tt < TH; ++tt)
 #pragma unroll
-    for (int c = 0; c < 2; ++c)
-      acc_out[(((uint64_t)t * groups + g) * 2 + c) * cstride + (uint64_t)p * N + z] = acc[2 * t + c].reduce(m);
+    for (int c = 0; c < 2; ++c) {
+      acc[tt][c].fold(A[tt][c]);
+      if ((k & 31u) == 31u) A[tt][c].fold(m);
+    }
+}
+
+// Result of thread (warp, lane): acc_out [T][G][2][dk][n] (skipped for groups past G).
+template <int T, int TH>
+BFV_HD void mac_store(uint64_t* out, int warp, int lane, const Acc128 (&A)[TH][2], const Modulus& m,
+                      uint32_t groups, uint32_t g0, uint32_t p, uint32_t z0, uint32_t dk, int logn) {
+  using S = MacShape<T, TH>;
+  const int h = warp % S::H, gl = warp / S::H;
+  const uint32_t g = g0 + gl;
+  if (g >= groups) return;
+  const uint64_t N = uint64_t(1) << logn;
+#pragma unroll
+  for (int tt = 0; tt < TH; ++tt)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint64_t t = (uint64_t)h * TH + tt;
+      out[((t * groups + g) * 2 + c) * dk * N + (uint64_t)p * N + z0 + lane] = A[tt][c].reduce(m);
+    }
+}
+
+// Forward transform of client ciphertext limbs into the product's operand form (split30).
+template <int LOGN, class Ex>
+BFV_HD void op_ntt_split(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* data, uint32_t dk, const Modulus* mods,
+                         const ulonglong2* fwd) {
+  const uint32_t p = (uint32_t)(blk % dk);
+  const Modulus m = mods[p];
+  uint64_t* a = data + (blk << LOGN);
+  auto ld = [a](int i) { return a[i]; };
+  auto st = [a](int i, uint64_t v) { a[i] = split30(v); };
+  ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
 }
 
 // Enc(0) preparation for item e (a tile-group pair): block (e, key-level prime p) stores

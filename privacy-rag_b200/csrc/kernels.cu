@@ -124,19 +124,84 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
 }
 
 // ---- layer pipeline: multi-tile product, Enc(0) preparation, INTT with epilogue -------
-// Block = 256 coefficients of one (data prime, group); consecutive blocks walk the groups
-// of one coefficient chunk, so the chunk's inputs (all tiles and blocks) stay in L2 while
-// every weight word is streamed from HBM once.
-template <int T>
-__global__ void __launch_bounds__(256) k_mac_tiles(const uint64_t* in, const uint64_t* w, uint64_t* acc,
-                                                   uint32_t inputs, uint32_t groups, uint32_t dk, int logn,
-                                                   uint32_t zchunks, const Modulus* mods) {
-  const uint32_t g = blockIdx.x % groups;
-  const uint32_t r = blockIdx.x / groups;
-  const uint32_t p = r / zchunks, zc = r % zchunks;
-  const uint32_t z = zc * blockDim.x + threadIdx.x;
-  const Modulus m = mods[p];
-  mac_tiles_item<T>(g, p, z, in, w, acc, inputs, groups, dk, logn, m);
+__device__ __forceinline__ void cp_async16(uint64_t* dst, const uint64_t* src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  const int bytes = src ? 16 : 0;  // 0: zero-fill, nothing is read
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src ? src : dst), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Persistent product kernel: one 16-warp block per SM walks work units u = blockIdx.x +
+// i * gridDim.x, unit = (data prime, 32 coefficients, GB groups) with the group block
+// fastest, so the blocks running at one time share a coefficient chunk (its inputs stay in
+// L2) while every weight word is streamed from HBM once.  Staging runs kMacStages - 1
+// chunks ahead through cp.async, across unit boundaries.  Bodies in block_ops.cuh.
+constexpr int kMacStages = 4;
+
+template <int T, int TH>
+__global__ void __launch_bounds__(512, 1)
+    k_mac_split(const uint64_t* in, const uint64_t* w, uint64_t* out, uint32_t inputs, uint32_t groups,
+                uint32_t gblocks, uint32_t units, uint32_t dk, int logn, const Modulus* mods) {
+  using S = MacShape<T, TH>;
+  extern __shared__ uint64_t smem[];
+  const uint32_t zchunks = (1u << logn) >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t chunks = (inputs + S::kBc - 1) / S::kBc;
+  const uint32_t my_units = blockIdx.x < units ? (units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const uint64_t steps = (uint64_t)my_units * chunks;
+  // step s -> unit blockIdx.x + (s / chunks) * gridDim.x, chunk s % chunks
+  auto issue = [&](uint64_t s) {
+    if (s < steps) {
+      const uint32_t u = blockIdx.x + (uint32_t)(s / chunks) * gridDim.x, k = (uint32_t)(s % chunks);
+      const uint32_t gq = u % gblocks, r = u / gblocks;
+      const uint32_t p = r / zchunks, z0 = (r % zchunks) * 32;
+      uint64_t* buf = smem + (s % kMacStages) * S::kBufWords;
+      for (int seg = threadIdx.x; seg < S::kSegs; seg += S::kThreads) {
+        int dst;
+        const uint64_t* src =
+            mac_stage_src<T, TH>(seg, k * S::kBc, in, w, inputs, groups, gq * S::GB, p, z0, dk, logn, &dst);
+        cp_async16(buf + dst, src);
+      }
+    }
+    cp_async_commit();  // one group per step, empty past the end, so the wait count holds
+  };
+  Mac30 acc[TH][2];
+  Acc128 A[TH][2];
+  for (int s = 0; s < kMacStages - 1; ++s) issue(s);
+  for (uint64_t s = 0; s < steps; ++s) {
+    cp_async_wait<kMacStages - 2>();
+    __syncthreads();  // step s is in shared memory; every warp is done with step s - 1
+    issue(s + kMacStages - 1);
+    const uint32_t u = blockIdx.x + (uint32_t)(s / chunks) * gridDim.x, k = (uint32_t)(s % chunks);
+    const uint32_t r = u / gblocks, p = r / zchunks;
+    const Modulus& m = mods[p];
+    mac_chunk<T, TH>(smem + (s % kMacStages) * S::kBufWords, warp, lane, acc, A, m, k);
+    if (k + 1 == chunks) {
+      mac_store<T, TH>(out, warp, lane, A, m, groups, (u % gblocks) * S::GB, p, (r % zchunks) * 32, dk, logn);
+#pragma unroll
+      for (int tt = 0; tt < TH; ++tt)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) A[tt][c] = Acc128{};
+    }
+  }
+  cp_async_wait<0>();
+}
+
+template <int T, int TH>
+constexpr size_t mac_smem_bytes() {
+  return kMacStages * (size_t)MacShape<T, TH>::kBufWords * sizeof(uint64_t);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_ntt_split(uint64_t* data, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
+  extern __shared__ uint64_t smem[];
+  op_ntt_split<LOGN>(BlockExec{}, smem, blockIdx.x, data, dk, mods, fwd);
 }
 
 template <int LOGN>
@@ -313,6 +378,11 @@ static cudaError_t configure_for() {
   chk(allow_smem(k_ks_finish<L>, (size_t(1) << L) * 8));
   chk(allow_smem(k_client_phase<L>, s));
   chk(allow_smem(k_enc0_prep<L>, s));
+  chk(allow_smem(k_ntt_split<L>, s));
+  chk(allow_smem(k_mac_split<8, 4>, mac_smem_bytes<8, 4>()));
+  chk(allow_smem(k_mac_split<4, 4>, mac_smem_bytes<4, 4>()));
+  chk(allow_smem(k_mac_split<2, 2>, mac_smem_bytes<2, 2>()));
+  chk(allow_smem(k_mac_split<1, 1>, mac_smem_bytes<1, 1>()));
   chk(allow_smem(k_intt_protect<L>, s));
   if constexpr (L == 14) {
     chk(allow_smem(k_token_lift_ntt<L>, s));
@@ -528,13 +598,28 @@ cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint6
   return cudaGetLastError();
 }
 
+template <int T, int TH>
+static cudaError_t mac_split_launch(const DevParams& P, const uint64_t* in, uint64_t inputs, const uint64_t* w,
+                                    uint64_t groups, uint64_t* out, cudaStream_t st) {
+  using S = MacShape<T, TH>;
+  const size_t smem = mac_smem_bytes<T, TH>();
+  const uint64_t gblocks = (groups + S::GB - 1) / S::GB;
+  const uint64_t units = (uint64_t)P.dk * (P.n >> 5) * gblocks;
+  if (units > 0xffffffffull) return cudaErrorInvalidValue;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const unsigned grid = (unsigned)(units < (uint64_t)sms ? units : (uint64_t)sms);
+  k_mac_split<T, TH><<<grid, S::kThreads, smem, st>>>(in, w, out, (uint32_t)inputs, (uint32_t)groups,
+                                                      (uint32_t)gblocks, (uint32_t)units, P.dk, P.logn, P.mod);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t tiles, uint64_t inputs,
                              const uint64_t* w, uint64_t groups, uint64_t* acc, cudaStream_t st) {
   if (!tiles || !groups) return cudaSuccess;
-  const uint32_t threads = P.n < 256 ? P.n : 256;
-  const uint32_t zchunks = P.n / threads;
-  const uint64_t blocks = (uint64_t)P.dk * zchunks * groups;
-  if (blocks > 0x7fffffffull || inputs > 0xffffffffull || groups > 0xffffffffull) return cudaErrorInvalidValue;
+  if (P.n < 32 || inputs > 0xffffffffull || groups > 0xffffffffull) return cudaErrorInvalidValue;
   const uint64_t in_tile = inputs * 2 * P.dk * (uint64_t)P.n, acc_tile = groups * 2 * P.dk * (uint64_t)P.n;
   uint64_t t0 = 0;
   while (t0 < tiles) {
@@ -542,13 +627,13 @@ cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t ti
     const int T = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
     const uint64_t* ip = in + t0 * in_tile;
     uint64_t* ap = acc + t0 * acc_tile;
+    cudaError_t e;
     switch (T) {
-      case 8: k_mac_tiles<8><<<(unsigned)blocks, threads, 0, st>>>(ip, w, ap, (uint32_t)inputs, (uint32_t)groups, P.dk, P.logn, zchunks, P.mod); break;
-      case 4: k_mac_tiles<4><<<(unsigned)blocks, threads, 0, st>>>(ip, w, ap, (uint32_t)inputs, (uint32_t)groups, P.dk, P.logn, zchunks, P.mod); break;
-      case 2: k_mac_tiles<2><<<(unsigned)blocks, threads, 0, st>>>(ip, w, ap, (uint32_t)inputs, (uint32_t)groups, P.dk, P.logn, zchunks, P.mod); break;
-      default: k_mac_tiles<1><<<(unsigned)blocks, threads, 0, st>>>(ip, w, ap, (uint32_t)inputs, (uint32_t)groups, P.dk, P.logn, zchunks, P.mod); break;
+      case 8: e = mac_split_launch<8, 4>(P, ip, inputs, w, groups, ap, st); break;
+      case 4: e = mac_split_launch<4, 4>(P, ip, inputs, w, groups, ap, st); break;
+      case 2: e = mac_split_launch<2, 2>(P, ip, inputs, w, groups, ap, st); break;
+      default: e = mac_split_launch<1, 1>(P, ip, inputs, w, groups, ap, st); break;
     }
-    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     t0 += T;
   }
@@ -562,6 +647,15 @@ uint64_t mac_tiles_launches(uint64_t tiles) {
     ++c;
   }
   return c;
+}
+
+cudaError_t launch_ntt_split(const DevParams& P, uint64_t* data, uint64_t polys, cudaStream_t st) {
+  if (!polys) return cudaSuccess;
+  if (polys > 0x7fffffffull) return cudaErrorInvalidValue;
+  BFV_DISPATCH(P.logn, {
+    k_ntt_split<L_><<<(unsigned)polys, threads_for<L_>(), smem_bytes<L_>(), st>>>(data, P.dk, P.mod, P.fwd);
+  });
+  return cudaGetLastError();
 }
 
 cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const uint64_t* pk, uint64_t items,

@@ -7,6 +7,7 @@
 // per-prime records and the twiddle tables) come from the product library's host-only
 // context, so they are the same values the kernels receive.
 #include <cstdint>
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -48,6 +49,39 @@ uint32_t inv_mod_2n(uint32_t g, uint32_t two_n) {
     case 14: { constexpr int L_ = 14; __VA_ARGS__; } break; \
     default: return -1;                                    \
   }
+
+// One launch of the product kernel for T tiles: every block's staging (zero fill where the
+// source is null), chunk loop and store, run thread by thread.
+template <int T, int TH>
+static void emu_mac_launch(const uint64_t* in, const uint64_t* w, uint64_t* out, uint32_t inputs, uint32_t groups,
+                           uint32_t dk, int logn, const Modulus* mods) {
+  using S = MacShape<T, TH>;
+  const uint32_t gblocks = (groups + S::GB - 1) / S::GB, zchunks = (1u << logn) >> 5;
+  const uint32_t chunks = (inputs + S::kBc - 1) / S::kBc;
+  struct Thread {
+    Mac30 acc[TH][2];
+    Acc128 A[TH][2];
+  };
+  std::vector<uint64_t> buf(S::kBufWords);
+  std::vector<Thread> th(S::kThreads);
+  for (uint64_t blk = 0; blk < (uint64_t)dk * zchunks * gblocks; ++blk) {
+    const uint32_t gq = blk % gblocks, r = blk / gblocks;
+    const uint32_t p = r / zchunks, z0 = (r % zchunks) * 32, g0 = gq * S::GB;
+    std::fill(th.begin(), th.end(), Thread{});
+    for (uint32_t k = 0; k < chunks; ++k) {
+      for (int seg = 0; seg < S::kSegs; ++seg) {
+        int dst = -1;
+        const uint64_t* src = mac_stage_src<T, TH>(seg, k * S::kBc, in, w, inputs, groups, g0, p, z0, dk, logn, &dst);
+        if (dst < 0 || dst + 2 > S::kBufWords || (dst & 1)) throw 1;
+        buf[dst] = src ? src[0] : 0;
+        buf[dst + 1] = src ? src[1] : 0;
+      }
+      for (int i = 0; i < S::kThreads; ++i) mac_chunk<T, TH>(buf.data(), i >> 5, i & 31, th[i].acc, th[i].A, mods[p], k);
+    }
+    for (int i = 0; i < S::kThreads; ++i)
+      mac_store<T, TH>(out, i >> 5, i & 31, th[i].A, mods[p], groups, g0, p, z0, dk, logn);
+  }
+}
 
 extern "C" {
 
@@ -149,7 +183,7 @@ int emu_matrix(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const 
 
 // Layer pipeline over T tiles: cts [T][I][2][dk][n] coefficient form, ring [G][I][n],
 // masks [T][G][n] or null, samples [T][G][3][k][n] or null (pk [2][k][n]);
-// out [T][G][2][dk][n].  Tiles are taken in chunks of 8/4/2/1 as the launcher does, and
+// out [T][G][2][dk][n].  Tiles are taken in launches of 8/4/2/1 as the launcher does, and
 // out doubles as the product accumulator as on the device.
 int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd,
                      const uint64_t* inv, const uint64_t* cts, uint64_t tiles, uint64_t inputs, const uint64_t* ring,
@@ -164,25 +198,21 @@ int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, 
   EMU_DISPATCH(logn, {
     std::vector<uint64_t> s(SmemWords<L_>::value);
     for (uint64_t b = 0; b < tiles * inputs * 2 * dk; ++b)
-      op_ntt<L_>(HostExec{}, s.data(), b, false, in.data(), dk, 0, T.mods.data(), T.fwd, T.inv);
+      op_ntt_split<L_>(HostExec{}, s.data(), b, in.data(), dk, T.mods.data(), T.fwd);
     for (uint64_t b = 0; b < groups * inputs * dk; ++b)
       op_lift_ntt<L_>(HostExec{}, s.data(), b, ring, w.data(), dk, T.mods.data(), T.fwd);
     const uint64_t in_tile = inputs * 2 * dk * n, acc_tile = groups * 2 * dk * n;
     for (uint64_t t0 = 0; t0 < tiles;) {
       const uint64_t left = tiles - t0;
       const int TT = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
-      for (uint64_t g = 0; g < groups; ++g)
-        for (uint32_t p = 0; p < dk; ++p)
-          for (uint32_t z = 0; z < n; ++z) {
-            const uint64_t* ip = in.data() + t0 * in_tile;
-            uint64_t* ap = out + t0 * acc_tile;
-            switch (TT) {
-              case 8: mac_tiles_item<8>(g, p, z, ip, w.data(), ap, (uint32_t)inputs, groups, dk, L_, T.mods[p]); break;
-              case 4: mac_tiles_item<4>(g, p, z, ip, w.data(), ap, (uint32_t)inputs, groups, dk, L_, T.mods[p]); break;
-              case 2: mac_tiles_item<2>(g, p, z, ip, w.data(), ap, (uint32_t)inputs, groups, dk, L_, T.mods[p]); break;
-              default: mac_tiles_item<1>(g, p, z, ip, w.data(), ap, (uint32_t)inputs, groups, dk, L_, T.mods[p]); break;
-            }
-          }
+      const uint64_t* ip = in.data() + t0 * in_tile;
+      uint64_t* ap = out + t0 * acc_tile;
+      switch (TT) {
+        case 8: emu_mac_launch<8, 4>(ip, w.data(), ap, (uint32_t)inputs, (uint32_t)groups, dk, L_, T.mods.data()); break;
+        case 4: emu_mac_launch<4, 4>(ip, w.data(), ap, (uint32_t)inputs, (uint32_t)groups, dk, L_, T.mods.data()); break;
+        case 2: emu_mac_launch<2, 2>(ip, w.data(), ap, (uint32_t)inputs, (uint32_t)groups, dk, L_, T.mods.data()); break;
+        default: emu_mac_launch<1, 1>(ip, w.data(), ap, (uint32_t)inputs, (uint32_t)groups, dk, L_, T.mods.data()); break;
+      }
       t0 += TT;
     }
     if (samples)

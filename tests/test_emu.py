@@ -145,16 +145,18 @@ def test_matrix_mask_enc0_kernel_bodies(bfv, oracle, E, logn):
     assert np.array_equal(out2[0], oc.matrix_evaluate(cn, ring[0]))
 
 
-@pytest.mark.parametrize("tiles", [1, 3, 8])
-def test_matrix_tiles_kernel_bodies(bfv, oracle, E, tiles):
-    """Layer pipeline (multi-tile product, Enc(0) prep, INTT with folded Enc(0) and mask)
-    against the oracle's per-tile matrix evaluation + sub_plain + Enc(0) add."""
+@pytest.mark.parametrize("tiles,I,G", [(1, 3, 2), (3, 3, 2), (8, 3, 2), (2, 20, 19), (1, 264, 3)])
+def test_matrix_tiles_kernel_bodies(bfv, oracle, E, tiles, I, G):
+    """Layer pipeline (split-operand NTT, multi-tile product over 30-bit halves with its
+    shared-memory staging, Enc(0) prep, INTT with folded Enc(0) and mask) against the
+    oracle's per-tile matrix evaluation + sub_plain + Enc(0) add.  Cases cover partial and
+    several input chunks, more groups than one block holds, and more than 256 inputs (the
+    periodic reduction of the 128-bit sums)."""
     logn = 5
     hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
     k, dk, n = hc.k, hc.dk, 1 << logn
     tb = oracle.TestBfv(oc, seed=40 + tiles)
-    rng = np.random.default_rng(tiles)
-    I, G = 3, 2
+    rng = np.random.default_rng(tiles + I)
     cts = np.stack([np.stack([tb.encrypt(rng.integers(0, 1 << 59, size=n, dtype=np.uint64)) for _ in range(I)])
                     for _ in range(tiles)])
     ring = rng.integers(0, 1 << 59, size=(G, I, n), dtype=np.uint64)

@@ -360,7 +360,7 @@ def test_matrix_tiles_device(art, oracle, tiles):
     out = torch.empty((tiles, G, 2, dk, n), dtype=torch.int64, device="cuda")
     plain = torch.empty_like(out)
     torch.cuda.synchronize()
-    hc.ntt_device(d_in, tiles * I * 2 * dk, dk)
+    hc.matrix_tiles_inputs_device(d_in, tiles * I)
     hc.weights_ntt_device(d_ring, G * I, w)
     hc.matrix_tiles_device(d_in, tiles, I, w, G, out, masks=d_masks, samples=d_samples, pk=d_pk, scratch=scratch)
     hc.matrix_tiles_device(d_in, tiles, I, w, G, plain)

@@ -156,8 +156,7 @@ def test_layer_server_tiles_decrypt(bfv, oracle, setup):
         out = srv.output(p).cpu().numpy().view(np.uint64)
         tg, counts, mx = srv.targets[p.name]
         tg, counts = tg.cpu().numpy(), counts.cpu().numpy()
-        sel = srv.selected.cpu().numpy().view(np.uint64)
-        crt = srv.crt.cpu().numpy().view(np.uint64)
+        sel, crt = (a.cpu().numpy().view(np.uint64) for a in srv.gathered(p))
         w_u = w_int[p.name].astype(np.int64).astype(np.uint64) & np.uint64(MASK59)
         for t in range(tiles):
             for g in range(p.groups):
