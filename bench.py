@@ -229,6 +229,203 @@ def run_layer_legs(torch, bfvgpu, device, args):
     return out
 
 
+def run_model_leg(torch, bfvgpu, device, args, dist):
+    """Config 5: the linear protocol of all 28 Qwen3-0.6B-shaped layers for a 512-token
+    prefill (32 tiles of B = 16, run as 4 launches of 8 tiles per projection) and 64
+    single-token decode steps (B = 1), the output groups of every call sharded across the
+    ranks (bfvgpu.shard).  Per call: rank 0 broadcasts the client ciphertexts (NCCL), every
+    rank evaluates its groups, and c1 plus the targets' CRT limbs are gathered to rank 0
+    (NCCL, asynchronous, double-buffered).  Prefill weights are lifted and transformed once
+    per layer inside the timed region (one layer's NTT-form weights are 24 GB, so all 28 do
+    not stay resident on one GPU); the decode weights of all layers are transformed once per
+    pass and kept (1.5 GB per layer).  Int8 weights uniform in [-127, 127], seeded per layer;
+    client ciphertexts, masks and Enc(0) randomness synthetic and resident.  Time = device
+    events on the context stream, max over ranks."""
+    ctx = bfvgpu.Context.art002(device)
+    sp = ctx.stream()
+    stream = torch.cuda.ExternalStream(sp)
+    with torch.cuda.stream(stream):  # torch's allocations and copies ordered with the kernels
+        res = _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream)
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    ctx.close()
+    return res
+
+
+def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
+    from bfvgpu import layer as L
+    from bfvgpu import shard as S
+    rank = dist.get_rank() if dist else 0
+    world = dist.get_world_size() if dist else 1
+    n, k, dk = ctx.n, ctx.k, ctx.dk
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)  # same on every rank: rank 0's copy is what the broadcasts carry
+    q = torch.tensor(ctx.primes, dtype=torch.int64, device="cuda")
+    layers, tiles_total, tiles, decode_steps = args.model_layers, 32, 8, args.model_decode
+
+    def residues(shape, nprimes):
+        raw = torch.randint(0, 2 ** 62, shape, dtype=torch.int64, device="cuda", generator=g)
+        return torch.remainder(raw, q[:nprimes].view(*([1] * (len(shape) - 2)), nprimes, 1))
+
+    def small(shape, lo, hi):
+        v = torch.randint(lo, hi + 1, shape, dtype=torch.int64, device="cuda", generator=g)
+        return torch.remainder(v.unsqueeze(-2), q.view(k, 1))
+
+    pk = residues((2, k, n), k)
+    full_pre = [L.plan(nm, 16, kk, oo) for nm, kk, oo in L.QWEN3_06B_LAYER]
+    full_dec = [L.plan(nm, 1, kk, oo) for nm, kk, oo in L.QWEN3_06B_LAYER]
+    sh_pre = [S.shard_projection(p, rank, world)[0] for p in full_pre]
+    sh_dec = [S.shard_projection(p, rank, world)[0] for p in full_dec]
+    # int8 weights of every layer, this rank's rows only
+    w8 = [{p.name: S.weight_rows(torch.randint(-127, 128, (p.outputs, p.inner), dtype=torch.int8, device="cuda",
+                                               generator=g), p, rank, world).contiguous() for p in full_pre}
+          for _ in range(layers)]
+    pre = L.LayerServer(torch, ctx, pk, sh_pre, 16, tiles)
+    dec = L.LayerServer(torch, ctx, pk, sh_dec, 1, 1)
+
+    def call_buffers(projs, T, copies):
+        return ({p.name: [residues((T, p.inputs, 2, dk, n), dk) for _ in range(copies)] for p in projs},
+                {p.name: torch.randint(0, 2 ** 59, (T, max(p.groups, 1), n), dtype=torch.int64, device="cuda",
+                                       generator=g) for p in projs},
+                {p.name: torch.cat([small((T, max(p.groups, 1), 1, n), -1, 1),
+                                    small((T, max(p.groups, 1), 2, n), -5, 5)], dim=2) for p in projs})
+
+    multi = bool(dist) and world > 1
+    # inputs are double-buffered so the broadcast of call c+1 overlaps call c; broadcasts and
+    # result gathers use separate communicators so neither queues behind the other
+    cts_pre, masks_pre, samples_pre = call_buffers(sh_pre, tiles, 2 if multi else 1)
+    cts_dec, masks_dec, samples_dec = call_buffers(sh_dec, 1, 2 if multi else 1)
+    pg_in = dist.new_group(list(range(world))) if multi else None
+    pg_out = dist.new_group(list(range(world))) if multi else None
+    wcache = [dict() for _ in range(layers)]
+    stats = {"broadcast_bytes": 0, "gathered_bytes": 0, "calls": 0}
+
+    # the pass as a flat schedule: ("wpre", layer) / ("wdec", layer) weight preparation,
+    # ("call", phase, index, layer) one private_matrix call
+    def schedule(n_layers, n_steps):
+        ops = []
+        for l in range(n_layers):
+            ops.append(("wpre", l))
+            for _ in range(tiles_total // tiles):
+                ops.extend(("call", "pre", i, l) for i in range(4))
+        ops.append(("mark",))
+        for l in range(n_layers):
+            ops.append(("wdec", l))
+        ops.append(("mark",))
+        for _ in range(n_steps):
+            for l in range(n_layers):
+                ops.extend(("call", "dec", i, l) for i in range(4))
+        return ops
+
+    def operands(op, slot):
+        srv, sh, full, cts, masks, samples = ((pre, sh_pre, full_pre, cts_pre, masks_pre, samples_pre) if op[1] == "pre"
+                                              else (dec, sh_dec, full_dec, cts_dec, masks_dec, samples_dec))
+        p = sh[op[2]]
+        return srv, p, full[op[2]], cts[p.name][slot % len(cts[p.name])], masks[p.name], samples[p.name]
+
+    def run(ops, marks=None):
+        calls = [i for i, op in enumerate(ops) if op[0] == "call"]
+        nxt = {c: calls[j + 1] for j, c in enumerate(calls[:-1])}
+        bcast = {}
+        pending = [None, None]
+        slot = {c: j for j, c in enumerate(calls)}
+
+        def broadcast(ci):
+            buf = operands(ops[ci], slot[ci])[3]
+            bcast[ci] = dist.broadcast(buf, src=0, group=pg_in, async_op=True)
+            stats["broadcast_bytes"] += buf.numel() * 8
+
+        if multi and calls:
+            broadcast(calls[0])
+        for i, op in enumerate(ops):
+            if op[0] == "mark":
+                if marks is not None:
+                    marks.pop(0).record(stream)
+                continue
+            if op[0] == "wpre":
+                rings = {p.name: L.pack_weights_device(torch, w8[op[1]][p.name].long(), p, n) for p in sh_pre
+                         if p.groups}
+                pre.w_ntt = {}
+                if rings:
+                    pre.prepare_weights(rings, stream=sp)
+                continue
+            if op[0] == "wdec":
+                rings = {p.name: L.pack_weights_device(torch, w8[op[1]][p.name].long(), p, n) for p in sh_dec
+                         if p.groups}
+                dec.w_ntt = {}
+                if rings:
+                    dec.prepare_weights(rings, stream=sp)
+                wcache[op[1]] = dec.w_ntt
+                continue
+            srv, p_local, p_full, cts, masks, samples = operands(op, slot[i])
+            if op[1] == "dec":
+                dec.w_ntt = wcache[op[3]]
+            if multi:
+                if i in nxt:
+                    broadcast(nxt[i])      # starts once the call two back has released its buffer
+                bcast.pop(i).wait()        # this call's inputs are in place
+            if p_local.groups:
+                srv.run_projection(p_local, cts, masks, samples, stream=sp)
+            stats["calls"] += 1
+            if not multi:
+                continue
+            j = stats["calls"] % 2
+            if pending[j] is not None:
+                pending[j].wait()
+            T = srv.tiles
+            c1 = srv.output(p_local)[:, :, 1].contiguous()
+            crt = srv.gathered(p_local)[1].view(T, p_local.groups, -1, dk).contiguous()
+            w1, _ = S.gather_groups(torch, dist, c1, p_full.groups, world, async_op=True, group=pg_out)
+            w2, _ = S.gather_groups(torch, dist, crt, p_full.groups, world, async_op=True, group=pg_out)
+            pending[j] = _Both(w1, w2)
+            stats["gathered_bytes"] += (c1.numel() + crt.numel()) * 8
+        for w in pending:
+            if w is not None:
+                w.wait()
+
+    # warm-up: one layer of every kind of operation
+    run(schedule(1, 1))
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for key in stats:
+        stats[key] = 0
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev[0].record(stream)
+    run(schedule(layers, decode_steps), marks=[ev[1], ev[2]])
+    ev[3].record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([ev[0].elapsed_time(ev[3]), ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]),
+                      ev[2].elapsed_time(ev[3])], dtype=torch.float64, device="cuda")
+    if dist and world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total, pre_ms, dw_ms, dec_ms = (float(x) for x in t.tolist())
+    tokens = tiles_total * 16 + decode_steps
+    res = {"ms": total, "unit": "ms per pass (28 layers: 512-token prefill + 64 decode steps)",
+           "tokens_per_s": tokens / (total / 1e3), "n_gpus": world, "layers": layers,
+           "prefill_ms": pre_ms, "decode_weights_ms": dw_ms, "decode_ms": dec_ms,
+           "decode_ms_per_step": dec_ms / max(1, decode_steps),
+           "sharding": "output groups of every call, contiguous ranges per rank; NCCL broadcast of inputs "
+                       "(prefetched one call ahead) and gather of c1 + target CRT limbs to rank 0 (asynchronous)",
+           "calls_per_rank": stats["calls"], "broadcast_bytes_per_rank": stats["broadcast_bytes"],
+           "gathered_bytes_per_rank": stats["gathered_bytes"],
+           "prefill_mac_modmuls": layers * tiles_total * sum(p.groups * p.inputs * 2 * dk * n for p in full_pre),
+           "note": "ART-002 (n=16384, 6+1 x 60-bit, t=2^59); weights synthetic int8; inputs resident"}
+    return res
+
+
+class _Both:
+    """Two outstanding collectives waited together."""
+
+    def __init__(self, a, b):
+        self.a, self.b = a, b
+
+    def wait(self):
+        self.a.wait()
+        self.b.wait()
+
+
 # ----------------------------------------------------------------------------------------------
 def run_reference(args):
     rank, world, _ = env_rank()
@@ -282,6 +479,10 @@ def main():
     ap.add_argument("--layer", type=int, default=1, help="0 skips the config-3/4 legs")
     ap.add_argument("--layer-tiles", type=int, default=8, help="16-token tiles in the config-4 leg")
     ap.add_argument("--layer-only", action="store_true", help="run only the config-3/4 legs (profiling)")
+    ap.add_argument("--model", type=int, default=1, help="0 skips the config-5 leg (28 layers, sharded)")
+    ap.add_argument("--model-only", action="store_true", help="run only the config-5 leg")
+    ap.add_argument("--model-layers", type=int, default=28)
+    ap.add_argument("--model-decode", type=int, default=64, help="decode steps in the config-5 leg")
     ap.add_argument("--layer-shape", default=None,
                     help="K,O: with --layer-only, one B=16 projection of this shape instead of config 3/4 "
                          "(small profiling case)")
@@ -305,6 +506,13 @@ def main():
 
     if args.layer_only:
         print(json.dumps({"layer_legs": run_layer_legs(torch, bfvgpu, local, args)}), flush=True)
+        return 0
+    if args.model_only:
+        res = run_model_leg(torch, bfvgpu, local, args, dist)
+        if rank == 0:
+            print(json.dumps({"model_config5": res}), flush=True)
+        if dist:
+            dist.destroy_process_group()
         return 0
 
     primes2 = bfvgpu.find_primes(N2, BITS2)
@@ -405,6 +613,7 @@ def main():
 
     # ---- secondary: ct-pt matvec (config 3) and one decoder layer (config 4), ART-002 ----
     layer_res = run_layer_legs(torch, bfvgpu, local, args) if args.layer else None
+    model_res = run_model_leg(torch, bfvgpu, local, args, dist) if args.model else None
 
     # ---- secondary: NTT round trips (config 1) ----
     primes1 = bfvgpu.find_primes(N1, BITS1)
@@ -506,6 +715,7 @@ def main():
                                               "matches_hoisted": plain_match},
                       "matvec_config3": layer_res and layer_res["config3"],
                       "layer_config4": layer_res and layer_res["config4"],
+                      "model_config5": model_res,
                       "ntt": {"value": ntts_per_s, "unit": "NTTs/s",
                               "config": "config1: n=4096, primes 36/36/37-bit, 384 limb-polys fwd+inv",
                               "avg_launch_ms": ntt_launch_s * 1e3,

@@ -77,10 +77,12 @@ class LayerServer:
 
     def __init__(self, torch, ctx: Context, pk_device, projections=QWEN3_06B_LAYER, batch: int = 16,
                  tiles: int = 1):
+        """projections: (name, K, O) triples planned here with matrix_packing(batch, K, O), or
+        Projection records (a shard of a larger call keeps the call's packing)."""
         self.torch = torch
         self.ctx = ctx
         self.pk = pk_device
-        self.proj = [plan(nm, batch, k, o) for nm, k, o in projections]
+        self.proj = [p if isinstance(p, Projection) else plan(p[0], batch, p[1], p[2]) for p in projections]
         self.batch = batch
         self.tiles = tiles
         t, n, dk = torch, ctx.n, ctx.dk
