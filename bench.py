@@ -147,6 +147,65 @@ def cpu_ntt_sample(seconds: float = 4.0):
     return done / dt, cores
 
 
+def cpu_layer_sample(seconds: float = 15.0):
+    """The reference's CPU server loop for one output group (bfv_matrix.inc:169-233: lift and
+    NTT of the group's weight blocks, product with the transformed inputs, INTT, sub_plain of
+    the mask, Enc(0) add), restated by the oracle, run on all host threads (one group per
+    thread, concurrently) for groups of 64, 48 and 16 input blocks -- the shapes of configs
+    3/4 -- plus the input transforms (Matrix construction).  Returns the rates from which the
+    per-call CPU times are extrapolated: {inputs: groups/s}, NTT-of-inputs ciphertexts/s."""
+    from concurrent.futures import ThreadPoolExecutor
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    oc = O.art002()
+    cores = cpu_count()
+    n, dk, k = oc.n, oc.data_k, oc.k
+    rng = np.random.default_rng(6)
+    rates, done_all = {}, []
+    budget = seconds / 4
+    pk = oc.uniform(301, 2 * k, prime_count=k).reshape(2, k, n)
+    samples = np.stack([oc.uniform(302, k), oc.uniform(303, k), oc.uniform(304, k)]).reshape(3, k, n)
+    with ThreadPoolExecutor(cores) as ex:
+        for inputs in (64, 48, 16):
+            cts = oc.uniform(305, inputs * 2 * dk).reshape(inputs, 2, dk, n)
+            cn = oc.matrix_open(cts, threads=cores)
+            rings = [rng.integers(-127, 128, size=(inputs, n)).astype(np.int64).astype(np.uint64)
+                     & np.uint64((1 << 59) - 1) for _ in range(cores)]
+            mask = rng.integers(0, 1 << 59, size=n, dtype=np.uint64)
+
+            def group(i):
+                e = oc.matrix_evaluate(cn, rings[i], threads=1)
+                e[0] = oc.sub_plain(e[0], mask)
+                return oc.add(e, oc.enc0(samples, pk))
+
+            done, t0 = 0, time.perf_counter()
+            while time.perf_counter() - t0 < budget:
+                list(ex.map(group, range(cores)))
+                done += cores
+            rates[inputs] = done / (time.perf_counter() - t0)
+            done_all.append(f"{done} groups of {inputs} blocks")
+        cts = oc.uniform(306, cores * 2 * dk).reshape(cores, 2, dk, n)
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget:
+            oc.matrix_open(cts, threads=cores)
+            done += cores
+        open_rate = done / (time.perf_counter() - t0)
+    sample = (f"ART-002 oracle on {cores} threads: " + ", ".join(done_all) + f", {done} input ciphertext "
+              "transforms; per-call times extrapolated from these rates (the reference transforms every "
+              "group's weights in every call)")
+    return rates, open_rate, cores, sample
+
+
+def cpu_call_ms(rates, open_rate, projections, tiles):
+    """Extrapolated CPU time (ms) of `tiles` tiles of the given Projection calls."""
+    total = 0.0
+    for p in projections:
+        rate = rates.get(p.inputs) or min(rates.values()) * 64 / p.inputs
+        total += tiles * (p.groups / rate + p.inputs / open_rate)
+    return 1e3 * total
+
+
 # ----------------------------------------------------------------------------------------------
 def run_layer_legs(torch, bfvgpu, device, args):
     """Config 3: q_proj 2048x1024 for one token (B = 1); config 4: the four linear calls of
@@ -689,6 +748,24 @@ def main():
         nv, _ = cpu_ntt_sample()
         cpu = {"value": v, "unit": "keyswitches/s", "cores": cores, "kind": "port", "sample": sample,
                "ntt_value": nv, "ntt_unit": "NTTs/s"}
+        if layer_res or model_res:
+            from bfvgpu import layer as L
+            rates, open_rate, lcores, lsample = cpu_layer_sample()
+            pre = [L.plan(nm, 16, kk, oo) for nm, kk, oo in L.QWEN3_06B_LAYER]
+            dec = [L.plan(nm, 1, kk, oo) for nm, kk, oo in L.QWEN3_06B_LAYER]
+
+            def base(ms, unit):
+                return {"value": ms, "unit": unit, "cores": lcores, "kind": "port", "sample": lsample}
+
+            if layer_res:
+                layer_res["config3"]["cpu_baseline"] = base(
+                    cpu_call_ms(rates, open_rate, [L.plan("q_proj", 1, 1024, 2048)], 1), "ms per matvec")
+                layer_res["config4"]["cpu_baseline"] = base(
+                    cpu_call_ms(rates, open_rate, pre, args.layer_tiles), "ms per layer (all tiles)")
+            if model_res:
+                ms5 = model_res["layers"] * (cpu_call_ms(rates, open_rate, pre, 32)
+                                             + args.model_decode * cpu_call_ms(rates, open_rate, dec, 1))
+                model_res["cpu_baseline"] = base(ms5, "ms per pass (extrapolated from the sampled rates)")
 
     line = {
         "metric": "keyswitches/s (n=8192, 4x50-bit + 60-bit special prime, dnum=4, Galois rotation)",
