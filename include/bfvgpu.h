@@ -164,6 +164,16 @@ int32_t bfvgpu_matrix_groups_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_
                                     const uint64_t *w, uint64_t groups, const uint64_t *mask,
                                     const uint64_t *enc0_x, uint64_t *out, void *stream);
 
+/* Synchronises the context's device and returns (then clears) the error bits its kernels
+ * recorded: bit 0 = a tensor-core product step whose completion wait expired (the block
+ * freed its tensor memory and stopped; the output of that launch is incomplete).  Returns
+ * BFVGPU_E_CUDA when any bit was set.  No counterpart in the reference (its kernels have
+ * no waits). */
+int32_t bfvgpu_ctx_check(bfvgpu_ctx *ctx, uint32_t *flags);
+/* Selects the ct-pt product of bfvgpu_matrix_tiles_device: 0 (default) = tcgen05 kind::i8
+ * for launches of 8 tiles with at most 64 input blocks, CUDA cores otherwise; 1 = CUDA
+ * cores always.  Results are identical. */
+int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx *ctx, int32_t path);
 /* Words of device scratch bfvgpu_matrix_tiles_device needs: 0 without Enc(0), else
  * tiles * groups * (k + 2) * n. */
 uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx *ctx, uint64_t tiles, uint64_t groups,

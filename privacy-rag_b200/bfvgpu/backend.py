@@ -168,6 +168,16 @@ class Context:
                                                 groups, self._dptr(mask) or None, self._dptr(enc0_x) or None,
                                                 self._dptr(out), stream), "matrix_groups_device")
 
+    def check(self) -> int:
+        """Synchronise and return the kernel-recorded error bits (raises if any is set)."""
+        flags = U32(0)
+        check(lib().bfvgpu_ctx_check(self._h, ctypes.byref(flags)), "ctx_check")
+        return int(flags.value)
+
+    def set_product_path(self, path: int) -> None:
+        """0: tcgen05 product for 8-tile launches (default); 1: CUDA cores only."""
+        check(lib().bfvgpu_ctx_set_product_path(self._h, path), "set_product_path")
+
     def matrix_tiles_inputs_device(self, cts, count: int, stream: int | None = None):
         """Transform client ciphertexts [count][2][dk][n] in place into the operand form of
         matrix_tiles_device (NTT slots with their 30-bit halves split)."""

@@ -164,6 +164,8 @@ struct Context {
   }
 };
 
+constexpr size_t kErrBytes = 256;
+
 static void build_context(Context& c, uint32_t n, const uint64_t* primes, uint32_t dk, uint32_t special, uint64_t t,
                           int device) {
   if (!primes || n == 0 || (n & (n - 1))) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_DEGREE");
@@ -300,7 +302,7 @@ static void build_context(Context& c, uint32_t n, const uint64_t* primes, uint32
                q_bytes = dk * 8;
   auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
   const size_t total = up(mod_bytes) + 2 * up(tab_bytes) + up(qjp_bytes) + up(part_bytes) + up(cinv_bytes) +
-                       up(q_bytes);
+                       up(q_bytes) + up(kErrBytes);
   cuda_check(cudaMalloc(&c.dmem, total), "cudaMalloc(tables)");
   char* base = (char*)c.dmem;
   size_t off = 0;
@@ -317,6 +319,8 @@ static void build_context(Context& c, uint32_t n, const uint64_t* primes, uint32
   c.P.crt_part = (const uint64_t*)place(part.data(), part_bytes);
   c.P.crt_inv = (const uint64_t*)place(cinv.data(), cinv_bytes);
   c.P.crt_q = (const uint64_t*)place(Q.data(), q_bytes);
+  static const uint32_t zeros[kErrBytes / 4] = {};
+  c.P.err = (uint32_t*)place(zeros, kErrBytes);
   cuda_check(cudaStreamSynchronize(c.stream), "upload tables");
 }
 
@@ -705,6 +709,26 @@ int32_t bfvgpu_matrix_groups_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_
     Protect prot{mask, enc0_x};
     cuda_check(launch_mac_intt(ctx->c.P, in, w, out, inputs, groups, prot, pick(ctx, stream)), "mac_intt");
     count_launch();
+  });
+}
+
+int32_t bfvgpu_ctx_check(bfvgpu_ctx* ctx, uint32_t* flags) {
+  return guard([&] {
+    if (!ctx || !flags) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    *flags = 0;
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    cuda_check(cudaDeviceSynchronize(), "ctx_check");
+    cuda_check(cudaMemcpy(flags, ctx->c.P.err, 4, cudaMemcpyDeviceToHost), "ctx_check");
+    cuda_check(cudaMemset(ctx->c.P.err, 0, 4), "ctx_check");
+    if (*flags) fail(BFVGPU_E_CUDA, "E_BFVGPU_KERNEL_TIMEOUT");
+  });
+}
+
+int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx* ctx, int32_t path) {
+  return guard([&] {
+    if (!ctx || path < 0 || path > 1) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    ctx->c.P.product_path = path;
   });
 }
 

@@ -19,10 +19,13 @@
 //   k_client_phase .... client_phase (ntt.cu:96-98, :181-199)
 //   k_token_* ......... TokenWeights::evaluate_device (resident.cu:71-107, :200-221)
 //   k_packing_prepare . packing_prepare (switch.cu:78-87)
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include "kernels.cuh"
 #include "block_ops.cuh"
+#include "mac_tc.cuh"
 
 namespace bfvgpu {
 
@@ -190,6 +193,213 @@ __global__ void __launch_bounds__(512, 1)
     }
   }
   cp_async_wait<0>();
+}
+
+// ---- the same contraction on tcgen05 (8 tiles, at most 64 input blocks) ------------------
+// Persistent: one 16-warp block per SM walks units (data prime, 16 slots, 32 groups), group
+// chunk fastest.  Thread 0 is the producer and MMA issuer: per slot pair it loads the two
+// A boxes (inputs, 4 tiles each) by TMA into one of two A buffers, per round (16 groups)
+// the two B boxes (weights) into one of two B buffers, issues 2 M-blocks x K/32 MMAs into
+// TMEM columns [256 mb, 256 mb + 256) and commits to an mbarrier.  All 16 warps then drain
+// TMEM (warp w: lanes 32 (w%4).., M-block and 8 groups from w/4), recombine the byte-limb
+// sums of their slot, reduce mod q into the unit's output buffer, which is written out as
+// 128-byte rows when the unit ends.  Every mbarrier wait is bounded: on expiry the block
+// records kErrMmaTimeout in *err, frees TMEM and returns.  Layouts and descriptors:
+// mac_tc.cuh.
+constexpr uint32_t kErrMmaTimeout = 1;
+constexpr uint32_t kMbarPolls = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done = 0;
+  for (uint32_t it = 0; it < kMbarPolls && !done; ++it)
+    asm volatile(
+        "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P1;\n\t}"
+        : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %0;" ::"r"(bytes), "r"(bar) : "memory");
+}
+
+template <int KPAD>
+__global__ void __launch_bounds__(512, 1)
+    k_mac_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, uint64_t* out,
+             uint32_t groups, uint32_t gchunks, uint32_t units, uint32_t dk, int logn, const Modulus* mods,
+             uint32_t* err) {
+  using S = tc::Smem<KPAD>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023) & ~1023u;
+  uint8_t* sm = smem_raw + (base - raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t N = 1u << logn, zblocks = N / tc::kSlots;
+  const uint32_t barA = base + S::kBar, barB = barA + 16, barM = barA + 32;  // [2], [2], [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kBar + 40);
+  const uint64_t pA = reinterpret_cast<uint64_t>(&tmA), pB = reinterpret_cast<uint64_t>(&tmB);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(base + S::kBar + 40));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    for (uint32_t b = 0; b < 5; ++b) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(barA + 8 * b) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  const uint32_t my_units = blockIdx.x < units ? (units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const uint32_t rounds = my_units * tc::kRoundsPerUnit;
+  // round R -> unit, slot pair (global pair index R / kRoundsPerPair), group round
+  auto coords = [&](uint32_t R, uint32_t* gc, uint32_t* p, uint32_t* z0, uint32_t* zp, uint32_t* gr) {
+    const uint32_t u = blockIdx.x + (R / tc::kRoundsPerUnit) * gridDim.x;
+    tc::unit_coords(u, gchunks, zblocks, gc, p, z0);
+    const uint32_t rr = R % tc::kRoundsPerUnit;
+    *zp = rr / tc::kRoundsPerPair;
+    *gr = rr % tc::kRoundsPerPair;
+  };
+  auto load_a = [&](uint32_t P) {  // slot pair P (global index) -> A buffer P % 2
+    uint32_t gc, p, z0, zp, gr;
+    coords(P * tc::kRoundsPerPair, &gc, &p, &z0, &zp, &gr);
+    const uint32_t bar = barA + 8 * (P & 1), z = z0 + zp * tc::kPair;
+    mbar_expect(bar, 2 * S::kABox);
+#pragma unroll
+    for (uint32_t mb = 0; mb < 2; ++mb)
+      asm volatile(
+          "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+          ::"r"(base + S::kA + (P & 1) * S::kABuf + mb * S::kABox), "l"(pA), "r"((int)z), "r"(0), "r"(0),
+          "r"((int)(4 * mb)), "r"((int)p), "r"(bar) : "memory");
+  };
+  auto load_b = [&](uint32_t R) {  // round R -> B buffer R % 2
+    uint32_t gc, p, z0, zp, gr;
+    coords(R, &gc, &p, &z0, &zp, &gr);
+    const uint32_t bar = barB + 8 * (R & 1), z = z0 + zp * tc::kPair;
+    mbar_expect(bar, S::kBBox);
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        ::"r"(base + S::kB + (R & 1) * S::kBBox), "l"(pB), "r"((int)z), "r"(0),
+        "r"((int)(gc * tc::kGroups + gr * tc::kGroupsRound)), "r"((int)p), "r"(bar) : "memory");
+  };
+  auto issue_mma = [&](uint32_t R) {
+    const uint32_t P = R / tc::kRoundsPerPair;
+#pragma unroll
+    for (uint32_t mb = 0; mb < 2; ++mb)
+#pragma unroll
+      for (uint32_t kk = 0; kk < KPAD / 32; ++kk) {
+        const uint64_t ad = tc::a_desc<KPAD>(base, P & 1, mb, kk), bd = tc::b_desc<KPAD>(base, R & 1, kk);
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem + 256 * mb),
+            "l"(ad), "l"(bd), "r"(tc::kIdesc), "r"(kk) : "memory");
+      }
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(barM)
+                 : "memory");
+  };
+
+  // producer state (thread 0 only): next pair / round whose loads are to be issued
+  bool failed = false;
+  if (tid == 0 && rounds) {
+    load_a(0);
+    load_b(0);
+    if (rounds > 1) load_b(1);
+  }
+  const uint32_t quarter = warp & 3, mb = warp >> 3, gh = (warp >> 2) & 1;
+  const uint32_t m = quarter * 32 + lane, tc4 = m >> 4, zs = (m >> 3) & 1, i = m & 7;
+  const uint32_t tcx = mb * 8 + tc4;
+  for (uint32_t R = 0; R < rounds; ++R) {
+    const uint32_t P = R / tc::kRoundsPerPair;
+    const bool first_of_pair = (R % tc::kRoundsPerPair) == 0;
+    if (tid == 0) {
+      bool ok = true;
+      if (first_of_pair) {
+        ok = mbar_wait(barA + 8 * (P & 1), (P >> 1) & 1);
+        // the other A buffer was last read by pair P - 1, whose MMAs have completed
+        if (ok && (P + 1) * tc::kRoundsPerPair < rounds) load_a(P + 1);
+      }
+      ok = ok && mbar_wait(barB + 8 * (R & 1), (R >> 1) & 1);
+      if (ok) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        issue_mma(R);
+      } else {
+        failed = true;
+      }
+    }
+    const bool ok = tid == 0 ? !failed : true;
+    if (__syncthreads_or(!ok)) {
+      failed = true;
+      break;
+    }
+    const bool done = mbar_wait(barM, R & 1);
+    if (__syncthreads_or(!done)) {
+      failed = true;
+      break;
+    }
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (tid == 0 && R + 2 < rounds) load_b(R + 2);  // B buffer R % 2 is free again
+    uint32_t gc, p, z0, zp, gr;
+    coords(R, &gc, &p, &z0, &zp, &gr);
+    const Modulus& mod = mods[p];
+    uint64_t vlo[8], vhi[8];
+#pragma unroll
+    for (uint32_t h = 0; h < 4; ++h) {
+      uint32_t D[32];
+      const uint32_t taddr = tmem + ((quarter * 32) << 16) + 256 * mb + 128 * gh + 32 * h;
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+          : "=r"(D[0]), "=r"(D[1]), "=r"(D[2]), "=r"(D[3]), "=r"(D[4]), "=r"(D[5]), "=r"(D[6]), "=r"(D[7]),
+            "=r"(D[8]), "=r"(D[9]), "=r"(D[10]), "=r"(D[11]), "=r"(D[12]), "=r"(D[13]), "=r"(D[14]),
+            "=r"(D[15]), "=r"(D[16]), "=r"(D[17]), "=r"(D[18]), "=r"(D[19]), "=r"(D[20]), "=r"(D[21]),
+            "=r"(D[22]), "=r"(D[23]), "=r"(D[24]), "=r"(D[25]), "=r"(D[26]), "=r"(D[27]), "=r"(D[28]),
+            "=r"(D[29]), "=r"(D[30]), "=r"(D[31])
+          : "r"(taddr));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      tc::lane_values2(D, zs, i, vlo + 2 * h, vhi + 2 * h);
+    }
+    // reduce-scatter over the 8 lanes of one (tc, zs): lane i ends with group k = i
+#pragma unroll
+    for (int lev = 4; lev >= 1; lev >>= 1) {
+      const bool sel = i & lev;
+#pragma unroll
+      for (int q = 0; q < lev; ++q) {
+        const uint64_t kl = sel ? vlo[q + lev] : vlo[q], kh = sel ? vhi[q + lev] : vhi[q];
+        const uint64_t sl = sel ? vlo[q] : vlo[q + lev], sh = sel ? vhi[q] : vhi[q + lev];
+        vlo[q] = kl;
+        vhi[q] = kh;
+        tc::add128(vlo[q], vhi[q], __shfl_xor_sync(0xffffffffu, sl, lev), __shfl_xor_sync(0xffffffffu, sh, lev));
+      }
+    }
+    uint64_t* ob = reinterpret_cast<uint64_t*>(sm + S::kOut);
+    ob[tc::out_buf_word(zp * tc::kPair + zs, tcx, gr * tc::kGroupsRound + gh * 8 + i)] = reduce128(vlo[0], vhi[0], mod);
+    if (R % tc::kRoundsPerUnit == tc::kRoundsPerUnit - 1) {
+      __syncthreads();
+      const uint32_t rtc = tid >> 5, rgl = tid & 31, g = gc * tc::kGroups + rgl;
+      if (g < groups) {
+        uint64_t* dst = out + tc::out_row(rtc, g, groups, p, z0, dk, N);
+#pragma unroll
+        for (int zz = 0; zz < tc::kSlots; zz += 2) {
+          ulonglong2 v;
+          v.x = ob[tc::out_buf_word(zz, rtc, rgl)];
+          v.y = ob[tc::out_buf_word(zz + 1, rtc, rgl)];
+          *reinterpret_cast<ulonglong2*>(dst + zz) = v;
+        }
+      }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();  // TMEM and the output buffer are free for the next round
+  }
+  if (failed && tid == 0) atomicOr(err, kErrMmaTimeout);
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
 }
 
 template <int T, int TH>
@@ -383,6 +593,8 @@ static cudaError_t configure_for() {
   chk(allow_smem(k_mac_split<4, 4>, mac_smem_bytes<4, 4>()));
   chk(allow_smem(k_mac_split<2, 2>, mac_smem_bytes<2, 2>()));
   chk(allow_smem(k_mac_split<1, 1>, mac_smem_bytes<1, 1>()));
+  chk(allow_smem(k_mac_tc<32>, tc::Smem<32>::kLaunchBytes));
+  chk(allow_smem(k_mac_tc<64>, tc::Smem<64>::kLaunchBytes));
   chk(allow_smem(k_intt_protect<L>, s));
   if constexpr (L == 14) {
     chk(allow_smem(k_token_lift_ntt<L>, s));
@@ -616,6 +828,71 @@ static cudaError_t mac_split_launch(const DevParams& P, const uint64_t* in, uint
   return cudaGetLastError();
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Tensor maps of one launch: inputs [8 tiles][I][2][dk][n] viewed as (z, b, c, t, p) with box
+// (2, KPAD, 2, 4, 1); weights [G][I][dk][n] viewed as (z, b, g, p) with box (2, KPAD, 16, 1);
+// both u64, no swizzle (dense box images), zero fill past the extents.
+template <int KPAD>
+static cudaError_t encode_mac_maps(const DevParams& P, const uint64_t* in, uint64_t inputs, const uint64_t* w,
+                                   uint64_t groups, CUtensorMap* a, CUtensorMap* b) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t n = P.n, dk = P.dk, I = inputs, G = groups;
+  const cuuint64_t dimA[5] = {n, I, 2, (cuuint64_t)tc::kTiles, dk};
+  const cuuint64_t strA[4] = {2 * dk * n * 8, dk * n * 8, I * 2 * dk * n * 8, n * 8};
+  const cuuint32_t boxA[5] = {2, (cuuint32_t)KPAD, 2, 4, 1};
+  const cuuint64_t dimB[4] = {n, I, G, dk};
+  const cuuint64_t strB[3] = {dk * n * 8, I * dk * n * 8, n * 8};
+  const cuuint32_t boxB[4] = {2, (cuuint32_t)KPAD, (cuuint32_t)tc::kGroupsRound, 1};
+  const cuuint32_t ones[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(a, CU_TENSOR_MAP_DATA_TYPE_UINT64, 5, const_cast<uint64_t*>(in), dimA, strA, boxA, ones,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  r = enc(b, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, const_cast<uint64_t*>(w), dimB, strB, boxB, ones,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int KPAD>
+static cudaError_t mac_tc_launch(const DevParams& P, const uint64_t* in, uint64_t inputs, const uint64_t* w,
+                                 uint64_t groups, uint64_t* out, cudaStream_t st) {
+  const uint64_t gchunks = (groups + tc::kGroups - 1) / tc::kGroups;
+  const uint64_t units = (uint64_t)P.dk * (P.n / tc::kSlots) * gchunks;
+  if (units > 0xffffffffull / tc::kRoundsPerUnit) return cudaErrorInvalidValue;
+  CUtensorMap a, b;
+  cudaError_t e = encode_mac_maps<KPAD>(P, in, inputs, w, groups, &a, &b);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const unsigned grid = (unsigned)(units < (uint64_t)sms ? units : (uint64_t)sms);
+  k_mac_tc<KPAD><<<grid, tc::kThreads, tc::Smem<KPAD>::kLaunchBytes, st>>>(
+      a, b, out, (uint32_t)groups, (uint32_t)gchunks, (uint32_t)units, P.dk, P.logn, P.mod, P.err);
+  return cudaGetLastError();
+}
+
+bool mac_tc_applies(const DevParams& P, uint64_t tiles_in_launch, uint64_t inputs) {
+  return P.product_path == 0 && tiles_in_launch == tc::kTiles && inputs >= 1 && inputs <= tc::kMaxK &&
+         P.n >= (uint32_t)tc::kSlots && P.err != nullptr;
+}
+
 cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t tiles, uint64_t inputs,
                              const uint64_t* w, uint64_t groups, uint64_t* acc, cudaStream_t st) {
   if (!tiles || !groups) return cudaSuccess;
@@ -628,6 +905,13 @@ cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t ti
     const uint64_t* ip = in + t0 * in_tile;
     uint64_t* ap = acc + t0 * acc_tile;
     cudaError_t e;
+    if (mac_tc_applies(P, T, inputs)) {
+      e = inputs <= 32 ? mac_tc_launch<32>(P, ip, inputs, w, groups, ap, st)
+                       : mac_tc_launch<64>(P, ip, inputs, w, groups, ap, st);
+      if (e != cudaSuccess) return e;
+      t0 += T;
+      continue;
+    }
     switch (T) {
       case 8: e = mac_split_launch<8, 4>(P, ip, inputs, w, groups, ap, st); break;
       case 4: e = mac_split_launch<4, 4>(P, ip, inputs, w, groups, ap, st); break;

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "block_ops.cuh"
+#include "mac_tc.cuh"
 
 using namespace bfvgpu;
 
@@ -80,6 +81,111 @@ static void emu_mac_launch(const uint64_t* in, const uint64_t* w, uint64_t* out,
     }
     for (int i = 0; i < S::kThreads; ++i)
       mac_store<T, TH>(out, i >> 5, i & 31, th[i].A, mods[p], groups, g0, p, z0, dk, logn);
+  }
+}
+
+// One launch of the tensor-core product (8 tiles), unit by unit as the persistent kernel
+// walks them: per slot pair the A boxes and per round the B box are built as the TMA writes
+// them (dense box images, zero fill past the extents), the int8 MMA is evaluated from those
+// images at the canonical MN-major layout without swizzle (operand byte (mn, k) at
+// (mn/16)*K*16 + k*16 + mn%16), then every warp's TMEM drain (lane = TMEM lane of its
+// quarter, 32-column loads), the byte-limb recombination of its slot and the shuffle
+// reduce-scatter are replayed lane by lane, followed by the mod-q reduction, the output
+// buffer and its flush.
+template <int KPAD>
+static void emu_mac_tc_launch(const uint64_t* in, const uint64_t* w, uint64_t* out, uint32_t inputs,
+                              uint32_t groups, uint32_t dk, int logn, const Modulus* mods) {
+  using S = tc::Smem<KPAD>;
+  const uint32_t N = 1u << logn, zblocks = N / tc::kSlots;
+  const uint32_t gchunks = (groups + tc::kGroups - 1) / tc::kGroups;
+  const uint32_t units = dk * zblocks * gchunks;
+  const uint64_t out_words = 8ull * groups * 2 * dk << logn;
+  std::vector<uint8_t> A(2 * S::kABox), B(S::kBBox);
+  std::vector<uint64_t> ob(tc::kSlots * 16 * tc::kGroups);
+  std::vector<uint32_t> D(128 * 512);
+  auto put = [](std::vector<uint8_t>& img, uint32_t box_base, uint32_t lin, uint64_t v) {
+    const uint32_t off = box_base + lin;
+    if (off + 8 > img.size() || (off & 7)) throw 2;
+    std::memcpy(&img[off], &v, 8);
+  };
+  for (uint32_t u = 0; u < units; ++u) {
+    uint32_t gc, p, z0;
+    tc::unit_coords(u, gchunks, zblocks, &gc, &p, &z0);
+    for (uint32_t zp = 0; zp < tc::kSlots / tc::kPair; ++zp) {
+      const uint32_t z = z0 + zp * tc::kPair;
+      if (z & 1) throw 5;  // TMA x coordinate: 16-byte multiple
+      // A boxes: (z..z+1, c, t4 + 4 mb, b < KPAD, p)
+      for (uint32_t mb = 0; mb < 2; ++mb)
+        for (uint32_t b = 0; b < KPAD; ++b)
+          for (uint32_t t4 = 0; t4 < 4; ++t4)
+            for (uint32_t c = 0; c < 2; ++c)
+              for (uint32_t zs = 0; zs < 2; ++zs) {
+                const uint32_t t = 4 * mb + t4;
+                const uint64_t v = b < inputs ? in[((((uint64_t)t * inputs + b) * 2 + c) * dk + p) * N + z + zs] : 0;
+                put(A, mb * S::kABox, tc::a_img<KPAD>(b, t4, c, zs), v);
+              }
+      for (uint32_t gr = 0; gr < tc::kRoundsPerPair; ++gr) {
+        for (uint32_t b = 0; b < KPAD; ++b)
+          for (uint32_t gl = 0; gl < tc::kGroupsRound; ++gl)
+            for (uint32_t zs = 0; zs < 2; ++zs) {
+              const uint32_t g = gc * tc::kGroups + gr * tc::kGroupsRound + gl;
+              const uint64_t v = (b < inputs && g < groups) ? w[(((uint64_t)g * inputs + b) * dk + p) * N + z + zs] : 0;
+              put(B, 0, tc::b_img<KPAD>(b, gl, zs), v);
+            }
+        // MMA: D[m][mb*256 + n] = sum_k A_mb[m][k] . B[k][n]
+        for (uint32_t mb = 0; mb < 2; ++mb)
+          for (uint32_t m = 0; m < 128; ++m)
+            for (uint32_t n = 0; n < 256; ++n) {
+              uint32_t acc = 0;
+              for (uint32_t k = 0; k < KPAD; ++k)
+                acc += (uint32_t)A[mb * S::kABox + (m >> 4) * KPAD * 16 + k * 16 + (m & 15)] *
+                       (uint32_t)B[(n >> 4) * KPAD * 16 + k * 16 + (n & 15)];
+              D[m * 512 + 256 * mb + n] = acc;
+            }
+        for (uint32_t warp = 0; warp < 16; ++warp) {
+          const uint32_t quarter = warp & 3, mb = warp >> 3, gh = (warp >> 2) & 1;
+          uint64_t vlo[32][8], vhi[32][8];
+          for (uint32_t lane = 0; lane < 32; ++lane) {
+            const uint32_t m = quarter * 32 + lane, zs = (m >> 3) & 1, i = m & 7;
+            for (uint32_t h = 0; h < 4; ++h) {
+              uint32_t cols[32];
+              for (uint32_t c = 0; c < 32; ++c) cols[c] = D[m * 512 + 256 * mb + 128 * gh + 32 * h + c];
+              tc::lane_values2(cols, zs, i, vlo[lane] + 2 * h, vhi[lane] + 2 * h);
+            }
+          }
+          for (int lev = 4; lev >= 1; lev >>= 1) {
+            uint64_t nlo[32][8], nhi[32][8], slo[32][8], shi[32][8];
+            for (uint32_t lane = 0; lane < 32; ++lane) {
+              const bool sel = (lane & 7) & lev;
+              for (int q = 0; q < lev; ++q) {
+                nlo[lane][q] = sel ? vlo[lane][q + lev] : vlo[lane][q];
+                nhi[lane][q] = sel ? vhi[lane][q + lev] : vhi[lane][q];
+                slo[lane][q] = sel ? vlo[lane][q] : vlo[lane][q + lev];
+                shi[lane][q] = sel ? vhi[lane][q] : vhi[lane][q + lev];
+              }
+            }
+            for (uint32_t lane = 0; lane < 32; ++lane)
+              for (int q = 0; q < lev; ++q) {
+                vlo[lane][q] = nlo[lane][q];
+                vhi[lane][q] = nhi[lane][q];
+                tc::add128(vlo[lane][q], vhi[lane][q], slo[lane ^ lev][q], shi[lane ^ lev][q]);
+              }
+          }
+          for (uint32_t lane = 0; lane < 32; ++lane) {
+            const uint32_t m = quarter * 32 + lane, tc4 = m >> 4, zs = (m >> 3) & 1, i = m & 7;
+            ob[tc::out_buf_word(zp * tc::kPair + zs, mb * 8 + tc4, gr * tc::kGroupsRound + gh * 8 + i)] =
+                reduce128(vlo[lane][0], vhi[lane][0], mods[p]);
+          }
+        }
+      }
+    }
+    for (uint32_t tid = 0; tid < 512; ++tid) {
+      const uint32_t rtc = tid >> 5, rgl = tid & 31, g = gc * tc::kGroups + rgl;
+      if (g >= groups) continue;
+      const uint64_t row = tc::out_row(rtc, g, groups, p, z0, dk, N);
+      if ((row & 1) || row + tc::kSlots > out_words) throw 4;  // 16-byte stores
+      for (uint32_t zz = 0; zz < tc::kSlots; ++zz) out[row + zz] = ob[tc::out_buf_word(zz, rtc, rgl)];
+    }
   }
 }
 
@@ -188,7 +294,7 @@ int emu_matrix(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const 
 int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd,
                      const uint64_t* inv, const uint64_t* cts, uint64_t tiles, uint64_t inputs, const uint64_t* ring,
                      uint64_t groups, const uint64_t* masks, const uint64_t* samples, const uint64_t* pk,
-                     uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog, uint64_t* out) {
+                     uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog, uint64_t* out, int path) {
   Tabs T = tabs(k, mods16, fwd, inv);
   const uint64_t n = 1ull << logn;
   const uint64_t items = tiles * groups;
@@ -207,6 +313,14 @@ int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, 
       const int TT = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
       const uint64_t* ip = in.data() + t0 * in_tile;
       uint64_t* ap = out + t0 * acc_tile;
+      if (path == 0 && TT == tc::kTiles && inputs <= (uint64_t)tc::kMaxK && n >= (uint64_t)tc::kSlots) {
+        if (inputs <= 32)
+          emu_mac_tc_launch<32>(ip, w.data(), ap, (uint32_t)inputs, (uint32_t)groups, dk, L_, T.mods.data());
+        else
+          emu_mac_tc_launch<64>(ip, w.data(), ap, (uint32_t)inputs, (uint32_t)groups, dk, L_, T.mods.data());
+        t0 += TT;
+        continue;
+      }
       switch (TT) {
         case 8: emu_mac_launch<8, 4>(ip, w.data(), ap, (uint32_t)inputs, (uint32_t)groups, dk, L_, T.mods.data()); break;
         case 4: emu_mac_launch<4, 4>(ip, w.data(), ap, (uint32_t)inputs, (uint32_t)groups, dk, L_, T.mods.data()); break;

@@ -145,13 +145,16 @@ def test_matrix_mask_enc0_kernel_bodies(bfv, oracle, E, logn):
     assert np.array_equal(out2[0], oc.matrix_evaluate(cn, ring[0]))
 
 
-@pytest.mark.parametrize("tiles,I,G", [(1, 3, 2), (3, 3, 2), (8, 3, 2), (2, 20, 19), (1, 264, 3)])
-def test_matrix_tiles_kernel_bodies(bfv, oracle, E, tiles, I, G):
+@pytest.mark.parametrize("tiles,I,G,path", [(1, 3, 2, 0), (3, 3, 2, 0), (8, 3, 2, 1), (2, 20, 19, 0),
+                                             (1, 264, 3, 0), (8, 3, 2, 0), (9, 40, 33, 0), (8, 64, 3, 0)])
+def test_matrix_tiles_kernel_bodies(bfv, oracle, E, tiles, I, G, path):
     """Layer pipeline (split-operand NTT, multi-tile product over 30-bit halves with its
     shared-memory staging, Enc(0) prep, INTT with folded Enc(0) and mask) against the
     oracle's per-tile matrix evaluation + sub_plain + Enc(0) add.  Cases cover partial and
     several input chunks, more groups than one block holds, and more than 256 inputs (the
-    periodic reduction of the 128-bit sums)."""
+    periodic reduction of the 128-bit sums); with path 0, launches of 8 tiles take the
+    tcgen05 product (K padded to 32 and 64, a partial group chunk), emulated from its
+    shared-memory operand layouts, TMEM drain and shuffle recombination."""
     logn = 5
     hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
     k, dk, n = hc.k, hc.dk, 1 << logn
@@ -165,10 +168,10 @@ def test_matrix_tiles_kernel_bodies(bfv, oracle, E, tiles, I, G):
     samples = np.stack([np.stack([tb.samples() for _ in range(G)]) for _ in range(tiles)])
     out = np.zeros((tiles, G, 2, dk, n), dtype=np.uint64)
     E.emu_matrix_tiles(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), tiles, I, p(ring), G, p(masks), p(samples),
-                       p(tb.pk), oc.q_mod_t, oc.upper_half, 1 << 59, 59, p(out))
+                       p(tb.pk), oc.q_mod_t, oc.upper_half, 1 << 59, 59, p(out), path)
     plain = np.zeros_like(out)
     E.emu_matrix_tiles(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), tiles, I, p(ring), G, None, None, None,
-                       oc.q_mod_t, oc.upper_half, 1 << 59, 59, p(plain))
+                       oc.q_mod_t, oc.upper_half, 1 << 59, 59, p(plain), path)
     for t in range(tiles):
         cn = oc.matrix_open(cts[t])
         for g in range(G):

@@ -337,10 +337,11 @@ def test_matrix_groups_mask_enc0_crt(art, oracle):
             assert v == oracle.crt(e[0][:, t], oc.primes[:6])
 
 
-@pytest.mark.parametrize("tiles", [3, 9])
-def test_matrix_tiles_device(art, oracle, tiles):
-    """Layer pipeline through bfvgpu_matrix_tiles_device (tiles in launches of 8/2/1) against
-    the oracle's per-tile evaluate + sub_plain + Enc(0); also without mask and Enc(0)."""
+@pytest.mark.parametrize("tiles,path", [(3, 0), (9, 0), (9, 1)])
+def test_matrix_tiles_device(art, oracle, tiles, path):
+    """Layer pipeline through bfvgpu_matrix_tiles_device (tiles in launches of 8/2/1; path 0
+    takes tcgen05 for the 8-tile launch, path 1 CUDA cores only) against the oracle's
+    per-tile evaluate + sub_plain + Enc(0); also without mask and Enc(0)."""
     import torch
     hc, oc = art
     n, k, dk = oc.n, oc.k, oc.data_k
@@ -360,11 +361,16 @@ def test_matrix_tiles_device(art, oracle, tiles):
     out = torch.empty((tiles, G, 2, dk, n), dtype=torch.int64, device="cuda")
     plain = torch.empty_like(out)
     torch.cuda.synchronize()
-    hc.matrix_tiles_inputs_device(d_in, tiles * I)
-    hc.weights_ntt_device(d_ring, G * I, w)
-    hc.matrix_tiles_device(d_in, tiles, I, w, G, out, masks=d_masks, samples=d_samples, pk=d_pk, scratch=scratch)
-    hc.matrix_tiles_device(d_in, tiles, I, w, G, plain)
-    torch.cuda.synchronize()
+    hc.set_product_path(path)
+    try:
+        hc.matrix_tiles_inputs_device(d_in, tiles * I)
+        hc.weights_ntt_device(d_ring, G * I, w)
+        hc.matrix_tiles_device(d_in, tiles, I, w, G, out, masks=d_masks, samples=d_samples, pk=d_pk,
+                               scratch=scratch)
+        hc.matrix_tiles_device(d_in, tiles, I, w, G, plain)
+        assert hc.check() == 0
+    finally:
+        hc.set_product_path(0)
     got, got_plain = out.cpu().numpy().view(np.uint64), plain.cpu().numpy().view(np.uint64)
     for t in range(tiles):
         cn = oc.matrix_open(cts[t], threads=8)
@@ -374,6 +380,44 @@ def test_matrix_tiles_device(art, oracle, tiles):
             e[0] = oc.sub_plain(e[0], masks[t, g])
             e = oc.add(e, oc.enc0(samples[t, g], tb.pk))
             assert np.array_equal(got[t, g], e), (t, g)
+
+
+def test_matrix_tiles_tensor_core_vs_cuda_core(art, oracle):
+    """8 tiles, 40 input blocks (K padded to 64), 33 groups (a partial 32-group chunk): the
+    tcgen05 product equals the CUDA-core product on every word, and spot (tile, group)
+    pairs equal the oracle."""
+    import torch
+    hc, oc = art
+    n, k, dk = oc.n, oc.k, oc.data_k
+    tiles, I, G = 8, 40, 33
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7)
+    q = torch.tensor(oc.primes[:dk], dtype=torch.int64, device="cuda").view(dk, 1)
+    cts = torch.remainder(torch.randint(0, 2 ** 62, (tiles, I, 2, dk, n), dtype=torch.int64, device="cuda",
+                                        generator=gen), q)
+    cts[0, 0, 0, 0, :64] = q[0] - 1  # boundary residues
+    cts[1, 1, 1, 2, :64] = 0
+    ring = torch.randint(-127, 128, (G, I, n), dtype=torch.int64, device="cuda", generator=gen) & ((1 << 59) - 1)
+    d_in = cts.clone()
+    w = torch.empty((G, I, dk, n), dtype=torch.int64, device="cuda")
+    out_tc = torch.empty((tiles, G, 2, dk, n), dtype=torch.int64, device="cuda")
+    out_cc = torch.empty_like(out_tc)
+    hc.matrix_tiles_inputs_device(d_in, tiles * I)
+    hc.weights_ntt_device(ring, G * I, w)
+    hc.matrix_tiles_device(d_in, tiles, I, w, G, out_tc)
+    hc.set_product_path(1)
+    try:
+        hc.matrix_tiles_device(d_in, tiles, I, w, G, out_cc)
+    finally:
+        hc.set_product_path(0)
+    assert hc.check() == 0
+    assert torch.equal(out_tc, out_cc)
+    got = out_tc.cpu().numpy().view(np.uint64)
+    cts_h = cts.cpu().numpy().view(np.uint64)
+    ring_h = ring.cpu().numpy().view(np.uint64)
+    for t, g in [(0, 0), (1, 32), (7, 17)]:
+        cn = oc.matrix_open(cts_h[t], threads=8)
+        assert np.array_equal(got[t, g], oc.matrix_evaluate(cn, ring_h[g], threads=8)), (t, g)
 
 
 # ---- resident token ----------------------------------------------------------------------------

@@ -125,7 +125,8 @@ def test_public_shape_rejections(bfv):
             engine.validate(shape, outputs, fx, fw, linear=linear)
 
 
-def test_layer_server_tiles_decrypt(bfv, oracle, setup):
+@pytest.mark.parametrize("tiles", [3, 8])
+def test_layer_server_tiles_decrypt(bfv, oracle, setup, tiles):
     """LayerServer (multi-tile product, folded Enc(0), mask, target gather with CRT) on two
     small projections and three token tiles: every target decrypts to sum_j x.w minus the
     mask at that coefficient (mod 2^59), and the gathered c0 residues and CRT limbs are the
@@ -135,7 +136,7 @@ def test_layer_server_tiles_decrypt(bfv, oracle, setup):
     from bfvgpu.layout import MASK59, pack_inputs
     hc, oc, tb = setup
     n, k, dk = oc.n, oc.k, oc.data_k
-    tiles, batch = 3, 2
+    batch = 2
     rng = np.random.default_rng(77)
     pk = torch.from_numpy(tb.pk.view(np.int64)).cuda()
     srv = L.LayerServer(torch, hc, pk, (("a", 300, 200), ("b", 130, 600)), batch, tiles)
@@ -152,7 +153,7 @@ def test_layer_server_tiles_decrypt(bfv, oracle, setup):
         masks = rng.integers(0, 1 << 59, size=(tiles, p.groups, n), dtype=np.uint64)
         samples = np.stack([np.stack([tb.samples() for _ in range(p.groups)]) for _ in range(tiles)])
         srv.run_projection(p, dev(cts), dev(masks), dev(samples))
-        torch.cuda.synchronize()
+        assert hc.check() == 0
         out = srv.output(p).cpu().numpy().view(np.uint64)
         tg, counts, mx = srv.targets[p.name]
         tg, counts = tg.cpu().numpy(), counts.cpu().numpy()
