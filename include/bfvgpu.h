@@ -182,6 +182,11 @@ uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx *ctx, uint64_t tiles
  * form) into the operand form of bfvgpu_matrix_tiles_device: every canonical NTT slot v
  * is stored as ((v >> 30) << 32) | (v mod 2^30).  Needs data primes < 2^60 and n >= 32. */
 int32_t bfvgpu_matrix_tiles_inputs_device(bfvgpu_ctx *ctx, uint64_t *cts, uint64_t count, void *stream);
+/* The public key pk [2][k][n] (NTT form) prepared for bfvgpu_matrix_tiles_device: pk_prep
+ * [2][k][n][2] words = {v, floor(v 2^64 / q)} with v = pk . q_special^-1 mod q for the data
+ * primes and v = pk for the special prime.  Once per key. */
+int32_t bfvgpu_matrix_tiles_prepare_pk_device(bfvgpu_ctx *ctx, const uint64_t *pk, uint64_t *pk_prep,
+                                              void *stream);
 /* Server product of `tiles` token tiles that share one weight matrix (the four calls per
  * tile of Transformer::layer_from_shares, model.hpp:173-238, batched over tiles; per tile
  * and group the result is Matrix::evaluate of matrix.cu:90-106 plus the mask and Enc(0) of
@@ -190,11 +195,11 @@ int32_t bfvgpu_matrix_tiles_inputs_device(bfvgpu_ctx *ctx, uint64_t *cts, uint64
  * in [tiles][inputs][2][dk][n] from bfvgpu_matrix_tiles_inputs_device, w
  * [groups][inputs][dk][n] NTT form (bfvgpu_weights_ntt_device), masks
  * [tiles][groups][n] ring-59 words or NULL, samples [tiles][groups][3][k][n] or NULL (then
- * pk and scratch may be NULL), pk [2][k][n] NTT form, out [tiles][groups][2][dk][n].  Each
- * weight word is read once for all tiles. */
+ * pk_prep and scratch may be NULL), pk_prep from bfvgpu_matrix_tiles_prepare_pk_device, out
+ * [tiles][groups][2][dk][n].  Each weight word is read once for all tiles. */
 int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_t tiles, uint64_t inputs,
                                    const uint64_t *w, uint64_t groups, const uint64_t *masks,
-                                   const uint64_t *samples, const uint64_t *pk, uint64_t *scratch,
+                                   const uint64_t *samples, const uint64_t *pk_prep, uint64_t *scratch,
                                    uint64_t *out, void *stream);
 
 /* Enc(0) polynomials before the divide-and-round, for the matrix epilogue: samples

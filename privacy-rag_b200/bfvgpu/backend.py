@@ -184,18 +184,23 @@ class Context:
         check(lib().bfvgpu_matrix_tiles_inputs_device(self._h, self._dptr(cts), count, stream),
               "matrix_tiles_inputs_device")
 
+    def matrix_tiles_prepare_pk_device(self, pk, pk_prep, stream: int | None = None):
+        """pk [2][k][n] (NTT form) -> pk_prep [2][k][n][2] for matrix_tiles_device."""
+        check(lib().bfvgpu_matrix_tiles_prepare_pk_device(self._h, self._dptr(pk), self._dptr(pk_prep), stream),
+              "matrix_tiles_prepare_pk_device")
+
     def matrix_tiles_scratch_words(self, tiles: int, groups: int, enc0: bool = True) -> int:
         return int(lib().bfvgpu_matrix_tiles_scratch_words(self._h, tiles, groups, int(bool(enc0))))
 
     def matrix_tiles_device(self, inputs_ntt, tiles: int, inputs: int, weights_ntt, groups: int, out, masks=None,
-                            samples=None, pk=None, scratch=None, stream: int | None = None):
+                            samples=None, pk_prep=None, scratch=None, stream: int | None = None):
         """out [tiles][groups][2][dk][n] = product of each tile's inputs [tiles][inputs][2][dk][n]
         (from matrix_tiles_inputs_device) with the shared NTT-form weights
-        [groups][inputs][dk][n], plus
-        Enc(0) from samples [tiles][groups][3][k][n] and minus the Delta-scaled masks."""
+        [groups][inputs][dk][n], plus Enc(0) from samples [tiles][groups][3][k][n] (public key
+        from matrix_tiles_prepare_pk_device) and minus the Delta-scaled masks."""
         check(lib().bfvgpu_matrix_tiles_device(self._h, self._dptr(inputs_ntt), tiles, inputs,
                                                self._dptr(weights_ntt), groups, self._dptr(masks) or None,
-                                               self._dptr(samples) or None, self._dptr(pk) or None,
+                                               self._dptr(samples) or None, self._dptr(pk_prep) or None,
                                                self._dptr(scratch) or None, self._dptr(out), stream),
               "matrix_tiles_device")
 

@@ -81,7 +81,8 @@ class LayerServer:
         Projection records (a shard of a larger call keeps the call's packing)."""
         self.torch = torch
         self.ctx = ctx
-        self.pk = pk_device
+        self.pk = torch.empty((2, ctx.k, ctx.n, 2), dtype=torch.int64, device=pk_device.device)
+        ctx.matrix_tiles_prepare_pk_device(pk_device, self.pk)
         self.proj = [p if isinstance(p, Projection) else plan(p[0], batch, p[1], p[2]) for p in projections]
         self.batch = batch
         self.tiles = tiles
@@ -128,6 +129,6 @@ class LayerServer:
         I, G, T = p.inputs, p.groups, self.tiles
         ctx.matrix_tiles_inputs_device(cts, T * I, stream=stream)
         ctx.matrix_tiles_device(cts, T, I, self.w_ntt[p.name], G, self.out, masks=masks, samples=samples,
-                                pk=self.pk, scratch=self.scratch, stream=stream)
+                                pk_prep=self.pk, scratch=self.scratch, stream=stream)
         tg, counts, mx = self.targets[p.name]
         ctx.gather_targets_device(self.out, T * G, tg, counts, mx, self.selected, self.crt, stream=stream)

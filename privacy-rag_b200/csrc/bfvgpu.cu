@@ -754,13 +754,24 @@ int32_t bfvgpu_matrix_tiles_inputs_device(bfvgpu_ctx* ctx, uint64_t* cts, uint64
   });
 }
 
+int32_t bfvgpu_matrix_tiles_prepare_pk_device(bfvgpu_ctx* ctx, const uint64_t* pk, uint64_t* pk_prep, void* stream) {
+  return guard([&] {
+    if (!ctx || !pk || !pk_prep) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    cuda_check(launch_pk_prep(ctx->c.P, pk, reinterpret_cast<ulonglong2*>(pk_prep), pick(ctx, stream)), "pk_prep");
+    count_launch();
+  });
+}
+
 int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t tiles, uint64_t inputs,
                                    const uint64_t* w, uint64_t groups, const uint64_t* masks, const uint64_t* samples,
-                                   const uint64_t* pk, uint64_t* scratch, uint64_t* out, void* stream) {
+                                   const uint64_t* pk_prep, uint64_t* scratch, uint64_t* out, void* stream) {
   return guard([&] {
     if (!ctx || !in || !w || !out || !inputs) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
     require_product_ring(ctx->c);
-    if (samples && (!pk || !scratch)) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (samples && (!pk_prep || !scratch)) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
     if (samples && ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
     require_device(ctx->c);
     DeviceScope scope(ctx->c.device);
@@ -773,10 +784,13 @@ int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t
     cuda_check(launch_mac_tiles(ctx->c.P, in, tiles, inputs, w, groups, out, st), "mac_tiles");
     count_launch(mac_tiles_launches(tiles));
     if (samples) {
-      cuda_check(launch_enc0_prep(ctx->c.P, samples, pk, items, U, xs, st), "enc0_prep");
+      cuda_check(launch_enc0_prep(ctx->c.P, samples, reinterpret_cast<const ulonglong2*>(pk_prep), items, U, xs, st),
+                 "enc0_prep");
       count_launch();
     }
-    cuda_check(launch_intt_protect(ctx->c.P, out, items, U, pk, xs, samples, masks, out, st), "intt_protect");
+    cuda_check(launch_intt_protect(ctx->c.P, out, items, U, reinterpret_cast<const ulonglong2*>(pk_prep), xs, samples,
+                                   masks, out, st),
+               "intt_protect");
     count_launch();
   });
 }

@@ -530,11 +530,38 @@ BFV_HD void op_ntt_split(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* data
   ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
 }
 
+// Shoup companion floor(v 2^64 / q) of v < q, by exact division: v 2^64 - r (r = v 2^64 mod q)
+// is a multiple of q, so the quotient is -r . q^-1 mod 2^64 (q odd).
+BFV_HD uint64_t shoup_companion(uint64_t v, const Modulus& m) {
+  const uint64_t r = reduce128(0, v, m);
+  uint64_t inv = m.q;  // q^-1 mod 2^64 by Newton's iteration (3 -> 96 correct bits)
+#pragma unroll
+  for (int it = 0; it < 5; ++it) inv *= 2 - m.q * inv;
+  return (uint64_t(0) - r) * inv;
+}
+
+// Public key prepared for the layer pipeline: pk_prep[c][p][z] = {v, floor(v 2^64 / q_p)} with
+// v = pk_c,p . q_s^-1 mod q_p for the data primes (the moddown scale folded in) and
+// v = pk_c,s for the special prime.  One work item per (c, p, z).
+BFV_HD void pk_prep_item(uint64_t item, const uint64_t* pk, ulonglong2* prep, uint32_t k, int logn,
+                         const Modulus* mods) {
+  const uint64_t N = uint64_t(1) << logn;
+  const uint32_t p = (uint32_t)((item >> logn) % k);
+  const Modulus& m = mods[p];
+  const uint64_t x = pk[item];
+  const uint64_t v = p + 1 == k ? x : shoup(x, m.inv_special, m.inv_special_q, m.q);
+  ulonglong2 w;
+  w.x = v;
+  w.y = shoup_companion(v, m);
+  prep[item] = w;
+  (void)N;
+}
+
 // Enc(0) preparation for item e (a tile-group pair): block (e, key-level prime p) stores
 // U[e][p] = NTT(u); the special-prime block also produces the special-prime coefficients
 // xs[e][c] = INTT(U . pk_c) + e_c that the divide-and-round needs.
 template <int LOGN, class Ex>
-BFV_HD void op_enc0_prep(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* samples, const uint64_t* pk,
+BFV_HD void op_enc0_prep(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* samples, const ulonglong2* pk,
                          uint64_t* U, uint64_t* xs, uint32_t k, const Modulus* mods, const ulonglong2* fwd,
                          const ulonglong2* inv) {
   constexpr uint64_t N = uint64_t(1) << LOGN;
@@ -550,10 +577,13 @@ BFV_HD void op_enc0_prep(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t
   }
   if (p != k - 1) return;
   for (uint32_t c = 0; c < 2; ++c) {
-    const uint64_t* pkc = pk + ((uint64_t)c * k + p) * N;
+    const ulonglong2* pkc = pk + ((uint64_t)c * k + p) * N;
     const uint64_t* ec = samples + ((e * 3 + 1 + c) * k + p) * N;
     uint64_t* xo = xs + (e * 2 + c) * N;
-    auto ld = [=](int i) { return mul_mod(Up[i], pkc[i], m); };
+    auto ld = [=](int i) {
+      const ulonglong2 w = pkc[i];
+      return shoup(Up[i], w.x, w.y, m.q);
+    };
     auto st = [=](int i, uint64_t v) { xo[i] = add_mod(v, ec[i], m.q); };
     ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
   }
@@ -565,7 +595,7 @@ BFV_HD void op_enc0_prep(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t
 // moddown_p(x) = (x_p - corr(x_s)) q_s^-1 is linear in x_p.
 template <int LOGN, class Ex>
 BFV_HD void op_intt_protect(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* acc, uint64_t* out,
-                            const uint64_t* U, const uint64_t* pk, const uint64_t* xs, const uint64_t* samples,
+                            const uint64_t* U, const ulonglong2* pk, const uint64_t* xs, const uint64_t* samples,
                             const uint64_t* mask, uint32_t k, uint32_t dk, const Modulus* mods,
                             const ulonglong2* inv, uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
   constexpr uint64_t N = uint64_t(1) << LOGN;
@@ -576,14 +606,17 @@ BFV_HD void op_intt_protect(const Ex& ex, uint64_t* s, uint64_t blk, const uint6
   uint64_t* o = out + (e * 2 * dk + cp) * N;
   const bool enc0 = U != nullptr;
   const uint64_t* Up = enc0 ? U + (e * k + p) * N : nullptr;
-  const uint64_t* pkc = enc0 ? pk + ((uint64_t)c * k + p) * N : nullptr;
+  const ulonglong2* pkc = enc0 ? pk + ((uint64_t)c * k + p) * N : nullptr;
   const uint64_t* xsc = enc0 ? xs + (e * 2 + c) * N : nullptr;
   const uint64_t* ec = enc0 ? samples + ((e * 3 + 1 + c) * k + p) * N : nullptr;
   const uint64_t* mk = (mask && c == 0) ? mask + e * N : nullptr;
   const Modulus* ms = mods + (k - 1);
   auto ld = [=](int i) {
     uint64_t v = a[i];
-    if (enc0) v = add_mod(v, shoup(mul_mod(Up[i], pkc[i], m), m.inv_special, m.inv_special_q, m.q), m.q);
+    if (enc0) {
+      const ulonglong2 w = pkc[i];  // pk . q_s^-1 with its Shoup companion
+      v = add_mod(v, shoup(Up[i], w.x, w.y, m.q), m.q);
+    }
     return v;
   };
   auto st = [=](int i, uint64_t v) {

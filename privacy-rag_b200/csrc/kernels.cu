@@ -414,9 +414,15 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
   op_ntt_split<LOGN>(BlockExec{}, smem, blockIdx.x, data, dk, mods, fwd);
 }
 
+__global__ void k_pk_prep(const uint64_t* pk, ulonglong2* prep, uint64_t items, uint32_t k, int logn,
+                          const Modulus* mods) {
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < items; e += (uint64_t)gridDim.x * blockDim.x)
+    pk_prep_item(e, pk, prep, k, logn, mods);
+}
+
 template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
-    k_enc0_prep(const uint64_t* samples, const uint64_t* pk, uint64_t* U, uint64_t* xs, uint32_t k,
+    k_enc0_prep(const uint64_t* samples, const ulonglong2* pk, uint64_t* U, uint64_t* xs, uint32_t k,
                 const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv) {
   extern __shared__ uint64_t smem[];
   op_enc0_prep<LOGN>(BlockExec{}, smem, blockIdx.x, samples, pk, U, xs, k, mods, fwd, inv);
@@ -424,7 +430,7 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
 
 template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
-    k_intt_protect(const uint64_t* acc, uint64_t* out, const uint64_t* U, const uint64_t* pk, const uint64_t* xs,
+    k_intt_protect(const uint64_t* acc, uint64_t* out, const uint64_t* U, const ulonglong2* pk, const uint64_t* xs,
                    const uint64_t* samples, const uint64_t* mask, uint32_t k, uint32_t dk, const Modulus* mods,
                    const ulonglong2* inv, uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
   extern __shared__ uint64_t smem[];
@@ -942,7 +948,13 @@ cudaError_t launch_ntt_split(const DevParams& P, uint64_t* data, uint64_t polys,
   return cudaGetLastError();
 }
 
-cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const uint64_t* pk, uint64_t items,
+cudaError_t launch_pk_prep(const DevParams& P, const uint64_t* pk, ulonglong2* prep, cudaStream_t st) {
+  const uint64_t items = 2ull * P.k * P.n;
+  k_pk_prep<<<elementwise_blocks(items), 256, 0, st>>>(pk, prep, items, P.k, P.logn, P.mod);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const ulonglong2* pk, uint64_t items,
                              uint64_t* U, uint64_t* xs, cudaStream_t st) {
   if (!items) return cudaSuccess;
   if (items * P.k > 0x7fffffffull) return cudaErrorInvalidValue;
@@ -954,7 +966,7 @@ cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const 
 }
 
 cudaError_t launch_intt_protect(const DevParams& P, const uint64_t* acc, uint64_t items, const uint64_t* U,
-                                const uint64_t* pk, const uint64_t* xs, const uint64_t* samples, const uint64_t* mask,
+                                const ulonglong2* pk, const uint64_t* xs, const uint64_t* samples, const uint64_t* mask,
                                 uint64_t* out, cudaStream_t st) {
   if (!items) return cudaSuccess;
   if (items * 2 * P.dk > 0x7fffffffull) return cudaErrorInvalidValue;

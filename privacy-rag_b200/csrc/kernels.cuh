@@ -128,17 +128,19 @@ cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint6
 //                ntt_split, w [G][I][dk][n] NTT form, all primes < 2^60, n >= 32.  Tiles
 //                run in launches of 8/4/2/1 (mac_tiles_launches counts them).
 //  enc0_prep:    U [E][k][n] = NTT(u); xs [E][2][n] = special-prime coefficients of
-//                INTT(U . pk_c) + e_c; samples [E][3][k][n].
+//                INTT(U . pk_c) + e_c; samples [E][3][k][n]; pk prepared by pk_prep.
 //  intt_protect: out [E][2][dk][n] = INTT(acc) + Enc(0) (if U) - Delta mask (if mask
 //                [E][n]), the Enc(0) data-prime part folded into the transform's input.
 cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t tiles, uint64_t inputs,
                              const uint64_t* w, uint64_t groups, uint64_t* acc, cudaStream_t st);
 uint64_t mac_tiles_launches(uint64_t tiles);
 cudaError_t launch_ntt_split(const DevParams& P, uint64_t* data, uint64_t polys, cudaStream_t st);
-cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const uint64_t* pk, uint64_t items,
+//  pk_prep:      prep [2][k][n] = {v, Shoup companion}, v = pk . q_s^-1 (data primes), pk (special)
+cudaError_t launch_pk_prep(const DevParams& P, const uint64_t* pk, ulonglong2* prep, cudaStream_t st);
+cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const ulonglong2* pk, uint64_t items,
                              uint64_t* U, uint64_t* xs, cudaStream_t st);
 cudaError_t launch_intt_protect(const DevParams& P, const uint64_t* acc, uint64_t items, const uint64_t* U,
-                                const uint64_t* pk, const uint64_t* xs, const uint64_t* samples, const uint64_t* mask,
+                                const ulonglong2* pk, const uint64_t* xs, const uint64_t* samples, const uint64_t* mask,
                                 uint64_t* out, cudaStream_t st);
 
 }  // namespace bfvgpu

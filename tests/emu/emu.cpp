@@ -301,6 +301,8 @@ int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, 
   std::vector<uint64_t> in(cts, cts + tiles * inputs * 2 * dk * n);
   std::vector<uint64_t> w(groups * inputs * dk * n);
   std::vector<uint64_t> U(items * k * n), xs(items * 2 * n);
+  std::vector<ulonglong2> pkp(pk ? 2 * k * n : 0);
+  for (uint64_t e = 0; e < pkp.size(); ++e) pk_prep_item(e, pk, pkp.data(), k, logn, T.mods.data());
   EMU_DISPATCH(logn, {
     std::vector<uint64_t> s(SmemWords<L_>::value);
     for (uint64_t b = 0; b < tiles * inputs * 2 * dk; ++b)
@@ -331,9 +333,10 @@ int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, 
     }
     if (samples)
       for (uint64_t b = 0; b < items * k; ++b)
-        op_enc0_prep<L_>(HostExec{}, s.data(), b, samples, pk, U.data(), xs.data(), k, T.mods.data(), T.fwd, T.inv);
+        op_enc0_prep<L_>(HostExec{}, s.data(), b, samples, pkp.data(), U.data(), xs.data(), k, T.mods.data(), T.fwd,
+                         T.inv);
     for (uint64_t b = 0; b < items * 2 * dk; ++b)
-      op_intt_protect<L_>(HostExec{}, s.data(), b, out, out, samples ? U.data() : nullptr, pk, xs.data(), samples,
+      op_intt_protect<L_>(HostExec{}, s.data(), b, out, out, samples ? U.data() : nullptr, pkp.data(), xs.data(), samples,
                           masks, k, dk, T.mods.data(), T.inv, q_mod_t, upper_half, t, tlog);
   });
   return 0;

@@ -365,7 +365,9 @@ def test_matrix_tiles_device(art, oracle, tiles, path):
     try:
         hc.matrix_tiles_inputs_device(d_in, tiles * I)
         hc.weights_ntt_device(d_ring, G * I, w)
-        hc.matrix_tiles_device(d_in, tiles, I, w, G, out, masks=d_masks, samples=d_samples, pk=d_pk,
+        pk_prep = torch.empty((2, k, n, 2), dtype=torch.int64, device="cuda")
+        hc.matrix_tiles_prepare_pk_device(d_pk, pk_prep)
+        hc.matrix_tiles_device(d_in, tiles, I, w, G, out, masks=d_masks, samples=d_samples, pk_prep=pk_prep,
                                scratch=scratch)
         hc.matrix_tiles_device(d_in, tiles, I, w, G, plain)
         assert hc.check() == 0
