@@ -62,6 +62,7 @@ typedef struct bfvgpu_ctx bfvgpu_ctx;
 typedef struct bfvgpu_ntt bfvgpu_ntt;
 typedef struct bfvgpu_matrix bfvgpu_matrix;
 typedef struct bfvgpu_switch bfvgpu_switch;
+typedef struct bfvgpu_rotations bfvgpu_rotations;
 typedef struct bfvgpu_enc0 bfvgpu_enc0;
 typedef struct bfvgpu_token bfvgpu_token;
 
@@ -269,6 +270,19 @@ int32_t bfvgpu_switch_packing_pair(bfvgpu_switch *s, const uint64_t *left, const
 int32_t bfvgpu_switch_timing(const bfvgpu_switch *s, double *upload_ms, double *kernel_ms, double *download_ms);
 int32_t bfvgpu_switch_close(bfvgpu_switch *s, bfvgpu_cleanup *cleanup);
 int32_t bfvgpu_switch_release(bfvgpu_switch *s);
+
+/* ---- Rotations: many Switch elements over one ciphertext batch (no single counterpart in the
+ * reference; each element's result equals Switch::apply with that element's key) ---------- */
+/* keys [count][dk][2][k][n] NTT form, galois_elts [count] (odd, < 2n): uploaded and prepared
+ * once here, as Switch uploads its key at construction. */
+int32_t bfvgpu_rotations_open(bfvgpu_ctx *ctx, const uint64_t *keys, const uint32_t *galois_elts,
+                              uint64_t count, bfvgpu_rotations **out);
+/* cts [m][2][dk][n] -> out [count][m][2][dk][n]: one upload of the batch, its digit transforms
+ * once, then every element with its results copied back while the next element computes.
+ * Host buffers should be pinned for full transfer speed. */
+int32_t bfvgpu_rotations_apply(bfvgpu_rotations *r, const uint64_t *cts, uint64_t m, uint64_t *out);
+int32_t bfvgpu_rotations_close(bfvgpu_rotations *r, bfvgpu_cleanup *cleanup);
+int32_t bfvgpu_rotations_release(bfvgpu_rotations *r);
 
 /* ---- PublicZero (IV1/native/gpu/enc0/enc0.hpp:15-25) ------------------------------------ */
 int32_t bfvgpu_enc0_open(bfvgpu_ctx *ctx, const uint64_t *pk, bfvgpu_enc0 **out);

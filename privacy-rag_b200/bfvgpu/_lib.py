@@ -102,6 +102,10 @@ _SIGNATURES = {
     "bfvgpu_switch_open": (I32, [VP, U64P, U32, ctypes.POINTER(VP)]),
     "bfvgpu_switch_apply": (I32, [VP, U64P, U64P]),
     "bfvgpu_switch_apply_many": (I32, [VP, U64P, U64, U64P]),
+    "bfvgpu_rotations_open": (I32, [VP, U64P, U32P, U64, ctypes.POINTER(VP)]),
+    "bfvgpu_rotations_apply": (I32, [VP, U64P, U64, U64P]),
+    "bfvgpu_rotations_close": (I32, [VP, ctypes.POINTER(Cleanup)]),
+    "bfvgpu_rotations_release": (I32, [VP]),
     "bfvgpu_switch_packing_pair": (I32, [VP, U64P, U64P, VP, U32, U64P]),
     "bfvgpu_switch_timing": (I32, [VP, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                                    ctypes.POINTER(ctypes.c_double)]),

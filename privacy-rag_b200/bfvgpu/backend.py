@@ -384,6 +384,40 @@ class Switch(_Handle):
         return {"upload_ms": a.value, "kernel_ms": b.value, "download_ms": c.value}
 
 
+class Rotations(_Handle):
+    """Many Galois elements over one ciphertext batch: keys prepared once at construction,
+    the batch uploaded and its digits transformed once per apply, every element's result
+    streamed back while the next element computes."""
+
+    _close_fn = "bfvgpu_rotations_close"
+    _release_fn = "bfvgpu_rotations_release"
+
+    def __init__(self, ctx: Context, keys, elements):
+        super().__init__(ctx)
+        self.elements = [int(e) for e in elements]
+        k = u64(keys)
+        if k.size != len(self.elements) * ctx.dk * 2 * ctx.k * ctx.n:
+            raise ValueError("E_NTT_CONTEXT")
+        arr = (U32 * len(self.elements))(*self.elements)
+        h = VP()
+        check(lib().bfvgpu_rotations_open(ctx.handle, ptr(k), arr, len(self.elements), ctypes.byref(h)), "Rotations")
+        self._h = h
+
+    def apply(self, cts, out=None) -> np.ndarray:
+        """cts [m][2][dk][n] -> [elements][m][2][dk][n] (into `out` when given, e.g. pinned)."""
+        a = u64(cts)
+        per = 2 * self.ctx.dk * self.ctx.n
+        if a.size == 0 or a.size % per:
+            raise ValueError("E_SWITCH_CIPHERTEXT")
+        m = a.size // per
+        if out is None:
+            out = np.empty((len(self.elements), m, 2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
+        elif out.dtype != np.uint64 or out.size != len(self.elements) * m * per or not out.flags.c_contiguous:
+            raise ValueError("E_SWITCH_OUTPUT")
+        check(lib().bfvgpu_rotations_apply(self._h, ptr(a), m, ptr(out)), "Rotations.apply")
+        return out
+
+
 class PublicZero(_Handle):
     """Enc(0) from explicit samples (u ternary, e0, e1) with a bound public key."""
 

@@ -484,6 +484,16 @@ struct bfvgpu_switch {
   double upload_ms = 0, kernel_ms = 0, download_ms = 0;
 };
 
+struct bfvgpu_rotations {
+  Holder h;
+  std::vector<uint32_t> elts;
+  uint64_t pw = 0, cap = 0;
+  uint64_t* prepared = nullptr;  // [rotations][pw]
+  uint64_t *cts = nullptr, *hoisted = nullptr, *x = nullptr, *out[2] = {nullptr, nullptr};
+  cudaStream_t copy = nullptr;
+  cudaEvent_t computed[2] = {nullptr, nullptr}, copied[2] = {nullptr, nullptr};
+};
+
 struct bfvgpu_enc0 {
   Holder h;
   uint64_t *pk = nullptr, *samples = nullptr, *u_ntt = nullptr, *x = nullptr, *out = nullptr, *plain = nullptr;
@@ -1266,6 +1276,115 @@ int32_t bfvgpu_switch_close(bfvgpu_switch* s, bfvgpu_cleanup* cleanup) {
 int32_t bfvgpu_switch_release(bfvgpu_switch* s) {
   if (!s) return BFVGPU_OK;
   bfvgpu_switch_close(s, nullptr);
+  delete s;
+  return BFVGPU_OK;
+}
+
+// ---- Rotations: one ciphertext batch through many Galois keyswitches -----------------------
+// Keys [r][dk][2][k][n] are uploaded and prepared (slot-permuted, with their corrections) once
+// at open, as Switch uploads its key at construction; apply uploads the batch once, hoists its
+// digit transforms and runs every element, copying each element's results back on a second
+// stream while the next element computes (two device output buffers).
+int32_t bfvgpu_rotations_open(bfvgpu_ctx* ctx, const uint64_t* keys, const uint32_t* galois_elts, uint64_t count,
+                              bfvgpu_rotations** out) {
+  return guard([&] {
+    if (!ctx || !keys || !galois_elts || !count || !out) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    *out = nullptr;
+    const Context& c = ctx->c;
+    if (c.k != c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_NTT_CONTEXT");
+    for (uint64_t r = 0; r < count; ++r)
+      if (!(galois_elts[r] & 1) || galois_elts[r] >= 2 * c.n) fail(BFVGPU_E_ELEMENT, "E_BFVGPU_GALOIS_ELEMENT");
+    const uint64_t kw = (uint64_t)c.dk * 2 * c.k * c.n;
+    check_canonical_host(c, keys, count * c.dk * 2 * c.k, c.k, 0);
+    auto s = std::make_unique<bfvgpu_rotations>();
+    s->h.ctx = &ctx->c;
+    s->elts.assign(galois_elts, galois_elts + count);
+    s->pw = (2ull * c.dk + 2) * c.k * c.n;
+    require_device(c);
+    DeviceScope scope(c.device);
+    s->h.run([&] {
+      s->prepared = s->h.alloc(count * s->pw);
+      constexpr uint64_t kBatch = 16;
+      uint64_t* tmp = s->h.alloc((count < kBatch ? count : kBatch) * kw);
+      for (uint64_t first = 0; first < count; first += kBatch) {
+        const uint64_t m = count - first < kBatch ? count - first : kBatch;
+        s->h.h2d(tmp, keys + first * kw, m * kw);
+        cuda_check(launch_ks_keyprep(c.P, tmp, s->elts.data() + first, m, s->prepared + first * s->pw, c.stream),
+                   "keyprep");
+        count_launch(2);
+      }
+      cuda_check(cudaStreamCreateWithFlags(&s->copy, cudaStreamNonBlocking), "cudaStreamCreate");
+      for (int i = 0; i < 2; ++i) {
+        cuda_check(cudaEventCreateWithFlags(&s->computed[i], cudaEventDisableTiming), "cudaEventCreate");
+        cuda_check(cudaEventCreateWithFlags(&s->copied[i], cudaEventDisableTiming), "cudaEventCreate");
+      }
+      s->h.sync();
+    });
+    *out = s.release();
+  });
+}
+
+int32_t bfvgpu_rotations_apply(bfvgpu_rotations* s, const uint64_t* cts, uint64_t count, uint64_t* out) {
+  return guard([&] {
+    if (!s || !cts || !out || !count) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    s->h.check_open("E_SWITCH_CLOSED");
+    const Context& c = *s->h.ctx;
+    check_canonical_host(c, cts, count * 2 * c.dk, c.dk, 0);
+    DeviceScope scope(c.device);
+    s->h.run([&] {
+      const uint64_t ctw = 2ull * c.dk * c.n;
+      if (count > s->cap) {
+        s->cts = s->h.grow(s->cts, count * ctw);
+        s->hoisted = s->h.grow(s->hoisted, count * c.dk * c.k * c.n + (count + 1) / 2);
+        s->x = s->h.grow(s->x, count * 2 * c.k * c.n);
+        s->out[0] = s->h.grow(s->out[0], count * ctw);
+        s->out[1] = s->h.grow(s->out[1], count * ctw);
+        s->cap = count;
+      }
+      s->h.h2d(s->cts, cts, count * ctw);
+      const uint32_t* zflag = (const uint32_t*)(s->hoisted + count * c.dk * c.k * c.n);
+      cuda_check(launch_ks_hoist(c.P, s->cts, count, s->hoisted, (uint32_t*)zflag, c.stream), "hoist");
+      count_launch();
+      for (uint64_t r = 0; r < s->elts.size(); ++r) {
+        const int b = (int)(r & 1);
+        if (r >= 2) cuda_check(cudaStreamWaitEvent(c.stream, s->copied[b], 0), "wait");
+        cuda_check(launch_ks_rotate(c.P, s->cts, count, s->hoisted, zflag, s->prepared + r * s->pw, s->elts[r], s->x,
+                                    s->out[b], c.stream),
+                   "rotate");
+        count_launch(2);
+        cuda_check(cudaEventRecord(s->computed[b], c.stream), "event");
+        cuda_check(cudaStreamWaitEvent(s->copy, s->computed[b], 0), "wait");
+        cuda_check(cudaMemcpyAsync(out + r * count * ctw, s->out[b], count * ctw * 8, cudaMemcpyDeviceToHost, s->copy),
+                   "D2H");
+        cuda_check(cudaEventRecord(s->copied[b], s->copy), "event");
+      }
+      cuda_check(cudaStreamSynchronize(s->copy), "cudaStreamSynchronize");
+      s->h.sync();
+    });
+  });
+}
+
+int32_t bfvgpu_rotations_close(bfvgpu_rotations* s, bfvgpu_cleanup* cleanup) {
+  if (!s) return BFVGPU_E_ARGUMENT;
+  const bool was_open = !s->h.cleanup.closed;
+  if (s->copy) cudaStreamSynchronize(s->copy);
+  const bfvgpu_cleanup c = s->h.release();
+  if (was_open && c.closed) {
+    for (int i = 0; i < 2; ++i) {
+      if (s->computed[i]) cudaEventDestroy(s->computed[i]);
+      if (s->copied[i]) cudaEventDestroy(s->copied[i]);
+      s->computed[i] = s->copied[i] = nullptr;
+    }
+    if (s->copy) cudaStreamDestroy(s->copy);
+    s->copy = nullptr;
+  }
+  if (cleanup) *cleanup = c;
+  return BFVGPU_OK;
+}
+
+int32_t bfvgpu_rotations_release(bfvgpu_rotations* s) {
+  if (!s) return BFVGPU_OK;
+  bfvgpu_rotations_close(s, nullptr);
   delete s;
   return BFVGPU_OK;
 }

@@ -231,6 +231,34 @@ def test_keyswitch_hoisted_device(which, request, oracle):
         assert np.array_equal(got, exp), elt
 
 
+def test_rotations_object(cfg2, oracle):
+    """bfvgpu.Rotations (one upload, hoisted digits, every element streamed back) equals
+    Switch.apply_many per element and the oracle; a ciphertext with zero c1 words included."""
+    import bfvgpu
+    hc, oc = cfg2
+    n, k, dk = oc.n, oc.k, oc.data_k
+    count = 5
+    cts = oc.uniform(71, count * 2 * dk).reshape(count, 2, dk, n)
+    cts[2, 1, 1, ::7] = 0
+    elts = [3, pow(3, 5, 2 * n), 2 * n - 1]
+    keys = np.stack([oc.uniform(80 + i, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n) for i in range(len(elts))])
+    rot = bfvgpu.Rotations(hc, keys, elts)
+    try:
+        got = rot.apply(cts)
+        again = rot.apply(cts[:2])  # smaller batch on the same object
+    finally:
+        assert rot.close()["closed"]
+    for i, elt in enumerate(elts):
+        sw = bfvgpu.Switch(hc, keys[i], elt)
+        try:
+            ref = sw.apply_many(cts)
+        finally:
+            sw.close()
+        assert np.array_equal(got[i], ref), elt
+        assert np.array_equal(again[i], ref[:2]), elt
+    assert np.array_equal(got[0], oc.keyswitch_many(cts, keys[0], [elts[0]], threads=8)[0])
+
+
 def test_packing_pair(art, oracle):
     import bfvgpu
     hc, oc = art
