@@ -80,97 +80,111 @@ BFV_HD uint64_t reduce_4q(uint64_t v, uint64_t q) {
   return v;
 }
 
-// One radix-2^R Cooley-Tukey unit of forward pass starting at level L.
-template <int LOGN, int R, bool FIRST, bool LAST, class Ld, class St>
-BFV_HD void fwd_unit(uint64_t* s, int u, int L, const ulonglong2* tw, uint64_t q, const Ld& ld,
+// U radix-2^R Cooley-Tukey units of the forward pass starting at level L: units u0 + j*us
+// (j < U), interleaved so that one thread has U independent butterfly chains in flight.
+template <int LOGN, int R, bool FIRST, bool LAST, int U, class Ld, class St>
+BFV_HD void fwd_unit(uint64_t* s, int u0, int us, int L, const ulonglong2* tw, uint64_t q, const Ld& ld,
                      const St& st) {
   constexpr int K = 1 << R;
   const int shift = LOGN - L - R;  // smallest gap of the pass is 2^shift
-  const int o = u & ((1 << shift) - 1);
-  const int gl = u >> shift;
-  const int base = (gl << (LOGN - L)) + o;
-  const int sbase = spad(base);
-  uint64_t x[K];
+  int base[U], sbase[U], gl[U];
+  uint64_t x[U][K];
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int idx = base + (k << shift);
-    if constexpr (FIRST)
-      x[k] = ld(idx);
-    else
-      x[k] = s[spad_unit(base, sbase, k << shift)];
+  for (int j = 0; j < U; ++j) {
+    const int u = u0 + j * us;
+    const int o = u & ((1 << shift) - 1);
+    gl[j] = u >> shift;
+    base[j] = (gl[j] << (LOGN - L)) + o;
+    sbase[j] = spad(base[j]);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if constexpr (FIRST)
+        x[j][k] = ld(base[j] + (k << shift));
+      else
+        x[j][k] = s[spad_unit(base[j], sbase[j], k << shift)];
+    }
   }
   const uint64_t two_q = 2 * q;
 #pragma unroll
   for (int t = 0; t < R; ++t) {
     const int hs = R - t - 1;  // half = 2^hs pairs per twiddle group
-    ulonglong2 w = tw[(1 << (L + t)) + (gl << t)];
 #pragma unroll
     for (int pr = 0; pr < K / 2; ++pr) {
-      const int j = pr >> hs, kk = pr & ((1 << hs) - 1);
-      const int k = (j << (hs + 1)) + kk;
-      if (kk == 0 && j > 0) w = tw[(1 << (L + t)) + (gl << t) + j];
-      uint64_t a = x[k];
-      if (a >= two_q) a -= two_q;
-      const uint64_t b = shoup_lazy(x[k + (1 << hs)], w.x, w.y, q);
-      x[k] = a + b;
-      x[k + (1 << hs)] = a + two_q - b;
+      const int jj = pr >> hs, kk = pr & ((1 << hs) - 1);
+      const int k = (jj << (hs + 1)) + kk;
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const ulonglong2 w = tw[(1 << (L + t)) + (gl[j] << t) + jj];
+        uint64_t a = x[j][k];
+        if (a >= two_q) a -= two_q;
+        const uint64_t b = shoup_lazy(x[j][k + (1 << hs)], w.x, w.y, q);
+        x[j][k] = a + b;
+        x[j][k + (1 << hs)] = a + two_q - b;
+      }
     }
   }
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int idx = base + (k << shift);
-    if constexpr (LAST)
-      st(idx, reduce_4q(x[k], q));
-    else
-      s[spad_unit(base, sbase, k << shift)] = x[k];
-  }
+  for (int j = 0; j < U; ++j)
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if constexpr (LAST)
+        st(base[j] + (k << shift), reduce_4q(x[j][k], q));
+      else
+        s[spad_unit(base[j], sbase[j], k << shift)] = x[j][k];
+    }
 }
 
-// One radix-2^R Gentleman-Sande unit of inverse pass starting at level L.
-template <int LOGN, int R, bool FIRST, bool LAST, class Ld, class St>
-BFV_HD void inv_unit(uint64_t* s, int u, int L, const ulonglong2* tw, uint64_t q, uint64_t invn,
+// U radix-2^R Gentleman-Sande units of the inverse pass starting at level L.
+template <int LOGN, int R, bool FIRST, bool LAST, int U, class Ld, class St>
+BFV_HD void inv_unit(uint64_t* s, int u0, int us, int L, const ulonglong2* tw, uint64_t q, uint64_t invn,
                      uint64_t invn_q, const Ld& ld, const St& st) {
   constexpr int K = 1 << R;
   constexpr int N = 1 << LOGN;
-  const int o = u & ((1 << L) - 1);
-  const int gg = u >> L;
-  const int base = (gg << (L + R)) + o;
-  const int sbase = spad(base);
-  uint64_t x[K];
+  int base[U], sbase[U], gg[U];
+  uint64_t x[U][K];
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int idx = base + (k << L);
-    if constexpr (FIRST)
-      x[k] = ld(idx);
-    else
-      x[k] = s[spad_unit(base, sbase, k << L)];
+  for (int j = 0; j < U; ++j) {
+    const int u = u0 + j * us;
+    const int o = u & ((1 << L) - 1);
+    gg[j] = u >> L;
+    base[j] = (gg[j] << (L + R)) + o;
+    sbase[j] = spad(base[j]);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if constexpr (FIRST)
+        x[j][k] = ld(base[j] + (k << L));
+      else
+        x[j][k] = s[spad_unit(base[j], sbase[j], k << L)];
+    }
   }
   const uint64_t two_q = 2 * q;
 #pragma unroll
   for (int t = 0; t < R; ++t) {
     const int l = L + t;
-    const int root0 = N - (N >> l) + 1 + (gg << (R - t - 1));
-    ulonglong2 w = tw[root0];
 #pragma unroll
     for (int pr = 0; pr < K / 2; ++pr) {
-      const int j = pr >> t, kk = pr & ((1 << t) - 1);
-      const int k = (j << (t + 1)) + kk;
-      if (kk == 0 && j > 0) w = tw[root0 + j];
-      const uint64_t a = x[k], b = x[k + (1 << t)];
-      uint64_t sum = a + b;
-      if (sum >= two_q) sum -= two_q;
-      x[k] = sum;
-      x[k + (1 << t)] = shoup_lazy(a + two_q - b, w.x, w.y, q);
+      const int jj = pr >> t, kk = pr & ((1 << t) - 1);
+      const int k = (jj << (t + 1)) + kk;
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const ulonglong2 w = tw[N - (N >> l) + 1 + (gg[j] << (R - t - 1)) + jj];
+        const uint64_t a = x[j][k], b = x[j][k + (1 << t)];
+        uint64_t sum = a + b;
+        if (sum >= two_q) sum -= two_q;
+        x[j][k] = sum;
+        x[j][k + (1 << t)] = shoup_lazy(a + two_q - b, w.x, w.y, q);
+      }
     }
   }
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int idx = base + (k << L);
-    if constexpr (LAST)
-      st(idx, shoup(x[k], invn, invn_q, q));
-    else
-      s[spad_unit(base, sbase, k << L)] = x[k];
-  }
+  for (int j = 0; j < U; ++j)
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if constexpr (LAST)
+        st(base[j] + (k << L), shoup(x[j][k], invn, invn_q, q));
+      else
+        s[spad_unit(base[j], sbase[j], k << L)] = x[j][k];
+    }
 }
 
 // Executors: device (threads of one block + __syncthreads) and host (all units in turn).
@@ -180,6 +194,17 @@ struct BlockExec {
   __device__ __forceinline__ void run(int units, F&& f) const {
     for (int u = threadIdx.x; u < units; u += blockDim.x) f(u);
   }
+  // f(u0, us) covers units u0 and u0 + us; every unit once when units % (2 blockDim) == 0,
+  // else each unit alone through f1(u).
+  template <class F2, class F1>
+  __device__ __forceinline__ void run2(int units, F2&& f2, F1&& f1) const {
+    const int t = blockDim.x;
+    if (units % (2 * t) == 0) {
+      for (int u = threadIdx.x; u < units; u += 2 * t) f2(u, t);
+    } else {
+      for (int u = threadIdx.x; u < units; u += t) f1(u);
+    }
+  }
   __device__ __forceinline__ void sync() const { __syncthreads(); }
 };
 #endif
@@ -188,7 +213,24 @@ struct HostExec {
   void run(int units, F&& f) const {
     for (int u = 0; u < units; ++u) f(u);
   }
+  // the pairs of a block of units/2 threads: (u, u + units/2)
+  template <class F2, class F1>
+  void run2(int units, F2&& f2, F1&& f1) const {
+    if (units % 2 == 0) {
+      const int t = units / 2;
+      for (int u = 0; u < t; ++u) f2(u, t);
+    } else {
+      for (int u = 0; u < units; ++u) f1(u);
+    }
+  }
   void sync() const {}
+};
+
+// Units per thread per pass: two interleaved units at n = 16384 (one 512-thread block per SM,
+// registers to spare); one below, where three blocks share an SM under an 80-register cap.
+template <int LOGN>
+struct DualUnits {
+  static constexpr bool value = LOGN >= 14;
 };
 
 template <int LOGN, int MAXR, int P, class Ex, class Ld, class St>
@@ -199,7 +241,12 @@ BFV_HD void fwd_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t
     constexpr int R = S::fwd_r(P);
     constexpr int L = S::fwd_level(P);
     constexpr bool first = P == 0, last = P == S::passes - 1;
-    ex.run(1 << (LOGN - R), [&](int u) { fwd_unit<LOGN, R, first, last>(s, u, L, tw, q, ld, st); });
+    if constexpr (DualUnits<LOGN>::value)
+      ex.run2(
+          1 << (LOGN - R), [&](int u0, int us) { fwd_unit<LOGN, R, first, last, 2>(s, u0, us, L, tw, q, ld, st); },
+          [&](int u) { fwd_unit<LOGN, R, first, last, 1>(s, u, 0, L, tw, q, ld, st); });
+    else
+      ex.run(1 << (LOGN - R), [&](int u) { fwd_unit<LOGN, R, first, last, 1>(s, u, 0, L, tw, q, ld, st); });
     ex.sync();
     fwd_passes<LOGN, MAXR, P + 1>(ex, s, tw, q, ld, st);
   }
@@ -213,8 +260,14 @@ BFV_HD void inv_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t
     constexpr int R = S::inv_r(P);
     constexpr int L = S::inv_level(P);
     constexpr bool first = P == 0, last = P == S::passes - 1;
-    ex.run(1 << (LOGN - R),
-           [&](int u) { inv_unit<LOGN, R, first, last>(s, u, L, tw, q, invn, invn_q, ld, st); });
+    if constexpr (DualUnits<LOGN>::value)
+      ex.run2(
+          1 << (LOGN - R),
+          [&](int u0, int us) { inv_unit<LOGN, R, first, last, 2>(s, u0, us, L, tw, q, invn, invn_q, ld, st); },
+          [&](int u) { inv_unit<LOGN, R, first, last, 1>(s, u, 0, L, tw, q, invn, invn_q, ld, st); });
+    else
+      ex.run(1 << (LOGN - R),
+             [&](int u) { inv_unit<LOGN, R, first, last, 1>(s, u, 0, L, tw, q, invn, invn_q, ld, st); });
     ex.sync();
     inv_passes<LOGN, MAXR, P + 1>(ex, s, tw, q, invn, invn_q, ld, st);
   }
