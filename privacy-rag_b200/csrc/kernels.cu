@@ -224,8 +224,27 @@ __device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %0;" ::"r"(bytes), "r"(bar) : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Barrier `id` over `count` threads that also ORs `pred` across them.
+__device__ __forceinline__ bool bar_or(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(count) : "memory");
+  return r != 0;
+}
+
+// Warp roles: warps 0-7 drain TMEM buffer 0 (M-block 0, tiles 0-3), warps 8-15 buffer 1
+// (M-block 1, tiles 4-7), lane 0 of warp 16 loads operands and issues the MMAs.  Round R =
+// ((unit * 8 + slot pair) * 2 + group round) * 2 + M-block; round R uses TMEM buffer R % 2, so
+// the MMA of one M-block runs while the other consumer group recombines.
+constexpr int kMacTcThreads = 17 * 32;
+
 template <int KPAD>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(kMacTcThreads, 1)
     k_mac_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, uint64_t* out,
              uint32_t groups, uint32_t gchunks, uint32_t units, uint32_t dk, int logn, const Modulus* mods,
              uint32_t* err) {
@@ -236,16 +255,20 @@ __global__ void __launch_bounds__(512, 1)
   uint8_t* sm = smem_raw + (base - raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t N = 1u << logn, zblocks = N / tc::kSlots;
-  const uint32_t barA = base + S::kBar, barB = barA + 16, barM = barA + 32;  // [2], [2], [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kBar + 40);
+  // barriers: fullA[2], fullB[2], mma_done[2], tmem_free[2]; then the TMEM base and an abort flag
+  const uint32_t barA = base + S::kBar, barB = barA + 16, barM = barA + 32, barF = barA + 48;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + S::kBar + 64);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(sm + S::kBar + 68);
   const uint64_t pA = reinterpret_cast<uint64_t>(&tmA), pB = reinterpret_cast<uint64_t>(&tmB);
 
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(base + S::kBar + 40));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(base + S::kBar + 64));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    for (uint32_t b = 0; b < 5; ++b) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(barA + 8 * b) : "memory");
+    for (uint32_t b = 0; b < 6; ++b) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(barA + 8 * b) : "memory");
+    for (uint32_t b = 0; b < 2; ++b) asm volatile("mbarrier.init.shared::cta.b64 [%0], 256;" ::"r"(barF + 8 * b) : "memory");
+    *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -254,146 +277,146 @@ __global__ void __launch_bounds__(512, 1)
   const uint32_t tmem = *tmem_slot;
 
   const uint32_t my_units = blockIdx.x < units ? (units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const uint32_t rounds = my_units * tc::kRoundsPerUnit;
-  // round R -> unit, slot pair (global pair index R / kRoundsPerPair), group round
+  constexpr uint32_t kRoundsPerUnit = tc::kRoundsPerUnit * 2;  // x 2 M-blocks
+  const uint32_t rounds = my_units * kRoundsPerUnit;
+  // round R -> unit coordinates, slot pair zp, group round gr (M-block = R % 2)
   auto coords = [&](uint32_t R, uint32_t* gc, uint32_t* p, uint32_t* z0, uint32_t* zp, uint32_t* gr) {
-    const uint32_t u = blockIdx.x + (R / tc::kRoundsPerUnit) * gridDim.x;
+    const uint32_t u = blockIdx.x + (R / kRoundsPerUnit) * gridDim.x;
     tc::unit_coords(u, gchunks, zblocks, gc, p, z0);
-    const uint32_t rr = R % tc::kRoundsPerUnit;
+    const uint32_t rr = (R % kRoundsPerUnit) >> 1;
     *zp = rr / tc::kRoundsPerPair;
     *gr = rr % tc::kRoundsPerPair;
   };
-  auto load_a = [&](uint32_t P) {  // slot pair P (global index) -> A buffer P % 2
-    uint32_t gc, p, z0, zp, gr;
-    coords(P * tc::kRoundsPerPair, &gc, &p, &z0, &zp, &gr);
-    const uint32_t bar = barA + 8 * (P & 1), z = z0 + zp * tc::kPair;
-    mbar_expect(bar, 2 * S::kABox);
-#pragma unroll
-    for (uint32_t mb = 0; mb < 2; ++mb)
-      asm volatile(
-          "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
-          ::"r"(base + S::kA + (P & 1) * S::kABuf + mb * S::kABox), "l"(pA), "r"((int)z), "r"(0), "r"(0),
-          "r"((int)(4 * mb)), "r"((int)p), "r"(bar) : "memory");
-  };
-  auto load_b = [&](uint32_t R) {  // round R -> B buffer R % 2
-    uint32_t gc, p, z0, zp, gr;
-    coords(R, &gc, &p, &z0, &zp, &gr);
-    const uint32_t bar = barB + 8 * (R & 1), z = z0 + zp * tc::kPair;
-    mbar_expect(bar, S::kBBox);
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
-        ::"r"(base + S::kB + (R & 1) * S::kBBox), "l"(pB), "r"((int)z), "r"(0),
-        "r"((int)(gc * tc::kGroups + gr * tc::kGroupsRound)), "r"((int)p), "r"(bar) : "memory");
-  };
-  auto issue_mma = [&](uint32_t R) {
-    const uint32_t P = R / tc::kRoundsPerPair;
-#pragma unroll
-    for (uint32_t mb = 0; mb < 2; ++mb)
-#pragma unroll
-      for (uint32_t kk = 0; kk < KPAD / 32; ++kk) {
-        const uint64_t ad = tc::a_desc<KPAD>(base, P & 1, mb, kk), bd = tc::b_desc<KPAD>(base, R & 1, kk);
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem + 256 * mb),
-            "l"(ad), "l"(bd), "r"(tc::kIdesc), "r"(kk) : "memory");
-      }
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(barM)
-                 : "memory");
-  };
 
-  // producer state (thread 0 only): next pair / round whose loads are to be issued
-  bool failed = false;
-  if (tid == 0 && rounds) {
-    load_a(0);
-    load_b(0);
-    if (rounds > 1) load_b(1);
-  }
-  const uint32_t quarter = warp & 3, mb = warp >> 3, gh = (warp >> 2) & 1;
-  const uint32_t m = quarter * 32 + lane, tc4 = m >> 4, zs = (m >> 3) & 1, i = m & 7;
-  const uint32_t tcx = mb * 8 + tc4;
-  for (uint32_t R = 0; R < rounds; ++R) {
-    const uint32_t P = R / tc::kRoundsPerPair;
-    const bool first_of_pair = (R % tc::kRoundsPerPair) == 0;
-    if (tid == 0) {
+  if (warp == 16) {
+    // ---- producer: TMA loads and MMA issue ----
+    if (lane == 0 && rounds) {
+      auto load_a = [&](uint32_t P) {  // slot pair P (block-local index) -> A buffer P % 2
+        uint32_t gc, p, z0, zp, gr;
+        coords(P * 4, &gc, &p, &z0, &zp, &gr);
+        const uint32_t bar = barA + 8 * (P & 1), z = z0 + zp * tc::kPair;
+        mbar_expect(bar, 2 * S::kABox);
+#pragma unroll
+        for (uint32_t mb = 0; mb < 2; ++mb)
+          asm volatile(
+              "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+              ::"r"(base + S::kA + (P & 1) * S::kABuf + mb * S::kABox), "l"(pA), "r"((int)z), "r"(0), "r"(0),
+              "r"((int)(4 * mb)), "r"((int)p), "r"(bar) : "memory");
+      };
+      auto load_b = [&](uint32_t Q) {  // (pair, group round) Q -> B buffer Q % 2
+        uint32_t gc, p, z0, zp, gr;
+        coords(Q * 2, &gc, &p, &z0, &zp, &gr);
+        const uint32_t bar = barB + 8 * (Q & 1), z = z0 + zp * tc::kPair;
+        mbar_expect(bar, S::kBBox);
+        asm volatile(
+            "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+            ::"r"(base + S::kB + (Q & 1) * S::kBBox), "l"(pB), "r"((int)z), "r"(0),
+            "r"((int)(gc * tc::kGroups + gr * tc::kGroupsRound)), "r"((int)p), "r"(bar) : "memory");
+      };
+      const uint32_t pairs = rounds / 4, qs = rounds / 2;
+      load_a(0);
+      load_b(0);
       bool ok = true;
-      if (first_of_pair) {
-        ok = mbar_wait(barA + 8 * (P & 1), (P >> 1) & 1);
-        // the other A buffer was last read by pair P - 1, whose MMAs have completed
-        if (ok && (P + 1) * tc::kRoundsPerPair < rounds) load_a(P + 1);
-      }
-      ok = ok && mbar_wait(barB + 8 * (R & 1), (R >> 1) & 1);
-      if (ok) {
+      for (uint32_t R = 0; R < rounds && ok; ++R) {
+        const uint32_t mb = R & 1, Q = R >> 1, P = R >> 2;
+        if (mb == 0) {
+          if ((R & 3) == 0) ok = ok && mbar_wait(barA + 8 * (P & 1), (P >> 1) & 1);
+          ok = ok && mbar_wait(barB + 8 * (Q & 1), (Q >> 1) & 1);
+          // the buffers for the next pair / group round were last read by round R - 1
+          if (ok && R >= 1) ok = mbar_wait(barM + 8 * ((R - 1) & 1), ((R - 1) >> 1) & 1);
+          if (ok && (R & 3) == 0 && P + 1 < pairs) load_a(P + 1);
+          if (ok && Q + 1 < qs) load_b(Q + 1);
+        }
+        // the consumer of this TMEM buffer has finished round R - 2
+        if (ok && R >= 2) ok = mbar_wait(barF + 8 * mb, ((R >> 1) - 1) & 1);
+        if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        issue_mma(R);
-      } else {
-        failed = true;
+#pragma unroll
+        for (uint32_t kk = 0; kk < KPAD / 32; ++kk) {
+          const uint64_t ad = tc::a_desc<KPAD>(base, P & 1, mb, kk), bd = tc::b_desc<KPAD>(base, Q & 1, kk);
+          asm volatile(
+              "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem + 256 * mb),
+              "l"(ad), "l"(bd), "r"(tc::kIdesc), "r"(kk) : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(barM + 8 * mb)
+                     : "memory");
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(err, kErrMmaTimeout);
       }
     }
-    const bool ok = tid == 0 ? !failed : true;
-    if (__syncthreads_or(!ok)) {
-      failed = true;
-      break;
-    }
-    const bool done = mbar_wait(barM, R & 1);
-    if (__syncthreads_or(!done)) {
-      failed = true;
-      break;
-    }
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (tid == 0 && R + 2 < rounds) load_b(R + 2);  // B buffer R % 2 is free again
-    uint32_t gc, p, z0, zp, gr;
-    coords(R, &gc, &p, &z0, &zp, &gr);
-    const Modulus& mod = mods[p];
-    uint64_t vlo[8], vhi[8];
-#pragma unroll
-    for (uint32_t h = 0; h < 4; ++h) {
-      uint32_t D[32];
-      const uint32_t taddr = tmem + ((quarter * 32) << 16) + 256 * mb + 128 * gh + 32 * h;
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-          : "=r"(D[0]), "=r"(D[1]), "=r"(D[2]), "=r"(D[3]), "=r"(D[4]), "=r"(D[5]), "=r"(D[6]), "=r"(D[7]),
-            "=r"(D[8]), "=r"(D[9]), "=r"(D[10]), "=r"(D[11]), "=r"(D[12]), "=r"(D[13]), "=r"(D[14]),
-            "=r"(D[15]), "=r"(D[16]), "=r"(D[17]), "=r"(D[18]), "=r"(D[19]), "=r"(D[20]), "=r"(D[21]),
-            "=r"(D[22]), "=r"(D[23]), "=r"(D[24]), "=r"(D[25]), "=r"(D[26]), "=r"(D[27]), "=r"(D[28]),
-            "=r"(D[29]), "=r"(D[30]), "=r"(D[31])
-          : "r"(taddr));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      tc::lane_values2(D, zs, i, vlo + 2 * h, vhi + 2 * h);
-    }
-    // reduce-scatter over the 8 lanes of one (tc, zs): lane i ends with group k = i
-#pragma unroll
-    for (int lev = 4; lev >= 1; lev >>= 1) {
-      const bool sel = i & lev;
-#pragma unroll
-      for (int q = 0; q < lev; ++q) {
-        const uint64_t kl = sel ? vlo[q + lev] : vlo[q], kh = sel ? vhi[q + lev] : vhi[q];
-        const uint64_t sl = sel ? vlo[q] : vlo[q + lev], sh = sel ? vhi[q] : vhi[q + lev];
-        vlo[q] = kl;
-        vhi[q] = kh;
-        tc::add128(vlo[q], vhi[q], __shfl_xor_sync(0xffffffffu, sl, lev), __shfl_xor_sync(0xffffffffu, sh, lev));
-      }
-    }
+  } else {
+    // ---- consumers: group g drains TMEM buffer g (M-block g) every other round ----
+    const uint32_t g = warp >> 3, wq = warp & 7;
+    const uint32_t quarter = wq & 3, gh = wq >> 2;
+    const uint32_t m = quarter * 32 + lane, tc4 = m >> 4, zs = (m >> 3) & 1, i = m & 7;
+    const uint32_t tcx = g * 8 + tc4;
     uint64_t* ob = reinterpret_cast<uint64_t*>(sm + S::kOut);
-    ob[tc::out_buf_word(zp * tc::kPair + zs, tcx, gr * tc::kGroupsRound + gh * 8 + i)] = reduce128(vlo[0], vhi[0], mod);
-    if (R % tc::kRoundsPerUnit == tc::kRoundsPerUnit - 1) {
-      __syncthreads();
-      const uint32_t rtc = tid >> 5, rgl = tid & 31, g = gc * tc::kGroups + rgl;
-      if (g < groups) {
-        uint64_t* dst = out + tc::out_row(rtc, g, groups, p, z0, dk, N);
+    for (uint32_t R = g; R < rounds; R += 2) {
+      const bool done = mbar_wait(barM + 8 * g, (R >> 1) & 1) && !*abort_flag;
+      if (bar_or(1 + g, 256, !done)) {
+        if (threadIdx.x == 0) atomicOr(err, kErrMmaTimeout);
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      uint32_t gc, p, z0, zp, gr;
+      coords(R, &gc, &p, &z0, &zp, &gr);
+      const Modulus& mod = mods[p];
+      uint64_t vlo[8], vhi[8];
 #pragma unroll
-        for (int zz = 0; zz < tc::kSlots; zz += 2) {
-          ulonglong2 v;
-          v.x = ob[tc::out_buf_word(zz, rtc, rgl)];
-          v.y = ob[tc::out_buf_word(zz + 1, rtc, rgl)];
-          *reinterpret_cast<ulonglong2*>(dst + zz) = v;
+      for (uint32_t h = 0; h < 4; ++h) {
+        uint32_t D[32];
+        const uint32_t taddr = tmem + ((quarter * 32) << 16) + 256 * g + 128 * gh + 32 * h;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(D[0]), "=r"(D[1]), "=r"(D[2]), "=r"(D[3]), "=r"(D[4]), "=r"(D[5]), "=r"(D[6]), "=r"(D[7]),
+              "=r"(D[8]), "=r"(D[9]), "=r"(D[10]), "=r"(D[11]), "=r"(D[12]), "=r"(D[13]), "=r"(D[14]),
+              "=r"(D[15]), "=r"(D[16]), "=r"(D[17]), "=r"(D[18]), "=r"(D[19]), "=r"(D[20]), "=r"(D[21]),
+              "=r"(D[22]), "=r"(D[23]), "=r"(D[24]), "=r"(D[25]), "=r"(D[26]), "=r"(D[27]), "=r"(D[28]),
+              "=r"(D[29]), "=r"(D[30]), "=r"(D[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        tc::lane_values2(D, zs, i, vlo + 2 * h, vhi + 2 * h);
+      }
+      // TMEM buffer g is free once every thread of the group has its values in registers
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(barF + 8 * g);
+      // reduce-scatter over the 8 lanes of one (tc, zs): lane i ends with group k = i
+#pragma unroll
+      for (int lev = 4; lev >= 1; lev >>= 1) {
+        const bool sel = i & lev;
+#pragma unroll
+        for (int q = 0; q < lev; ++q) {
+          const uint64_t kl = sel ? vlo[q + lev] : vlo[q], kh = sel ? vhi[q + lev] : vhi[q];
+          const uint64_t sl = sel ? vlo[q] : vlo[q + lev], sh = sel ? vhi[q] : vhi[q + lev];
+          vlo[q] = kl;
+          vhi[q] = kh;
+          tc::add128(vlo[q], vhi[q], __shfl_xor_sync(0xffffffffu, sl, lev), __shfl_xor_sync(0xffffffffu, sh, lev));
         }
       }
+      ob[tc::out_buf_word(zp * tc::kPair + zs, tcx, gr * tc::kGroupsRound + gh * 8 + i)] = reduce128(vlo[0], vhi[0], mod);
+      if ((R % kRoundsPerUnit) + 2 >= kRoundsPerUnit) {  // this group's last round of the unit
+        asm volatile("bar.sync %0, 256;" ::"r"(1 + g) : "memory");
+        // flush the group's rows: tc in [8 g, 8 g + 8) x 32 groups, one row per thread
+        const uint32_t t8 = (warp & 7) * 32 + lane, rtc = g * 8 + (t8 >> 5), rgl = t8 & 31;
+        const uint32_t gg = gc * tc::kGroups + rgl;
+        if (gg < groups) {
+          uint64_t* dst = out + tc::out_row(rtc, gg, groups, p, z0, dk, N);
+#pragma unroll
+          for (int zz = 0; zz < tc::kSlots; zz += 2) {
+            ulonglong2 v;
+            v.x = ob[tc::out_buf_word(zz, rtc, rgl)];
+            v.y = ob[tc::out_buf_word(zz + 1, rtc, rgl)];
+            *reinterpret_cast<ulonglong2*>(dst + zz) = v;
+          }
+        }
+        asm volatile("bar.sync %0, 256;" ::"r"(1 + g) : "memory");
+      }
     }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();  // TMEM and the output buffer are free for the next round
   }
-  if (failed && tid == 0) atomicOr(err, kErrMmaTimeout);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0) {
@@ -889,7 +912,7 @@ static cudaError_t mac_tc_launch(const DevParams& P, const uint64_t* in, uint64_
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   const unsigned grid = (unsigned)(units < (uint64_t)sms ? units : (uint64_t)sms);
-  k_mac_tc<KPAD><<<grid, tc::kThreads, tc::Smem<KPAD>::kLaunchBytes, st>>>(
+  k_mac_tc<KPAD><<<grid, kMacTcThreads, tc::Smem<KPAD>::kLaunchBytes, st>>>(
       a, b, out, (uint32_t)groups, (uint32_t)gchunks, (uint32_t)units, P.dk, P.logn, P.mod, P.err);
   return cudaGetLastError();
 }

@@ -50,8 +50,8 @@ struct Smem {
   static constexpr uint32_t kB = kA + 2 * kABuf;                // [2 buffers] boxes
   static constexpr uint32_t kOut = kB + 2 * kBBox;              // [16 z][16 tc][32 g] u64
   static constexpr uint32_t kOutBytes = kSlots * 16 * kGroups * 8;
-  static constexpr uint32_t kBar = kOut + kOutBytes;            // fullA[2], fullB[2], mma, TMEM base
-  static constexpr uint32_t kBytes = kBar + 48;
+  static constexpr uint32_t kBar = kOut + kOutBytes;            // 8 mbarriers, TMEM base, abort flag
+  static constexpr uint32_t kBytes = kBar + 80;
   // Requested dynamic size: slack for the 1024-byte alignment, and above half an SM's shared
   // memory so that one block holds an SM (and all 512 TMEM columns) alone.
   static constexpr uint32_t kLaunchBytes = (kBytes + 1024) > 120 * 1024 ? (kBytes + 1024) : 120 * 1024;
