@@ -108,6 +108,22 @@ class LayerServer:
                 self.w_ntt[p.name] = w
             self.ctx.weights_ntt_device(ring, p.groups * p.inputs, w, stream=stream)
 
+    def prepare_weights_from(self, weights, layer: int, rows_of=None, stream=None) -> None:
+        """Lift + NTT the calls of decoder layer `layer` from a QuantizedWeights set (the
+        reference's quantized f12 directory).  rows_of(projection) -> (lo, hi) selects a shard
+        of each call's stacked rows (default: all of them)."""
+        from .weights import ring_words
+        rings = {}
+        calls = dict(weights.layer_calls(layer))
+        for p in self.proj:
+            mats = calls[p.name]
+            rows = rows_of(p) if rows_of else None
+            w = self.torch.from_numpy(ring_words(mats, rows)).to(self.pk.device)
+            if w.shape != (p.outputs, p.inner):
+                raise ValueError("BAD_SHAPE")
+            rings[p.name] = pack_weights_device(self.torch, w, p, self.ctx.n)
+        self.prepare_weights(rings, stream=stream)
+
     def output(self, p: Projection):
         """[tiles][G][2][dk][n] view of the last run of projection p."""
         n, dk = self.ctx.n, self.ctx.dk

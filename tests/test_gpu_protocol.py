@@ -174,3 +174,32 @@ def test_layer_server_tiles_decrypt(bfv, oracle, setup, tiles):
                     assert np.array_equal(sel[e, :, i], out[t, g, 0, :, z])
                     v = sum(int(crt[e, i, l]) << (64 * l) for l in range(dk))
                     assert v == oracle.crt(out[t, g, 0, :, z], oc.primes[:dk])
+
+
+def test_layer_weights_from_quantized_directory(bfv, oracle, setup, tmp_path):
+    """LayerServer.prepare_weights_from: a quantized f12 layer (the reference's checkpoint
+    format) stacked per joint call, packed, lifted and transformed on the GPU equals the
+    oracle's lift + NTT of the reference packing (layout.pack_weights of the reader blocks)
+    for sampled (call, group, block) pairs."""
+    import torch
+    import test_weights as TW
+    from bfvgpu import layer as L
+    from bfvgpu import weights as W
+    from bfvgpu.layout import pack_weights
+    hc, oc, tb = setup
+    n, dk = oc.n, oc.data_k
+    TW.write_layer(str(tmp_path), seed=11)
+    qw = W.QuantizedWeights(str(tmp_path))
+    pk = torch.from_numpy(tb.pk.view(np.int64)).cuda()
+    srv = L.LayerServer(torch, hc, pk, L.QWEN3_06B_LAYER, 16, 1)
+    srv.prepare_weights_from(qw, 0)
+    torch.cuda.synchronize()
+    calls = dict(qw.layer_calls(0))
+    for p, g, b in [(srv.proj[0], 0, 0), (srv.proj[0], 127, 63), (srv.proj[2], 64, 17), (srv.proj[3], 5, 47)]:
+        rows = W.ring_words(calls[p.name], (g * p.cap, min((g + 1) * p.cap, p.outputs))).astype(np.uint64)
+        block = rows[:, b * p.d:(b + 1) * p.d]
+        ring = pack_weights([block], p.d, p.batch, n)
+        lifted = oc.lift(ring)[0]
+        expect = oc.ntt(lifted, prime_count=dk)
+        got = srv.w_ntt[p.name][g, b].cpu().numpy().view(np.uint64)
+        assert np.array_equal(got, expect), (p.name, g, b)
