@@ -198,11 +198,15 @@ def cpu_layer_sample(seconds: float = 15.0):
 
 
 def cpu_call_ms(rates, open_rate, projections, tiles):
-    """Extrapolated CPU time (ms) of `tiles` tiles of the given Projection calls."""
+    """Extrapolated CPU time (ms) of `tiles` tiles of the given Projection calls: a group's
+    time is fitted as a + b * inputs through the sampled shapes (least squares)."""
+    xs = np.array(sorted(rates), dtype=np.float64)
+    ys = np.array([1.0 / rates[x] for x in sorted(rates)])
+    b, a = np.polyfit(xs, ys, 1)
     total = 0.0
     for p in projections:
-        rate = rates.get(p.inputs) or min(rates.values()) * 64 / p.inputs
-        total += tiles * (p.groups / rate + p.inputs / open_rate)
+        per_group = 1.0 / rates[p.inputs] if p.inputs in rates else max(a + b * p.inputs, 1e-9)
+        total += tiles * (p.groups * per_group + p.inputs / open_rate)
     return 1e3 * total
 
 
@@ -232,7 +236,12 @@ def run_layer_legs(torch, bfvgpu, device, args):
 
     pk = residues((2, k, n), k)
     out = {}
-    legs = (("config3", (("q_proj", 1024, 2048),), 1, 1), ("config4", L.QWEN3_06B_LAYER, 16, args.layer_tiles))
+    # attention: one head's shared-matrix pair for one 16-row block (BatchOps::matrix,
+    # batch_matrix.inc:83-118): scores (16 x 128) . K^T (128 -> 1280), then probabilities
+    # (16 x 1280) . V (1280 -> 128); both "weight" operands are fresh shares per call, so the
+    # step transforms them every time (nothing cached)
+    legs = (("config3", (("q_proj", 1024, 2048),), 1, 1), ("config4", L.QWEN3_06B_LAYER, 16, args.layer_tiles),
+            ("attention", (("scores", 128, 1280), ("values", 1280, 128)), 16, 1))
     if getattr(args, "layer_shape", None):
         kk, oo = (int(v) for v in args.layer_shape.split(","))
         legs = (("probe", (("probe", kk, oo),), 16, args.layer_tiles),)
@@ -260,7 +269,7 @@ def run_layer_legs(torch, bfvgpu, device, args):
 
         step()
         torch.cuda.synchronize()
-        reps = 3 if label == "config3" else 1
+        reps = 1 if label in ("config4", "probe") else 3
         evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2 + len(srv.proj))] for _ in range(reps)]
         for r in range(reps):
             evs[r][0].record(stream)
@@ -271,7 +280,9 @@ def run_layer_legs(torch, bfvgpu, device, args):
         per = [sum(e[1 + i].elapsed_time(e[2 + i]) for e in evs) / reps for i in range(len(srv.proj))]
         weight_ntts = sum(p.groups * p.inputs * dk for p in srv.proj)
         mac = tiles * sum(p.groups * p.inputs * 2 * dk * n for p in srv.proj)
-        out[label] = {"ms": ms, "unit": "ms per matvec" if label == "config3" else "ms per layer (all tiles)",
+        unit = {"config3": "ms per matvec", "attention": "ms per head and 16-row block (2 calls)"}.get(
+            label, "ms per layer (all tiles)")
+        out[label] = {"ms": ms, "unit": unit,
                       "ms_weights_ntt": w_ms, "ms_with_cached_weights": ms - w_ms,
                       "ms_per_call": {p.name: per[i] for i, p in enumerate(srv.proj)},
                       "tiles": tiles, "batch": batch,
@@ -756,6 +767,10 @@ def main():
             def base(ms, unit):
                 return {"value": ms, "unit": unit, "cores": lcores, "kind": "port", "sample": lsample}
 
+            if layer_res and "attention" in layer_res:
+                att = [L.plan("scores", 16, 128, 1280), L.plan("values", 16, 1280, 128)]
+                layer_res["attention"]["cpu_baseline"] = base(cpu_call_ms(rates, open_rate, att, 1),
+                                                              "ms per head and 16-row block (2 calls)")
             if layer_res:
                 layer_res["config3"]["cpu_baseline"] = base(
                     cpu_call_ms(rates, open_rate, [L.plan("q_proj", 1, 1024, 2048)], 1), "ms per matvec")
@@ -793,6 +808,7 @@ def main():
                                               "matches_hoisted": plain_match},
                       "matvec_config3": layer_res and layer_res["config3"],
                       "layer_config4": layer_res and layer_res["config4"],
+                      "attention_pair": layer_res and layer_res.get("attention"),
                       "model_config5": model_res,
                       "ntt": {"value": ntts_per_s, "unit": "NTTs/s",
                               "config": "config1: n=4096, primes 36/36/37-bit, 384 limb-polys fwd+inv",

@@ -125,21 +125,25 @@ def test_public_shape_rejections(bfv):
             engine.validate(shape, outputs, fx, fw, linear=linear)
 
 
-@pytest.mark.parametrize("tiles", [3, 8])
-def test_layer_server_tiles_decrypt(bfv, oracle, setup, tiles):
-    """LayerServer (multi-tile product, folded Enc(0), mask, target gather with CRT) on two
-    small projections and three token tiles: every target decrypts to sum_j x.w minus the
-    mask at that coefficient (mod 2^59), and the gathered c0 residues and CRT limbs are the
-    output ciphertext's own."""
+@pytest.mark.parametrize("tiles,batch,projections", [
+    (3, 2, (("a", 300, 200), ("b", 130, 600))),
+    (8, 2, (("a", 300, 200), ("b", 130, 600))),
+    # one head's attention pair (BatchOps::matrix shapes): 16 x 128 . 128 x 1280, 16 x 1280 . 1280 x 128
+    (1, 16, (("scores", 128, 1280), ("values", 1280, 128))),
+])
+def test_layer_server_tiles_decrypt(bfv, oracle, setup, tiles, batch, projections):
+    """LayerServer (multi-tile product, folded Enc(0), mask, target gather with CRT) on small
+    projections over 3 and 8 token tiles (8: the tensor-core product) and on one attention
+    head pair: every target decrypts to sum_j x.w minus the mask at that coefficient (mod
+    2^59), and the gathered c0 residues and CRT limbs are the output ciphertext's own."""
     import torch
     from bfvgpu import layer as L
     from bfvgpu.layout import MASK59, pack_inputs
     hc, oc, tb = setup
     n, k, dk = oc.n, oc.k, oc.data_k
-    batch = 2
     rng = np.random.default_rng(77)
     pk = torch.from_numpy(tb.pk.view(np.int64)).cuda()
-    srv = L.LayerServer(torch, hc, pk, (("a", 300, 200), ("b", 130, 600)), batch, tiles)
+    srv = L.LayerServer(torch, hc, pk, projections, batch, tiles)
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int64)).cuda()
     rings, w_int = {}, {}
     for p in srv.proj:
