@@ -361,6 +361,8 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
                                     small((T, max(p.groups, 1), 2, n), -5, 5)], dim=2) for p in projs})
 
     multi = bool(dist) and world > 1
+    if multi:
+        ctx.set_reserved_sms(8)  # room for NCCL's kernels beside the persistent products
     # inputs are double-buffered so the broadcast of call c+1 overlaps call c; broadcasts and
     # result gathers use separate communicators so neither queues behind the other
     cts_pre, masks_pre, samples_pre = call_buffers(sh_pre, tiles, 2 if multi else 1)

@@ -171,6 +171,10 @@ int32_t bfvgpu_matrix_groups_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_
  * BFVGPU_E_CUDA when any bit was set.  No counterpart in the reference (its kernels have
  * no waits). */
 int32_t bfvgpu_ctx_check(bfvgpu_ctx *ctx, uint32_t *flags);
+/* Leaves `sms` streaming multiprocessors out of the persistent product kernels' grids (0 by
+ * default), so that a collective running beside them (NCCL broadcasts and gathers of a
+ * sharded call) finds free SMs.  Results are unchanged. */
+int32_t bfvgpu_ctx_set_reserved_sms(bfvgpu_ctx *ctx, int32_t sms);
 /* Selects the ct-pt product of bfvgpu_matrix_tiles_device: 0 (default) = tcgen05 kind::i8
  * for launches of 8 tiles with at most 64 input blocks, CUDA cores otherwise; 1 = CUDA
  * cores always.  Results are identical. */

@@ -174,6 +174,10 @@ class Context:
         check(lib().bfvgpu_ctx_check(self._h, ctypes.byref(flags)), "ctx_check")
         return int(flags.value)
 
+    def set_reserved_sms(self, sms: int) -> None:
+        """SMs the persistent product kernels leave free (for collectives running beside them)."""
+        check(lib().bfvgpu_ctx_set_reserved_sms(self._h, sms), "set_reserved_sms")
+
     def set_product_path(self, path: int) -> None:
         """0: tcgen05 product for 8-tile launches (default); 1: CUDA cores only."""
         check(lib().bfvgpu_ctx_set_product_path(self._h, path), "set_product_path")

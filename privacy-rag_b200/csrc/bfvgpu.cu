@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -148,6 +149,9 @@ struct Context {
   std::vector<Modulus> mods;
   std::vector<uint64_t> fwd_h, inv_h;  // [k][n][2]
   cudaStream_t stream = nullptr;
+  cudaStream_t aux = nullptr;                     // side stream for independent work of one call
+  cudaEvent_t fork = nullptr, join = nullptr;     // ordering between a caller's stream and aux
+  std::mutex aux_mutex;                           // one call at a time uses aux
   void* dmem = nullptr;  // one public allocation holding all tables
   DevParams P;
 
@@ -157,7 +161,11 @@ struct Context {
       cudaGetDevice(&prev);
       cudaSetDevice(device);
       if (stream) cudaStreamSynchronize(stream);
+      if (aux) cudaStreamSynchronize(aux);
       if (dmem) cudaFree(dmem);
+      if (fork) cudaEventDestroy(fork);
+      if (join) cudaEventDestroy(join);
+      if (aux) cudaStreamDestroy(aux);
       if (stream) cudaStreamDestroy(stream);
       if (prev >= 0) cudaSetDevice(prev);
     }
@@ -296,6 +304,9 @@ static void build_context(Context& c, uint32_t n, const uint64_t* primes, uint32
   DeviceScope scope(device);
   cuda_check(configure_kernels(logn), "configure_kernels");
   cuda_check(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  cuda_check(cudaStreamCreateWithFlags(&c.aux, cudaStreamNonBlocking), "cudaStreamCreate");
+  cuda_check(cudaEventCreateWithFlags(&c.fork, cudaEventDisableTiming), "cudaEventCreate");
+  cuda_check(cudaEventCreateWithFlags(&c.join, cudaEventDisableTiming), "cudaEventCreate");
   const size_t mod_bytes = c.k * sizeof(Modulus);
   const size_t tab_bytes = (size_t)c.k * n * 16;
   const size_t qjp_bytes = qjp.size() * 8, part_bytes = part.size() * 8, cinv_bytes = cinv.size() * 8,
@@ -735,6 +746,13 @@ int32_t bfvgpu_ctx_check(bfvgpu_ctx* ctx, uint32_t* flags) {
   });
 }
 
+int32_t bfvgpu_ctx_set_reserved_sms(bfvgpu_ctx* ctx, int32_t sms) {
+  return guard([&] {
+    if (!ctx || sms < 0 || sms > 64) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    ctx->c.P.reserved_sms = sms;
+  });
+}
+
 int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx* ctx, int32_t path) {
   return guard([&] {
     if (!ctx || path < 0 || path > 1) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
@@ -789,15 +807,23 @@ int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t
     uint64_t* U = samples ? scratch : nullptr;
     uint64_t* xs = samples ? scratch + items * ctx->c.k * (uint64_t)ctx->c.n : nullptr;
     cudaStream_t st = pick(ctx, stream);
-    // out doubles as the product accumulator: each INTT block reads its whole limb
-    // before writing it back.
-    cuda_check(launch_mac_tiles(ctx->c.P, in, tiles, inputs, w, groups, out, st), "mac_tiles");
-    count_launch(mac_tiles_launches(tiles));
+    Context& c = ctx->c;
+    std::lock_guard<std::mutex> lock(c.aux_mutex);
+    // Enc(0) preparation depends only on the key and the randomness: it runs on the side
+    // stream, filling the SMs the product leaves idle, and joins before the output transform.
     if (samples) {
-      cuda_check(launch_enc0_prep(ctx->c.P, samples, reinterpret_cast<const ulonglong2*>(pk_prep), items, U, xs, st),
+      cuda_check(cudaEventRecord(c.fork, st), "event");
+      cuda_check(cudaStreamWaitEvent(c.aux, c.fork, 0), "wait");
+      cuda_check(launch_enc0_prep(c.P, samples, reinterpret_cast<const ulonglong2*>(pk_prep), items, U, xs, c.aux),
                  "enc0_prep");
       count_launch();
+      cuda_check(cudaEventRecord(c.join, c.aux), "event");
     }
+    // out doubles as the product accumulator: each INTT block reads its whole limb
+    // before writing it back.
+    cuda_check(launch_mac_tiles(c.P, in, tiles, inputs, w, groups, out, st), "mac_tiles");
+    count_launch(mac_tiles_launches(tiles));
+    if (samples) cuda_check(cudaStreamWaitEvent(st, c.join, 0), "wait");
     cuda_check(launch_intt_protect(ctx->c.P, out, items, U, reinterpret_cast<const ulonglong2*>(pk_prep), xs, samples,
                                    masks, out, st),
                "intt_protect");

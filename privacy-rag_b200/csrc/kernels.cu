@@ -851,7 +851,8 @@ static cudaError_t mac_split_launch(const DevParams& P, const uint64_t* in, uint
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  const unsigned grid = (unsigned)(units < (uint64_t)sms ? units : (uint64_t)sms);
+  const uint64_t avail = sms > P.reserved_sms ? (uint64_t)(sms - P.reserved_sms) : 1;
+  const unsigned grid = (unsigned)(units < avail ? units : avail);
   k_mac_split<T, TH><<<grid, S::kThreads, smem, st>>>(in, w, out, (uint32_t)inputs, (uint32_t)groups,
                                                       (uint32_t)gblocks, (uint32_t)units, P.dk, P.logn, P.mod);
   return cudaGetLastError();
@@ -911,7 +912,8 @@ static cudaError_t mac_tc_launch(const DevParams& P, const uint64_t* in, uint64_
   e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  const unsigned grid = (unsigned)(units < (uint64_t)sms ? units : (uint64_t)sms);
+  const uint64_t avail = sms > P.reserved_sms ? (uint64_t)(sms - P.reserved_sms) : 1;
+  const unsigned grid = (unsigned)(units < avail ? units : avail);
   k_mac_tc<KPAD><<<grid, kMacTcThreads, tc::Smem<KPAD>::kLaunchBytes, st>>>(
       a, b, out, (uint32_t)groups, (uint32_t)gchunks, (uint32_t)units, P.dk, P.logn, P.mod, P.err);
   return cudaGetLastError();

@@ -27,6 +27,7 @@ struct DevParams {
   const uint64_t* crt_q = nullptr;    // [dk] limbs of Q
   uint32_t* err = nullptr;            // kernel-recorded error bits (bfvgpu_ctx_check)
   int product_path = 0;               // 0: tcgen05 where it applies, 1: CUDA cores only
+  int reserved_sms = 0;               // SMs the persistent product kernels leave free
 };
 
 // Smallest and largest supported log2(n).
