@@ -365,7 +365,7 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
         ctx.set_reserved_sms(8)  # room for NCCL's kernels beside the persistent products
     # inputs are double-buffered so the broadcast of call c+1 overlaps call c; broadcasts and
     # result gathers use separate communicators so neither queues behind the other
-    cts_pre, masks_pre, samples_pre = call_buffers(sh_pre, tiles, 2 if multi else 1)
+    cts_pre, masks_pre, samples_pre = call_buffers(sh_pre, tiles, 1)
     cts_dec, masks_dec, samples_dec = call_buffers(sh_dec, 1, 2 if multi else 1)
     pg_in = dist.new_group(list(range(world))) if multi else None
     pg_out = dist.new_group(list(range(world))) if multi else None
@@ -395,20 +395,45 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
         p = sh[op[2]]
         return srv, p, full[op[2]], cts[p.name][slot % len(cts[p.name])], masks[p.name], samples[p.name]
 
+    # prefill calls distribute their inputs through an InputExchange (scatter, per-rank
+    # transform of a slice, all-gather), decode calls through a broadcast and a local transform
+    exchange = {p.name: S.InputExchange(torch, dist, pg_in, tiles * p.inputs, 2 * dk * n, "cuda")
+                for p in sh_pre} if multi else {}
+
+    def transform(si, so, slots):
+        ctx.matrix_tiles_inputs_device(si, slots, out=so, stream=sp)
+
     def run(ops, marks=None):
         calls = [i for i, op in enumerate(ops) if op[0] == "call"]
-        nxt = {c: calls[j + 1] for j, c in enumerate(calls[:-1])}
-        bcast = {}
+        after = {c: calls[j + 1:j + 3] for j, c in enumerate(calls)}
+        works = {}
         pending = [None, None]
         slot = {c: j for j, c in enumerate(calls)}
 
-        def broadcast(ci):
-            buf = operands(ops[ci], slot[ci])[3]
-            bcast[ci] = dist.broadcast(buf, src=0, group=pg_in, async_op=True)
-            stats["broadcast_bytes"] += buf.numel() * 8
+        def stage_far(ci):   # two calls ahead: the scatter of an exchanged call
+            op = ops[ci]
+            if op[1] == "pre":
+                name = sh_pre[op[2]].name
+                works[ci] = exchange[name].scatter(operands(op, slot[ci])[3])
+                stats["broadcast_bytes"] += exchange[name].per * exchange[name].words * 8
+
+        def stage_near(ci):  # one call ahead: transform + all-gather, or the broadcast
+            op = ops[ci]
+            if op[1] == "pre":
+                works.pop(ci).wait()
+                ex = exchange[sh_pre[op[2]].name]
+                works[ci] = ex.gather(transform)
+                stats["broadcast_bytes"] += (ex.world - 1) * ex.per * ex.words * 8
+            else:
+                buf = operands(op, slot[ci])[3]
+                works[ci] = dist.broadcast(buf, src=0, group=pg_in, async_op=True)
+                stats["broadcast_bytes"] += buf.numel() * 8
 
         if multi and calls:
-            broadcast(calls[0])
+            stage_far(calls[0])
+            stage_near(calls[0])
+            if len(calls) > 1:
+                stage_far(calls[1])
         for i, op in enumerate(ops):
             if op[0] == "mark":
                 if marks is not None:
@@ -432,12 +457,18 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
             srv, p_local, p_full, cts, masks, samples = operands(op, slot[i])
             if op[1] == "dec":
                 dec.w_ntt = wcache[op[3]]
+            transformed = None
             if multi:
-                if i in nxt:
-                    broadcast(nxt[i])      # starts once the call two back has released its buffer
-                bcast.pop(i).wait()        # this call's inputs are in place
+                ahead = after[i]
+                if len(ahead) > 1:
+                    stage_far(ahead[1])
+                if ahead:
+                    stage_near(ahead[0])
+                works.pop(i).wait()        # this call's inputs are in place
+                if op[1] == "pre":
+                    transformed = exchange[p_local.name].full
             if p_local.groups:
-                srv.run_projection(p_local, cts, masks, samples, stream=sp)
+                srv.run_projection(p_local, cts, masks, samples, stream=sp, transformed=transformed)
             stats["calls"] += 1
             if not multi:
                 continue
@@ -478,8 +509,9 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
            "tokens_per_s": tokens / (total / 1e3), "n_gpus": world, "layers": layers,
            "prefill_ms": pre_ms, "decode_weights_ms": dw_ms, "decode_ms": dec_ms,
            "decode_ms_per_step": dec_ms / max(1, decode_steps),
-           "sharding": "output groups of every call, contiguous ranges per rank; NCCL broadcast of inputs "
-                       "(prefetched one call ahead) and gather of c1 + target CRT limbs to rank 0 (asynchronous)",
+           "sharding": "output groups of every call, contiguous ranges per rank; prefill inputs scattered by "
+                       "rank 0, transformed per slice and all-gathered (two calls ahead), decode inputs "
+                       "broadcast (one call ahead); c1 + target CRT limbs gathered to rank 0 (asynchronous)",
            "calls_per_rank": stats["calls"], "broadcast_bytes_per_rank": stats["broadcast_bytes"],
            "gathered_bytes_per_rank": stats["gathered_bytes"],
            "prefill_mac_modmuls": layers * tiles_total * sum(p.groups * p.inputs * 2 * dk * n for p in full_pre),

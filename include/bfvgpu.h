@@ -183,10 +183,12 @@ int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx *ctx, int32_t path);
  * tiles * groups * (k + 2) * n. */
 uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx *ctx, uint64_t tiles, uint64_t groups,
                                            int32_t enc0);
-/* Forward NTT, in place, of `count` client ciphertexts [count][2][dk][n] (coefficient
- * form) into the operand form of bfvgpu_matrix_tiles_device: every canonical NTT slot v
- * is stored as ((v >> 30) << 32) | (v mod 2^30).  Needs data primes < 2^60 and n >= 32. */
-int32_t bfvgpu_matrix_tiles_inputs_device(bfvgpu_ctx *ctx, uint64_t *cts, uint64_t count, void *stream);
+/* Forward NTT of `count` client ciphertexts [count][2][dk][n] (coefficient form) into out
+ * (the same size; may be cts itself) in the operand form of bfvgpu_matrix_tiles_device:
+ * every canonical NTT slot v is stored as ((v >> 30) << 32) | (v mod 2^30).  Needs data
+ * primes < 2^60 and n >= 32. */
+int32_t bfvgpu_matrix_tiles_inputs_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count, uint64_t *out,
+                                          void *stream);
 /* The public key pk [2][k][n] (NTT form) prepared for bfvgpu_matrix_tiles_device: pk_prep
  * [2][k][n][2] words = {v, floor(v 2^64 / q)} with v = pk . q_special^-1 mod q for the data
  * primes and v = pk for the special prime.  Once per key. */

@@ -80,7 +80,7 @@ _SIGNATURES = {
     "bfvgpu_ctx_check": (I32, [VP, U32P]),
     "bfvgpu_ctx_set_product_path": (I32, [VP, I32]),
     "bfvgpu_ctx_set_reserved_sms": (I32, [VP, I32]),
-    "bfvgpu_matrix_tiles_inputs_device": (I32, [VP, VP, U64, VP]),
+    "bfvgpu_matrix_tiles_inputs_device": (I32, [VP, VP, U64, VP, VP]),
     "bfvgpu_matrix_tiles_prepare_pk_device": (I32, [VP, VP, VP, VP]),
     "bfvgpu_matrix_tiles_scratch_words": (U64, [VP, U64, U64, I32]),
     "bfvgpu_matrix_tiles_device": (I32, [VP, VP, U64, U64, VP, U64, VP, VP, VP, VP, VP, VP]),

@@ -182,10 +182,11 @@ class Context:
         """0: tcgen05 product for 8-tile launches (default); 1: CUDA cores only."""
         check(lib().bfvgpu_ctx_set_product_path(self._h, path), "set_product_path")
 
-    def matrix_tiles_inputs_device(self, cts, count: int, stream: int | None = None):
-        """Transform client ciphertexts [count][2][dk][n] in place into the operand form of
-        matrix_tiles_device (NTT slots with their 30-bit halves split)."""
-        check(lib().bfvgpu_matrix_tiles_inputs_device(self._h, self._dptr(cts), count, stream),
+    def matrix_tiles_inputs_device(self, cts, count: int, out=None, stream: int | None = None):
+        """Transform client ciphertexts [count][2][dk][n] into out (default: in place) in the
+        operand form of matrix_tiles_device (NTT slots with their 30-bit halves split)."""
+        check(lib().bfvgpu_matrix_tiles_inputs_device(self._h, self._dptr(cts), count,
+                                                      self._dptr(cts if out is None else out), stream),
               "matrix_tiles_inputs_device")
 
     def matrix_tiles_prepare_pk_device(self, pk, pk_prep, stream: int | None = None):

@@ -89,7 +89,9 @@ class LayerServer:
         t, n, dk = torch, ctx.n, ctx.dk
         dev = pk_device.device
         maxg = max(p.groups for p in self.proj)
+        maxi = max(p.inputs for p in self.proj)
         self.w_ntt = {}
+        self.inp = t.empty(tiles * maxi * 2 * dk * n, dtype=t.int64, device=dev)  # transformed inputs
         self.scratch = t.empty(max(1, ctx.matrix_tiles_scratch_words(tiles, maxg)), dtype=t.int64, device=dev)
         self.out = t.empty(tiles * maxg * 2 * dk * n, dtype=t.int64, device=dev)
         self.targets = {p.name: targets_device(t, p, dev, tiles) for p in self.proj}
@@ -136,15 +138,19 @@ class LayerServer:
         return (self.selected.view(-1)[: e * dk * mx].view(e, dk, mx),
                 self.crt.view(-1)[: e * mx * dk].view(e, mx, dk))
 
-    def run_projection(self, p: Projection, cts, masks, samples, stream=None):
-        """One private_matrix call for every tile: cts [tiles][I][2][dk][n] client
-        ciphertexts in coefficient form (transformed in place), masks [tiles][G][n], samples
-        [tiles][G][3][k][n].  Leaves the re-randomised results in output(p) (c1 goes to the
-        client) and the targets' c0 residues / CRT limbs in self.selected / self.crt."""
+    def run_projection(self, p: Projection, cts, masks, samples, stream=None, transformed=None):
+        """One private_matrix call for every tile: cts [tiles][I][2][dk][n] client ciphertexts
+        in coefficient form (left unchanged; their transform goes to self.inp), or None with
+        `transformed` holding them already in the product's operand form (InputExchange);
+        masks [tiles][G][n], samples [tiles][G][3][k][n].  Leaves the re-randomised results in
+        output(p) (c1 goes to the client) and the targets' c0 residues / CRT limbs in
+        self.selected / self.crt."""
         ctx = self.ctx
         I, G, T = p.inputs, p.groups, self.tiles
-        ctx.matrix_tiles_inputs_device(cts, T * I, stream=stream)
-        ctx.matrix_tiles_device(cts, T, I, self.w_ntt[p.name], G, self.out, masks=masks, samples=samples,
+        if transformed is None:
+            transformed = self.inp
+            ctx.matrix_tiles_inputs_device(cts, T * I, out=transformed, stream=stream)
+        ctx.matrix_tiles_device(transformed, T, I, self.w_ntt[p.name], G, self.out, masks=masks, samples=samples,
                                 pk_prep=self.pk, scratch=self.scratch, stream=stream)
         tg, counts, mx = self.targets[p.name]
         ctx.gather_targets_device(self.out, T * G, tg, counts, mx, self.selected, self.crt, stream=stream)

@@ -64,3 +64,43 @@ def gather_groups(torch, dist, local, groups: int, world: int, dst: int = 0, asy
     if async_op:
         return work, finish
     return finish()
+
+
+class InputExchange:
+    """One call's client ciphertexts from the protocol rank to every rank in the product's
+    operand form, with the transform itself sharded: the protocol rank scatters equal slices
+    of the batch, each rank transforms its slice, and an all-gather assembles the whole
+    transformed batch on every rank (the same bytes on the links as a broadcast, a 1/world
+    share of the transform).  `count` ciphertexts of `words` words each are padded to a
+    multiple of world; the padding slots carry no data anyone reads."""
+
+    def __init__(self, torch, dist, group, count: int, words: int, device, src: int = 0):
+        self.torch, self.dist, self.group, self.src = torch, dist, group, src
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.per = -(-count // self.world)
+        self.count, self.words = count, words
+        self.slice_in = torch.empty((self.per, words), dtype=torch.int64, device=device)
+        self.slice_out = torch.empty((self.per, words), dtype=torch.int64, device=device)
+        self.full = torch.empty((self.per * self.world, words), dtype=torch.int64, device=device)
+
+    def scatter(self, source, async_op: bool = True):
+        """source [count][words] on the protocol rank (ignored elsewhere) -> this rank's slice."""
+        chunks = None
+        if self.rank == self.src:
+            flat = source.reshape(-1, self.words)
+            if flat.shape[0] != self.count:
+                raise ValueError("BAD_SHAPE")
+            chunks = [flat[r * self.per:(r + 1) * self.per] for r in range(self.world)]
+            if chunks[-1].shape[0] < self.per:  # pad the last chunk
+                pad = self.torch.zeros((self.per, self.words), dtype=flat.dtype, device=flat.device)
+                pad[: chunks[-1].shape[0]] = chunks[-1]
+                chunks[-1] = pad
+            chunks = [c.contiguous() for c in chunks]
+        return self.dist.scatter(self.slice_in, chunks, src=self.src, group=self.group, async_op=async_op)
+
+    def gather(self, transform, async_op: bool = True):
+        """transform(slice_in, slice_out, slots) on this rank's slice, then the all-gather into
+        self.full ([per*world][words]; rows past `count` are padding)."""
+        transform(self.slice_in, self.slice_out, self.per)
+        return self.dist.all_gather_into_tensor(self.full, self.slice_out, group=self.group, async_op=async_op)

@@ -771,13 +771,14 @@ static void require_product_ring(const Context& c) {
     if (c.q[p] >> 60) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_PRODUCT_PRIME");
 }
 
-int32_t bfvgpu_matrix_tiles_inputs_device(bfvgpu_ctx* ctx, uint64_t* cts, uint64_t count, void* stream) {
+int32_t bfvgpu_matrix_tiles_inputs_device(bfvgpu_ctx* ctx, const uint64_t* cts, uint64_t count, uint64_t* out,
+                                          void* stream) {
   return guard([&] {
-    if (!ctx || !cts) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (!ctx || !cts || !out) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
     require_product_ring(ctx->c);
     require_device(ctx->c);
     DeviceScope scope(ctx->c.device);
-    cuda_check(launch_ntt_split(ctx->c.P, cts, count * 2 * ctx->c.dk, pick(ctx, stream)), "ntt_split");
+    cuda_check(launch_ntt_split(ctx->c.P, cts, out, count * 2 * ctx->c.dk, pick(ctx, stream)), "ntt_split");
     count_launch();
   });
 }

@@ -520,13 +520,14 @@ BFV_HD void mac_store(uint64_t* out, int warp, int lane, const Acc128 (&A)[TH][2
 
 // Forward transform of client ciphertext limbs into the product's operand form (split30).
 template <int LOGN, class Ex>
-BFV_HD void op_ntt_split(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* data, uint32_t dk, const Modulus* mods,
-                         const ulonglong2* fwd) {
+BFV_HD void op_ntt_split(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* data, uint64_t* out, uint32_t dk,
+                         const Modulus* mods, const ulonglong2* fwd) {
   const uint32_t p = (uint32_t)(blk % dk);
   const Modulus m = mods[p];
-  uint64_t* a = data + (blk << LOGN);
+  const uint64_t* a = data + (blk << LOGN);
+  uint64_t* o = out + (blk << LOGN);
   auto ld = [a](int i) { return a[i]; };
-  auto st = [a](int i, uint64_t v) { a[i] = split30(v); };
+  auto st = [o](int i, uint64_t v) { o[i] = split30(v); };
   ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
 }
 

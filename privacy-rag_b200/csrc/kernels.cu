@@ -432,9 +432,9 @@ constexpr size_t mac_smem_bytes() {
 
 template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
-    k_ntt_split(uint64_t* data, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
+    k_ntt_split(const uint64_t* data, uint64_t* out, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
   extern __shared__ uint64_t smem[];
-  op_ntt_split<LOGN>(BlockExec{}, smem, blockIdx.x, data, dk, mods, fwd);
+  op_ntt_split<LOGN>(BlockExec{}, smem, blockIdx.x, data, out, dk, mods, fwd);
 }
 
 __global__ void k_pk_prep(const uint64_t* pk, ulonglong2* prep, uint64_t items, uint32_t k, int logn,
@@ -964,11 +964,12 @@ uint64_t mac_tiles_launches(uint64_t tiles) {
   return c;
 }
 
-cudaError_t launch_ntt_split(const DevParams& P, uint64_t* data, uint64_t polys, cudaStream_t st) {
+cudaError_t launch_ntt_split(const DevParams& P, const uint64_t* data, uint64_t* out, uint64_t polys,
+                             cudaStream_t st) {
   if (!polys) return cudaSuccess;
   if (polys > 0x7fffffffull) return cudaErrorInvalidValue;
   BFV_DISPATCH(P.logn, {
-    k_ntt_split<L_><<<(unsigned)polys, threads_for<L_>(), smem_bytes<L_>(), st>>>(data, P.dk, P.mod, P.fwd);
+    k_ntt_split<L_><<<(unsigned)polys, threads_for<L_>(), smem_bytes<L_>(), st>>>(data, out, P.dk, P.mod, P.fwd);
   });
   return cudaGetLastError();
 }

@@ -123,8 +123,8 @@ cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint6
 
 // Layer pipeline over T tiles that share one weight matrix (E = T * groups items, item
 // e = t * groups + g):
-//  ntt_split:    forward NTT of client limbs [polys][n] (prime i % dk) in place, stored in
-//                the product's operand form (split30 of each canonical slot).
+//  ntt_split:    forward NTT of client limbs [polys][n] (prime i % dk) into out (may be the
+//                input), stored in the product's operand form (split30 of each canonical slot).
 //  mac_tiles:    acc [T][G][2][dk][n] = sum_b in[t][b][c] . w[g][b]; in [T][I][2][dk][n] from
 //                ntt_split, w [G][I][dk][n] NTT form, all primes < 2^60, n >= 32.  Tiles
 //                run in launches of 8/4/2/1 (mac_tiles_launches counts them).
@@ -135,7 +135,8 @@ cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint6
 cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t tiles, uint64_t inputs,
                              const uint64_t* w, uint64_t groups, uint64_t* acc, cudaStream_t st);
 uint64_t mac_tiles_launches(uint64_t tiles);
-cudaError_t launch_ntt_split(const DevParams& P, uint64_t* data, uint64_t polys, cudaStream_t st);
+cudaError_t launch_ntt_split(const DevParams& P, const uint64_t* data, uint64_t* out, uint64_t polys,
+                             cudaStream_t st);
 //  pk_prep:      prep [2][k][n] = {v, Shoup companion}, v = pk . q_s^-1 (data primes), pk (special)
 cudaError_t launch_pk_prep(const DevParams& P, const uint64_t* pk, ulonglong2* prep, cudaStream_t st);
 cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const ulonglong2* pk, uint64_t items,

@@ -306,7 +306,7 @@ int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, 
   EMU_DISPATCH(logn, {
     std::vector<uint64_t> s(SmemWords<L_>::value);
     for (uint64_t b = 0; b < tiles * inputs * 2 * dk; ++b)
-      op_ntt_split<L_>(HostExec{}, s.data(), b, in.data(), dk, T.mods.data(), T.fwd);
+      op_ntt_split<L_>(HostExec{}, s.data(), b, in.data(), in.data(), dk, T.mods.data(), T.fwd);
     for (uint64_t b = 0; b < groups * inputs * dk; ++b)
       op_lift_ntt<L_>(HostExec{}, s.data(), b, ring, w.data(), dk, T.mods.data(), T.fwd);
     const uint64_t in_tile = inputs * 2 * dk * n, acc_tile = groups * 2 * dk * n;

@@ -391,7 +391,7 @@ def test_matrix_tiles_device(art, oracle, tiles, path):
     torch.cuda.synchronize()
     hc.set_product_path(path)
     try:
-        hc.matrix_tiles_inputs_device(d_in, tiles * I)
+        hc.matrix_tiles_inputs_device(d_in, tiles * I)  # in place
         hc.weights_ntt_device(d_ring, G * I, w)
         pk_prep = torch.empty((2, k, n, 2), dtype=torch.int64, device="cuda")
         hc.matrix_tiles_prepare_pk_device(d_pk, pk_prep)

@@ -102,3 +102,47 @@ def test_gather_groups_gloo(world, groups):
         pr.join(timeout=60)
         assert pr.exitcode == 0
     assert all(res)
+
+
+def _exchange_worker(rank, world, port, count, words, q):
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ex = S.InputExchange(torch, dist, None, count, words, "cpu")
+        source = (torch.arange(count * words, dtype=torch.int64).view(count, words) * 7 + 5) if rank == 0 else None
+        seen = []
+
+        def transform(si, so, slots):
+            seen.append(int(slots))
+            so.copy_(si * 3 + 1)
+
+        w = ex.scatter(source)
+        w.wait()
+        g = ex.gather(transform)
+        g.wait()
+        want = (torch.arange(count * words, dtype=torch.int64).view(count, words) * 7 + 5) * 3 + 1
+        q.put(bool(torch.equal(ex.full[:count], want)) and seen == [ex.per])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,count", [(2, 8), (3, 7)])
+def test_input_exchange_gloo(world, count):
+    """Scatter from the protocol rank, per-rank transform of the slice, all-gather: every
+    rank ends with the transform of the whole batch (count not a multiple of world: the
+    padding is ignored)."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, world, port, count, 5, q)) for r in range(world)]
+    for pr in procs:
+        pr.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for pr in procs:
+        pr.join(timeout=60)
+        assert pr.exitcode == 0
+    assert all(res)
