@@ -761,8 +761,10 @@ int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx* ctx, int32_t path) {
 }
 
 uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx* ctx, uint64_t tiles, uint64_t groups, int32_t enc0) {
-  if (!ctx || !enc0) return 0;
-  return tiles * groups * (ctx->c.k + 2) * (uint64_t)ctx->c.n;
+  if (!ctx) return 0;
+  // U [items][k][n] + xs [items][2][n] (Enc(0) only) + E [items][2][dk][n]
+  const uint64_t items = tiles * groups, n = ctx->c.n;
+  return items * ((enc0 ? ctx->c.k + 2 : 0) + 2ull * ctx->c.dk) * n;
 }
 
 static void require_product_ring(const Context& c) {
@@ -805,18 +807,27 @@ int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t
     require_device(ctx->c);
     DeviceScope scope(ctx->c.device);
     const uint64_t items = tiles * groups;
+    if ((samples || masks) && !scratch) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
     uint64_t* U = samples ? scratch : nullptr;
     uint64_t* xs = samples ? scratch + items * ctx->c.k * (uint64_t)ctx->c.n : nullptr;
+    uint64_t* E = (samples || masks)
+                      ? scratch + (samples ? items * (ctx->c.k + 2) * (uint64_t)ctx->c.n : 0)
+                      : nullptr;
     cudaStream_t st = pick(ctx, stream);
     Context& c = ctx->c;
     std::lock_guard<std::mutex> lock(c.aux_mutex);
-    // Enc(0) preparation depends only on the key and the randomness: it runs on the side
-    // stream, filling the SMs the product leaves idle, and joins before the output transform.
-    if (samples) {
+    // Enc(0) preparation and the additive output term depend only on the key, the randomness
+    // and the masks: they run on the side stream, beside the product, and join before the
+    // output transform.
+    if (E) {
       cuda_check(cudaEventRecord(c.fork, st), "event");
       cuda_check(cudaStreamWaitEvent(c.aux, c.fork, 0), "wait");
-      cuda_check(launch_enc0_prep(c.P, samples, reinterpret_cast<const ulonglong2*>(pk_prep), items, U, xs, c.aux),
-                 "enc0_prep");
+      if (samples) {
+        cuda_check(launch_enc0_prep(c.P, samples, reinterpret_cast<const ulonglong2*>(pk_prep), items, U, xs, c.aux),
+                   "enc0_prep");
+        count_launch();
+      }
+      cuda_check(launch_enc0_fin(c.P, samples, xs, masks, items, E, c.aux), "enc0_fin");
       count_launch();
       cuda_check(cudaEventRecord(c.join, c.aux), "event");
     }
@@ -824,9 +835,8 @@ int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t
     // before writing it back.
     cuda_check(launch_mac_tiles(c.P, in, tiles, inputs, w, groups, out, st), "mac_tiles");
     count_launch(mac_tiles_launches(tiles));
-    if (samples) cuda_check(cudaStreamWaitEvent(st, c.join, 0), "wait");
-    cuda_check(launch_intt_protect(ctx->c.P, out, items, U, reinterpret_cast<const ulonglong2*>(pk_prep), xs, samples,
-                                   masks, out, st),
+    if (E) cuda_check(cudaStreamWaitEvent(st, c.join, 0), "wait");
+    cuda_check(launch_intt_protect(c.P, out, items, U, reinterpret_cast<const ulonglong2*>(pk_prep), E, out, st),
                "intt_protect");
     count_launch();
   });

@@ -590,41 +590,52 @@ BFV_HD void op_enc0_prep(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t
   }
 }
 
+// Additive output term of item e, component c, data prime p, coefficient z (elementwise,
+// after op_enc0_prep, beside the product):
+//   E = (e_c,p - corr(x_s,c)) . q_s^-1  (if Enc(0))  -  [c = 0] Delta . mask  (if masked)
+// i.e. everything op_intt_protect adds after its transform except the part that must go
+// through it.  Layout E [items][2][dk][n].
+BFV_HD void enc0_fin_item(uint64_t item, const uint64_t* samples, const uint64_t* xs, const uint64_t* mask,
+                          uint64_t* E, uint32_t k, uint32_t dk, int logn, const Modulus* mods, uint64_t q_mod_t,
+                          uint64_t upper_half, uint64_t t, int tlog) {
+  const uint64_t N = uint64_t(1) << logn;
+  const uint64_t z = item & (N - 1), r = item >> logn;
+  const uint32_t p = (uint32_t)(r % dk), c = (uint32_t)((r / dk) & 1);
+  const uint64_t e = r / (2 * dk);
+  const Modulus& m = mods[p];
+  uint64_t v = 0;
+  if (samples)
+    v = moddown_elem(samples[((e * 3 + 1 + c) * k + p) * N + z], xs[(e * 2 + c) * N + z], m, mods[k - 1]);
+  if (mask && c == 0) v = sub_mod(v, scale_plain_coeff(mask[e * N + z], q_mod_t, upper_half, t, tlog, m), m.q);
+  E[item] = v;
+}
+
 // INTT of the accumulated product with the Enc(0) and mask epilogue, block (e, c, p):
-//   out = INTT(acc + U_p . pk_c,p . q_s^-1) + (e_c,p - corr(xs_c)) . q_s^-1  [- Delta mask]
+//   out = INTT(acc + U_p . pk_c,p . q_s^-1) + E[e][c][p]
 // which equals INTT(acc) + moddown(INTT(U . pk_c) + e_c) - Delta mask exactly, because
-// moddown_p(x) = (x_p - corr(x_s)) q_s^-1 is linear in x_p.
+// moddown_p(x) = (x_p - corr(x_s)) q_s^-1 is linear in x_p.  U (with pk) and E may be null.
 template <int LOGN, class Ex>
 BFV_HD void op_intt_protect(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* acc, uint64_t* out,
-                            const uint64_t* U, const ulonglong2* pk, const uint64_t* xs, const uint64_t* samples,
-                            const uint64_t* mask, uint32_t k, uint32_t dk, const Modulus* mods,
-                            const ulonglong2* inv, uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
+                            const uint64_t* U, const ulonglong2* pk, const uint64_t* E, uint32_t k, uint32_t dk,
+                            const Modulus* mods, const ulonglong2* inv) {
   constexpr uint64_t N = uint64_t(1) << LOGN;
   const uint64_t e = blk / (2 * dk);
   const uint32_t cp = (uint32_t)(blk % (2 * dk)), c = cp / dk, p = cp % dk;
   const Modulus m = mods[p];
   const uint64_t* a = acc + (e * 2 * dk + cp) * N;
   uint64_t* o = out + (e * 2 * dk + cp) * N;
-  const bool enc0 = U != nullptr;
-  const uint64_t* Up = enc0 ? U + (e * k + p) * N : nullptr;
-  const ulonglong2* pkc = enc0 ? pk + ((uint64_t)c * k + p) * N : nullptr;
-  const uint64_t* xsc = enc0 ? xs + (e * 2 + c) * N : nullptr;
-  const uint64_t* ec = enc0 ? samples + ((e * 3 + 1 + c) * k + p) * N : nullptr;
-  const uint64_t* mk = (mask && c == 0) ? mask + e * N : nullptr;
-  const Modulus* ms = mods + (k - 1);
+  const uint64_t* Up = U ? U + (e * k + p) * N : nullptr;
+  const ulonglong2* pkc = U ? pk + ((uint64_t)c * k + p) * N : nullptr;
+  const uint64_t* Ep = E ? E + (e * 2 * dk + cp) * N : nullptr;
   auto ld = [=](int i) {
     uint64_t v = a[i];
-    if (enc0) {
+    if (Up) {
       const ulonglong2 w = pkc[i];  // pk . q_s^-1 with its Shoup companion
       v = add_mod(v, shoup(Up[i], w.x, w.y, m.q), m.q);
     }
     return v;
   };
-  auto st = [=](int i, uint64_t v) {
-    if (enc0) v = add_mod(v, moddown_elem(ec[i], xsc[i], m, *ms), m.q);
-    if (mk) v = sub_mod(v, scale_plain_coeff(mk[i], q_mod_t, upper_half, t, tlog, m), m.q);
-    o[i] = v;
-  };
+  auto st = [=](int i, uint64_t v) { o[i] = Ep ? add_mod(v, Ep[i], m.q) : v; };
   ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
 }
 

@@ -451,14 +451,19 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
   op_enc0_prep<LOGN>(BlockExec{}, smem, blockIdx.x, samples, pk, U, xs, k, mods, fwd, inv);
 }
 
+__global__ void k_enc0_fin(const uint64_t* samples, const uint64_t* xs, const uint64_t* mask, uint64_t* E,
+                           uint64_t items, uint32_t k, uint32_t dk, int logn, const Modulus* mods, uint64_t q_mod_t,
+                           uint64_t upper_half, uint64_t t, int tlog) {
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < items; e += (uint64_t)gridDim.x * blockDim.x)
+    enc0_fin_item(e, samples, xs, mask, E, k, dk, logn, mods, q_mod_t, upper_half, t, tlog);
+}
+
 template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
-    k_intt_protect(const uint64_t* acc, uint64_t* out, const uint64_t* U, const ulonglong2* pk, const uint64_t* xs,
-                   const uint64_t* samples, const uint64_t* mask, uint32_t k, uint32_t dk, const Modulus* mods,
-                   const ulonglong2* inv, uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
+    k_intt_protect(const uint64_t* acc, uint64_t* out, const uint64_t* U, const ulonglong2* pk, const uint64_t* E,
+                   uint32_t k, uint32_t dk, const Modulus* mods, const ulonglong2* inv) {
   extern __shared__ uint64_t smem[];
-  op_intt_protect<LOGN>(BlockExec{}, smem, blockIdx.x, acc, out, U, pk, xs, samples, mask, k, dk, mods, inv, q_mod_t,
-                        upper_half, t, tlog);
+  op_intt_protect<LOGN>(BlockExec{}, smem, blockIdx.x, acc, out, U, pk, E, k, dk, mods, inv);
 }
 
 // Galois elements of up to kKeyBatch keys and their inverses mod 2n, passed by value.
@@ -991,14 +996,22 @@ cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const 
   return cudaGetLastError();
 }
 
+cudaError_t launch_enc0_fin(const DevParams& P, const uint64_t* samples, const uint64_t* xs, const uint64_t* mask,
+                            uint64_t items, uint64_t* E, cudaStream_t st) {
+  if (!items || (!samples && !mask)) return cudaSuccess;
+  const uint64_t total = items * 2 * P.dk * (uint64_t)P.n;
+  k_enc0_fin<<<elementwise_blocks(total), 256, 0, st>>>(samples, xs, mask, E, total, P.k, P.dk, P.logn, P.mod,
+                                                         P.q_mod_t, P.upper_half, P.t, P.tlog);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_intt_protect(const DevParams& P, const uint64_t* acc, uint64_t items, const uint64_t* U,
-                                const ulonglong2* pk, const uint64_t* xs, const uint64_t* samples, const uint64_t* mask,
-                                uint64_t* out, cudaStream_t st) {
+                                const ulonglong2* pk, const uint64_t* E, uint64_t* out, cudaStream_t st) {
   if (!items) return cudaSuccess;
   if (items * 2 * P.dk > 0x7fffffffull) return cudaErrorInvalidValue;
   BFV_DISPATCH(P.logn, {
     k_intt_protect<L_><<<(unsigned)(items * 2 * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(
-        acc, out, U, pk, xs, samples, mask, P.k, P.dk, P.mod, P.inv, P.q_mod_t, P.upper_half, P.t, P.tlog);
+        acc, out, U, pk, E, P.k, P.dk, P.mod, P.inv);
   });
   return cudaGetLastError();
 }

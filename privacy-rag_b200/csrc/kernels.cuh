@@ -130,8 +130,8 @@ cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint6
 //                run in launches of 8/4/2/1 (mac_tiles_launches counts them).
 //  enc0_prep:    U [E][k][n] = NTT(u); xs [E][2][n] = special-prime coefficients of
 //                INTT(U . pk_c) + e_c; samples [E][3][k][n]; pk prepared by pk_prep.
-//  intt_protect: out [E][2][dk][n] = INTT(acc) + Enc(0) (if U) - Delta mask (if mask
-//                [E][n]), the Enc(0) data-prime part folded into the transform's input.
+//  intt_protect: out [E][2][dk][n] = INTT(acc + U . pk') + E, i.e. INTT(acc) + Enc(0) (if U)
+//                - Delta mask (if masked), the Enc(0) data-prime part folded into the input.
 cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t tiles, uint64_t inputs,
                              const uint64_t* w, uint64_t groups, uint64_t* acc, cudaStream_t st);
 uint64_t mac_tiles_launches(uint64_t tiles);
@@ -141,8 +141,11 @@ cudaError_t launch_ntt_split(const DevParams& P, const uint64_t* data, uint64_t*
 cudaError_t launch_pk_prep(const DevParams& P, const uint64_t* pk, ulonglong2* prep, cudaStream_t st);
 cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const ulonglong2* pk, uint64_t items,
                              uint64_t* U, uint64_t* xs, cudaStream_t st);
+// enc0_fin: E [items][2][dk][n], the additive output term (Enc(0) divide-and-round part and
+// the Delta-scaled mask) after enc0_prep; nothing when samples and mask are both null.
+cudaError_t launch_enc0_fin(const DevParams& P, const uint64_t* samples, const uint64_t* xs, const uint64_t* mask,
+                            uint64_t items, uint64_t* E, cudaStream_t st);
 cudaError_t launch_intt_protect(const DevParams& P, const uint64_t* acc, uint64_t items, const uint64_t* U,
-                                const ulonglong2* pk, const uint64_t* xs, const uint64_t* samples, const uint64_t* mask,
-                                uint64_t* out, cudaStream_t st);
+                                const ulonglong2* pk, const uint64_t* E, uint64_t* out, cudaStream_t st);
 
 }  // namespace bfvgpu

@@ -300,7 +300,7 @@ int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, 
   const uint64_t items = tiles * groups;
   std::vector<uint64_t> in(cts, cts + tiles * inputs * 2 * dk * n);
   std::vector<uint64_t> w(groups * inputs * dk * n);
-  std::vector<uint64_t> U(items * k * n), xs(items * 2 * n);
+  std::vector<uint64_t> U(items * k * n), xs(items * 2 * n), E(items * 2 * dk * n);
   std::vector<ulonglong2> pkp(pk ? 2 * k * n : 0);
   for (uint64_t e = 0; e < pkp.size(); ++e) pk_prep_item(e, pk, pkp.data(), k, logn, T.mods.data());
   EMU_DISPATCH(logn, {
@@ -335,9 +335,13 @@ int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, 
       for (uint64_t b = 0; b < items * k; ++b)
         op_enc0_prep<L_>(HostExec{}, s.data(), b, samples, pkp.data(), U.data(), xs.data(), k, T.mods.data(), T.fwd,
                          T.inv);
+    const bool fin = samples || masks;
+    if (fin)
+      for (uint64_t e = 0; e < items * 2 * dk * n; ++e)
+        enc0_fin_item(e, samples, xs.data(), masks, E.data(), k, dk, L_, T.mods.data(), q_mod_t, upper_half, t, tlog);
     for (uint64_t b = 0; b < items * 2 * dk; ++b)
-      op_intt_protect<L_>(HostExec{}, s.data(), b, out, out, samples ? U.data() : nullptr, pkp.data(), xs.data(), samples,
-                          masks, k, dk, T.mods.data(), T.inv, q_mod_t, upper_half, t, tlog);
+      op_intt_protect<L_>(HostExec{}, s.data(), b, out, out, samples ? U.data() : nullptr, pkp.data(),
+                          fin ? E.data() : nullptr, k, dk, T.mods.data(), T.inv);
   });
   return 0;
 }

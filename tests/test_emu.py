@@ -172,12 +172,16 @@ def test_matrix_tiles_kernel_bodies(bfv, oracle, E, tiles, I, G, path):
     plain = np.zeros_like(out)
     E.emu_matrix_tiles(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), tiles, I, p(ring), G, None, None, None,
                        oc.q_mod_t, oc.upper_half, 1 << 59, 59, p(plain), path)
+    masked = np.zeros_like(out)  # masks without Enc(0): the additive term is -Delta mask alone
+    E.emu_matrix_tiles(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), tiles, I, p(ring), G, p(masks), None, None,
+                       oc.q_mod_t, oc.upper_half, 1 << 59, 59, p(masked), path)
     for t in range(tiles):
         cn = oc.matrix_open(cts[t])
         for g in range(G):
             e = oc.matrix_evaluate(cn, ring[g])
             assert np.array_equal(plain[t, g], e), (t, g)
             e[0] = oc.sub_plain(e[0], masks[t, g])
+            assert np.array_equal(masked[t, g], e), (t, g)
             e = oc.add(e, oc.enc0(samples[t, g], tb.pk))
             assert np.array_equal(out[t, g], e), (t, g)
 

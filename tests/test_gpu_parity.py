@@ -387,7 +387,7 @@ def test_matrix_tiles_device(art, oracle, tiles, path):
     w = torch.empty((G, I, dk, n), dtype=torch.int64, device="cuda")
     scratch = torch.empty(hc.matrix_tiles_scratch_words(tiles, G), dtype=torch.int64, device="cuda")
     out = torch.empty((tiles, G, 2, dk, n), dtype=torch.int64, device="cuda")
-    plain = torch.empty_like(out)
+    plain, masked = torch.empty_like(out), torch.empty_like(out)
     torch.cuda.synchronize()
     hc.set_product_path(path)
     try:
@@ -398,16 +398,19 @@ def test_matrix_tiles_device(art, oracle, tiles, path):
         hc.matrix_tiles_device(d_in, tiles, I, w, G, out, masks=d_masks, samples=d_samples, pk_prep=pk_prep,
                                scratch=scratch)
         hc.matrix_tiles_device(d_in, tiles, I, w, G, plain)
+        hc.matrix_tiles_device(d_in, tiles, I, w, G, masked, masks=d_masks, scratch=scratch)
         assert hc.check() == 0
     finally:
         hc.set_product_path(0)
     got, got_plain = out.cpu().numpy().view(np.uint64), plain.cpu().numpy().view(np.uint64)
+    got_masked = masked.cpu().numpy().view(np.uint64)
     for t in range(tiles):
         cn = oc.matrix_open(cts[t], threads=8)
         for g in range(G):
             e = oc.matrix_evaluate(cn, ring[g], threads=8)
             assert np.array_equal(got_plain[t, g], e), (t, g)
             e[0] = oc.sub_plain(e[0], masks[t, g])
+            assert np.array_equal(got_masked[t, g], e), (t, g)
             e = oc.add(e, oc.enc0(samples[t, g], tb.pk))
             assert np.array_equal(got[t, g], e), (t, g)
 
