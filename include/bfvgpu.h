@@ -176,11 +176,12 @@ int32_t bfvgpu_ctx_check(bfvgpu_ctx *ctx, uint32_t *flags);
  * sharded call) finds free SMs.  Results are unchanged. */
 int32_t bfvgpu_ctx_set_reserved_sms(bfvgpu_ctx *ctx, int32_t sms);
 /* Selects the ct-pt product of bfvgpu_matrix_tiles_device: 0 (default) = tcgen05 kind::i8
- * for launches of 8 tiles with at most 64 input blocks, CUDA cores otherwise; 1 = CUDA
- * cores always.  Results are identical. */
+ * for launches of 8 tiles with at most 64 input blocks, CUDA cores with TMA-staged operands
+ * otherwise; 1 = the TMA-staged CUDA-core product always; 2 = the CUDA-core product with
+ * per-thread asynchronous-copy staging (comparison).  Results are identical. */
 int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx *ctx, int32_t path);
-/* Words of device scratch bfvgpu_matrix_tiles_device needs: 0 without Enc(0), else
- * tiles * groups * (k + 2) * n. */
+/* Words of device scratch bfvgpu_matrix_tiles_device needs for tiles * groups outputs:
+ * items * (k + 2 + 2 dk) * n with Enc(0) (enc0 != 0), items * 2 dk * n for a mask alone. */
 uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx *ctx, uint64_t tiles, uint64_t groups,
                                            int32_t enc0);
 /* Forward NTT of `count` client ciphertexts [count][2][dk][n] (coefficient form) into out
@@ -202,7 +203,8 @@ int32_t bfvgpu_matrix_tiles_prepare_pk_device(bfvgpu_ctx *ctx, const uint64_t *p
  * in [tiles][inputs][2][dk][n] from bfvgpu_matrix_tiles_inputs_device, w
  * [groups][inputs][dk][n] NTT form (bfvgpu_weights_ntt_device), masks
  * [tiles][groups][n] ring-59 words or NULL, samples [tiles][groups][3][k][n] or NULL (then
- * pk_prep and scratch may be NULL), pk_prep from bfvgpu_matrix_tiles_prepare_pk_device, out
+ * pk_prep may be NULL), pk_prep from bfvgpu_matrix_tiles_prepare_pk_device, scratch of
+ * bfvgpu_matrix_tiles_scratch_words words (NULL only without masks and samples), out
  * [tiles][groups][2][dk][n].  Each weight word is read once for all tiles. */
 int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_t tiles, uint64_t inputs,
                                    const uint64_t *w, uint64_t groups, const uint64_t *masks,

@@ -179,7 +179,8 @@ class Context:
         check(lib().bfvgpu_ctx_set_reserved_sms(self._h, sms), "set_reserved_sms")
 
     def set_product_path(self, path: int) -> None:
-        """0: tcgen05 product for 8-tile launches (default); 1: CUDA cores only."""
+        """0: tcgen05 product for 8-tile launches (default); 1: TMA-staged CUDA-core product only;
+        2: CUDA-core product with per-thread asynchronous-copy staging."""
         check(lib().bfvgpu_ctx_set_product_path(self._h, path), "set_product_path")
 
     def matrix_tiles_inputs_device(self, cts, count: int, out=None, stream: int | None = None):

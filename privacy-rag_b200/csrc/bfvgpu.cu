@@ -755,7 +755,7 @@ int32_t bfvgpu_ctx_set_reserved_sms(bfvgpu_ctx* ctx, int32_t sms) {
 
 int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx* ctx, int32_t path) {
   return guard([&] {
-    if (!ctx || path < 0 || path > 1) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (!ctx || path < 0 || path > 2) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
     ctx->c.P.product_path = path;
   });
 }

@@ -430,6 +430,93 @@ constexpr size_t mac_smem_bytes() {
   return kMacStages * (size_t)MacShape<T, TH>::kBufWords * sizeof(uint64_t);
 }
 
+// The same persistent product with its operands staged by the tensor memory accelerator:
+// per step one tiled copy brings the chunk's inputs (box 32 coefficients x 1 prime x 2
+// components x 8 blocks x T tiles of [T][I][2][dk][n]) and one its weights (32 x 1 x 8
+// blocks x GB groups of [G][I][dk][n]) into the stage buffer, in exactly the layout
+// mac_chunk reads, with zeros past the input blocks and groups.  One thread issues both
+// copies for step s + kMacStages - 1 after the block barrier of step s; every thread waits
+// on the stage's mbarrier (bounded: on expiry the block records kErrMacTimeout, waits for its
+// copies still in flight and returns).  Instead of 2,304 16-byte asynchronous copies per
+// step spread over the block's threads, two instructions move the 36-48 KiB.
+constexpr uint32_t kErrMacTimeout = 2;
+
+template <int T, int TH>
+__global__ void __launch_bounds__(MacShape<T, TH>::kThreads, 1)
+    k_mac_stream(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmW, uint64_t* out,
+                 uint32_t inputs, uint32_t groups, uint32_t gblocks, uint32_t units, uint32_t dk, int logn,
+                 const Modulus* mods, uint32_t* err) {
+  using S = MacShape<T, TH>;
+  constexpr uint32_t kStageBytes = S::kBufWords * 8;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 127) & ~127u;
+  const uint64_t* buf0 = reinterpret_cast<const uint64_t*>(smem_raw + (base - raw));
+  const uint32_t bar0 = base + kMacStages * kStageBytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t zchunks = (1u << logn) >> 5;
+  const uint32_t chunks = (inputs + S::kBc - 1) / S::kBc;
+  const uint32_t my_units = blockIdx.x < units ? (units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const uint64_t steps = (uint64_t)my_units * chunks;
+  const uint64_t pIn = reinterpret_cast<uint64_t>(&tmIn), pW = reinterpret_cast<uint64_t>(&tmW);
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < kMacStages; ++b) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * b) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // step s -> unit blockIdx.x + (s / chunks) * gridDim.x, chunk s % chunks (thread 0 only)
+  auto issue = [&](uint64_t s) {
+    if (s >= steps) return;
+    const uint32_t u = blockIdx.x + (uint32_t)(s / chunks) * gridDim.x, k = (uint32_t)(s % chunks);
+    const uint32_t gq = u % gblocks, r = u / gblocks;
+    const int p = (int)(r / zchunks), z0 = (int)((r % zchunks) * 32), b0 = (int)(k * S::kBc);
+    const uint32_t st = (uint32_t)(s % kMacStages), bar = bar0 + 8 * st, dst = base + st * kStageBytes;
+    mbar_expect(bar, kStageBytes);
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+        ::"r"(dst), "l"(pIn), "r"(z0), "r"(p), "r"(0), "r"(b0), "r"(0), "r"(bar) : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        ::"r"(dst + (uint32_t)S::kInWords * 8), "l"(pW), "r"(z0), "r"(p), "r"(b0), "r"((int)(gq * S::GB)), "r"(bar)
+        : "memory");
+  };
+  if (threadIdx.x == 0)
+    for (int s = 0; s < kMacStages - 1; ++s) issue(s);
+  Mac30 acc[TH][2];
+  Acc128 A[TH][2];
+  uint64_t s = 0;
+  bool failed = false;
+  for (; s < steps; ++s) {
+    const bool ok = mbar_wait(bar0 + 8 * (uint32_t)(s % kMacStages), (uint32_t)((s / kMacStages) & 1));
+    if (__syncthreads_or(!ok)) {  // step s is in shared memory; every warp is done with step s - 1
+      failed = true;
+      break;
+    }
+    if (threadIdx.x == 0) issue(s + kMacStages - 1);
+    const uint32_t u = blockIdx.x + (uint32_t)(s / chunks) * gridDim.x, k = (uint32_t)(s % chunks);
+    const uint32_t r = u / gblocks, p = r / zchunks;
+    const Modulus& m = mods[p];
+    mac_chunk<T, TH>(buf0 + (s % kMacStages) * S::kBufWords, warp, lane, acc, A, m, k);
+    if (k + 1 == chunks) {
+      mac_store<T, TH>(out, warp, lane, A, m, groups, (u % gblocks) * S::GB, p, (r % zchunks) * 32, dk, logn);
+#pragma unroll
+      for (int tt = 0; tt < TH; ++tt)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) A[tt][c] = Acc128{};
+    }
+  }
+  if (failed && threadIdx.x == 0) {
+    atomicOr(err, kErrMacTimeout);
+    for (uint64_t d = s; d < s + kMacStages - 1 && d < steps; ++d)  // copies still in flight
+      mbar_wait(bar0 + 8 * (uint32_t)(d % kMacStages), (uint32_t)((d / kMacStages) & 1));
+  }
+}
+
+template <int T, int TH>
+constexpr size_t mac_stream_smem_bytes() {
+  return 128 + kMacStages * ((size_t)MacShape<T, TH>::kBufWords * sizeof(uint64_t) + 8);
+}
+
 template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_ntt_split(const uint64_t* data, uint64_t* out, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
@@ -627,6 +714,10 @@ static cudaError_t configure_for() {
   chk(allow_smem(k_mac_split<4, 4>, mac_smem_bytes<4, 4>()));
   chk(allow_smem(k_mac_split<2, 2>, mac_smem_bytes<2, 2>()));
   chk(allow_smem(k_mac_split<1, 1>, mac_smem_bytes<1, 1>()));
+  chk(allow_smem(k_mac_stream<8, 4>, mac_stream_smem_bytes<8, 4>()));
+  chk(allow_smem(k_mac_stream<4, 4>, mac_stream_smem_bytes<4, 4>()));
+  chk(allow_smem(k_mac_stream<2, 2>, mac_stream_smem_bytes<2, 2>()));
+  chk(allow_smem(k_mac_stream<1, 1>, mac_stream_smem_bytes<1, 1>()));
   chk(allow_smem(k_mac_tc<32>, tc::Smem<32>::kLaunchBytes));
   chk(allow_smem(k_mac_tc<64>, tc::Smem<64>::kLaunchBytes));
   chk(allow_smem(k_intt_protect<L>, s));
@@ -904,6 +995,54 @@ static cudaError_t encode_mac_maps(const DevParams& P, const uint64_t* in, uint6
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// Tensor maps of a streamed product launch: inputs [T][I][2][dk][n] as (z, p, c, b, t) with
+// box (32, 1, 2, 8, T); weights [G][I][dk][n] as (z, p, b, g) with box (32, 1, 8, GB).
+template <int T, int TH>
+static cudaError_t encode_stream_maps(const DevParams& P, const uint64_t* in, uint64_t inputs, const uint64_t* w,
+                                      uint64_t groups, CUtensorMap* mi, CUtensorMap* mw) {
+  using S = MacShape<T, TH>;
+  auto enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t n = P.n, dk = P.dk, I = inputs, G = groups;
+  const cuuint64_t dimI[5] = {n, dk, 2, I, (cuuint64_t)T};
+  const cuuint64_t strI[4] = {n * 8, dk * n * 8, 2 * dk * n * 8, I * 2 * dk * n * 8};
+  const cuuint32_t boxI[5] = {32, 1, 2, (cuuint32_t)S::kBc, (cuuint32_t)T};
+  const cuuint64_t dimW[4] = {n, dk, I, G};
+  const cuuint64_t strW[3] = {n * 8, dk * n * 8, I * dk * n * 8};
+  const cuuint32_t boxW[4] = {32, 1, (cuuint32_t)S::kBc, (cuuint32_t)S::GB};
+  const cuuint32_t ones[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(mi, CU_TENSOR_MAP_DATA_TYPE_UINT64, 5, const_cast<uint64_t*>(in), dimI, strI, boxI, ones,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  r = enc(mw, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, const_cast<uint64_t*>(w), dimW, strW, boxW, ones,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int T, int TH>
+static cudaError_t mac_stream_launch(const DevParams& P, const uint64_t* in, uint64_t inputs, const uint64_t* w,
+                                     uint64_t groups, uint64_t* out, cudaStream_t st) {
+  using S = MacShape<T, TH>;
+  const uint64_t gblocks = (groups + S::GB - 1) / S::GB;
+  const uint64_t units = (uint64_t)P.dk * (P.n >> 5) * gblocks;
+  if (units > 0xffffffffull) return cudaErrorInvalidValue;
+  CUtensorMap mi, mw;
+  cudaError_t e = encode_stream_maps<T, TH>(P, in, inputs, w, groups, &mi, &mw);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t avail = sms > P.reserved_sms ? (uint64_t)(sms - P.reserved_sms) : 1;
+  const unsigned grid = (unsigned)(units < avail ? units : avail);
+  k_mac_stream<T, TH><<<grid, S::kThreads, mac_stream_smem_bytes<T, TH>(), st>>>(
+      mi, mw, out, (uint32_t)inputs, (uint32_t)groups, (uint32_t)gblocks, (uint32_t)units, P.dk, P.logn, P.mod,
+      P.err);
+  return cudaGetLastError();
+}
+
 template <int KPAD>
 static cudaError_t mac_tc_launch(const DevParams& P, const uint64_t* in, uint64_t inputs, const uint64_t* w,
                                  uint64_t groups, uint64_t* out, cudaStream_t st) {
@@ -948,11 +1087,20 @@ cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t ti
       t0 += T;
       continue;
     }
-    switch (T) {
-      case 8: e = mac_split_launch<8, 4>(P, ip, inputs, w, groups, ap, st); break;
-      case 4: e = mac_split_launch<4, 4>(P, ip, inputs, w, groups, ap, st); break;
-      case 2: e = mac_split_launch<2, 2>(P, ip, inputs, w, groups, ap, st); break;
-      default: e = mac_split_launch<1, 1>(P, ip, inputs, w, groups, ap, st); break;
+    if (P.product_path == 2 || !P.err || inputs > 0x7fffffffull) {  // cp.async-staged form
+      switch (T) {
+        case 8: e = mac_split_launch<8, 4>(P, ip, inputs, w, groups, ap, st); break;
+        case 4: e = mac_split_launch<4, 4>(P, ip, inputs, w, groups, ap, st); break;
+        case 2: e = mac_split_launch<2, 2>(P, ip, inputs, w, groups, ap, st); break;
+        default: e = mac_split_launch<1, 1>(P, ip, inputs, w, groups, ap, st); break;
+      }
+    } else {
+      switch (T) {
+        case 8: e = mac_stream_launch<8, 4>(P, ip, inputs, w, groups, ap, st); break;
+        case 4: e = mac_stream_launch<4, 4>(P, ip, inputs, w, groups, ap, st); break;
+        case 2: e = mac_stream_launch<2, 2>(P, ip, inputs, w, groups, ap, st); break;
+        default: e = mac_stream_launch<1, 1>(P, ip, inputs, w, groups, ap, st); break;
+      }
     }
     if (e != cudaSuccess) return e;
     t0 += T;

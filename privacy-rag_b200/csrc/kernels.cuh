@@ -26,7 +26,8 @@ struct DevParams {
   const uint64_t* crt_inv = nullptr;  // [dk][2] Shoup pair of (Q/q_j)^-1 mod q_j
   const uint64_t* crt_q = nullptr;    // [dk] limbs of Q
   uint32_t* err = nullptr;            // kernel-recorded error bits (bfvgpu_ctx_check)
-  int product_path = 0;               // 0: tcgen05 where it applies, 1: CUDA cores only
+  int product_path = 0;               // 0: tcgen05 where it applies, 1: CUDA cores only (TMA-staged),
+                                      // 2: CUDA cores with per-thread asynchronous-copy staging
   int reserved_sms = 0;               // SMs the persistent product kernels leave free
 };
 

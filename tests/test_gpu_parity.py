@@ -365,11 +365,13 @@ def test_matrix_groups_mask_enc0_crt(art, oracle):
             assert v == oracle.crt(e[0][:, t], oc.primes[:6])
 
 
-@pytest.mark.parametrize("tiles,path", [(3, 0), (9, 0), (9, 1)])
+@pytest.mark.parametrize("tiles,path", [(3, 0), (9, 0), (9, 1), (3, 2), (9, 2)])
 def test_matrix_tiles_device(art, oracle, tiles, path):
     """Layer pipeline through bfvgpu_matrix_tiles_device (tiles in launches of 8/2/1; path 0
-    takes tcgen05 for the 8-tile launch, path 1 CUDA cores only) against the oracle's
-    per-tile evaluate + sub_plain + Enc(0); also without mask and Enc(0)."""
+    takes tcgen05 for the 8-tile launch and the TMA-staged CUDA-core product for the rest,
+    path 1 the TMA-staged CUDA-core product only, path 2 the CUDA-core product with
+    per-thread asynchronous-copy staging) against the oracle's per-tile evaluate + sub_plain
+    + Enc(0); also without Enc(0), and without mask and Enc(0)."""
     import torch
     hc, oc = art
     n, k, dk = oc.n, oc.k, oc.data_k
