@@ -825,7 +825,7 @@ int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t
       if (samples) {
         cuda_check(launch_enc0_prep(c.P, samples, reinterpret_cast<const ulonglong2*>(pk_prep), items, U, xs, c.aux),
                    "enc0_prep");
-        count_launch();
+        count_launch(2);
       }
       cuda_check(launch_enc0_fin(c.P, samples, xs, masks, items, E, c.aux), "enc0_fin");
       count_launch();

@@ -559,35 +559,41 @@ BFV_HD void pk_prep_item(uint64_t item, const uint64_t* pk, ulonglong2* prep, ui
 }
 
 // Enc(0) preparation for item e (a tile-group pair): block (e, key-level prime p) stores
-// U[e][p] = NTT(u); the special-prime block also produces the special-prime coefficients
-// xs[e][c] = INTT(U . pk_c) + e_c that the divide-and-round needs.
+// U[e][p] = NTT(u).
 template <int LOGN, class Ex>
-BFV_HD void op_enc0_prep(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* samples, const ulonglong2* pk,
-                         uint64_t* U, uint64_t* xs, uint32_t k, const Modulus* mods, const ulonglong2* fwd,
-                         const ulonglong2* inv) {
+BFV_HD void op_enc0_prep(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* samples, uint64_t* U, uint32_t k,
+                         const Modulus* mods, const ulonglong2* fwd) {
   constexpr uint64_t N = uint64_t(1) << LOGN;
   const uint64_t e = blk / k;
   const uint32_t p = (uint32_t)(blk % k);
   const Modulus m = mods[p];
   const uint64_t* u = samples + (e * 3 * k + p) * N;
   uint64_t* Up = U + (e * k + p) * N;
-  {
-    auto ld = [u](int i) { return u[i]; };
-    auto st = [Up](int i, uint64_t v) { Up[i] = v; };
-    ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
-  }
-  if (p != k - 1) return;
-  for (uint32_t c = 0; c < 2; ++c) {
-    const ulonglong2* pkc = pk + ((uint64_t)c * k + p) * N;
-    const uint64_t* ec = samples + ((e * 3 + 1 + c) * k + p) * N;
-    uint64_t* xo = xs + (e * 2 + c) * N;
-    auto ld = [=](int i) {
-      const ulonglong2 w = pkc[i];
-      return shoup(Up[i], w.x, w.y, m.q);
-    };
-    auto st = [=](int i, uint64_t v) { xo[i] = add_mod(v, ec[i], m.q); };
-    ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
-  }
+  auto ld = [u](int i) { return u[i]; };
+  auto st = [Up](int i, uint64_t v) { Up[i] = v; };
+  ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
+}
+
+// Special-prime coefficients of item e's Enc(0), block (e, c): xs[e][c] = INTT(U_s . pk_c,s)
+// + e_c,s, which the divide-and-round by q_s needs (after op_enc0_prep; a block of its own
+// so that no block runs more than one transform).
+template <int LOGN, class Ex>
+BFV_HD void op_enc0_xs(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* samples, const ulonglong2* pk,
+                       const uint64_t* U, uint64_t* xs, uint32_t k, const Modulus* mods, const ulonglong2* inv) {
+  constexpr uint64_t N = uint64_t(1) << LOGN;
+  const uint64_t e = blk >> 1;
+  const uint32_t c = (uint32_t)(blk & 1), p = k - 1;
+  const Modulus m = mods[p];
+  const uint64_t* Up = U + (e * k + p) * N;
+  const ulonglong2* pkc = pk + ((uint64_t)c * k + p) * N;
+  const uint64_t* ec = samples + ((e * 3 + 1 + c) * k + p) * N;
+  uint64_t* xo = xs + (e * 2 + c) * N;
+  auto ld = [=](int i) {
+    const ulonglong2 w = pkc[i];
+    return shoup(Up[i], w.x, w.y, m.q);
+  };
+  auto st = [=](int i, uint64_t v) { xo[i] = add_mod(v, ec[i], m.q); };
+  ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
 }
 
 // Additive output term of item e, component c, data prime p, coefficient z (elementwise,

@@ -532,10 +532,17 @@ __global__ void k_pk_prep(const uint64_t* pk, ulonglong2* prep, uint64_t items, 
 
 template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
-    k_enc0_prep(const uint64_t* samples, const ulonglong2* pk, uint64_t* U, uint64_t* xs, uint32_t k,
-                const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv) {
+    k_enc0_prep(const uint64_t* samples, uint64_t* U, uint32_t k, const Modulus* mods, const ulonglong2* fwd) {
   extern __shared__ uint64_t smem[];
-  op_enc0_prep<LOGN>(BlockExec{}, smem, blockIdx.x, samples, pk, U, xs, k, mods, fwd, inv);
+  op_enc0_prep<LOGN>(BlockExec{}, smem, blockIdx.x, samples, U, k, mods, fwd);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_enc0_xs(const uint64_t* samples, const ulonglong2* pk, const uint64_t* U, uint64_t* xs, uint32_t k,
+              const Modulus* mods, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_enc0_xs<LOGN>(BlockExec{}, smem, blockIdx.x, samples, pk, U, xs, k, mods, inv);
 }
 
 __global__ void k_enc0_fin(const uint64_t* samples, const uint64_t* xs, const uint64_t* mask, uint64_t* E,
@@ -709,6 +716,7 @@ static cudaError_t configure_for() {
   chk(allow_smem(k_ks_finish<L>, (size_t(1) << L) * 8));
   chk(allow_smem(k_client_phase<L>, s));
   chk(allow_smem(k_enc0_prep<L>, s));
+  chk(allow_smem(k_enc0_xs<L>, s));
   chk(allow_smem(k_ntt_split<L>, s));
   chk(allow_smem(k_mac_split<8, 4>, mac_smem_bytes<8, 4>()));
   chk(allow_smem(k_mac_split<4, 4>, mac_smem_bytes<4, 4>()));
@@ -1138,8 +1146,14 @@ cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const 
   if (!items) return cudaSuccess;
   if (items * P.k > 0x7fffffffull) return cudaErrorInvalidValue;
   BFV_DISPATCH(P.logn, {
-    k_enc0_prep<L_><<<(unsigned)(items * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(samples, pk, U, xs, P.k,
-                                                                                         P.mod, P.fwd, P.inv);
+    k_enc0_prep<L_><<<(unsigned)(items * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(samples, U, P.k, P.mod,
+                                                                                         P.fwd);
+  });
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  BFV_DISPATCH(P.logn, {
+    k_enc0_xs<L_><<<(unsigned)(items * 2), threads_for<L_>(), smem_bytes<L_>(), st>>>(samples, pk, U, xs, P.k,
+                                                                                    P.mod, P.inv);
   });
   return cudaGetLastError();
 }

@@ -129,8 +129,9 @@ cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint6
 //  mac_tiles:    acc [T][G][2][dk][n] = sum_b in[t][b][c] . w[g][b]; in [T][I][2][dk][n] from
 //                ntt_split, w [G][I][dk][n] NTT form, all primes < 2^60, n >= 32.  Tiles
 //                run in launches of 8/4/2/1 (mac_tiles_launches counts them).
-//  enc0_prep:    U [E][k][n] = NTT(u); xs [E][2][n] = special-prime coefficients of
-//                INTT(U . pk_c) + e_c; samples [E][3][k][n]; pk prepared by pk_prep.
+//  enc0_prep:    U [E][k][n] = NTT(u) (one launch, a block per (item, prime)), then xs
+//                [E][2][n] = special-prime coefficients of INTT(U . pk_c) + e_c (a second
+//                launch, a block per (item, c)); samples [E][3][k][n]; pk from pk_prep.
 //  intt_protect: out [E][2][dk][n] = INTT(acc + U . pk') + E, i.e. INTT(acc) + Enc(0) (if U)
 //                - Delta mask (if masked), the Enc(0) data-prime part folded into the input.
 cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t tiles, uint64_t inputs,

@@ -331,10 +331,12 @@ int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, 
       }
       t0 += TT;
     }
-    if (samples)
+    if (samples) {
       for (uint64_t b = 0; b < items * k; ++b)
-        op_enc0_prep<L_>(HostExec{}, s.data(), b, samples, pkp.data(), U.data(), xs.data(), k, T.mods.data(), T.fwd,
-                         T.inv);
+        op_enc0_prep<L_>(HostExec{}, s.data(), b, samples, U.data(), k, T.mods.data(), T.fwd);
+      for (uint64_t b = 0; b < items * 2; ++b)
+        op_enc0_xs<L_>(HostExec{}, s.data(), b, samples, pkp.data(), U.data(), xs.data(), k, T.mods.data(), T.inv);
+    }
     const bool fin = samples || masks;
     if (fin)
       for (uint64_t e = 0; e < items * 2 * dk * n; ++e)
