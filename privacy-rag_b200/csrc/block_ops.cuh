@@ -597,23 +597,27 @@ BFV_HD void op_enc0_xs(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* 
 }
 
 // Additive output term of item e, component c, data prime p, coefficient z (elementwise,
-// after op_enc0_prep, beside the product):
+// after op_enc0_prep / op_enc0_xs, beside the product):
 //   E = (e_c,p - corr(x_s,c)) . q_s^-1  (if Enc(0))  -  [c = 0] Delta . mask  (if masked)
 // i.e. everything op_intt_protect adds after its transform except the part that must go
-// through it.  Layout E [items][2][dk][n].
-BFV_HD void enc0_fin_item(uint64_t item, const uint64_t* samples, const uint64_t* xs, const uint64_t* mask,
-                          uint64_t* E, uint32_t k, uint32_t dk, int logn, const Modulus* mods, uint64_t q_mod_t,
-                          uint64_t upper_half, uint64_t t, int tlog) {
+// through it.  Layout E [items][2][dk][n]; row r = (e * 2 + c) * dk + p.
+BFV_HD uint64_t enc0_fin_elem(uint64_t e, uint32_t c, uint32_t p, uint64_t z, const uint64_t* samples,
+                              const uint64_t* xs, const uint64_t* mask, uint32_t k, int logn, const Modulus* mods,
+                              uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
   const uint64_t N = uint64_t(1) << logn;
-  const uint64_t z = item & (N - 1), r = item >> logn;
-  const uint32_t p = (uint32_t)(r % dk), c = (uint32_t)((r / dk) & 1);
-  const uint64_t e = r / (2 * dk);
   const Modulus& m = mods[p];
   uint64_t v = 0;
   if (samples)
     v = moddown_elem(samples[((e * 3 + 1 + c) * k + p) * N + z], xs[(e * 2 + c) * N + z], m, mods[k - 1]);
   if (mask && c == 0) v = sub_mod(v, scale_plain_coeff(mask[e * N + z], q_mod_t, upper_half, t, tlog, m), m.q);
-  E[item] = v;
+  return v;
+}
+BFV_HD void enc0_fin_item(uint64_t item, const uint64_t* samples, const uint64_t* xs, const uint64_t* mask,
+                          uint64_t* E, uint32_t k, uint32_t dk, int logn, const Modulus* mods, uint64_t q_mod_t,
+                          uint64_t upper_half, uint64_t t, int tlog) {
+  const uint64_t z = item & ((uint64_t(1) << logn) - 1), r = item >> logn;
+  E[item] = enc0_fin_elem(r / (2 * dk), (uint32_t)((r / dk) & 1), (uint32_t)(r % dk), z, samples, xs, mask, k, logn,
+                          mods, q_mod_t, upper_half, t, tlog);
 }
 
 // INTT of the accumulated product with the Enc(0) and mask epilogue, block (e, c, p):

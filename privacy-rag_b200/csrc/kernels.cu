@@ -464,12 +464,31 @@ __global__ void __launch_bounds__(MacShape<T, TH>::kThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  // step s -> unit blockIdx.x + (s / chunks) * gridDim.x, chunk s % chunks (thread 0 only)
-  auto issue = [&](uint64_t s) {
+  // Step s = (unit blockIdx.x + i * gridDim.x, chunk k) with s = i * chunks + k, walked by
+  // cursors (no division per step): one for the consumers, one for the issuing thread.
+  const int zshift = logn - 5;
+  struct Cursor {
+    uint32_t k, u, gq, p, z0;
+  };
+  auto place = [&](Cursor& c, uint32_t u) {
+    c.u = u;
+    c.gq = u % gblocks;
+    const uint32_t r = u / gblocks;
+    c.p = r >> zshift;
+    c.z0 = (r & (zchunks - 1)) << 5;
+  };
+  auto advance = [&](Cursor& c) {
+    if (++c.k == chunks) {
+      c.k = 0;
+      place(c, c.u + gridDim.x);
+    }
+  };
+  Cursor ic{0, 0, 0, 0, 0}, cc{0, 0, 0, 0, 0};
+  place(ic, blockIdx.x);
+  place(cc, blockIdx.x);
+  auto issue = [&](uint64_t s) {  // thread 0: step s, at the issue cursor, which then advances
     if (s >= steps) return;
-    const uint32_t u = blockIdx.x + (uint32_t)(s / chunks) * gridDim.x, k = (uint32_t)(s % chunks);
-    const uint32_t gq = u % gblocks, r = u / gblocks;
-    const int p = (int)(r / zchunks), z0 = (int)((r % zchunks) * 32), b0 = (int)(k * S::kBc);
+    const int p = (int)ic.p, z0 = (int)ic.z0, b0 = (int)(ic.k * S::kBc);
     const uint32_t st = (uint32_t)(s % kMacStages), bar = bar0 + 8 * st, dst = base + st * kStageBytes;
     mbar_expect(bar, kStageBytes);
     asm volatile(
@@ -477,8 +496,9 @@ __global__ void __launch_bounds__(MacShape<T, TH>::kThreads, 1)
         ::"r"(dst), "l"(pIn), "r"(z0), "r"(p), "r"(0), "r"(b0), "r"(0), "r"(bar) : "memory");
     asm volatile(
         "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
-        ::"r"(dst + (uint32_t)S::kInWords * 8), "l"(pW), "r"(z0), "r"(p), "r"(b0), "r"((int)(gq * S::GB)), "r"(bar)
+        ::"r"(dst + (uint32_t)S::kInWords * 8), "l"(pW), "r"(z0), "r"(p), "r"(b0), "r"((int)(ic.gq * S::GB)), "r"(bar)
         : "memory");
+    advance(ic);
   };
   if (threadIdx.x == 0)
     for (int s = 0; s < kMacStages - 1; ++s) issue(s);
@@ -493,17 +513,16 @@ __global__ void __launch_bounds__(MacShape<T, TH>::kThreads, 1)
       break;
     }
     if (threadIdx.x == 0) issue(s + kMacStages - 1);
-    const uint32_t u = blockIdx.x + (uint32_t)(s / chunks) * gridDim.x, k = (uint32_t)(s % chunks);
-    const uint32_t r = u / gblocks, p = r / zchunks;
-    const Modulus& m = mods[p];
-    mac_chunk<T, TH>(buf0 + (s % kMacStages) * S::kBufWords, warp, lane, acc, A, m, k);
-    if (k + 1 == chunks) {
-      mac_store<T, TH>(out, warp, lane, A, m, groups, (u % gblocks) * S::GB, p, (r % zchunks) * 32, dk, logn);
+    const Modulus& m = mods[cc.p];
+    mac_chunk<T, TH>(buf0 + (s % kMacStages) * S::kBufWords, warp, lane, acc, A, m, cc.k);
+    if (cc.k + 1 == chunks) {
+      mac_store<T, TH>(out, warp, lane, A, m, groups, cc.gq * S::GB, cc.p, cc.z0, dk, logn);
 #pragma unroll
       for (int tt = 0; tt < TH; ++tt)
 #pragma unroll
         for (int c = 0; c < 2; ++c) A[tt][c] = Acc128{};
     }
+    advance(cc);
   }
   if (failed && threadIdx.x == 0) {
     atomicOr(err, kErrMacTimeout);
@@ -545,11 +564,30 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
   op_enc0_xs<LOGN>(BlockExec{}, smem, blockIdx.x, samples, pk, U, xs, k, mods, inv);
 }
 
-__global__ void k_enc0_fin(const uint64_t* samples, const uint64_t* xs, const uint64_t* mask, uint64_t* E,
-                           uint64_t items, uint32_t k, uint32_t dk, int logn, const Modulus* mods, uint64_t q_mod_t,
-                           uint64_t upper_half, uint64_t t, int tlog) {
-  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < items; e += (uint64_t)gridDim.x * blockDim.x)
-    enc0_fin_item(e, samples, xs, mask, E, k, dk, logn, mods, q_mod_t, upper_half, t, tlog);
+// Rows (e, c, p) of E along y (grid-stride), kFinPer x 256 coefficients of a row per block
+// along x; the row's coordinates are decoded once per block.
+constexpr int kFinPer = 4;
+__global__ void __launch_bounds__(256) k_enc0_fin(const uint64_t* samples, const uint64_t* xs, const uint64_t* mask,
+                                                  uint64_t* E, uint64_t rows, uint32_t k, uint32_t dk, int logn,
+                                                  const Modulus* mods, uint64_t q_mod_t, uint64_t upper_half,
+                                                  uint64_t t, int tlog) {
+  const uint32_t N = 1u << logn;
+  for (uint64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const uint64_t e = r / (2 * dk);
+    const uint32_t cp = (uint32_t)(r % (2 * dk)), c = cp / dk, p = cp % dk;
+    const uint32_t z0 = blockIdx.x * (256 * kFinPer) + threadIdx.x;
+    uint64_t v[kFinPer];
+#pragma unroll
+    for (int j = 0; j < kFinPer; ++j) {
+      const uint32_t z = z0 + j * 256;
+      if (z < N) v[j] = enc0_fin_elem(e, c, p, z, samples, xs, mask, k, logn, mods, q_mod_t, upper_half, t, tlog);
+    }
+#pragma unroll
+    for (int j = 0; j < kFinPer; ++j) {
+      const uint32_t z = z0 + j * 256;
+      if (z < N) E[r * N + z] = v[j];
+    }
+  }
 }
 
 template <int LOGN>
@@ -1161,9 +1199,10 @@ cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const 
 cudaError_t launch_enc0_fin(const DevParams& P, const uint64_t* samples, const uint64_t* xs, const uint64_t* mask,
                             uint64_t items, uint64_t* E, cudaStream_t st) {
   if (!items || (!samples && !mask)) return cudaSuccess;
-  const uint64_t total = items * 2 * P.dk * (uint64_t)P.n;
-  k_enc0_fin<<<elementwise_blocks(total), 256, 0, st>>>(samples, xs, mask, E, total, P.k, P.dk, P.logn, P.mod,
-                                                         P.q_mod_t, P.upper_half, P.t, P.tlog);
+  const uint64_t rows = items * 2 * P.dk;
+  const dim3 grid((P.n + 256 * kFinPer - 1) / (256 * kFinPer), (unsigned)(rows < 65535 ? rows : 65535));
+  k_enc0_fin<<<grid, 256, 0, st>>>(samples, xs, mask, E, rows, P.k, P.dk, P.logn, P.mod, P.q_mod_t, P.upper_half,
+                                   P.t, P.tlog);
   return cudaGetLastError();
 }
 
