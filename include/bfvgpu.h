@@ -63,6 +63,7 @@ typedef struct bfvgpu_ntt bfvgpu_ntt;
 typedef struct bfvgpu_matrix bfvgpu_matrix;
 typedef struct bfvgpu_switch bfvgpu_switch;
 typedef struct bfvgpu_rotations bfvgpu_rotations;
+typedef struct bfvgpu_slots bfvgpu_slots;
 typedef struct bfvgpu_enc0 bfvgpu_enc0;
 typedef struct bfvgpu_token bfvgpu_token;
 
@@ -291,6 +292,31 @@ int32_t bfvgpu_rotations_open(bfvgpu_ctx *ctx, const uint64_t *keys, const uint3
 int32_t bfvgpu_rotations_apply(bfvgpu_rotations *r, const uint64_t *cts, uint64_t m, uint64_t *out);
 int32_t bfvgpu_rotations_close(bfvgpu_rotations *r, bfvgpu_cleanup *cleanup);
 int32_t bfvgpu_rotations_release(bfvgpu_rotations *r);
+
+/* ---- Slot-packed matrix-vector product: BFV batching with rotate-and-sum -----------------
+ * The slot variant of the ct-pt matvec (the benchmark's config 3: W [O][K] times a vector of
+ * K values in Z_t, t = 1 mod 2n).  The reference's matrix protocol packs coefficients, not
+ * slots, so this has no counterpart there; it reuses this library's hoisted rotations and
+ * its multi-block ct-pt product.  Slots form two rows of n/2; the input ciphertext holds
+ * x[i mod K] in row 0 and x[(i + K/2) mod K] in row 1 (K even, K | n/2, O <= n/2).  With
+ * baby * giant = K/2 the result's row 0 holds y[i] = sum_j W[i][j] x[j] at slots i < O:
+ *   y = sum_g rot(sum_b pt[g][b] . rot(x, b), g*baby), then row 0 + row 1 (swap + add),
+ * where pt[g][b] is the diagonal pair (g*baby + b, K/2 + g*baby + b) pre-rotated by
+ * -g*baby.  Keys [baby - 1 + giant - 1 + 1][dk][2][k][n] (host, NTT form) for the Galois
+ * elements 3^b (b = 1..baby-1), 3^(g*baby) (g = 1..giant-1) and 2n - 1, in that order;
+ * plain [giant][baby][n] (device) the encoded plaintext polynomials (coefficients < t),
+ * transformed once here.  Per product: one hoist and baby-1 rotations in one launch pair,
+ * the input transform, one product launch over all giant*baby plaintexts, one hoist and
+ * giant-1 paired rotations, a sum and the row swap. */
+int32_t bfvgpu_slots_open(bfvgpu_ctx *ctx, const uint64_t *keys, uint32_t baby, uint32_t giant,
+                          const uint64_t *plain, bfvgpu_slots **out);
+/* ct [2][dk][n] -> out [2][dk][n], coefficient form; device pointers (stream NULL: the
+ * context stream). */
+int32_t bfvgpu_slots_apply_device(bfvgpu_slots *s, const uint64_t *ct, uint64_t *out, void *stream);
+/* The same from host buffers (upload, product, download, synchronise). */
+int32_t bfvgpu_slots_apply(bfvgpu_slots *s, const uint64_t *ct, uint64_t *out);
+int32_t bfvgpu_slots_close(bfvgpu_slots *s, bfvgpu_cleanup *cleanup);
+int32_t bfvgpu_slots_release(bfvgpu_slots *s);
 
 /* ---- PublicZero (IV1/native/gpu/enc0/enc0.hpp:15-25) ------------------------------------ */
 int32_t bfvgpu_enc0_open(bfvgpu_ctx *ctx, const uint64_t *pk, bfvgpu_enc0 **out);

@@ -107,6 +107,11 @@ _SIGNATURES = {
     "bfvgpu_rotations_apply": (I32, [VP, U64P, U64, U64P]),
     "bfvgpu_rotations_close": (I32, [VP, ctypes.POINTER(Cleanup)]),
     "bfvgpu_rotations_release": (I32, [VP]),
+    "bfvgpu_slots_open": (I32, [VP, U64P, U32, U32, VP, ctypes.POINTER(VP)]),
+    "bfvgpu_slots_apply_device": (I32, [VP, VP, VP, VP]),
+    "bfvgpu_slots_apply": (I32, [VP, U64P, U64P]),
+    "bfvgpu_slots_close": (I32, [VP, ctypes.POINTER(Cleanup)]),
+    "bfvgpu_slots_release": (I32, [VP]),
     "bfvgpu_switch_packing_pair": (I32, [VP, U64P, U64P, VP, U32, U64P]),
     "bfvgpu_switch_timing": (I32, [VP, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                                    ctypes.POINTER(ctypes.c_double)]),

@@ -424,6 +424,44 @@ class Rotations(_Handle):
         return out
 
 
+class SlotMatvec(_Handle):
+    """Slot-packed ct-pt matrix-vector product (BFV batching, rotate-and-sum with baby-step
+    giant-step diagonals; bfvgpu.slots builds the plaintexts and the input packing).  Keys
+    [baby-1 + giant-1 + 1][dk][2][k][n] (host) for 3^b, 3^(g*baby) and 2n-1; plain
+    [giant][baby][n] encoded plaintext polynomials on the device."""
+
+    _close_fn = "bfvgpu_slots_close"
+    _release_fn = "bfvgpu_slots_release"
+
+    def __init__(self, ctx: Context, keys, baby: int, giant: int, plain):
+        super().__init__(ctx)
+        self.baby, self.giant = int(baby), int(giant)
+        k = u64(keys)
+        if k.size != (self.baby + self.giant - 1) * ctx.dk * 2 * ctx.k * ctx.n:
+            raise ValueError("E_SLOTS_KEYS")
+        if plain.numel() != self.giant * self.baby * ctx.n:
+            raise ValueError("E_SLOTS_PLAIN")
+        h = VP()
+        check(lib().bfvgpu_slots_open(ctx.handle, ptr(k), self.baby, self.giant, Context._dptr(plain),
+                                      ctypes.byref(h)), "SlotMatvec")
+        self._h = h
+
+    def apply_device(self, ct, out, stream: int | None = None) -> None:
+        """ct, out: device tensors of [2][dk][n] words (coefficient form)."""
+        check(lib().bfvgpu_slots_apply_device(self._h, Context._dptr(ct), Context._dptr(out), stream),
+              "SlotMatvec.apply_device")
+
+    def apply(self, ct, out=None) -> np.ndarray:
+        """Host ciphertext [2][dk][n] -> host result [2][dk][n]."""
+        a = u64(ct)
+        if a.size != 2 * self.ctx.dk * self.ctx.n:
+            raise ValueError("E_SLOTS_CIPHERTEXT")
+        if out is None:
+            out = np.empty((2, self.ctx.dk, self.ctx.n), dtype=np.uint64)
+        check(lib().bfvgpu_slots_apply(self._h, ptr(a), ptr(out)), "SlotMatvec.apply")
+        return out
+
+
 class PublicZero(_Handle):
     """Enc(0) from explicit samples (u ternary, e0, e1) with a bound public key."""
 

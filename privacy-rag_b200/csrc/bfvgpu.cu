@@ -505,6 +505,17 @@ struct bfvgpu_rotations {
   cudaEvent_t computed[2] = {nullptr, nullptr}, copied[2] = {nullptr, nullptr};
 };
 
+struct bfvgpu_slots {
+  Holder h;
+  uint32_t baby = 0, giant = 0;
+  std::vector<uint32_t> elts;  // baby (3^b), giant (3^(g baby)), swap (2n - 1)
+  uint64_t pw = 0;
+  uint64_t* prepared = nullptr;  // [baby - 1 + giant - 1 + 1][pw]
+  uint64_t* pt = nullptr;        // [giant][baby][dk][n] NTT-form plaintexts
+  uint64_t *ct = nullptr, *hoisted = nullptr, *x = nullptr, *rot = nullptr, *in = nullptr, *part = nullptr,
+           *giant_out = nullptr, *sum = nullptr, *swapped = nullptr, *out = nullptr;
+};
+
 struct bfvgpu_enc0 {
   Holder h;
   uint64_t *pk = nullptr, *samples = nullptr, *u_ntt = nullptr, *x = nullptr, *out = nullptr, *plain = nullptr;
@@ -1422,6 +1433,147 @@ int32_t bfvgpu_rotations_close(bfvgpu_rotations* s, bfvgpu_cleanup* cleanup) {
 int32_t bfvgpu_rotations_release(bfvgpu_rotations* s) {
   if (!s) return BFVGPU_OK;
   bfvgpu_rotations_close(s, nullptr);
+  delete s;
+  return BFVGPU_OK;
+}
+
+// ---- slot-packed matrix-vector product (BFV batching, baby-step giant-step diagonals) ---------
+// Galois element of a left rotation of both slot rows by r: 3^r mod 2n.
+static uint32_t row_rotation_elt(uint64_t r, uint32_t n) {
+  const uint64_t m = 2ull * n;
+  uint64_t g = 1, b = 3;
+  for (r %= n / 2; r; r >>= 1, b = b * b % m)
+    if (r & 1) g = g * b % m;
+  return (uint32_t)g;
+}
+
+int32_t bfvgpu_slots_open(bfvgpu_ctx* ctx, const uint64_t* keys, uint32_t baby, uint32_t giant, const uint64_t* plain,
+                          bfvgpu_slots** out) {
+  return guard([&] {
+    if (!ctx || !keys || !plain || !out || baby < 1 || giant < 1) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    *out = nullptr;
+    const Context& c = ctx->c;
+    if (c.k != c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_NTT_CONTEXT");
+    require_product_ring(c);
+    if ((uint64_t)baby * giant > c.n / 2 || baby > 4096 || giant > 4096) fail(BFVGPU_E_SHAPE, "E_SLOTS_SHAPE");
+    auto s = std::make_unique<bfvgpu_slots>();
+    s->h.ctx = &ctx->c;
+    s->baby = baby;
+    s->giant = giant;
+    for (uint32_t b = 1; b < baby; ++b) s->elts.push_back(row_rotation_elt(b, c.n));
+    for (uint32_t g = 1; g < giant; ++g) s->elts.push_back(row_rotation_elt((uint64_t)g * baby, c.n));
+    s->elts.push_back(2 * c.n - 1);
+    const uint64_t nkeys = s->elts.size(), kw = (uint64_t)c.dk * 2 * c.k * c.n;
+    check_canonical_host(c, keys, nkeys * c.dk * 2 * c.k, c.k, 0);
+    s->pw = (2ull * c.dk + 2) * c.k * c.n;
+    require_device(c);
+    DeviceScope scope(c.device);
+    s->h.run([&] {
+      const uint64_t ctw = 2ull * c.dk * c.n, most = baby > giant ? baby : giant;
+      s->prepared = s->h.alloc(nkeys * s->pw);
+      constexpr uint64_t kBatch = 16;
+      uint64_t* tmp = s->h.alloc((nkeys < kBatch ? nkeys : kBatch) * kw);
+      for (uint64_t first = 0; first < nkeys; first += kBatch) {
+        const uint64_t m = nkeys - first < kBatch ? nkeys - first : kBatch;
+        s->h.h2d(tmp, keys + first * kw, m * kw);
+        cuda_check(launch_ks_keyprep(c.P, tmp, s->elts.data() + first, m, s->prepared + first * s->pw, c.stream),
+                   "keyprep");
+        count_launch(2);
+      }
+      s->pt = s->h.alloc((uint64_t)giant * baby * c.dk * c.n);
+      cuda_check(launch_lift_ntt(c.P, plain, s->pt, (uint64_t)giant * baby, c.stream), "lift_ntt");
+      count_launch();
+      s->ct = s->h.alloc(ctw);
+      s->hoisted = s->h.alloc(most * c.dk * c.k * c.n + (most + 1) / 2);
+      s->x = s->h.alloc(most * 2 * c.k * c.n);
+      s->rot = s->h.alloc(baby * ctw);
+      s->in = s->h.alloc(baby * ctw);
+      s->part = s->h.alloc(giant * ctw);
+      s->giant_out = s->h.alloc(giant * ctw);
+      s->sum = s->h.alloc(ctw);
+      s->swapped = s->h.alloc(ctw);
+      s->out = s->h.alloc(ctw);
+      s->h.sync();
+    });
+    *out = s.release();
+  });
+}
+
+// One product on the context's device: ct [2][dk][n] -> out [2][dk][n] (device pointers).
+static void slots_eval(bfvgpu_slots* s, const uint64_t* ct, uint64_t* out, cudaStream_t st) {
+  const Context& c = *s->h.ctx;
+  const uint64_t ctw = 2ull * c.dk * c.n, B = s->baby, G = s->giant;
+  uint32_t* zflag = (uint32_t*)(s->hoisted + (B > G ? B : G) * c.dk * c.k * c.n);
+  // baby steps: rot[b] = rotate(ct, b) from one hoisted decomposition
+  cuda_check(cudaMemcpyAsync(s->rot, ct, ctw * 8, cudaMemcpyDeviceToDevice, st), "D2D");
+  if (B > 1) {
+    cuda_check(launch_ks_hoist(c.P, ct, 1, s->hoisted, zflag, st), "hoist");
+    cuda_check(launch_ks_rotate_multi(c.P, ct, 1, s->hoisted, zflag, s->prepared, s->elts.data(), B - 1, 0, s->x,
+                                      s->rot + ctw, st),
+               "rotate");
+    count_launch(1 + 2 * ((B - 1 + 255) / 256));
+  }
+  // part[g] = sum_b pt[g][b] . rot[b] (coefficient form)
+  cuda_check(launch_ntt_split(c.P, s->rot, s->in, B * 2 * c.dk, st), "ntt_split");
+  cuda_check(launch_mac_tiles(c.P, s->in, 1, B, s->pt, G, s->part, st), "mac_tiles");
+  cuda_check(launch_intt_protect(c.P, s->part, G, nullptr, nullptr, nullptr, s->part, st), "intt_protect");
+  count_launch(2 + mac_tiles_launches(1));
+  // giant steps: giant_out[g] = rotate(part[g], g * baby), paired from one hoist of parts 1..G-1
+  cuda_check(cudaMemcpyAsync(s->giant_out, s->part, ctw * 8, cudaMemcpyDeviceToDevice, st), "D2D");
+  if (G > 1) {
+    cuda_check(launch_ks_hoist(c.P, s->part + ctw, G - 1, s->hoisted, zflag, st), "hoist");
+    cuda_check(launch_ks_rotate_multi(c.P, s->part + ctw, G - 1, s->hoisted, zflag, s->prepared + (B - 1) * s->pw,
+                                      s->elts.data() + (B - 1), G - 1, 1, s->x, s->giant_out + ctw, st),
+               "rotate");
+    count_launch(1 + 2 * ((G - 1 + 255) / 256));
+  }
+  cuda_check(launch_sum_cts(c.P, s->giant_out, G, s->sum, st), "sum");
+  // row swap: out = sum + sigma_{2n-1}(sum)
+  cuda_check(launch_ks_hoist(c.P, s->sum, 1, s->hoisted, zflag, st), "hoist");
+  cuda_check(launch_ks_rotate_multi(c.P, s->sum, 1, s->hoisted, zflag, s->prepared + (B + G - 2) * s->pw,
+                                    s->elts.data() + (B + G - 2), 1, 1, s->x, s->swapped, st),
+             "rotate");
+  cuda_check(cudaMemcpyAsync(out, s->sum, ctw * 8, cudaMemcpyDeviceToDevice, st), "D2D");
+  cuda_check(launch_add(c.P, out, s->swapped, 2 * c.dk, st), "add");
+  count_launch(5);
+}
+
+int32_t bfvgpu_slots_apply_device(bfvgpu_slots* s, const uint64_t* ct, uint64_t* out, void* stream) {
+  return guard([&] {
+    if (!s || !ct || !out) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    s->h.check_open("E_SWITCH_CLOSED");
+    DeviceScope scope(s->h.ctx->device);
+    s->h.run([&] { slots_eval(s, ct, out, stream ? (cudaStream_t)stream : s->h.ctx->stream); });
+  });
+}
+
+int32_t bfvgpu_slots_apply(bfvgpu_slots* s, const uint64_t* ct, uint64_t* out) {
+  return guard([&] {
+    if (!s || !ct || !out) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    s->h.check_open("E_SWITCH_CLOSED");
+    const Context& c = *s->h.ctx;
+    check_canonical_host(c, ct, 2 * c.dk, c.dk, 0);
+    DeviceScope scope(c.device);
+    s->h.run([&] {
+      const uint64_t ctw = 2ull * c.dk * c.n;
+      s->h.h2d(s->ct, ct, ctw);
+      slots_eval(s, s->ct, s->out, c.stream);
+      s->h.d2h(out, s->out, ctw);
+      s->h.sync();
+    });
+  });
+}
+
+int32_t bfvgpu_slots_close(bfvgpu_slots* s, bfvgpu_cleanup* cleanup) {
+  if (!s) return BFVGPU_E_ARGUMENT;
+  const bfvgpu_cleanup c = s->h.release();
+  if (cleanup) *cleanup = c;
+  return BFVGPU_OK;
+}
+
+int32_t bfvgpu_slots_release(bfvgpu_slots* s) {
+  if (!s) return BFVGPU_OK;
+  bfvgpu_slots_close(s, nullptr);
   delete s;
   return BFVGPU_OK;
 }

@@ -637,6 +637,48 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
   op_ks_finish<LOGN>(BlockExec{}, smem, blockIdx.x, x, cts, out, ginv, k, dk, mods);
 }
 
+// Hoisted rotations of many (element, ciphertext) pairs in one launch pair.  paired != 0:
+// ciphertext i with element i (blocks (i, c, p); x [count][2][k][n], out [count][2][dk][n]);
+// else every element e with every ciphertext (x [m][count][2][k][n], out [m][count][2][dk][n]).
+// Element e uses prepared key e (prepared + e * prepared_words).
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_ks_rotate_multi(const uint64_t* cts, uint64_t count, const uint64_t* Y, const uint32_t* zflag,
+                      const uint64_t* prepared, uint64_t prepared_words, EltBatch eb, int paired, uint64_t* x,
+                      uint32_t k, uint32_t dk, const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd,
+                      const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  const uint64_t per = paired ? 2ull * k : count * 2 * k;
+  const uint64_t e = blockIdx.x / per, blk = paired ? blockIdx.x : blockIdx.x % per;
+  uint64_t* xe = paired ? x : x + ((e * count * 2 * k) << LOGN);
+  op_ks_rotate<LOGN>(BlockExec{}, smem, blk, cts, Y, zflag, prepared + e * prepared_words, xe, eb.elt[e], k, dk, mods,
+                     qjp, fwd, inv);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_ks_finish_multi(const uint64_t* x, const uint64_t* cts, uint64_t count, uint64_t* out, EltBatch eb, int paired,
+                      uint32_t k, uint32_t dk, const Modulus* mods) {
+  extern __shared__ uint64_t smem[];
+  const uint64_t per = paired ? (uint64_t)dk : count * dk;
+  const uint64_t e = blockIdx.x / per, blk = paired ? blockIdx.x : blockIdx.x % per;
+  const uint64_t* xe = paired ? x : x + ((e * count * 2 * k) << LOGN);
+  uint64_t* oe = paired ? out : out + ((e * count * 2 * dk) << LOGN);
+  op_ks_finish<LOGN>(BlockExec{}, smem, blk, xe, cts, oe, eb.ginv[e], k, dk, mods);
+}
+
+// out [G][2][dk][n] -> acc [2][dk][n] = sum over the G ciphertexts (mod q_p), elementwise.
+__global__ void k_sum_cts(const uint64_t* in, uint64_t groups, uint64_t* acc, uint32_t dk, int logn,
+                          const Modulus* mods) {
+  const uint64_t words = (2ull * dk) << logn;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < words; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t q = mods[(i >> logn) % dk].q;
+    uint64_t v = 0;
+    for (uint64_t g = 0; g < groups; ++g) v = add_mod(v, in[g * words + i], q);
+    acc[i] = v;
+  }
+}
+
 // c0 target gather (+ CRT): thread = (group, target)
 __global__ void k_gather_targets(const uint64_t* out, const uint64_t* targets, const uint32_t* counts,
                                  uint32_t max_count, uint32_t dk, int logn, const Modulus* mods,
@@ -752,6 +794,8 @@ static cudaError_t configure_for() {
   chk(allow_smem(k_ks_negntt<L>, s));
   chk(allow_smem(k_ks_rotate<L>, s));
   chk(allow_smem(k_ks_finish<L>, (size_t(1) << L) * 8));
+  chk(allow_smem(k_ks_rotate_multi<L>, s));
+  chk(allow_smem(k_ks_finish_multi<L>, (size_t(1) << L) * 8));
   chk(allow_smem(k_client_phase<L>, s));
   chk(allow_smem(k_enc0_prep<L>, s));
   chk(allow_smem(k_enc0_xs<L>, s));
@@ -906,6 +950,47 @@ cudaError_t launch_ks_rotate(const DevParams& P, const uint64_t* cts, uint64_t c
     k_ks_finish<L_><<<(unsigned)(count * P.dk), threads_for<L_>(), (size_t(1) << L_) * 8, st>>>(x, cts, out, ginv,
                                                                                                P.k, P.dk, P.mod);
   });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ks_rotate_multi(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
+                                   const uint32_t* zflag, const uint64_t* prepared, const uint32_t* elts,
+                                   uint64_t elements, int paired, uint64_t* x, uint64_t* out, cudaStream_t st) {
+  if (!count || !elements) return cudaSuccess;
+  if (P.k != P.dk + 1 || (paired && elements != count)) return cudaErrorInvalidValue;
+  const uint64_t pw = (2ull * P.dk + 2) * P.k * P.n;
+  const uint64_t ctw = 2ull * P.dk * P.n, yw = (uint64_t)P.dk * P.k * P.n, xw = 2ull * P.k * P.n;
+  for (uint64_t first = 0; first < elements; first += kKeyBatch) {
+    const uint64_t m = elements - first < (uint64_t)kKeyBatch ? elements - first : (uint64_t)kKeyBatch;
+    EltBatch eb{};
+    for (uint64_t r = 0; r < m; ++r) {
+      eb.elt[r] = elts[first + r];
+      eb.ginv[r] = inverse_mod_2n(elts[first + r], 2 * P.n);
+    }
+    // paired: this chunk's ciphertexts are first..first+m; else all ciphertexts, elements first..
+    const uint64_t c0 = paired ? first : 0, cn = paired ? m : count;
+    const uint64_t* cp = cts + c0 * ctw;
+    const uint64_t* yp = Y + c0 * yw;
+    const uint32_t* zp = zflag + c0;
+    uint64_t* xp = paired ? x + c0 * xw : x;
+    uint64_t* op = paired ? out + c0 * ctw : out + first * count * ctw;
+    const uint64_t rot_blocks = m * (paired ? 1 : cn) * 2 * P.k, fin_blocks = m * (paired ? 1 : cn) * P.dk;
+    if (rot_blocks > 0x7fffffffull) return cudaErrorInvalidValue;
+    BFV_DISPATCH(P.logn, {
+      k_ks_rotate_multi<L_><<<(unsigned)rot_blocks, threads_for<L_>(), smem_bytes<L_>(), st>>>(
+          cp, cn, yp, zp, prepared + first * pw, pw, eb, paired, xp, P.k, P.dk, P.mod, P.qjp, P.fwd, P.inv);
+      k_ks_finish_multi<L_><<<(unsigned)fin_blocks, threads_for<L_>(), (size_t(1) << L_) * 8, st>>>(
+          xp, cp, cn, op, eb, paired, P.k, P.dk, P.mod);
+    });
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_sum_cts(const DevParams& P, const uint64_t* in, uint64_t groups, uint64_t* acc, cudaStream_t st) {
+  const uint64_t words = (2ull * P.dk) << P.logn;
+  k_sum_cts<<<elementwise_blocks(words), 256, 0, st>>>(in, groups, acc, P.dk, P.logn, P.mod);
   return cudaGetLastError();
 }
 

@@ -84,6 +84,15 @@ cudaError_t launch_ks_keyprep(const DevParams& P, const uint64_t* keys, const ui
 cudaError_t launch_ks_rotate(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
                              const uint32_t* zflag, const uint64_t* prepared, uint32_t elt, uint64_t* x, uint64_t* out,
                              cudaStream_t st);
+// Hoisted rotations of many elements in one launch pair (chunks of 256 elements):
+// paired != 0 rotates ciphertext i by element i (elements == count; x [count][2][k][n],
+// out [count][2][dk][n]); else every element rotates every ciphertext (x
+// [elements][count][2][k][n], out [elements][count][2][dk][n]).  prepared [elements][..].
+cudaError_t launch_ks_rotate_multi(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
+                                   const uint32_t* zflag, const uint64_t* prepared, const uint32_t* elts,
+                                   uint64_t elements, int paired, uint64_t* x, uint64_t* out, cudaStream_t st);
+// acc [2][dk][n] = sum of the groups ciphertexts in [groups][2][dk][n].
+cudaError_t launch_sum_cts(const DevParams& P, const uint64_t* in, uint64_t groups, uint64_t* acc, cudaStream_t st);
 
 // Enc(0) pre-moddown polys: x [groups][2][k][n] = INTT(NTT(u) . pk_c) + e_c with
 // samples [groups][3][k][n]; scratch u_ntt [groups][k][n].
