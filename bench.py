@@ -299,6 +299,108 @@ def run_layer_legs(torch, bfvgpu, device, args):
     return out
 
 
+def run_slots_leg(torch, bfvgpu, device, args):
+    """Config 3 as BASELINE.json states it: W 2048x1024 int8 (uniform [-127, 127]) times one
+    token's 1024 values in Z_t with BFV slot packing and rotate-and-sum at n = 8192 (the
+    config-2 modulus chain, t = 65537).  bfvgpu.SlotMatvec: 31 hoisted baby-step rotations,
+    one product over 512 diagonal plaintexts, 15 giant-step rotations, the row swap.  Keys:
+    seeded random NTT-form (the cost of real keys).  Weight preparation (diagonals, encoding,
+    key upload and preparation, plaintext transforms) is timed separately; the per-matvec time
+    is device events on the context stream with the ciphertext resident, and `e2e_ms` runs the
+    host API (upload, product, download) per matvec."""
+    import bfvgpu.slots as S
+    primes = bfvgpu.find_primes(N2, BITS2)
+    ctx = bfvgpu.Context(N2, primes, 4, 1, T2, device=device)
+    pc = bfvgpu.Context(N2, [T2], 1, 0, 2, device=device)
+    lay = S.SlotLayout(N2, 1024, 2048, T2)
+    baby, giant = lay.steps
+    elts = S.rotation_elements(N2, baby, giant)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    q = torch.tensor(primes, dtype=torch.int64, device="cuda")
+    keys = torch.remainder(torch.randint(0, 2 ** 62, (len(elts), 4, 2, 5, N2), dtype=torch.int64, device="cuda",
+                                         generator=g), q.view(1, 1, 1, 5, 1)).cpu().numpy().view(np.uint64)
+    w = torch.randint(-127, 128, (2048, 1024), dtype=torch.int64, device="cuda", generator=g)
+    ct = torch.remainder(torch.randint(0, 2 ** 62, (2, 4, N2), dtype=torch.int64, device="cuda", generator=g),
+                         q[:4].view(1, 4, 1))
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    plain = lay.encode_device(torch, pc, lay.diagonals_device(torch, w))
+    sm = bfvgpu.SlotMatvec(ctx, keys, baby, giant, plain)
+    torch.cuda.synchronize()
+    prep_ms = 1e3 * (time.perf_counter() - t0)
+    out = torch.empty_like(ct)
+    for _ in range(3):
+        sm.apply_device(ct, out)
+    torch.cuda.synchronize()
+    reps = 20
+    launches0 = bfvgpu.launch_count()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(reps):
+        sm.apply_device(ct, out)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    launches = (bfvgpu.launch_count() - launches0) // reps
+    host_ct = torch.empty((2, 4, N2), dtype=torch.int64, pin_memory=True)
+    host_ct.copy_(ct.cpu())
+    hin = host_ct.numpy().view(np.uint64)
+    hout = torch.empty((2, 4, N2), dtype=torch.int64, pin_memory=True).numpy().view(np.uint64)
+    sm.apply(hin, out=hout)
+    t1 = time.perf_counter()
+    for _ in range(reps):
+        sm.apply(hin, out=hout)
+    e2e_ms = 1e3 * (time.perf_counter() - t1) / reps
+    match = bool(np.array_equal(hout, out.cpu().numpy().view(np.uint64)))
+    sm.close()
+    res = {"ms": ms, "unit": "ms per matvec (one token, 2048x1024)", "e2e_ms": e2e_ms,
+           "e2e_h2d_bytes": 2 * 4 * N2 * 8, "e2e_d2h_bytes": 2 * 4 * N2 * 8, "ms_weight_prep": prep_ms,
+           "baby": baby, "giant": giant, "keyswitches": len(elts), "diagonal_plaintexts": baby * giant,
+           "launches_per_matvec": int(launches), "host_matches_device": match,
+           "note": "n=8192, 4x50-bit + 60-bit special prime, t=65537; slots: x with period 1024 in both rows "
+                   "(row 1 shifted by 512), 1024 extended diagonals as 512 plaintext pairs, baby-step giant-step"}
+    del keys, plain
+    torch.cuda.empty_cache()
+    return res
+
+
+def cpu_slots_sample(baby: int = 32, giant: int = 16):
+    """The slot matvec's steps on the oracle, all host threads, one matvec: baby-1 keyswitches
+    of the input, the product of the baby rotations with giant x baby plaintexts (transformed
+    once, outside the timing, as the GPU object does), giant-1 keyswitches, the row swap."""
+    from concurrent.futures import ThreadPoolExecutor
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    primes = O.coeff_modulus(N2, BITS2)
+    oc = O.Ctx(N2, primes, data_k=4, t=T2)
+    cores = cpu_count()
+    m = 2 * N2
+    elts = [pow(3, b, m) for b in range(1, baby)] + [pow(3, gi * baby, m) for gi in range(1, giant)] + [m - 1]
+    keys = [oc.uniform(400 + i, 4 * 2 * 5, prime_count=5).reshape(4, 2, 5, N2) for i in range(len(elts))]
+    ct = oc.uniform(399, 2 * 4).reshape(2, 4, N2)
+    rng = np.random.default_rng(8)
+    pt = rng.integers(0, T2, size=(giant, baby, N2)).astype(np.uint64)
+    with ThreadPoolExecutor(cores) as ex:
+        t0 = time.perf_counter()
+        rots = list(ex.map(lambda i: oc.keyswitch(ct, keys[i], elts[i]), range(baby - 1)))
+        cn = oc.matrix_open(np.stack([ct] + rots), threads=cores)
+        parts = list(ex.map(lambda gi: oc.matrix_evaluate(cn, pt[gi], threads=1), range(giant)))
+        moved = list(ex.map(lambda gi: oc.keyswitch(parts[gi], keys[baby - 2 + gi], elts[baby - 2 + gi]),
+                            range(1, giant)))
+        acc = parts[0]
+        for r in moved:
+            acc = oc.add(acc, r)
+        oc.add(acc, oc.keyswitch(acc, keys[-1], elts[-1]))
+        dt = time.perf_counter() - t0
+    # matrix_evaluate also lifts and transforms the plaintexts; the GPU object holds them
+    # transformed, so the CPU figure is an upper bound by those giant*baby*4 transforms
+    return 1e3 * dt, cores, (f"one 2048x1024 slot matvec on the oracle ({baby - 1} + {giant - 1} + 1 keyswitches, "
+                             f"{giant}x{baby} plaintext products incl. their transforms) on {cores} threads")
+
+
 def run_model_leg(torch, bfvgpu, device, args, dist):
     """Config 5: the linear protocol of all 28 Qwen3-0.6B-shaped layers for a 512-token
     prefill (32 tiles of B = 16, run as 4 launches of 8 tiles per projection) and 64
@@ -588,6 +690,8 @@ def main():
     ap.add_argument("--model-only", action="store_true", help="run only the config-5 leg")
     ap.add_argument("--model-layers", type=int, default=28)
     ap.add_argument("--model-decode", type=int, default=64, help="decode steps in the config-5 leg")
+    ap.add_argument("--slots", type=int, default=1, help="0 skips the slot-packed matvec leg (config 3)")
+    ap.add_argument("--slots-only", action="store_true", help="run only the slot-packed matvec leg")
     ap.add_argument("--layer-shape", default=None,
                     help="K,O: with --layer-only, one B=16 projection of this shape instead of config 3/4 "
                          "(small profiling case)")
@@ -611,6 +715,14 @@ def main():
 
     if args.layer_only:
         print(json.dumps({"layer_legs": run_layer_legs(torch, bfvgpu, local, args)}), flush=True)
+        return 0
+    if args.slots_only:
+        res = run_slots_leg(torch, bfvgpu, local, args)
+        if not args.no_cpu:
+            ms, cores, sample = cpu_slots_sample()
+            res["cpu_baseline"] = {"value": ms, "unit": "ms per matvec", "cores": cores, "kind": "port",
+                                   "sample": sample}
+        print(json.dumps({"slots_config3": res}), flush=True)
         return 0
     if args.model_only:
         res = run_model_leg(torch, bfvgpu, local, args, dist)
@@ -718,6 +830,7 @@ def main():
 
     # ---- secondary: ct-pt matvec (config 3) and one decoder layer (config 4), ART-002 ----
     layer_res = run_layer_legs(torch, bfvgpu, local, args) if args.layer else None
+    slots_res = run_slots_leg(torch, bfvgpu, local, args) if args.slots else None
     model_res = run_model_leg(torch, bfvgpu, local, args, dist) if args.model else None
 
     # ---- secondary: NTT round trips (config 1) ----
@@ -792,6 +905,10 @@ def main():
         nv, _ = cpu_ntt_sample()
         cpu = {"value": v, "unit": "keyswitches/s", "cores": cores, "kind": "port", "sample": sample,
                "ntt_value": nv, "ntt_unit": "NTTs/s"}
+        if slots_res:
+            ms, scores, ssample = cpu_slots_sample()
+            slots_res["cpu_baseline"] = {"value": ms, "unit": "ms per matvec", "cores": scores, "kind": "port",
+                                         "sample": ssample}
         if layer_res or model_res:
             from bfvgpu import layer as L
             rates, open_rate, lcores, lsample = cpu_layer_sample()
@@ -840,6 +957,7 @@ def main():
                                               "path": "bfvgpu_keyswitch_device (no hoisting, Switch::apply)",
                                               "avg_launch_ms": 1e3 * sum(plain_per) / len(plain_per),
                                               "matches_hoisted": plain_match},
+                      "matvec_config3_slots": slots_res,
                       "matvec_config3": layer_res and layer_res["config3"],
                       "layer_config4": layer_res and layer_res["config4"],
                       "attention_pair": layer_res and layer_res.get("attention"),
