@@ -472,6 +472,7 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
     pg_in = dist.new_group(list(range(world))) if multi else None
     pg_out = dist.new_group(list(range(world))) if multi else None
     wcache = [dict() for _ in range(layers)]
+    aux = torch.cuda.Stream()  # side stream for the decode calls' protection prepared ahead
     stats = {"broadcast_bytes": 0, "gathered_bytes": 0, "calls": 0}
 
     # the pass as a flat schedule: ("wpre", layer) / ("wdec", layer) weight preparation,
@@ -531,6 +532,24 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
                 works[ci] = dist.broadcast(buf, src=0, group=pg_in, async_op=True)
                 stats["broadcast_bytes"] += buf.numel() * 8
 
+        # decode calls: the output protection (Enc(0) preparation, additive output term) of
+        # call c+1 is prepared on a side stream while call c computes; two protection slots
+        dec_seq = [c for c in calls if ops[c][1] == "dec"]
+        dpos = {c: j for j, c in enumerate(dec_seq)}
+        ready, freed = {}, {}
+
+        def protect(ci):
+            p = sh_dec[ops[ci][2]]
+            if not p.groups:
+                return
+            slot_k = dpos[ci] % 2
+            if slot_k in freed:
+                aux.wait_event(freed.pop(slot_k))
+            dec.prepare_protection(p, masks_dec[p.name], samples_dec[p.name], slot_k, stream=aux.cuda_stream)
+            ev_r = torch.cuda.Event()
+            ev_r.record(aux)
+            ready[ci] = ev_r
+
         if multi and calls:
             stage_far(calls[0])
             stage_near(calls[0])
@@ -569,7 +588,19 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
                 works.pop(i).wait()        # this call's inputs are in place
                 if op[1] == "pre":
                     transformed = exchange[p_local.name].full
-            if p_local.groups:
+            if p_local.groups and op[1] == "dec" and args.protect_ahead:
+                if i not in ready:
+                    protect(i)
+                nxt = dpos[i] + 1
+                if nxt < len(dec_seq):
+                    protect(dec_seq[nxt])
+                stream.wait_event(ready.pop(i))
+                srv.run_projection(p_local, cts, masks, samples, stream=sp, transformed=transformed,
+                                   protected=dpos[i] % 2)
+                ev_f = torch.cuda.Event()
+                ev_f.record(stream)
+                freed[dpos[i] % 2] = ev_f
+            elif p_local.groups:
                 srv.run_projection(p_local, cts, masks, samples, stream=sp, transformed=transformed)
             stats["calls"] += 1
             if not multi:
@@ -690,6 +721,8 @@ def main():
     ap.add_argument("--model-only", action="store_true", help="run only the config-5 leg")
     ap.add_argument("--model-layers", type=int, default=28)
     ap.add_argument("--model-decode", type=int, default=64, help="decode steps in the config-5 leg")
+    ap.add_argument("--protect-ahead", type=int, default=1,
+                    help="config-5 decode: prepare each call's Enc(0) and mask term during the previous call")
     ap.add_argument("--slots", type=int, default=1, help="0 skips the slot-packed matvec leg (config 3)")
     ap.add_argument("--slots-only", action="store_true", help="run only the slot-packed matvec leg")
     ap.add_argument("--layer-shape", default=None,

@@ -212,6 +212,22 @@ int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_t
                                    const uint64_t *samples, const uint64_t *pk_prep, uint64_t *scratch,
                                    uint64_t *out, void *stream);
 
+/* bfvgpu_matrix_tiles_device in two parts, for callers that prepare a call's output
+ * protection ahead of its inputs (the Enc(0) randomness and the masks do not depend on
+ * them), e.g. on a side stream while the previous call computes:
+ *  - protect: the Enc(0) preparation and additive output term of tiles * groups outputs
+ *    into scratch (bfvgpu_matrix_tiles_scratch_words words), from masks and/or samples;
+ *  - prepared: the product and the protected output transform reading that scratch; enc0
+ *    and masked say which of samples / masks the protect call had.  The caller orders the
+ *    two (same stream, or an event); out equals bfvgpu_matrix_tiles_device's. */
+int32_t bfvgpu_matrix_tiles_protect_device(bfvgpu_ctx *ctx, uint64_t tiles, uint64_t groups,
+                                           const uint64_t *masks, const uint64_t *samples,
+                                           const uint64_t *pk_prep, uint64_t *scratch, void *stream);
+int32_t bfvgpu_matrix_tiles_prepared_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_t tiles,
+                                            uint64_t inputs, const uint64_t *w, uint64_t groups,
+                                            int32_t enc0, int32_t masked, const uint64_t *pk_prep,
+                                            const uint64_t *scratch, uint64_t *out, void *stream);
+
 /* Enc(0) polynomials before the divide-and-round, for the matrix epilogue: samples
  * [groups][3][k][n] (ternary u, e0, e1), pk [2][k][n] NTT form; u_scratch [groups][k][n];
  * x_out [groups][2][k][n] = INTT(NTT(u) . pk_c) + e_c (enc0.cu:125-134).  Pass x_out as

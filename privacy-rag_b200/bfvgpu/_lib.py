@@ -107,6 +107,8 @@ _SIGNATURES = {
     "bfvgpu_rotations_apply": (I32, [VP, U64P, U64, U64P]),
     "bfvgpu_rotations_close": (I32, [VP, ctypes.POINTER(Cleanup)]),
     "bfvgpu_rotations_release": (I32, [VP]),
+    "bfvgpu_matrix_tiles_protect_device": (I32, [VP, U64, U64, VP, VP, VP, VP, VP]),
+    "bfvgpu_matrix_tiles_prepared_device": (I32, [VP, VP, U64, U64, VP, U64, I32, I32, VP, VP, VP, VP]),
     "bfvgpu_slots_open": (I32, [VP, U64P, U32, U32, VP, ctypes.POINTER(VP)]),
     "bfvgpu_slots_apply_device": (I32, [VP, VP, VP, VP]),
     "bfvgpu_slots_apply": (I32, [VP, U64P, U64P]),

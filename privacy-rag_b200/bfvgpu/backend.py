@@ -210,6 +210,25 @@ class Context:
                                                self._dptr(scratch) or None, self._dptr(out), stream),
               "matrix_tiles_device")
 
+    def matrix_tiles_protect_device(self, tiles: int, groups: int, scratch, masks=None, samples=None, pk_prep=None,
+                                    stream: int | None = None):
+        """The output protection of a matrix_tiles call (Enc(0) preparation and the additive
+        output term) into scratch, ahead of the call's inputs."""
+        check(lib().bfvgpu_matrix_tiles_protect_device(self._h, tiles, groups, self._dptr(masks) or None,
+                                                       self._dptr(samples) or None, self._dptr(pk_prep) or None,
+                                                       self._dptr(scratch), stream),
+              "matrix_tiles_protect_device")
+
+    def matrix_tiles_prepared_device(self, inputs_ntt, tiles: int, inputs: int, weights_ntt, groups: int, out,
+                                     enc0: bool, masked: bool, pk_prep=None, scratch=None,
+                                     stream: int | None = None):
+        """matrix_tiles_device with its protection already in scratch (matrix_tiles_protect_device)."""
+        check(lib().bfvgpu_matrix_tiles_prepared_device(self._h, self._dptr(inputs_ntt), tiles, inputs,
+                                                        self._dptr(weights_ntt), groups, int(bool(enc0)),
+                                                        int(bool(masked)), self._dptr(pk_prep) or None,
+                                                        self._dptr(scratch) or None, self._dptr(out), stream),
+              "matrix_tiles_prepared_device")
+
 
 class _Handle:
     _close_fn = ""

@@ -92,7 +92,9 @@ class LayerServer:
         maxi = max(p.inputs for p in self.proj)
         self.w_ntt = {}
         self.inp = t.empty(tiles * maxi * 2 * dk * n, dtype=t.int64, device=dev)  # transformed inputs
-        self.scratch = t.empty(max(1, ctx.matrix_tiles_scratch_words(tiles, maxg)), dtype=t.int64, device=dev)
+        self.scratch_words = max(1, ctx.matrix_tiles_scratch_words(tiles, maxg))
+        self.scratch = t.empty(self.scratch_words, dtype=t.int64, device=dev)
+        self.protect_slots = None  # two more scratch buffers, allocated by the first prepare_protection
         self.out = t.empty(tiles * maxg * 2 * dk * n, dtype=t.int64, device=dev)
         self.targets = {p.name: targets_device(t, p, dev, tiles) for p in self.proj}
         mx = max(v[2] for v in self.targets.values())
@@ -138,19 +140,36 @@ class LayerServer:
         return (self.selected.view(-1)[: e * dk * mx].view(e, dk, mx),
                 self.crt.view(-1)[: e * mx * dk].view(e, mx, dk))
 
-    def run_projection(self, p: Projection, cts, masks, samples, stream=None, transformed=None):
+    def prepare_protection(self, p: Projection, masks, samples, slot: int, stream=None) -> None:
+        """The Enc(0) preparation and additive output term of a later run of projection p
+        into protection slot `slot` (0/1), on `stream` -- ahead of the call's inputs, which
+        they do not depend on.  The caller orders it after the previous reader of the slot and
+        before the run that consumes it (run_projection(..., protected=slot))."""
+        if self.protect_slots is None:
+            self.protect_slots = [self.torch.empty(self.scratch_words, dtype=self.torch.int64,
+                                                   device=self.scratch.device) for _ in range(2)]
+        self.ctx.matrix_tiles_protect_device(self.tiles, p.groups, self.protect_slots[slot], masks=masks,
+                                             samples=samples, pk_prep=self.pk, stream=stream)
+
+    def run_projection(self, p: Projection, cts, masks, samples, stream=None, transformed=None, protected=None):
         """One private_matrix call for every tile: cts [tiles][I][2][dk][n] client ciphertexts
         in coefficient form (left unchanged; their transform goes to self.inp), or None with
         `transformed` holding them already in the product's operand form (InputExchange);
-        masks [tiles][G][n], samples [tiles][G][3][k][n].  Leaves the re-randomised results in
-        output(p) (c1 goes to the client) and the targets' c0 residues / CRT limbs in
-        self.selected / self.crt."""
+        masks [tiles][G][n], samples [tiles][G][3][k][n].  With `protected` = a slot filled by
+        prepare_protection, the call reads that slot instead of preparing Enc(0) and the mask
+        itself.  Leaves the re-randomised results in output(p) (c1 goes to the client) and the
+        targets' c0 residues / CRT limbs in self.selected / self.crt."""
         ctx = self.ctx
         I, G, T = p.inputs, p.groups, self.tiles
         if transformed is None:
             transformed = self.inp
             ctx.matrix_tiles_inputs_device(cts, T * I, out=transformed, stream=stream)
-        ctx.matrix_tiles_device(transformed, T, I, self.w_ntt[p.name], G, self.out, masks=masks, samples=samples,
-                                pk_prep=self.pk, scratch=self.scratch, stream=stream)
+        if protected is None:
+            ctx.matrix_tiles_device(transformed, T, I, self.w_ntt[p.name], G, self.out, masks=masks, samples=samples,
+                                    pk_prep=self.pk, scratch=self.scratch, stream=stream)
+        else:  # masks / samples only say which parts prepare_protection had
+            ctx.matrix_tiles_prepared_device(transformed, T, I, self.w_ntt[p.name], G, self.out,
+                                             enc0=samples is not None, masked=masks is not None, pk_prep=self.pk,
+                                             scratch=self.protect_slots[protected], stream=stream)
         tg, counts, mx = self.targets[p.name]
         ctx.gather_targets_device(self.out, T * G, tg, counts, mx, self.selected, self.crt, stream=stream)

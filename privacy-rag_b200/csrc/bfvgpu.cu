@@ -807,49 +807,106 @@ int32_t bfvgpu_matrix_tiles_prepare_pk_device(bfvgpu_ctx* ctx, const uint64_t* p
   });
 }
 
+// Scratch of the layer pipeline's output protection for `items` outputs:
+// U [items][k][n] and xs [items][2][n] (Enc(0)), then E [items][2][dk][n] (Enc(0) or mask).
+struct ProtectScratch {
+  uint64_t *U = nullptr, *xs = nullptr, *E = nullptr;
+};
+static ProtectScratch protect_layout(const Context& c, uint64_t items, bool enc0, bool masked, uint64_t* scratch) {
+  ProtectScratch ps;
+  if (enc0) {
+    ps.U = scratch;
+    ps.xs = scratch + items * c.k * (uint64_t)c.n;
+  }
+  if (enc0 || masked) ps.E = scratch + (enc0 ? items * (c.k + 2) * (uint64_t)c.n : 0);
+  return ps;
+}
+// Enc(0) preparation and the additive output term: they depend only on the key, the
+// randomness and the masks, not on the call's inputs.
+static void protect_prepare(Context& c, uint64_t items, const uint64_t* masks, const uint64_t* samples,
+                            const uint64_t* pk_prep, const ProtectScratch& ps, cudaStream_t st) {
+  if (samples) {
+    cuda_check(launch_enc0_prep(c.P, samples, reinterpret_cast<const ulonglong2*>(pk_prep), items, ps.U, ps.xs, st),
+               "enc0_prep");
+    count_launch(2);
+  }
+  cuda_check(launch_enc0_fin(c.P, samples, ps.xs, masks, items, ps.E, st), "enc0_fin");
+  count_launch();
+}
+// The product and the protected output transform (out doubles as the product accumulator:
+// each INTT block reads its whole limb before writing it back).
+static void product_finish(Context& c, const uint64_t* in, uint64_t tiles, uint64_t inputs, const uint64_t* w,
+                           uint64_t groups, const uint64_t* pk_prep, const ProtectScratch& ps, uint64_t* out,
+                           cudaStream_t st, cudaEvent_t before_transform) {
+  cuda_check(launch_mac_tiles(c.P, in, tiles, inputs, w, groups, out, st), "mac_tiles");
+  count_launch(mac_tiles_launches(tiles));
+  if (before_transform) cuda_check(cudaStreamWaitEvent(st, before_transform, 0), "wait");
+  cuda_check(launch_intt_protect(c.P, out, tiles * groups, ps.U, reinterpret_cast<const ulonglong2*>(pk_prep), ps.E,
+                                 out, st),
+             "intt_protect");
+  count_launch();
+}
+
+static void check_tiles_args(bfvgpu_ctx* ctx, const uint64_t* in, const uint64_t* w, const uint64_t* out,
+                             uint64_t inputs, bool enc0, bool masked, const uint64_t* pk_prep,
+                             const uint64_t* scratch) {
+  if (!ctx || !in || !w || !out || !inputs) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+  require_product_ring(ctx->c);
+  if ((enc0 && !pk_prep) || ((enc0 || masked) && !scratch)) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+  if (enc0 && ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+  require_device(ctx->c);
+}
+
 int32_t bfvgpu_matrix_tiles_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t tiles, uint64_t inputs,
                                    const uint64_t* w, uint64_t groups, const uint64_t* masks, const uint64_t* samples,
                                    const uint64_t* pk_prep, uint64_t* scratch, uint64_t* out, void* stream) {
   return guard([&] {
-    if (!ctx || !in || !w || !out || !inputs) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
-    require_product_ring(ctx->c);
-    if (samples && (!pk_prep || !scratch)) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
-    if (samples && ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
-    require_device(ctx->c);
+    check_tiles_args(ctx, in, w, out, inputs, samples != nullptr, masks != nullptr, pk_prep, scratch);
     DeviceScope scope(ctx->c.device);
-    const uint64_t items = tiles * groups;
-    if ((samples || masks) && !scratch) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
-    uint64_t* U = samples ? scratch : nullptr;
-    uint64_t* xs = samples ? scratch + items * ctx->c.k * (uint64_t)ctx->c.n : nullptr;
-    uint64_t* E = (samples || masks)
-                      ? scratch + (samples ? items * (ctx->c.k + 2) * (uint64_t)ctx->c.n : 0)
-                      : nullptr;
-    cudaStream_t st = pick(ctx, stream);
     Context& c = ctx->c;
+    const uint64_t items = tiles * groups;
+    const ProtectScratch ps = protect_layout(c, items, samples != nullptr, masks != nullptr, scratch);
+    cudaStream_t st = pick(ctx, stream);
     std::lock_guard<std::mutex> lock(c.aux_mutex);
-    // Enc(0) preparation and the additive output term depend only on the key, the randomness
-    // and the masks: they run on the side stream, beside the product, and join before the
-    // output transform.
-    if (E) {
+    // the protection runs on the side stream, beside the product, and joins before the
+    // output transform
+    if (ps.E) {
       cuda_check(cudaEventRecord(c.fork, st), "event");
       cuda_check(cudaStreamWaitEvent(c.aux, c.fork, 0), "wait");
-      if (samples) {
-        cuda_check(launch_enc0_prep(c.P, samples, reinterpret_cast<const ulonglong2*>(pk_prep), items, U, xs, c.aux),
-                   "enc0_prep");
-        count_launch(2);
-      }
-      cuda_check(launch_enc0_fin(c.P, samples, xs, masks, items, E, c.aux), "enc0_fin");
-      count_launch();
+      protect_prepare(c, items, masks, samples, pk_prep, ps, c.aux);
       cuda_check(cudaEventRecord(c.join, c.aux), "event");
     }
-    // out doubles as the product accumulator: each INTT block reads its whole limb
-    // before writing it back.
-    cuda_check(launch_mac_tiles(c.P, in, tiles, inputs, w, groups, out, st), "mac_tiles");
-    count_launch(mac_tiles_launches(tiles));
-    if (E) cuda_check(cudaStreamWaitEvent(st, c.join, 0), "wait");
-    cuda_check(launch_intt_protect(c.P, out, items, U, reinterpret_cast<const ulonglong2*>(pk_prep), E, out, st),
-               "intt_protect");
-    count_launch();
+    product_finish(c, in, tiles, inputs, w, groups, pk_prep, ps, out, st, ps.E ? c.join : nullptr);
+  });
+}
+
+int32_t bfvgpu_matrix_tiles_protect_device(bfvgpu_ctx* ctx, uint64_t tiles, uint64_t groups, const uint64_t* masks,
+                                           const uint64_t* samples, const uint64_t* pk_prep, uint64_t* scratch,
+                                           void* stream) {
+  return guard([&] {
+    if (!ctx || !scratch || (samples && !pk_prep)) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (samples && ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    require_product_ring(ctx->c);
+    require_device(ctx->c);
+    if (!samples && !masks) return;
+    DeviceScope scope(ctx->c.device);
+    Context& c = ctx->c;
+    const uint64_t items = tiles * groups;
+    protect_prepare(c, items, masks, samples, pk_prep,
+                    protect_layout(c, items, samples != nullptr, masks != nullptr, scratch), pick(ctx, stream));
+  });
+}
+
+int32_t bfvgpu_matrix_tiles_prepared_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t tiles, uint64_t inputs,
+                                            const uint64_t* w, uint64_t groups, int32_t enc0, int32_t masked,
+                                            const uint64_t* pk_prep, const uint64_t* scratch, uint64_t* out,
+                                            void* stream) {
+  return guard([&] {
+    check_tiles_args(ctx, in, w, out, inputs, enc0 != 0, masked != 0, pk_prep, scratch);
+    DeviceScope scope(ctx->c.device);
+    Context& c = ctx->c;
+    const ProtectScratch ps = protect_layout(c, tiles * groups, enc0 != 0, masked != 0, const_cast<uint64_t*>(scratch));
+    product_finish(c, in, tiles, inputs, w, groups, pk_prep, ps, out, pick(ctx, stream), nullptr);
   });
 }
 

@@ -401,7 +401,14 @@ def test_matrix_tiles_device(art, oracle, tiles, path):
                                scratch=scratch)
         hc.matrix_tiles_device(d_in, tiles, I, w, G, plain)
         hc.matrix_tiles_device(d_in, tiles, I, w, G, masked, masks=d_masks, scratch=scratch)
+        # the same call in two parts (protection prepared ahead, then product + transform)
+        split = torch.empty_like(out)
+        scratch2 = torch.empty_like(scratch)
+        hc.matrix_tiles_protect_device(tiles, G, scratch2, masks=d_masks, samples=d_samples, pk_prep=pk_prep)
+        hc.matrix_tiles_prepared_device(d_in, tiles, I, w, G, split, enc0=True, masked=True, pk_prep=pk_prep,
+                                        scratch=scratch2)
         assert hc.check() == 0
+        assert torch.equal(split, out)
     finally:
         hc.set_product_path(0)
     got, got_plain = out.cpu().numpy().view(np.uint64), plain.cpu().numpy().view(np.uint64)
