@@ -24,6 +24,18 @@ namespace bfvgpu {
 // ~16 registers, which lets 2-3 blocks share an SM (measured fastest on B200).
 constexpr int kMaxRadix = 3;
 
+// Read-only global load on the non-coherent path, for an operand that no kernel of the launch
+// writes: a transform's storer uses it for its epilogue operand so that the compiler may issue
+// the load ahead of the pass's stores to the output (which it cannot prove do not alias).
+BFV_HD uint64_t ldro(const uint64_t* p) {
+#if defined(__CUDA_ARCH__)
+  return __ldg(reinterpret_cast<const unsigned long long*>(p));
+#else
+  return *p;
+#endif
+}
+
+
 // Divide-and-round by the special prime q_s (last prime) of one coefficient:
 // (x_p - ((x_s + floor(q_s/2)) mod q_s mod q_p - floor(q_s/2) mod q_p)) * q_s^-1 mod q_p.
 BFV_HD uint64_t moddown_elem(uint64_t xv, uint64_t xs, const Modulus& mp, const Modulus& ms) {
@@ -101,11 +113,11 @@ BFV_HD void op_mac_intt(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t*
   const ProtectArgs pa = prot;
   auto st = [=](int i, uint64_t v) {
     if (x) {
-      const uint64_t xv = x[((uint64_t)c * k + p) * N + i];
-      const uint64_t xs = x[((uint64_t)c * k + k - 1) * N + i];
+      const uint64_t xv = ldro(x + ((uint64_t)c * k + p) * N + i);
+      const uint64_t xs = ldro(x + ((uint64_t)c * k + k - 1) * N + i);
       v = add_mod(v, moddown_elem(xv, xs, m, *ms), m.q);
     }
-    if (mask) v = sub_mod(v, scale_plain_coeff(mask[i], pa.q_mod_t, pa.upper_half, pa.t, pa.tlog, m), m.q);
+    if (mask) v = sub_mod(v, scale_plain_coeff(ldro(mask + i), pa.q_mod_t, pa.upper_half, pa.t, pa.tlog, m), m.q);
     o[i] = v;
   };
   ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
@@ -386,7 +398,7 @@ BFV_HD void op_enc0_x(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* s
     const uint64_t* e = samples + ((g * 3 + 1 + c) * k + p) * N;
     uint64_t* xo = x + ((g * 2 + c) * k + p) * N;
     auto ld = [=](int i) { return mul_mod(U[i], pkc[i], m); };
-    auto st = [=](int i, uint64_t v) { xo[i] = add_mod(v, e[i], m.q); };
+    auto st = [=](int i, uint64_t v) { xo[i] = add_mod(v, ldro(e + i), m.q); };
     ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
   }
 }
@@ -592,7 +604,7 @@ BFV_HD void op_enc0_xs(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* 
     const ulonglong2 w = pkc[i];
     return shoup(Up[i], w.x, w.y, m.q);
   };
-  auto st = [=](int i, uint64_t v) { xo[i] = add_mod(v, ec[i], m.q); };
+  auto st = [=](int i, uint64_t v) { xo[i] = add_mod(v, ldro(ec + i), m.q); };
   ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
 }
 
@@ -645,7 +657,7 @@ BFV_HD void op_intt_protect(const Ex& ex, uint64_t* s, uint64_t blk, const uint6
     }
     return v;
   };
-  auto st = [=](int i, uint64_t v) { o[i] = Ep ? add_mod(v, Ep[i], m.q) : v; };
+  auto st = [=](int i, uint64_t v) { o[i] = Ep ? add_mod(v, ldro(Ep + i), m.q) : v; };
   ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
 }
 
