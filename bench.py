@@ -41,6 +41,11 @@ T2 = 65537
 CTS = 256
 ROTATIONS = 128
 ALG_BYTES_PER_KS = 2 * 4 * N2 * 8 * 2 + (4 * 2 * 5 * N2 * 8) // CTS  # ct in + ct out + key/256
+# DRAM bytes of one rotation's launch pair (k_ks_rotate + k_ks_finish over the 256 ciphertexts),
+# from one ncu capture: rotate 476.0 MB (reads the hoisted digits Y, 1.31 MB per ciphertext,
+# every rotation; writes the pre-moddown limbs) + finish 326.1 MB.  About 3x the algorithmic
+# bytes: the hoisting trades the per-rotation digit transforms for re-reading Y.
+KS_TRAFFIC_PER_ROTATION = 802_038_528
 N1 = 4096
 BITS1 = [36, 36, 37]
 NTT_POLYS = 384  # 64 cts x 2 polys x 3 limbs
@@ -464,7 +469,7 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
 
     multi = bool(dist) and world > 1
     if multi:
-        ctx.set_reserved_sms(8)  # room for NCCL's kernels beside the persistent products
+        ctx.set_reserved_sms(args.reserved_sms)  # room for NCCL's kernels beside the persistent products
     # inputs are double-buffered so the broadcast of call c+1 overlaps call c; broadcasts and
     # result gathers use separate communicators so neither queues behind the other
     cts_pre, masks_pre, samples_pre = call_buffers(sh_pre, tiles, 1)
@@ -721,6 +726,8 @@ def main():
     ap.add_argument("--model-only", action="store_true", help="run only the config-5 leg")
     ap.add_argument("--model-layers", type=int, default=28)
     ap.add_argument("--model-decode", type=int, default=64, help="decode steps in the config-5 leg")
+    ap.add_argument("--reserved-sms", type=int, default=8,
+                    help="config 5 with N > 1: SMs the persistent product kernels leave to NCCL")
     ap.add_argument("--protect-ahead", type=int, default=1,
                     help="config-5 decode: prepare each call's Enc(0) and mask term during the previous call")
     ap.add_argument("--slots", type=int, default=1, help="0 skips the slot-packed matvec leg (config 3)")
@@ -982,7 +989,9 @@ def main():
                 "note": "every step uploads the 256 ciphertexts and reads back all their keyswitched outputs"},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "traffic": None, "peak_source": peak_kind,
+                     "frac": achieved / hbm_peak, "traffic": KS_TRAFFIC_PER_ROTATION, "peak_source": peak_kind,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_ks_rotate + "
+                                       "k_ks_finish pair (256 cts), recorded from one capture (profiles/)",
                      "kernel": "per-rotation launches k_ks_rotate + k_ks_finish (256 cts)",
                      "alg_bytes_per_launch": alg_bytes_launch, "avg_launch_ms": avg_launch * 1e3,
                      "note": "integer-pipe bound: 2k=10 inverse NTTs of n=8192 per keyswitch after hoisting"},

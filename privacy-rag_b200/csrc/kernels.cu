@@ -1285,7 +1285,10 @@ cudaError_t launch_enc0_fin(const DevParams& P, const uint64_t* samples, const u
                             uint64_t items, uint64_t* E, cudaStream_t st) {
   if (!items || (!samples && !mask)) return cudaSuccess;
   const uint64_t rows = items * 2 * P.dk;
-  const dim3 grid((P.n + 256 * kFinPer - 1) / (256 * kFinPer), (unsigned)(rows < 65535 ? rows : 65535));
+  // about 16 blocks per SM in all; each walks rows (grid-stride along y)
+  const unsigned gx = (P.n + 256 * kFinPer - 1) / (256 * kFinPer);
+  const uint64_t want = (148ull * 16 + gx - 1) / gx;
+  const dim3 grid(gx, (unsigned)(rows < want ? rows : want));
   k_enc0_fin<<<grid, 256, 0, st>>>(samples, xs, mask, E, rows, P.k, P.dk, P.logn, P.mod, P.q_mod_t, P.upper_half,
                                    P.t, P.tlog);
   return cudaGetLastError();
