@@ -406,6 +406,85 @@ def cpu_slots_sample(baby: int = 32, giant: int = 16):
                              f"{giant}x{baby} plaintext products incl. their transforms) on {cores} threads")
 
 
+def run_token_leg(torch, bfvgpu, device, args):
+    """Token lookup (the reference's token_packed_many, server side) for one 512-coordinate
+    tile of one slot at ART-002: the 512 raw products (19 input blocks x each coordinate's
+    19 x 8192 weight rows, |w| <= 2^20) as batched launches and the 511 merges of the packing
+    tree as 9 batched levels (two keyswitches per merge).  Inputs, weights, local shares and
+    the 18 level keys are synthetic, seeded and resident; device events on the context
+    stream."""
+    from bfvgpu import token as TK
+    ctx = bfvgpu.Context.art002(device)
+    n, k, dk = ctx.n, ctx.k, ctx.dk
+    slots = 1
+    q = torch.tensor(ctx.primes, dtype=torch.int64, device="cuda")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(9)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    with torch.cuda.stream(stream):
+        def residues(shape, nprimes):
+            raw = torch.randint(0, 2 ** 62, shape, dtype=torch.int64, device="cuda", generator=g)
+            return torch.remainder(raw, q[:nprimes].view(*([1] * (len(shape) - 2)), nprimes, 1))
+
+        inputs = residues((19, slots, 2, dk, n), dk)
+        keys_one = [residues((dk, 2, k, n), k) for _ in range(TK.LEVELS)]
+        keys_lev = [residues((dk, 2, k, n), k) for _ in range(TK.LEVELS)]
+        bound = 1 << 20
+        ring = torch.bitwise_and(torch.randint(-bound, bound + 1, (TK.TILE, 19 * 8192), dtype=torch.int64,
+                                               device="cuda", generator=g), (1 << 59) - 1)
+        local = torch.randint(0, 2 ** 59, (TK.TILE, slots), dtype=torch.int64, device="cuda", generator=g)
+        tile = TK.TokenTile(torch, ctx, inputs, slots, keys_one, keys_lev)
+        tile.run(ring, local)
+        torch.cuda.synchronize()
+        reps = 3
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches0 = bfvgpu.launch_count()
+        a.record(stream)
+        for _ in range(reps):
+            tile.run(ring, local)
+        b.record(stream)
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    res = {"ms": ms, "unit": "ms per 512-coordinate tile (one slot)", "coordinates": TK.TILE,
+           "merges": TK.TILE - 1, "keyswitches": 2 * (TK.TILE - 1),
+           "raw_weight_ntts": TK.TILE * 19 * dk, "launches_per_tile": (bfvgpu.launch_count() - launches0) // reps,
+           "note": "ART-002; raw products batched 64 coordinates per launch pair, packing tree as 9 batched "
+                   "levels; the tile's final mask / Enc(0) and target CRT (one ciphertext) not included"}
+    del tile, inputs, keys_one, keys_lev, ring, local
+    torch.cuda.empty_cache()
+    ctx.close()
+    return res
+
+
+def cpu_token_sample(coords: int = 8):
+    """The reference's per-coordinate order on the oracle, one thread per slot as its server
+    loop runs: `coords` raw products and the coords-1 stack merges, extrapolated to a
+    512-coordinate tile (x 512/coords)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    oc = O.art002()
+    n, dk, k = oc.n, oc.data_k, oc.k
+    rng = np.random.default_rng(10)
+    inputs = oc.uniform(500, 19 * 2 * dk).reshape(19, 1, 2, dk, n)
+    k1 = oc.uniform(501, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n)
+    kg = oc.uniform(502, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n)
+    bound = 1 << 20
+    t0 = time.perf_counter()
+    stack = [None] * 10
+    for j in range(coords):
+        ring = (rng.integers(-bound, bound + 1, size=19 * 8192) & ((1 << 59) - 1)).astype(np.uint64)
+        scaled = np.array([oc.scale_plain(int(rng.integers(0, 1 << 59)))], dtype=np.uint64)
+        current, level = oc.token_evaluate(inputs, 1, ring, scaled)[0], 0
+        while stack[level] is not None:
+            current = oc.packing_pair(stack[level], current, k1, kg, level)
+            stack[level], level = None, level + 1
+        stack[level] = current
+    dt = time.perf_counter() - t0
+    return 1e3 * dt * 512 / coords, 1, (f"{coords} coordinates (raw product + stack merges) on the ART-002 oracle, "
+                                        f"one thread, {dt:.1f}s, extrapolated x{512 // coords} to a tile")
+
+
 def run_model_leg(torch, bfvgpu, device, args, dist):
     """Config 5: the linear protocol of all 28 Qwen3-0.6B-shaped layers for a 512-token
     prefill (32 tiles of B = 16, run as 4 launches of 8 tiles per projection) and 64
@@ -731,6 +810,8 @@ def main():
     ap.add_argument("--protect-ahead", type=int, default=1,
                     help="config-5 decode: prepare each call's Enc(0) and mask term during the previous call")
     ap.add_argument("--slots", type=int, default=1, help="0 skips the slot-packed matvec leg (config 3)")
+    ap.add_argument("--token", type=int, default=1, help="0 skips the token lookup tile leg")
+    ap.add_argument("--token-only", action="store_true", help="run only the token lookup tile leg")
     ap.add_argument("--slots-only", action="store_true", help="run only the slot-packed matvec leg")
     ap.add_argument("--layer-shape", default=None,
                     help="K,O: with --layer-only, one B=16 projection of this shape instead of config 3/4 "
@@ -755,6 +836,14 @@ def main():
 
     if args.layer_only:
         print(json.dumps({"layer_legs": run_layer_legs(torch, bfvgpu, local, args)}), flush=True)
+        return 0
+    if args.token_only:
+        res = run_token_leg(torch, bfvgpu, local, args)
+        if not args.no_cpu:
+            ms, cores, sample = cpu_token_sample()
+            res["cpu_baseline"] = {"value": ms, "unit": "ms per 512-coordinate tile", "cores": cores, "kind": "port",
+                                   "sample": sample}
+        print(json.dumps({"token_tile": res}), flush=True)
         return 0
     if args.slots_only:
         res = run_slots_leg(torch, bfvgpu, local, args)
@@ -871,6 +960,7 @@ def main():
     # ---- secondary: ct-pt matvec (config 3) and one decoder layer (config 4), ART-002 ----
     layer_res = run_layer_legs(torch, bfvgpu, local, args) if args.layer else None
     slots_res = run_slots_leg(torch, bfvgpu, local, args) if args.slots else None
+    token_res = run_token_leg(torch, bfvgpu, local, args) if args.token else None
     model_res = run_model_leg(torch, bfvgpu, local, args, dist) if args.model else None
 
     # ---- secondary: NTT round trips (config 1) ----
@@ -945,6 +1035,10 @@ def main():
         nv, _ = cpu_ntt_sample()
         cpu = {"value": v, "unit": "keyswitches/s", "cores": cores, "kind": "port", "sample": sample,
                "ntt_value": nv, "ntt_unit": "NTTs/s"}
+        if token_res:
+            ms, tcores, tsample = cpu_token_sample()
+            token_res["cpu_baseline"] = {"value": ms, "unit": "ms per 512-coordinate tile", "cores": tcores,
+                                         "kind": "port", "sample": tsample}
         if slots_res:
             ms, scores, ssample = cpu_slots_sample()
             slots_res["cpu_baseline"] = {"value": ms, "unit": "ms per matvec", "cores": scores, "kind": "port",
@@ -1000,6 +1094,7 @@ def main():
                                               "avg_launch_ms": 1e3 * sum(plain_per) / len(plain_per),
                                               "matches_hoisted": plain_match},
                       "matvec_config3_slots": slots_res,
+                      "token_tile": token_res,
                       "matvec_config3": layer_res and layer_res["config3"],
                       "layer_config4": layer_res and layer_res["config4"],
                       "attention_pair": layer_res and layer_res.get("attention"),

@@ -352,6 +352,27 @@ int32_t bfvgpu_token_open(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t slots, 
  * out [slots][2][dk][n] (evaluate_finished + download). */
 int32_t bfvgpu_token_evaluate_finished(bfvgpu_token *t, const uint64_t *ring, const uint64_t *local,
                                        uint64_t *out);
+/* TokenWeights::evaluate_device (resident.cu:152-173) for `coords` coordinates at once, device
+ * pointers: inputs [19][slots][2][dk][n] the NTT-form input ciphertexts (slots <= 4), ring
+ * [coords][19][8192] each coordinate's ring-59 weight rows, local [coords][slots] the local
+ * shares added (Delta-scaled) at coefficient 8191; scratch of bfvgpu_token_many_scratch_words;
+ * out [coords][slots][2][dk][n] the raw products, as bfvgpu_token_evaluate_finished gives them
+ * one coordinate at a time.  n = 16384; no range checks on the device path. */
+uint64_t bfvgpu_token_many_scratch_words(const bfvgpu_ctx *ctx, uint64_t coords, uint64_t slots);
+int32_t bfvgpu_token_evaluate_many_device(bfvgpu_ctx *ctx, const uint64_t *inputs, uint64_t slots,
+                                          const uint64_t *ring, uint64_t coords, const uint64_t *local,
+                                          uint64_t *scratch, uint64_t *out, void *stream);
+/* One level of the token packing tree for many pairs (bfv_token_batch.inc:203-216 merges the
+ * same pairs one at a time through a binary-counter stack): pair (m, s) merges left =
+ * in[2m][s] and right = in[2m+1][s] as Switch::packing_pair does (switch.cu:155-185),
+ *   out[m][s] = ks_1(L + X^(n >> (level+1)) R) + ks_g(L - X^(n >> (level+1)) R),  g = 2^(level+1) + 1,
+ * with key_one / key_level [dk][2][k][n] (device, NTT form) the level's keys for 1 and g;
+ * in [2 pairs][slots][2][dk][n], out [pairs][slots][2][dk][n], scratch of
+ * bfvgpu_packing_level_scratch_words(ctx, pairs * slots). */
+uint64_t bfvgpu_packing_level_scratch_words(const bfvgpu_ctx *ctx, uint64_t count);
+int32_t bfvgpu_packing_level_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_t pairs, uint64_t slots,
+                                    uint32_t level, const uint64_t *key_one, const uint64_t *key_level,
+                                    uint64_t *scratch, uint64_t *out, void *stream);
 int32_t bfvgpu_token_close(bfvgpu_token *t, bfvgpu_cleanup *cleanup);
 int32_t bfvgpu_token_release(bfvgpu_token *t);
 

@@ -109,6 +109,10 @@ _SIGNATURES = {
     "bfvgpu_rotations_release": (I32, [VP]),
     "bfvgpu_matrix_tiles_protect_device": (I32, [VP, U64, U64, VP, VP, VP, VP, VP]),
     "bfvgpu_matrix_tiles_prepared_device": (I32, [VP, VP, U64, U64, VP, U64, I32, I32, VP, VP, VP, VP]),
+    "bfvgpu_token_many_scratch_words": (U64, [VP, U64, U64]),
+    "bfvgpu_token_evaluate_many_device": (I32, [VP, VP, U64, VP, U64, VP, VP, VP, VP]),
+    "bfvgpu_packing_level_scratch_words": (U64, [VP, U64]),
+    "bfvgpu_packing_level_device": (I32, [VP, VP, U64, U64, U32, VP, VP, VP, VP, VP]),
     "bfvgpu_slots_open": (I32, [VP, U64P, U32, U32, VP, ctypes.POINTER(VP)]),
     "bfvgpu_slots_apply_device": (I32, [VP, VP, VP, VP]),
     "bfvgpu_slots_apply": (I32, [VP, U64P, U64P]),

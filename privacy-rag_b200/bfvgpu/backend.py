@@ -210,6 +210,26 @@ class Context:
                                                self._dptr(scratch) or None, self._dptr(out), stream),
               "matrix_tiles_device")
 
+    def token_many_scratch_words(self, coords: int, slots: int) -> int:
+        return int(lib().bfvgpu_token_many_scratch_words(self._h, coords, slots))
+
+    def token_evaluate_many_device(self, inputs_ntt, slots: int, ring, coords: int, local, scratch, out,
+                                   stream: int | None = None):
+        """Raw token products of `coords` coordinates: out [coords][slots][2][dk][n]."""
+        check(lib().bfvgpu_token_evaluate_many_device(self._h, self._dptr(inputs_ntt), slots, self._dptr(ring), coords,
+                                                      self._dptr(local), self._dptr(scratch), self._dptr(out), stream),
+              "token_evaluate_many_device")
+
+    def packing_level_scratch_words(self, count: int) -> int:
+        return int(lib().bfvgpu_packing_level_scratch_words(self._h, count))
+
+    def packing_level_device(self, cts, pairs: int, slots: int, level: int, key_one, key_level, scratch, out,
+                             stream: int | None = None):
+        """One packing-tree level: cts [2 pairs][slots][2][dk][n] -> out [pairs][slots][2][dk][n]."""
+        check(lib().bfvgpu_packing_level_device(self._h, self._dptr(cts), pairs, slots, level, self._dptr(key_one),
+                                                self._dptr(key_level), self._dptr(scratch), self._dptr(out), stream),
+              "packing_level_device")
+
     def matrix_tiles_protect_device(self, tiles: int, groups: int, scratch, masks=None, samples=None, pk_prep=None,
                                     stream: int | None = None):
         """The output protection of a matrix_tiles call (Enc(0) preparation and the additive

@@ -1791,6 +1791,57 @@ int32_t bfvgpu_token_evaluate_finished(bfvgpu_token* t, const uint64_t* ring, co
     wipe_host(scaled.data(), scaled.size());
   });
 }
+uint64_t bfvgpu_token_many_scratch_words(const bfvgpu_ctx* ctx, uint64_t coords, uint64_t slots) {
+  return ctx ? coords * (19ull * ctx->c.dk * ctx->c.n + slots * ctx->c.dk) : 0;
+}
+
+int32_t bfvgpu_token_evaluate_many_device(bfvgpu_ctx* ctx, const uint64_t* inputs, uint64_t slots,
+                                          const uint64_t* ring, uint64_t coords, const uint64_t* local,
+                                          uint64_t* scratch, uint64_t* out, void* stream) {
+  return guard([&] {
+    if (!ctx || !inputs || !ring || !local || !scratch || !out || !slots || slots > 4)
+      fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (ctx->c.n != 16384) fail(BFVGPU_E_CONTEXT, "E_GPU_TOKEN_CONTEXT_LAYOUT");
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    uint64_t* w = scratch;
+    uint64_t* scaled = scratch + coords * 19ull * ctx->c.dk * ctx->c.n;
+    cuda_check(launch_token_evaluate_many(ctx->c.P, inputs, slots, ring, coords, local, scaled, w, out,
+                                          pick(ctx, stream)),
+               "token_many");
+    count_launch(3);
+  });
+}
+
+uint64_t bfvgpu_packing_level_scratch_words(const bfvgpu_ctx* ctx, uint64_t count) {
+  return ctx ? count * (6ull * ctx->c.dk * ctx->c.n + 2ull * ctx->c.k * ctx->c.n) : 0;
+}
+
+int32_t bfvgpu_packing_level_device(bfvgpu_ctx* ctx, const uint64_t* in, uint64_t pairs, uint64_t slots,
+                                    uint32_t level, const uint64_t* key_one, const uint64_t* key_level,
+                                    uint64_t* scratch, uint64_t* out, void* stream) {
+  return guard([&] {
+    if (!ctx || !in || !key_one || !key_level || !scratch || !out || !pairs || !slots)
+      fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    const Context& c = ctx->c;
+    if (c.k != c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    if ((2ull << level) >= c.n) fail(BFVGPU_E_STATE, "E_PACK_PAIR_STATE");
+    require_device(c);
+    DeviceScope scope(c.device);
+    const uint64_t count = pairs * slots, ctw = 2ull * c.dk * c.n;
+    uint64_t* sum = scratch;
+    uint64_t* diff = sum + count * ctw;
+    uint64_t* moved = diff + count * ctw;
+    uint64_t* ks = moved + count * ctw;
+    cudaStream_t st = pick(ctx, stream);
+    cuda_check(launch_packing_prepare_many(c.P, in, pairs, slots, sum, diff, level, st), "prepare");
+    cuda_check(launch_keyswitch(c.P, sum, key_one, 1, count, ks, out, st), "keyswitch");
+    cuda_check(launch_keyswitch(c.P, diff, key_level, (2u << level) + 1, count, ks, moved, st), "keyswitch");
+    cuda_check(launch_add(c.P, out, moved, count * 2 * c.dk, st), "add");
+    count_launch(6);
+  });
+}
+
 int32_t bfvgpu_token_close(bfvgpu_token* t, bfvgpu_cleanup* cleanup) {
   if (!t) return BFVGPU_E_ARGUMENT;
   const bfvgpu_cleanup c = t->h.release();

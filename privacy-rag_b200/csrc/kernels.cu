@@ -118,6 +118,36 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
   op_token_mac_intt<LOGN>(BlockExec{}, smem, blockIdx.x, in, w, scaled, out, slots, dk, mods, inv);
 }
 
+// The same two steps for many coordinates in one launch each: coordinate j's weights at
+// ring + j * 19 * 8192, its transforms at w + j * 19 * dk * n, its scaled local shares at
+// scaled + j * slots * dk and its products at out + j * slots * 2 * dk * n.
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_token_lift_ntt_many(const uint64_t* ring, uint64_t* w, uint32_t dk, const Modulus* mods, const ulonglong2* fwd) {
+  extern __shared__ uint64_t smem[];
+  const uint64_t per = (uint64_t)kTokenBlocks * dk, j = blockIdx.x / per;
+  op_token_lift_ntt<LOGN>(BlockExec{}, smem, blockIdx.x % per, ring + j * kTokenBlocks * kTokenWidth,
+                          w + ((j * per) << LOGN), dk, mods, fwd);
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_token_mac_intt_many(const uint64_t* in, const uint64_t* w, const uint64_t* scaled, uint64_t* out, uint32_t slots,
+                          uint32_t dk, const Modulus* mods, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  const uint64_t per = (uint64_t)slots * 2 * dk, j = blockIdx.x / per;
+  op_token_mac_intt<LOGN>(BlockExec{}, smem, blockIdx.x % per, in, w + ((j * kTokenBlocks * dk) << LOGN),
+                          scaled + j * slots * dk, out + ((j * per) << LOGN), slots, dk, mods, inv);
+}
+
+// scaled [count][dk] = the Delta-scaled plaintext coefficient of local [count] per data prime.
+__global__ void k_scale_local(const uint64_t* local, uint64_t count, uint64_t* scaled, uint32_t dk,
+                              const Modulus* mods, uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < count * dk;
+       e += (uint64_t)gridDim.x * blockDim.x)
+    scaled[e] = scale_plain_coeff(local[e / dk], q_mod_t, upper_half, t, tlog, mods[e % dk]);
+}
+
 template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_ks_hoist(const uint64_t* cts, uint64_t* Y, uint32_t* zflag, uint32_t k, uint32_t dk, const Modulus* mods,
@@ -729,6 +759,26 @@ __global__ void k_packing_prepare(const uint64_t* left, const uint64_t* right, u
   }
 }
 
+// One level of the packing tree for many pairs: pair (m, s) merges left = in[2m][s] with
+// right = in[2m+1][s] (ciphertexts [2][dk][n], `slots` per row) into sum / diff [m][s].
+__global__ void k_packing_prepare_many(const uint64_t* in, uint64_t pairs, uint64_t slots, uint64_t* sum,
+                                       uint64_t* diff, uint32_t dk, int logn, uint32_t shift, const Modulus* mods) {
+  const uint64_t N = uint64_t(1) << logn, ctw = 2ull * dk * N;
+  const uint64_t total = pairs * slots * ctw;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t ps = e / ctw, w = e - ps * ctw, m = ps / slots, sl = ps - m * slots;
+    const uint64_t j = w & (N - 1), base = w - j;
+    const uint64_t* left = in + ((2 * m) * slots + sl) * ctw;
+    const uint64_t* right = in + ((2 * m + 1) * slots + sl) * ctw;
+    const uint64_t q = mods[(w >> logn) % dk].q;
+    const uint64_t src = (j + N - shift) & (N - 1);
+    uint64_t v = right[base + src];
+    if (j < shift) v = neg_mod(v, q);
+    sum[e] = add_mod(left[w], v, q);
+    diff[e] = sub_mod(left[w], v, q);
+  }
+}
+
 // c0 [dk][n] += Delta-scaled plaintext coefficient (add_plain with the scaling variant),
 // for coefficients i < count (bfv_matrix.inc:40-46: encrypt_zero then add_plain_inplace).
 __global__ void k_add_plain(uint64_t* c0, const uint64_t* plain, uint64_t count, uint32_t dk, int logn,
@@ -814,6 +864,8 @@ static cudaError_t configure_for() {
   if constexpr (L == 14) {
     chk(allow_smem(k_token_lift_ntt<L>, s));
     chk(allow_smem(k_token_mac_intt<L>, s));
+    chk(allow_smem(k_token_lift_ntt_many<L>, s));
+    chk(allow_smem(k_token_mac_intt_many<L>, s));
   }
   return e;
 }
@@ -1041,6 +1093,31 @@ cudaError_t launch_token_evaluate(const DevParams& P, const uint64_t* inputs, ui
                                                                                         P.fwd);
   k_token_mac_intt<L_><<<(unsigned)(slots * 2 * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(
       inputs, wscratch, scaled, out, (uint32_t)slots, P.dk, P.mod, P.inv);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_token_evaluate_many(const DevParams& P, const uint64_t* inputs, uint64_t slots, const uint64_t* ring,
+                                       uint64_t coords, const uint64_t* local, uint64_t* scaled, uint64_t* wscratch,
+                                       uint64_t* out, cudaStream_t st) {
+  if (!coords || !slots) return cudaSuccess;
+  if (P.logn != 14 || coords * kTokenBlocks * P.dk > 0x7fffffffull || coords * slots * 2 * P.dk > 0x7fffffffull)
+    return cudaErrorInvalidValue;
+  constexpr int L_ = 14;
+  k_scale_local<<<elementwise_blocks(coords * slots * P.dk), 256, 0, st>>>(local, coords * slots, scaled, P.dk, P.mod,
+                                                                         P.q_mod_t, P.upper_half, P.t, P.tlog);
+  k_token_lift_ntt_many<L_><<<(unsigned)(coords * kTokenBlocks * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(
+      ring, wscratch, P.dk, P.mod, P.fwd);
+  k_token_mac_intt_many<L_><<<(unsigned)(coords * slots * 2 * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(
+      inputs, wscratch, scaled, out, (uint32_t)slots, P.dk, P.mod, P.inv);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_packing_prepare_many(const DevParams& P, const uint64_t* in, uint64_t pairs, uint64_t slots,
+                                        uint64_t* sum, uint64_t* diff, unsigned level, cudaStream_t st) {
+  if (!pairs || !slots) return cudaSuccess;
+  const uint64_t total = pairs * slots * 2 * (uint64_t)P.dk * P.n;
+  k_packing_prepare_many<<<elementwise_blocks(total), 256, 0, st>>>(in, pairs, slots, sum, diff, P.dk, P.logn,
+                                                                   P.n >> (level + 1), P.mod);
   return cudaGetLastError();
 }
 

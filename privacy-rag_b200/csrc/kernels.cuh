@@ -119,6 +119,16 @@ cudaError_t launch_check_canonical(const DevParams& P, const uint64_t* data, uin
 cudaError_t launch_token_evaluate(const DevParams& P, const uint64_t* inputs, uint64_t slots,
                                   const uint64_t* ring, const uint64_t* scaled, uint64_t* wscratch,
                                   uint64_t* acc, uint64_t* out, cudaStream_t st);
+// TokenWeights::evaluate_device for `coords` coordinates at once: ring [coords][19][8192] ring
+// words, local [coords][slots] local shares (Delta-scaled here into scaled [coords][slots][dk]),
+// wscratch [coords][19][dk][n], out [coords][slots][2][dk][n]; n = 16384 only.
+cudaError_t launch_token_evaluate_many(const DevParams& P, const uint64_t* inputs, uint64_t slots, const uint64_t* ring,
+                                       uint64_t coords, const uint64_t* local, uint64_t* scaled, uint64_t* wscratch,
+                                       uint64_t* out, cudaStream_t st);
+// One packing-tree level: in [2 pairs][slots] ciphertexts -> sum, diff [pairs][slots]
+// (left + X^(n >> (level+1)) right, left - ...).
+cudaError_t launch_packing_prepare_many(const DevParams& P, const uint64_t* in, uint64_t pairs, uint64_t slots,
+                                        uint64_t* sum, uint64_t* diff, unsigned level, cudaStream_t st);
 
 // Acyclic packing merge prologue (Switch::packing_prepare without its permutation, which
 // the keyswitch of the difference applies): sum = L + X^s R, diff = L - X^s R for

@@ -492,3 +492,65 @@ def test_token_weights(art, oracle):
     assert e.value.name == "BFVGPU_E_BOUND"
     c = tw.close()
     assert c["closed"] and c["wiped"] == c["freed"]
+
+
+def test_token_tile_batched(art, oracle):
+    """Raw token products of 8 coordinates in one batched call equal TokenWeights, one
+    coordinate at a time; the level-batched packing tree over them equals the reference's
+    binary-counter stack of pairwise merges (Switch.packing_pair, itself checked against the
+    oracle), for 2 slots."""
+    import torch
+    import bfvgpu
+    hc, oc = art
+    n, dk, k = oc.n, oc.data_k, oc.k
+    rng = np.random.default_rng(95)
+    slots, coords, bound = 2, 8, 1 << 20
+    cts = oc.uniform(96, slots * 19 * 2 * dk).reshape(slots, 19, 2, dk, n)
+    tw = bfvgpu.TokenWeights(hc, cts)
+    ring = (rng.integers(-bound, bound + 1, size=(coords, 19 * 8192)) & ((1 << 59) - 1)).astype(np.uint64)
+    local = rng.integers(0, 1 << 59, size=(coords, slots), dtype=np.uint64)
+    try:
+        ref = np.stack([tw.evaluate_finished(ring[j], local[j]) for j in range(coords)])  # [coords][slots][2][dk][n]
+    finally:
+        tw.close()
+    inputs_ntt = np.stack([oc.ntt(cts[s].reshape(-1, n), prime_count=dk).reshape(19, 2, dk, n)
+                           for s in range(slots)], axis=1)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int64)).cuda()
+    d_in, d_ring, d_local = dev(inputs_ntt), dev(ring), dev(local)
+    scratch = torch.empty(hc.token_many_scratch_words(coords, slots), dtype=torch.int64, device="cuda")
+    raw = torch.empty((coords, slots, 2, dk, n), dtype=torch.int64, device="cuda")
+    hc.token_evaluate_many_device(d_in, slots, d_ring, coords, d_local, scratch, raw)
+    torch.cuda.synchronize()
+    assert np.array_equal(raw.cpu().numpy().view(np.uint64), ref)
+    # packing tree: level l merges pairs of 2^l-coordinate blocks with the level's two keys
+    levels = 3
+    key_one = [oc.uniform(200 + l, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n) for l in range(levels)]
+    key_lev = [oc.uniform(300 + l, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n) for l in range(levels)]
+    # torch allocates and frees on the context's stream, so no buffer is reused while a
+    # level's kernels still read it
+    with torch.cuda.stream(torch.cuda.ExternalStream(hc.stream())):
+        d_one, d_lev = [dev(x) for x in key_one], [dev(x) for x in key_lev]
+        cur, count = raw, coords
+        scr = torch.empty(hc.packing_level_scratch_words((coords // 2) * slots), dtype=torch.int64, device="cuda")
+        for l in range(levels):
+            pairs = count // 2
+            out = torch.empty((pairs, slots, 2, dk, n), dtype=torch.int64, device="cuda")
+            hc.packing_level_device(cur, pairs, slots, l, d_one[l], d_lev[l], scr, out)
+            cur, count = out, pairs
+    torch.cuda.synchronize()
+    got = cur[0].cpu().numpy().view(np.uint64)
+    sw = [(bfvgpu.Switch(hc, key_one[l], 1), bfvgpu.Switch(hc, key_lev[l], (2 << l) + 1)) for l in range(levels)]
+    try:
+        for s in range(slots):
+            stack = [None] * (levels + 1)
+            for j in range(coords):
+                current, l = ref[j, s], 0
+                while stack[l] is not None:
+                    current = sw[l][0].packing_pair(stack[l], current, sw[l][1], l)
+                    stack[l], l = None, l + 1
+                stack[l] = current
+            assert np.array_equal(got[s], stack[levels]), s
+    finally:
+        for a, b in sw:
+            a.close()
+            b.close()
