@@ -342,6 +342,15 @@ int32_t bfvgpu_enc0_encrypt_from_samples(bfvgpu_enc0 *e, const uint64_t *samples
  * Enc(0) from samples, then c0 += Delta-scaled plain[i] for i < count (plain < t). */
 int32_t bfvgpu_enc0_encrypt_plain(bfvgpu_enc0 *e, const uint64_t *samples, const uint64_t *plain,
                                   uint64_t count, uint64_t *out);
+/* The client's encryption of a call's input blocks in one go (bfv_matrix.inc:31-49 encrypts
+ * them one Encryptor::encrypt at a time): device pointers, samples [cts][3][k][n] (ternary u,
+ * e0, e1), pk [2][k][n] NTT form, plain [cts][n] plaintext coefficients (< t; no range check
+ * on the device path), scratch of bfvgpu_encrypt_many_scratch_words; out [cts][2][dk][n] =
+ * moddown(Enc(0)) + Delta-scaled plain, what bfvgpu_enc0_encrypt_plain gives per ciphertext. */
+uint64_t bfvgpu_encrypt_many_scratch_words(const bfvgpu_ctx *ctx, uint64_t cts);
+int32_t bfvgpu_encrypt_many_device(bfvgpu_ctx *ctx, const uint64_t *samples, const uint64_t *pk,
+                                   const uint64_t *plain, uint64_t cts, uint64_t *scratch, uint64_t *out,
+                                   void *stream);
 int32_t bfvgpu_enc0_close(bfvgpu_enc0 *e, bfvgpu_cleanup *cleanup);
 int32_t bfvgpu_enc0_release(bfvgpu_enc0 *e);
 

@@ -113,6 +113,8 @@ _SIGNATURES = {
     "bfvgpu_token_evaluate_many_device": (I32, [VP, VP, U64, VP, U64, VP, VP, VP, VP]),
     "bfvgpu_packing_level_scratch_words": (U64, [VP, U64]),
     "bfvgpu_packing_level_device": (I32, [VP, VP, U64, U64, U32, VP, VP, VP, VP, VP]),
+    "bfvgpu_encrypt_many_scratch_words": (U64, [VP, U64]),
+    "bfvgpu_encrypt_many_device": (I32, [VP, VP, VP, VP, U64, VP, VP, VP]),
     "bfvgpu_slots_open": (I32, [VP, U64P, U32, U32, VP, ctypes.POINTER(VP)]),
     "bfvgpu_slots_apply_device": (I32, [VP, VP, VP, VP]),
     "bfvgpu_slots_apply": (I32, [VP, U64P, U64P]),

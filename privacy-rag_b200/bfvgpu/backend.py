@@ -210,6 +210,14 @@ class Context:
                                                self._dptr(scratch) or None, self._dptr(out), stream),
               "matrix_tiles_device")
 
+    def encrypt_many_scratch_words(self, cts: int) -> int:
+        return int(lib().bfvgpu_encrypt_many_scratch_words(self._h, cts))
+
+    def encrypt_many_device(self, samples, pk, plain, cts: int, scratch, out, stream: int | None = None):
+        """Client encryption of cts plaintexts [cts][n]: out [cts][2][dk][n] (device tensors)."""
+        check(lib().bfvgpu_encrypt_many_device(self._h, self._dptr(samples), self._dptr(pk), self._dptr(plain), cts,
+                                               self._dptr(scratch), self._dptr(out), stream), "encrypt_many_device")
+
     def token_many_scratch_words(self, coords: int, slots: int) -> int:
         return int(lib().bfvgpu_token_many_scratch_words(self._h, coords, slots))
 

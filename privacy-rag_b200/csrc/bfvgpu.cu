@@ -1715,6 +1715,26 @@ int32_t bfvgpu_enc0_encrypt_plain(bfvgpu_enc0* e, const uint64_t* samples, const
   });
 }
 
+uint64_t bfvgpu_encrypt_many_scratch_words(const bfvgpu_ctx* ctx, uint64_t cts) {
+  return ctx ? cts * 3ull * ctx->c.k * ctx->c.n : 0;
+}
+
+int32_t bfvgpu_encrypt_many_device(bfvgpu_ctx* ctx, const uint64_t* samples, const uint64_t* pk, const uint64_t* plain,
+                                   uint64_t cts, uint64_t* scratch, uint64_t* out, void* stream) {
+  return guard([&] {
+    if (!ctx || !samples || !pk || !plain || !scratch || !out) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    if (cts * ctx->c.k > 0x7fffffffull) fail(BFVGPU_E_SHAPE, "E_BFV_PACKED_SHAPE");
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    uint64_t* u_ntt = scratch;
+    uint64_t* x = scratch + cts * (uint64_t)ctx->c.k * ctx->c.n;
+    cuda_check(launch_encrypt_many(ctx->c.P, samples, pk, plain, cts, u_ntt, x, out, pick(ctx, stream)),
+               "encrypt_many");
+    count_launch(3);
+  });
+}
+
 int32_t bfvgpu_enc0_close(bfvgpu_enc0* e, bfvgpu_cleanup* cleanup) {
   if (!e) return BFVGPU_E_ARGUMENT;
   const bfvgpu_cleanup c = e->h.release();

@@ -741,6 +741,19 @@ __global__ void k_moddown(const uint64_t* x, uint64_t* out, uint64_t groups, uin
   }
 }
 
+// out [cts][2][dk][n]: c0 of ciphertext j += Delta-scaled plain [j][n] (coefficient form).
+__global__ void k_add_plain_many(uint64_t* out, const uint64_t* plain, uint64_t cts, uint32_t dk, int logn,
+                                 const Modulus* mods, uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
+  const uint64_t N = uint64_t(1) << logn, total = cts * dk * N;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t i = e & (N - 1), row = e >> logn, j = row / dk;
+    const uint32_t p = (uint32_t)(row % dk);
+    const Modulus& m = mods[p];
+    uint64_t* a = out + ((j * 2 * dk + p) << logn) + i;
+    *a = add_mod(*a, scale_plain_coeff(plain[(j << logn) + i], q_mod_t, upper_half, t, tlog, m), m.q);
+  }
+}
+
 // ---------------------------------------------------------------------------------
 // small elementwise kernels
 // ---------------------------------------------------------------------------------
@@ -1134,6 +1147,17 @@ cudaError_t launch_add_plain(const DevParams& P, uint64_t* c0, const uint64_t* p
   if (!count) return cudaSuccess;
   k_add_plain<<<elementwise_blocks(count * P.dk), 256, 0, st>>>(c0, plain, count, P.dk, P.logn, P.mod, P.q_mod_t,
                                                                P.upper_half, P.t, P.tlog);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_encrypt_many(const DevParams& P, const uint64_t* samples, const uint64_t* pk, const uint64_t* plain,
+                                uint64_t cts, uint64_t* u_ntt, uint64_t* x, uint64_t* out, cudaStream_t st) {
+  if (!cts) return cudaSuccess;
+  cudaError_t e = launch_enc0_x(P, samples, pk, u_ntt, x, cts, st);
+  if (e == cudaSuccess) e = launch_moddown(P, x, out, cts, st);
+  if (e != cudaSuccess) return e;
+  k_add_plain_many<<<elementwise_blocks(cts * P.dk * P.n), 256, 0, st>>>(out, plain, cts, P.dk, P.logn, P.mod,
+                                                                         P.q_mod_t, P.upper_half, P.t, P.tlog);
   return cudaGetLastError();
 }
 

@@ -140,6 +140,11 @@ cudaError_t launch_add_plain(const DevParams& P, uint64_t* c0, const uint64_t* p
                              cudaStream_t st);
 // a += b on [polys][n] data-prime polys.
 cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint64_t polys, cudaStream_t st);
+// Public-key encryption of cts plaintexts: samples [cts][3][k][n] (u, e0, e1), pk [2][k][n] NTT
+// form, plain [cts][n] -> out [cts][2][dk][n] = moddown(Enc(0)) + Delta plain; scratch u_ntt
+// [cts][k][n], x [cts][2][k][n].
+cudaError_t launch_encrypt_many(const DevParams& P, const uint64_t* samples, const uint64_t* pk, const uint64_t* plain,
+                                uint64_t cts, uint64_t* u_ntt, uint64_t* x, uint64_t* out, cudaStream_t st);
 
 // Layer pipeline over T tiles that share one weight matrix (E = T * groups items, item
 // e = t * groups + g):

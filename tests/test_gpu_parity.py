@@ -293,6 +293,34 @@ def test_enc0(art, oracle):
     assert c["closed"] and c["wiped"] == c["freed"]
 
 
+def test_encrypt_many_device(art, oracle):
+    """The client's batched encryption equals PublicZero.encrypt_plain per ciphertext and
+    decrypts to the plaintexts."""
+    import torch
+    import bfvgpu
+    hc, oc = art
+    n, k, dk = oc.n, oc.k, oc.data_k
+    tb = oracle.TestBfv(oc, seed=57)
+    rng = np.random.default_rng(58)
+    cts = 3
+    samples = np.stack([tb.samples() for _ in range(cts)])
+    plain = rng.integers(0, 1 << 59, size=(cts, n), dtype=np.uint64)
+    plain[0, :3] = [0, (1 << 59) - 1, 1]
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int64)).cuda()
+    out = torch.empty((cts, 2, dk, n), dtype=torch.int64, device="cuda")
+    scratch = torch.empty(hc.encrypt_many_scratch_words(cts), dtype=torch.int64, device="cuda")
+    hc.encrypt_many_device(dev(samples), dev(tb.pk), dev(plain), cts, scratch, out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint64)
+    pz = bfvgpu.PublicZero(hc, tb.pk)
+    try:
+        for j in range(cts):
+            assert np.array_equal(got[j], pz.encrypt(samples[j], plain[j])), j
+    finally:
+        pz.close()
+    assert tb.decrypt(got[0])[:8] == [int(v) for v in plain[0, :8]]
+
+
 def test_client_phase(art, oracle):
     import bfvgpu
     hc, oc = art
