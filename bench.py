@@ -563,10 +563,13 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
     # ("call", phase, index, layer) one private_matrix call
     def schedule(n_layers, n_steps):
         ops = []
+        # prefill: projection-major over the tile groups (qkv of every group, then o, ...), so
+        # a call's neighbours are either the same projection for another group (independent)
+        # or a later projection of a group whose previous call finished two calls earlier
         for l in range(n_layers):
             ops.append(("wpre", l))
-            for _ in range(tiles_total // tiles):
-                ops.extend(("call", "pre", i, l) for i in range(4))
+            for i in range(4):
+                ops.extend(("call", "pre", i, l) for _ in range(tiles_total // tiles))
         ops.append(("mark",))
         for l in range(n_layers):
             ops.append(("wdec", l))
@@ -584,8 +587,9 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
 
     # prefill calls distribute their inputs through an InputExchange (scatter, per-rank
     # transform of a slice, all-gather), decode calls through a broadcast and a local transform
-    exchange = {p.name: S.InputExchange(torch, dist, pg_in, tiles * p.inputs, 2 * dk * n, "cuda")
-                for p in sh_pre} if multi else {}
+    # three exchange buffers per projection: up to three prefill calls are staged at once
+    exchange = {(p.name, b): S.InputExchange(torch, dist, pg_in, tiles * p.inputs, 2 * dk * n, "cuda")
+                for p in sh_pre for b in range(3)} if multi else {}
 
     def transform(si, so, slots):
         ctx.matrix_tiles_inputs_device(si, slots, out=so, stream=sp)
@@ -600,15 +604,15 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
         def stage_far(ci):   # two calls ahead: the scatter of an exchanged call
             op = ops[ci]
             if op[1] == "pre":
-                name = sh_pre[op[2]].name
-                works[ci] = exchange[name].scatter(operands(op, slot[ci])[3])
-                stats["broadcast_bytes"] += exchange[name].per * exchange[name].words * 8
+                ex = exchange[(sh_pre[op[2]].name, pslot[ci] % 3)]
+                works[ci] = ex.scatter(operands(op, slot[ci])[3])
+                stats["broadcast_bytes"] += ex.per * ex.words * 8
 
         def stage_near(ci):  # one call ahead: transform + all-gather, or the broadcast
             op = ops[ci]
             if op[1] == "pre":
                 works.pop(ci).wait()
-                ex = exchange[sh_pre[op[2]].name]
+                ex = exchange[(sh_pre[op[2]].name, pslot[ci] % 3)]
                 works[ci] = ex.gather(transform)
                 stats["broadcast_bytes"] += (ex.world - 1) * ex.per * ex.words * 8
             else:
@@ -634,11 +638,13 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
             ev_r.record(aux)
             ready[ci] = ev_r
 
-        if multi and calls:
-            stage_far(calls[0])
-            stage_near(calls[0])
-            if len(calls) > 1:
-                stage_far(calls[1])
+        pre_calls = [c for c in calls if ops[c][1] == "pre"]
+        pslot = {c: j for j, c in enumerate(pre_calls)}
+        if multi and pre_calls:
+            stage_far(pre_calls[0])
+            stage_near(pre_calls[0])
+            if len(pre_calls) > 1:
+                stage_far(pre_calls[1])
         for i, op in enumerate(ops):
             if op[0] == "mark":
                 if marks is not None:
@@ -664,14 +670,18 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
                 dec.w_ntt = wcache[op[3]]
             transformed = None
             if multi:
-                ahead = after[i]
+                # prefill calls are staged ahead; a decode call's inputs exist only once the
+                # previous call's results went back to the client, so its broadcast starts here
+                ahead = [c for c in after[i] if ops[c][1] == "pre"]
                 if len(ahead) > 1:
                     stage_far(ahead[1])
                 if ahead:
                     stage_near(ahead[0])
+                if i not in works:
+                    stage_near(i)
                 works.pop(i).wait()        # this call's inputs are in place
                 if op[1] == "pre":
-                    transformed = exchange[p_local.name].full
+                    transformed = exchange[(p_local.name, pslot[i] % 3)].full
             if p_local.groups and op[1] == "dec" and args.protect_ahead:
                 if i not in ready:
                     protect(i)
@@ -726,9 +736,10 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
            "tokens_per_s": tokens / (total / 1e3), "n_gpus": world, "layers": layers,
            "prefill_ms": pre_ms, "decode_weights_ms": dw_ms, "decode_ms": dec_ms,
            "decode_ms_per_step": dec_ms / max(1, decode_steps),
-           "sharding": "output groups of every call, contiguous ranges per rank; prefill inputs scattered by "
-                       "rank 0, transformed per slice and all-gathered (two calls ahead), decode inputs "
-                       "broadcast (one call ahead); c1 + target CRT limbs gathered to rank 0 (asynchronous)",
+           "sharding": "output groups of every call, contiguous ranges per rank; prefill calls projection-major "
+                       "over the 4 tile groups, inputs scattered by rank 0, transformed per slice and all-gathered "
+                       "(two calls ahead); decode inputs broadcast when the call starts (each depends on the "
+                       "previous call); c1 + target CRT limbs gathered to rank 0 (asynchronous)",
            "calls_per_rank": stats["calls"], "broadcast_bytes_per_rank": stats["broadcast_bytes"],
            "gathered_bytes_per_rank": stats["gathered_bytes"],
            "prefill_mac_modmuls": layers * tiles_total * sum(p.groups * p.inputs * 2 * dk * n for p in full_pre),
