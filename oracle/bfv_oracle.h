@@ -14,7 +14,7 @@
  * Parity status: plaintext-level results (decrypt(target) = sum x*w mod t), parameter
  * values (IV1/artifacts/bfv_context.json), packing decisions and all
  * coefficient-domain integer steps are pinned.  NTT-domain values and key material
- * are pinned only against this restatement (SEAL is absent), see DESIGN.md.
+ * are pinned only against this restatement (SEAL is absent).
  *
  * Layouts follow the reference: a polynomial set is [..][prime][N] of uint64 words,
  * a ciphertext is [2][k][N], a keyswitch key is [digit][2][k+1][N] (NTT form).

@@ -79,7 +79,7 @@ def test_barrett_matches_exact(oracle):
             assert L.or_mul_barrett(a, b, q, r & ((1 << 64) - 1), r >> 64) == a * b % q
 
 
-SURVEY_PACKING = {
+SHAPE_PACKING = {
     # (B, K, O): (d, cap, returns, inputs) -- the per-shape decisions quoted for the
     # reference rule (q_proj at B=1; the four 16-token tile calls; the decode calls)
     (1, 1024, 2048): (64, 128, 16, 16),
@@ -95,7 +95,7 @@ SURVEY_PACKING = {
 
 
 def test_packing_decisions(oracle, bfv):
-    for (b, k, o), want in SURVEY_PACKING.items():
+    for (b, k, o), want in SHAPE_PACKING.items():
         p = oracle.matrix_packing(b, k, o)
         assert (p.reduction, p.columns, p.returns, p.inputs) == want, (b, k, o)
         q = bfv.matrix_packing(b, k, o)
