@@ -62,23 +62,18 @@ static uint64_t invmod(uint64_t a, uint64_t q) { /* q prime */
   return powmod(a, q - 2, q);
 }
 
-/* Barrett (1986) reduction of the 128-bit product a*b with the precomputed ratio
+/* Barrett (1986) reduction of the 128-bit product x = a*b with the precomputed ratio
  * r = floor((2^128-1)/q) held as two 64-bit limbs (r1:r0).  The quotient estimate
- * floor(a*b*r / 2^128) is assembled from 64-bit partial products exactly as the
- * reference's limb sequence does (matrix.cu:37-43); one conditional subtraction
- * makes the result canonical for a, b < q < 2^63. */
+ * floor(x*r / 2^128) is formed in 128-bit host arithmetic as hi*r1 plus the high half of
+ * the 2^64 column (lo*r1 + hi*r0 + high(lo*r0)); it is the estimate the reference's limb
+ * sequence produces (matrix.cu:37-43) and undershoots floor(x/q) by at most one, so one
+ * conditional subtraction makes the result canonical for a, b < q < 2^63. */
 uint64_t or_mul_barrett(uint64_t a, uint64_t b, uint64_t q, uint64_t r0, uint64_t r1) {
-  const u128 p = (u128)a * b;
-  const uint64_t lo = (uint64_t)p, hi = (uint64_t)(p >> 64);
-  const uint64_t carry0 = (uint64_t)(((u128)lo * r0) >> 64);
-  const u128 m1 = (u128)lo * r1;
-  const uint64_t low1 = (uint64_t)m1 + carry0;
-  const uint64_t high1 = (uint64_t)(m1 >> 64) + (low1 < carry0);
-  const u128 m2 = (u128)hi * r0;
-  const uint64_t low2 = low1 + (uint64_t)m2;
-  const uint64_t high2 = (uint64_t)(m2 >> 64) + (low2 < low1);
-  const uint64_t quotient = hi * r1 + high1 + high2;
-  const uint64_t rem = lo - quotient * q;
+  const u128 x = (u128)a * b;
+  const uint64_t lo = (uint64_t)x, hi = (uint64_t)(x >> 64);
+  const u128 column = (((u128)lo * r0) >> 64) + (u128)lo * r1 + (u128)hi * r0;
+  const uint64_t qhat = hi * r1 + (uint64_t)(column >> 64);
+  const uint64_t rem = lo - qhat * q;
   return rem >= q ? rem - q : rem;
 }
 

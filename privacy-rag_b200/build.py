@@ -6,6 +6,7 @@ so it travels with the repository snapshot to a GPU host.
 """
 from __future__ import annotations
 
+import concurrent.futures
 import os
 import subprocess
 import sys
@@ -14,8 +15,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "lib", "libbfvgpu.so")
-SOURCES = ["kernels.cu", "bfvgpu.cu", "noalloc.cu"]
-HEADERS = ["arith.cuh", "ntt_core.cuh", "block_ops.cuh", "kernels.cuh", "ctx_internal.h"]
+SOURCES = ["kernels.cu", "bfvgpu.cu", "noalloc.cu", "peak.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -26,19 +26,28 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
+def dependencies() -> list[str]:
+    """Every file the library is compiled from: the sources, every header beside them and
+    the public headers (a new header is picked up without editing this list)."""
+    deps = [os.path.join(CSRC, f) for f in SOURCES]
+    for d in (CSRC, os.path.join(ROOT, "include")):
+        deps += [os.path.join(d, f) for f in sorted(os.listdir(d)) if f.endswith((".cuh", ".h", ".hpp"))]
+    deps.append(os.path.abspath(__file__))
+    return deps
+
+
 def stale() -> bool:
     if not os.path.exists(LIB):
         return True
     t = os.path.getmtime(LIB)
-    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS] + [os.path.join(ROOT, "include", "bfvgpu.h")]
-    return any(os.path.getmtime(d) > t for d in deps)
+    return any(os.path.getmtime(d) > t for d in dependencies())
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not stale():
         return LIB
     os.makedirs(os.path.dirname(LIB), exist_ok=True)
-    objs = []
+    cmds, objs = [], []
     for src in SOURCES:
         obj = os.path.join(PKG, "lib", src.replace(".cu", ".o"))
         cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC,-O3",
@@ -46,8 +55,12 @@ def build(force: bool = False, verbose: bool = False) -> str:
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd))
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
         objs.append(obj)
+    # the translation units compile independently: run them side by side
+    with concurrent.futures.ThreadPoolExecutor(len(cmds)) as pool:
+        for f in [pool.submit(subprocess.run, c, check=True) for c in cmds]:
+            f.result()
     cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
     subprocess.run(cmd, check=True)
     for o in objs:

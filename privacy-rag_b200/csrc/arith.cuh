@@ -59,17 +59,20 @@ BFV_HD uint64_t shoup(uint64_t a, uint64_t w, uint64_t wq, uint64_t q) {
   return r >= q ? r - q : r;
 }
 
-// (hi*2^64 + lo) mod q for any 128-bit value.
+// (hi*2^64 + lo) mod q for any 128-bit value x.  Barrett: with r = floor((2^128-1)/q)
+// = r1*2^64 + r0, the product x*r splits into the columns 2^128 (hi*r1), 2^64
+// (hi*r0 + lo*r1, plus the high word of lo*r0) and 2^0.  The quotient estimate
+// floor(x*r / 2^128) is hi*r1 plus the high words of the 2^64-column terms plus the
+// carries out of summing their low words; it falls short of floor(x/q) by at most one,
+// which the final conditional subtraction corrects.
 BFV_HD uint64_t reduce128(uint64_t lo, uint64_t hi, const Modulus& m) {
-  const uint64_t carry0 = mulhi64(lo, m.r0);
-  const uint64_t round1 = lo * m.r1;
-  const uint64_t tmp = round1 + carry0;
-  const uint64_t high1 = mulhi64(lo, m.r1) + (tmp < round1);
-  const uint64_t round2 = hi * m.r0;
-  const uint64_t next = tmp + round2;
-  const uint64_t high2 = mulhi64(hi, m.r0) + (next < tmp);
-  const uint64_t quotient = hi * m.r1 + high1 + high2;
-  const uint64_t rem = lo - quotient * m.q;
+  const uint64_t lo_r1 = lo * m.r1, hi_r0 = hi * m.r0;
+  uint64_t column = mulhi64(lo, m.r0) + lo_r1;
+  uint64_t carries = column < lo_r1;
+  column += hi_r0;
+  carries += column < hi_r0;
+  const uint64_t qhat = hi * m.r1 + mulhi64(lo, m.r1) + mulhi64(hi, m.r0) + carries;
+  const uint64_t rem = lo - qhat * m.q;
   return rem >= m.q ? rem - m.q : rem;
 }
 

@@ -344,6 +344,11 @@ __global__ void __launch_bounds__(kMacTcThreads, 1)
             "r"((int)(gc * tc::kGroups + gr * tc::kGroupsRound)), "r"((int)p), "r"(bar) : "memory");
       };
       const uint32_t pairs = rounds / 4, qs = rounds / 2;
+      // the last A / B copy issued and the last round committed: each barrier has at most
+      // one operation outstanding (a copy is issued only after the previous one into the
+      // other buffer was seen complete, and MMAs complete in commit order), so on abort one
+      // wait per barrier drains everything this thread started
+      uint32_t a_last = 0, b_last = 0, m_next = 0;
       load_a(0);
       load_b(0);
       bool ok = true;
@@ -354,8 +359,14 @@ __global__ void __launch_bounds__(kMacTcThreads, 1)
           ok = ok && mbar_wait(barB + 8 * (Q & 1), (Q >> 1) & 1);
           // the buffers for the next pair / group round were last read by round R - 1
           if (ok && R >= 1) ok = mbar_wait(barM + 8 * ((R - 1) & 1), ((R - 1) >> 1) & 1);
-          if (ok && (R & 3) == 0 && P + 1 < pairs) load_a(P + 1);
-          if (ok && Q + 1 < qs) load_b(Q + 1);
+          if (ok && (R & 3) == 0 && P + 1 < pairs) {
+            load_a(P + 1);
+            a_last = P + 1;
+          }
+          if (ok && Q + 1 < qs) {
+            load_b(Q + 1);
+            b_last = Q + 1;
+          }
         }
         // the consumer of this TMEM buffer has finished round R - 2
         if (ok && R >= 2) ok = mbar_wait(barF + 8 * mb, ((R >> 1) - 1) & 1);
@@ -371,10 +382,17 @@ __global__ void __launch_bounds__(kMacTcThreads, 1)
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(barM + 8 * mb)
                      : "memory");
+        m_next = R + 1;
       }
       if (!ok) {
         *abort_flag = 1;
         atomicOr(err, kErrMmaTimeout);
+        // before the block frees its tensor memory and exits: the copies still writing its
+        // shared memory and the MMAs still reading it (each wait bounded; a copy or MMA
+        // already complete passes at once)
+        mbar_wait(barA + 8 * (a_last & 1), (a_last >> 1) & 1);
+        mbar_wait(barB + 8 * (b_last & 1), (b_last >> 1) & 1);
+        if (m_next) mbar_wait(barM + 8 * ((m_next - 1) & 1), ((m_next - 1) >> 1) & 1);
       }
     }
   } else {

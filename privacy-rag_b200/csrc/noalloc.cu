@@ -15,10 +15,17 @@
 // the GPU (different streams, or threads calling concurrently) race on it.  Nothing in
 // it needs to start at zero -- every word the kernels read in a call is first written in
 // the same call -- and it keeps the last call's contents afterwards.
+//
+// The cached address belongs to the CUDA primary context that was current when it was
+// looked up.  A process that resets the device (cudaDeviceReset) or otherwise destroys
+// that primary context must not call this entry point again on that device: the cache
+// is not invalidated, and the kernels would run with a stale address.
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <exception>
 #include <mutex>
+#include <new>
 #include <string>
 
 #include "bfvgpu.h"
@@ -56,17 +63,19 @@ int32_t fail(int32_t code, const std::string& what) {
 
 }  // namespace
 
-extern "C" int32_t bfvgpu_keyswitch_device_noalloc(bfvgpu_ctx* ctx, const uint64_t* cts, uint64_t count,
-                                                   const uint64_t* key, uint32_t galois_elt, uint64_t* out,
-                                                   void* stream) {
+namespace {
+
+int32_t keyswitch_noalloc(bfvgpu_ctx* ctx, const uint64_t* cts, uint64_t count, const uint64_t* key,
+                          uint32_t galois_elt, uint64_t* out, void* stream) {
   int device = -1;
   cudaStream_t ctx_stream = nullptr;
   const bfvgpu::DevParams* P = bfvgpu::internal_params(ctx, &device, &ctx_stream);
-  if (!P || !cts || !key || !out || count == 0) return fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+  if (!P || !cts || !key || !out) return fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
   if (device < 0) return fail(BFVGPU_E_DEVICE, "E_BFVGPU_HOST_ONLY_CONTEXT");
   if (device >= kMaxDevices) return fail(BFVGPU_E_DEVICE, "E_BFVGPU_NOALLOC_DEVICE_ORDINAL");
   if (P->k != P->dk + 1) return fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
   if (!(galois_elt & 1) || galois_elt >= 2 * P->n) return fail(BFVGPU_E_ELEMENT, "E_BFVGPU_GALOIS_ELEMENT");
+  if (count == 0) return BFVGPU_OK;  // an empty batch is a no-op, as in bfvgpu_keyswitch_device
   const uint64_t max_count = kNoAllocScratchWords / (2ull * P->k * P->n);
   if (count > max_count)
     return fail(BFVGPU_E_SHAPE, "E_BFVGPU_NOALLOC_SCRATCH_LIMIT: " + std::to_string(count) +
@@ -86,4 +95,20 @@ extern "C" int32_t bfvgpu_keyswitch_device_noalloc(bfvgpu_ctx* ctx, const uint64
   if (e != cudaSuccess) return fail(BFVGPU_E_CUDA, std::string("E_BFVGPU_CUDA: noalloc keyswitch: ") + cudaGetErrorString(e));
   bfvgpu::internal_count_launch(2);
   return BFVGPU_OK;
+}
+
+}  // namespace
+
+// No C++ exception crosses the ABI: host allocation failures while building an error
+// message map to BFVGPU_E_ALLOC, like every other entry point of the library.
+extern "C" int32_t bfvgpu_keyswitch_device_noalloc(bfvgpu_ctx* ctx, const uint64_t* cts, uint64_t count,
+                                                   const uint64_t* key, uint32_t galois_elt, uint64_t* out,
+                                                   void* stream) {
+  try {
+    return keyswitch_noalloc(ctx, cts, count, key, galois_elt, out, stream);
+  } catch (const std::bad_alloc&) {
+    return BFVGPU_E_ALLOC;
+  } catch (const std::exception&) {
+    return BFVGPU_E_ARGUMENT;
+  }
 }

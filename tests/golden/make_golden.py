@@ -1,8 +1,8 @@
 """Regenerate the golden fixtures of tests/golden/ from the reference checkout.
 
-Run in a container that has the reference mounted (default
-/root/reference/implementation_v1); the fixtures are committed so the GPU host,
-which has no reference checkout, can use them.
+Run where a reference checkout exists, with PRAG_REFERENCE naming its
+implementation_v1/ directory (required; there is no default path); the fixtures are
+committed so hosts without a reference checkout can use them.
 
 * art002_context.json -- the parameter known answers of IV1/artifacts/bfv_context.json
   (ART-002 primes, Q and bit sizes per level), copied as data.
@@ -23,7 +23,7 @@ import os
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("PRAG_REFERENCE", "/root/reference/implementation_v1")
+REF = os.environ.get("PRAG_REFERENCE", "")
 MASK = (1 << 59) - 1
 sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(HERE)), "privacy-rag_b200"))
 
@@ -121,8 +121,10 @@ def packing_fixture():
 
 
 if __name__ == "__main__":
-    if os.path.exists(REF):
+    if REF and os.path.exists(REF):
         context_fixture()
+    else:
+        print("PRAG_REFERENCE unset or missing: art002_context.json left as committed", file=sys.stderr)
     kat_fixture()
     packing_fixture()
     print("golden fixtures written to", HERE)

@@ -56,6 +56,9 @@ def test_noalloc_keyswitch_matches_allocating_entry_point(bfv):
         assert rc == 0, L.bfvgpu_last_error()
         torch.cuda.synchronize()
         assert torch.equal(out_na, out_ref), f"call {call}: differs from bfvgpu_keyswitch_device"
+    # an empty batch is a no-op, as for the allocating entry point
+    assert L.bfvgpu_keyswitch_device_noalloc(ctx.handle, d_cts.data_ptr(), 0, d_key.data_ptr(), 3,
+                                             out_na.data_ptr(), None) == 0
     # one ciphertext beyond the fixed array: refused before any device work
     rc = L.bfvgpu_keyswitch_device_noalloc(ctx.handle, d_cts.data_ptr(), count + 1, d_key.data_ptr(), 3,
                                            out_na.data_ptr(), None)
