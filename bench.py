@@ -3,22 +3,26 @@
 Headline (BASELINE.json metric, config 2): Galois automorphism + keyswitch of 256
 seeded random ciphertexts by rotations r = 1..128 (Galois element 3^r mod 2n), n = 8192,
 four ~50-bit ciphertext primes + one 60-bit special prime, t = 65537, dnum = 4 (alpha = 1).
-One step = all 32,768 keyswitches.  Secondary (config 1): NTT round trips of
-64 ciphertexts x 2 polys x 3 limbs at n = 4096.
+One step = all 32,768 keyswitches.  Secondary: NTT round trips (config 1: 64 ciphertexts x
+2 polys x 3 limbs at n = 4096; and n = 8192 on the config-2 primes), the slot-packed and
+coefficient-packed matvecs (config 3), one layer (config 4), the 28-layer pass (config 5),
+the attention pair and the token lookup tile.
 
-  value  keyswitches/s with inputs resident in HBM (device entry point)
-  e2e    the same through the reference-facing object API (bfvgpu.Switch.apply_many,
-         host buffers, pinned), H2D of each batch and D2H of every result inside the
-         timed region -- the reference's Switch::apply contract
+  value  keyswitches/s with inputs resident in HBM (device entry points)
+  e2e    the same through the reference-facing object API (bfvgpu.Rotations.apply, host
+         buffers, pinned): H2D of the batch and D2H of every result inside the timed region
+  roofline  HBM fraction of the per-rotation launch pair, and its integer fraction
+         (int_frac) against this GPU's measured integer-operation rates
   cpu_baseline  the CPU oracle (restatement of the reference's algorithm) on the host
          cores, a bounded sample
 
-Multi-GPU (torchrun): one rank per GPU, each runs the full config-2 workload on its
-own seeded inputs (independent ciphertexts, no data-path collective): weak scaling;
-value = all ranks' keyswitches / max-over-ranks time.
+Multi-GPU (torchrun): one rank per GPU; every rank holds the same seeded ciphertexts and
+keys and takes a contiguous range of the 128 rotations (independent keyswitches, no
+data-path collective): strong scaling, value = the job's keyswitches / max-over-ranks time.
 
 `--impl reference` times the reference algorithm's CPU implementation (the oracle;
-the SEAL-based original cannot be built here) on all host threads.
+the SEAL-based original cannot be built here) on all host threads: the same calls as the
+cpu_baseline sample, each step a bounded sample of the headline workload.
 """
 from __future__ import annotations
 
@@ -41,14 +45,13 @@ T2 = 65537
 CTS = 256
 ROTATIONS = 128
 ALG_BYTES_PER_KS = 2 * 4 * N2 * 8 * 2 + (4 * 2 * 5 * N2 * 8) // CTS  # ct in + ct out + key/256
-# DRAM bytes of one rotation's launch pair (k_ks_rotate + k_ks_finish over the 256 ciphertexts),
-# from one ncu capture: rotate 476.0 MB (reads the hoisted digits Y, 1.31 MB per ciphertext,
-# every rotation; writes the pre-moddown limbs) + finish 326.1 MB.  About 3x the algorithmic
-# bytes: the hoisting trades the per-rotation digit transforms for re-reading Y.
-KS_TRAFFIC_PER_ROTATION = 802_038_528
+# The DRAM traffic of one rotation's launch pair comes from an ncu capture whose summary
+# records it with a hash of the kernel sources it was taken on (traffic_record below).
+KS_PROFILE = os.path.join(ROOT, "profiles", "keyswitch_config2_hoisted_rotate.md")
 N1 = 4096
 BITS1 = [36, 36, 37]
 NTT_POLYS = 384  # 64 cts x 2 polys x 3 limbs
+HEADLINE_METRIC = "keyswitches/s (n=8192, 4x50-bit + 60-bit special prime, dnum=4, Galois rotation)"
 
 
 def log(*a):
@@ -117,22 +120,148 @@ def cpu_count() -> int:
         return os.cpu_count() or 1
 
 
+KS_CALL_CTS_PER_THREAD = 4  # ciphertexts per host thread in one oracle call
+KS_CALL_ELEMENTS = 4  # Galois elements (each with its own key) in one oracle call
+
+
+class OracleKeyswitch:
+    """The CPU keyswitch both CPU legs time (the `cpu_baseline` sample and `--impl reference`):
+    the oracle's restatement of the reference's per-apply Switch::apply (digit transforms per
+    keyswitch, no hoisting) on the config-2 parameters, one call = KS_CALL_CTS_PER_THREAD
+    ciphertexts per host thread x KS_CALL_ELEMENTS elements, spread over every host thread."""
+
+    def __init__(self, seed: int):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        O.build()
+        primes = O.coeff_modulus(N2, BITS2)
+        self.oc = O.Ctx(N2, primes, data_k=4, t=T2)
+        self.cores = cpu_count()
+        count = KS_CALL_CTS_PER_THREAD * self.cores
+        self.cts = self.oc.uniform(seed, count * 2 * 4).reshape(count, 2, 4, N2)
+        self.keys = self.oc.uniform(seed + 1, KS_CALL_ELEMENTS * 4 * 2 * 5, prime_count=5).reshape(
+            KS_CALL_ELEMENTS, 4, 2, 5, N2)
+        self.per_call = count * KS_CALL_ELEMENTS
+        self.calls = 0
+
+    def call(self):
+        """One call; returns the keyswitches it did."""
+        base = (self.calls * KS_CALL_ELEMENTS) % ROTATIONS
+        elts = [pow(3, 1 + (base + e) % ROTATIONS, 2 * N2) for e in range(KS_CALL_ELEMENTS)]
+        self.oc.keyswitch_many(self.cts, self.keys, elts, threads=self.cores)
+        self.calls += 1
+        return self.per_call
+
+    def sample_text(self, done, dt):
+        return (f"{done} keyswitches (n=8192, 4+1 primes, per-apply: digit transforms in every keyswitch) "
+                f"on {self.cores} threads in {dt:.1f}s, {self.per_call} per oracle call")
+
+
 def cpu_keyswitch_sample(seconds: float = 12.0):
-    """Oracle keyswitch on all host cores until ~`seconds` of wall time are spent."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    O.build()
-    primes = O.coeff_modulus(N2, BITS2)
-    oc = O.Ctx(N2, primes, data_k=4, t=T2)
-    cores = cpu_count()
-    cts = oc.uniform(101, cores * 2 * 4).reshape(cores, 2, 4, N2)
-    key = oc.uniform(102, 4 * 2 * 5, prime_count=5).reshape(4, 2, 5, N2)
+    """Oracle keyswitch on all host cores until ~`seconds` of wall time are spent (one warm-up
+    call first, so the thread pool and clocks are up)."""
+    ks = OracleKeyswitch(101)
+    ks.call()
     done, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds:
-        oc.keyswitch_many(cts, key, [3], threads=cores)
-        done += cores
+        done += ks.call()
     dt = time.perf_counter() - t0
-    return done / dt, cores, f"{done} keyswitches (n=8192, 4+1 primes) on {cores} threads in {dt:.1f}s"
+    return done / dt, ks.cores, ks.sample_text(done, dt)
+
+
+def kernel_sources_sha16() -> str:
+    """Hash of the CUDA sources (every file of privacy-rag_b200/csrc, sorted by name): an ncu
+    figure recorded with a different hash was taken on other kernels."""
+    import hashlib
+    h = hashlib.sha256()
+    csrc = os.path.join(PKG, "csrc")
+    for f in sorted(os.listdir(csrc)):
+        if f.endswith((".cu", ".cuh", ".h")):
+            h.update(f.encode())
+            with open(os.path.join(csrc, f), "rb") as fh:
+                h.update(fh.read())
+    return h.hexdigest()[:16]
+
+
+def traffic_record(path: str):
+    """(bytes, note) from the `traffic-record: bytes=B sources-sha16=H` line of an ncu summary:
+    B if H matches the current kernel sources, else None with the reason."""
+    import re
+    try:
+        text = open(path).read()
+    except OSError:
+        return None, "no capture summary"
+    m = re.search(r"traffic-record: bytes=(\d+) sources-sha16=([0-9a-f]{16})", text)
+    if not m:
+        return None, "no traffic record in the capture summary"
+    if m.group(2) != kernel_sources_sha16():
+        return None, f"capture taken on other kernel sources ({m.group(2)}; now {kernel_sources_sha16()})"
+    return int(m.group(1)), f"ncu dram__bytes_read.sum + dram__bytes_write.sum, {os.path.basename(path)}"
+
+
+# ---- integer roofline -------------------------------------------------------------------------
+PEAK_KINDS = {0: "butterfly", 1: "mac", 2: "modmul"}
+
+
+def measure_int_peaks(torch, ctx, reps: int = 5):
+    """Operations per second of the three integer operations the kernels are built from
+    (bfvgpu_int_peak_device: butterfly, 64x64->128 multiply-accumulate, Barrett modular
+    product), each from registers at full occupancy, timed with CUDA events on the
+    context stream (3 warm-up launches, then `reps`)."""
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    blocks, iters = sms * 16, 4096
+    sink = torch.empty(blocks * 256, dtype=torch.int64, device="cuda")
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    sp = ctx.stream()
+    rates = {}
+    for kind, name in PEAK_KINDS.items():
+        for _ in range(3):
+            ctx.int_peak_device(kind, blocks, iters, sink, stream=sp)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(stream)
+        ops = 0
+        for _ in range(reps):
+            ops += ctx.int_peak_device(kind, blocks, iters, sink, stream=sp)
+        b.record(stream)
+        torch.cuda.synchronize()
+        rates[name] = ops / (a.elapsed_time(b) / 1e3)
+    return rates
+
+
+def int_roofline(counts: dict, rates: dict, seconds: float) -> dict:
+    """Fraction of the integer roofline: the time the measured peak rates need for the
+    kernel's algorithmic operation counts, over its measured time."""
+    at_peak = sum(counts[k] / rates[k] for k in counts)
+    return {"bound": "int", "ops_per_launch": counts, "time_at_peak_ms": at_peak * 1e3,
+            "measured_ms": seconds * 1e3, "frac": at_peak / seconds}
+
+
+def ks_pair_counts(cts: int, n: int, k: int, dk: int) -> dict:
+    """Algorithmic integer operations of one hoisted rotation launch pair (k_ks_rotate +
+    k_ks_finish) over `cts` ciphertexts: per (ciphertext, component, key-level prime) the key
+    inner product of dk multiply-accumulates per coefficient, its reduction and an inverse NTT
+    (n/2 log n butterflies, n scalings by n^-1); per (ciphertext, component, data prime) one
+    divide-and-round product per coefficient."""
+    logn = n.bit_length() - 1
+    limbs = cts * 2 * k
+    return {"butterfly": limbs * (n // 2) * logn, "mac": limbs * n * dk,
+            "modmul": limbs * n * 2 + cts * 2 * dk * n}
+
+
+def ntt_counts(polys: int, n: int, inverse: bool) -> dict:
+    logn = n.bit_length() - 1
+    return {"butterfly": polys * (n // 2) * logn, "mac": 0, "modmul": polys * n if inverse else 0}
+
+
+def headline_config(world: int, rotations: int) -> dict:
+    """`config` of the headline line, shared by both arms (`--impl reference` times a bounded
+    sample of the same workload)."""
+    return {"workload": "config2: 256 random cts x rotations 1..128 (g = 3^r mod 2n), seeded random NTT-form "
+                        "keys; one job split across the ranks by rotation ranges",
+            "n": N2, "primes_bits": BITS2, "t": T2, "dnum": 4, "cts": CTS, "rotations": rotations,
+            "parallelism": f"rotation ranges x{world} (strong)" if world > 1 else "1 GPU",
+            "l2": "inputs+keys 448 MB > 126 MB L2; every rotation re-reads all cts"}
 
 
 def cpu_ntt_sample(seconds: float = 4.0):
@@ -760,37 +889,39 @@ class _Both:
 
 # ----------------------------------------------------------------------------------------------
 def run_reference(args):
+    """The reference arm: the oracle's per-apply keyswitch (the reference's algorithm; its SEAL
+    original cannot be built here) on every host thread, the same calls the cpu_baseline leg
+    times.  Each step is a bounded sample of the headline workload: as many oracle calls as
+    take about 1.5 s (calibrated on the warm-up calls), so the default driver run of 5 + 20
+    steps ends in about 40 s."""
     rank, world, _ = env_rank()
     if rank != 0:
         return 0
-    cores = cpu_count()
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    O.build()
-    primes = O.coeff_modulus(N2, BITS2)
-    oc = O.Ctx(N2, primes, data_k=4, t=T2)
-    cts = oc.uniform(201, cores * 2 * 4).reshape(cores, 2, 4, N2)
-    key = oc.uniform(202, 4 * 2 * 5, prime_count=5).reshape(4, 2, 5, N2)
-    for _ in range(args.warmup):
-        oc.keyswitch_many(cts[:1], key, [3], threads=1)
-    times = []
-    for s in range(args.steps):
+    ks = OracleKeyswitch(101)
+    t0 = time.perf_counter()
+    for _ in range(max(1, args.warmup)):
+        ks.call()
+    t_call = (time.perf_counter() - t0) / max(1, args.warmup)
+    calls = max(1, int(round(1.5 / max(t_call, 1e-6))))
+    times, done = [], 0
+    for _ in range(args.steps):
         t0 = time.perf_counter()
-        oc.keyswitch_many(cts, key, [pow(3, s + 1, 2 * N2)], threads=cores)
+        for _ in range(calls):
+            done += ks.call()
         times.append(time.perf_counter() - t0)
     total = sum(times)
-    value = cores * args.steps / total
+    value = done / total
     line = {
-        "metric": "keyswitches/s (n=8192, 4x50-bit + 60-bit special prime, dnum=4, Galois rotation)",
+        "metric": HEADLINE_METRIC,
         "value": value, "unit": "keyswitches/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "u64", "data": "synthetic",
-        "config": {"workload": "config2 keyswitch sample: one keyswitch per host thread per step",
-                   "n": N2, "primes_bits": BITS2, "t": T2, "dnum": 4},
+        "config": headline_config(world, ROTATIONS),
         "impl": "reference",
-        "cpu_baseline": {"value": value, "unit": "keyswitches/s", "cores": cores, "kind": "port",
-                         "sample": f"{cores} keyswitches per step x {args.steps} steps (CPU oracle restatement; "
-                                   "SEAL 4.1.2 is not buildable here)"},
+        "cpu_baseline": {"value": value, "unit": "keyswitches/s", "cores": ks.cores, "kind": "port",
+                         "sample": ks.sample_text(done, total) + f"; {calls} calls per step x {args.steps} steps "
+                                   "(CPU oracle restatement; SEAL 4.1.2 is not buildable here)"},
         "e2e": {"value": value, "unit": "keyswitches/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -841,8 +972,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     sys.path.insert(0, PKG)
     import build as B
-    if not os.path.exists(B.LIB):
-        B.build()
+    B.build()  # rebuilds when any source or header is newer than the library
     import bfvgpu
 
     if args.layer_only:
@@ -876,7 +1006,7 @@ def main():
     ctx = bfvgpu.Context(N2, primes2, 4, 1, T2, device=local)
     stream = torch.cuda.ExternalStream(ctx.stream())
     g = torch.Generator(device="cuda")
-    g.manual_seed(1234 + rank)
+    g.manual_seed(1234)  # the same job on every rank: each rank takes a range of its rotations
 
     def uniform(shape, primes_cycle):
         """Residues uniform in [0, q) per limb, generated on the device."""
@@ -888,22 +1018,28 @@ def main():
 
     cts = uniform((CTS, 2, 4, N2), primes2[:4]).contiguous()
     rotations = args.rotations
-    keys = uniform((rotations, 4 * 2, 5, N2), primes2).contiguous()  # [r][digit*2+c][p][n]
-    elts = galois_elements(N2, rotations)
+    all_keys = uniform((rotations, 4 * 2, 5, N2), primes2).contiguous()  # [r][digit*2+c][p][n]
+    all_elts = galois_elements(N2, rotations)
+    # strong scaling: rank r owns the contiguous rotation range [r_lo, r_hi) of the one job
+    r_lo, r_hi = rank * rotations // world, (rank + 1) * rotations // world
+    keys = all_keys[r_lo:r_hi].contiguous()
+    elts = all_elts[r_lo:r_hi]
+    own = r_hi - r_lo
+    del all_keys
     scratch = torch.empty(ctx.keyswitch_scratch_words(CTS), dtype=torch.int64, device="cuda")
     out = torch.empty_like(cts)
     hoisted = torch.empty(ctx.keyswitch_hoist_words(CTS), dtype=torch.int64, device="cuda")
     pw = ctx.keyswitch_prepared_words()
-    prepared = torch.empty(rotations * pw, dtype=torch.int64, device="cuda")
+    prepared = torch.empty(own * pw, dtype=torch.int64, device="cuda")
     torch.cuda.synchronize()
     sp = ctx.stream()
 
     def step_hoisted(ev_pairs=None):
-        """One step: prepare the 128 keys (inside the step), hoist the 256 ciphertexts,
-        then rotate every ciphertext by every element."""
+        """One step: prepare this rank's keys (inside the step), hoist the 256 ciphertexts,
+        then rotate every ciphertext by every element of this rank's range."""
         ctx.keyswitch_prepare_device(keys, elts, prepared, stream=sp)
         ctx.keyswitch_hoist_device(cts, CTS, hoisted, stream=sp)
-        for r in range(rotations):
+        for r in range(own):
             if ev_pairs is not None:
                 ev_pairs[r][0].record(stream)
             ctx.keyswitch_rotate_device(cts, CTS, hoisted, prepared[r * pw:(r + 1) * pw], elts[r], scratch, out,
@@ -914,7 +1050,7 @@ def main():
     def step_plain(ev_pairs=None):
         """The per-apply path (Switch::apply semantics): every keyswitch recomputes its
         digit transforms."""
-        for r in range(rotations):
+        for r in range(own):
             if ev_pairs is not None:
                 ev_pairs[r][0].record(stream)
             ctx.keyswitch_device(cts, CTS, keys[r], elts[r], scratch, out, stream=sp)
@@ -925,7 +1061,7 @@ def main():
         for _ in range(warmup):
             step_fn()
         torch.cuda.synchronize()
-        ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(rotations)]
+        ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(own)]
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
@@ -951,11 +1087,11 @@ def main():
 
     elapsed, per_launch, launches, clk = timed(step_hoisted, args.steps, args.warmup, clocks=True)
     hoisted_out = out[:2].clone()
-    total_ks = CTS * rotations * args.steps * world
+    total_ks = CTS * rotations * args.steps  # the whole job, all ranks together
     value = total_ks / elapsed
     ms_per_step = 1e3 * elapsed / args.steps
     plain_dt, plain_per, _, _ = timed(step_plain, 1, 1)
-    plain_value = CTS * rotations * world / plain_dt
+    plain_value = CTS * rotations / plain_dt
     plain_match = bool(torch.equal(out[:2], hoisted_out))
 
     # ---- roofline of the dominant launch group (prepare + rotate + finish per rotation) ----
@@ -967,6 +1103,10 @@ def main():
     avg_launch = sum(per_launch) / len(per_launch)
     alg_bytes_launch = ALG_BYTES_PER_KS * CTS
     achieved = alg_bytes_launch / avg_launch / 1e9
+    ks_traffic, ks_traffic_note = traffic_record(KS_PROFILE)
+    # ---- integer roofline: this GPU's measured rates of the kernels' integer operations ----
+    int_rates = measure_int_peaks(torch, ctx)
+    ks_int = int_roofline(ks_pair_counts(CTS, N2, 5, 4), int_rates, avg_launch)
 
     # ---- secondary: ct-pt matvec (config 3) and one decoder layer (config 4), ART-002 ----
     layer_res = run_layer_legs(torch, bfvgpu, local, args) if args.layer else None
@@ -999,8 +1139,42 @@ def main():
     ntt_launch_s = ntt_dt / (2 * reps)
     ntt_bytes = NTT_POLYS * N1 * 8 * 2
     ntt_ok = bool(torch.equal(big[0], ntt_data))
+    ntt_cnt = {key: (ntt_counts(NTT_POLYS, N1, False)[key] + ntt_counts(NTT_POLYS, N1, True)[key]) / 2
+               for key in PEAK_KINDS.values()}
+    ntt_int = int_roofline(ntt_cnt, int_rates, ntt_launch_s)
 
-    e2e_value, e2e_match, e2e_rot = None, None, min(rotations, args.e2e_rotations)
+    # ---- secondary: NTTs at n = 8192 on the config-2 data primes (the metric's degree):
+    # the 256 config-2 ciphertexts' limbs, 2048 limb-polys = 128 MiB per launch (> L2) ----
+    polys8 = CTS * 2 * 4
+    buf8 = [cts.clone().view(polys8, N2) for _ in range(2)]
+    ref8 = buf8[0].clone()
+    for _ in range(3):
+        for bb in buf8:
+            ctx.ntt_device(bb, polys8, 4, 0, False, stream=sp)
+            ctx.ntt_device(bb, polys8, 4, 0, True, stream=sp)
+    torch.cuda.synchronize()
+    reps8 = max(1, args.ntt_reps // 4)
+    a8, b8 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a8.record(stream)
+    for i in range(reps8):
+        bb = buf8[i % 2]
+        ctx.ntt_device(bb, polys8, 4, 0, False, stream=sp)
+        ctx.ntt_device(bb, polys8, 4, 0, True, stream=sp)
+    b8.record(stream)
+    torch.cuda.synchronize()
+    dt8 = a8.elapsed_time(b8) / 1e3
+    launch8 = dt8 / (2 * reps8)
+    cnt8 = {key: (ntt_counts(polys8, N2, False)[key] + ntt_counts(polys8, N2, True)[key]) / 2
+            for key in PEAK_KINDS.values()}
+    ntt8 = {"value": reps8 * 2 * polys8 / dt8, "unit": "NTTs/s",
+            "config": "n=8192, config-2 data primes (4 x 50-bit), 2048 limb-polys fwd+inv per round trip",
+            "avg_launch_ms": launch8 * 1e3, "achieved_gbs": polys8 * N2 * 16 / launch8 / 1e9,
+            "frac_hbm": polys8 * N2 * 16 / launch8 / 1e9 / hbm_peak,
+            "int_roofline": int_roofline(cnt8, int_rates, launch8),
+            "round_trip_identity": bool(torch.equal(buf8[0], ref8))}
+    del buf8, ref8
+
+    e2e_value, e2e_match, e2e_rot = None, None, min(own, args.e2e_rotations)
     if args.e2e_steps > 0:
         # ---- e2e through the public API with pinned host buffers: bfvgpu.Rotations uploads
         # the 256 ciphertexts, transforms their digits once and streams every element's
@@ -1078,28 +1252,30 @@ def main():
                 model_res["cpu_baseline"] = base(ms5, "ms per pass (extrapolated from the sampled rates)")
 
     line = {
-        "metric": "keyswitches/s (n=8192, 4x50-bit + 60-bit special prime, dnum=4, Galois rotation)",
+        "metric": HEADLINE_METRIC,
         "value": value, "unit": "keyswitches/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u64", "data": "synthetic",
-        "config": {"workload": "config2: 256 random cts x rotations 1..128 (g = 3^r mod 2n), seeded random "
-                               "NTT-form keys; hoisted digits, per-rotation key preparation inside the step", "n": N2, "primes_bits": BITS2, "t": T2, "dnum": 4,
-                   "cts": CTS, "rotations": rotations, "parallelism": f"replicas x{world} (weak)",
-                   "l2": "inputs+keys 448 MB > 126 MB L2; every rotation re-reads all cts"},
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+        "config": headline_config(world, rotations),
+        "method": "hoisted digits (one digit transform per ciphertext per step), key preparation inside the step",
         "e2e": {"value": e2e_value, "unit": "keyswitches/s",
                 "api": "bfvgpu.Rotations.apply (C ABI bfvgpu_rotations_apply, pinned host buffers)",
-                "h2d_bytes_per_step": CTS * 2 * 4 * N2 * 8,
-                "d2h_bytes_per_step": CTS * 2 * 4 * N2 * 8 * e2e_rot, "rotations_per_step": e2e_rot,
+                "h2d_bytes_per_step": CTS * 2 * 4 * N2 * 8 * world,
+                "d2h_bytes_per_step": CTS * 2 * 4 * N2 * 8 * e2e_rot * world, "rotations_per_step": e2e_rot * world,
                 "steps": args.e2e_steps, "matches_device_path": e2e_match,
-                "note": "every step uploads the 256 ciphertexts and reads back all their keyswitched outputs"},
+                "note": "every step, on every rank, uploads the 256 ciphertexts and reads back all their "
+                        "keyswitched outputs for the rank's elements (bytes: all ranks)"},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "traffic": KS_TRAFFIC_PER_ROTATION, "peak_source": peak_kind,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_ks_rotate + "
-                                       "k_ks_finish pair (256 cts), recorded from one capture (profiles/)",
+                     "frac": achieved / hbm_peak, "traffic": ks_traffic, "peak_source": peak_kind,
+                     "traffic_source": ks_traffic_note,
                      "kernel": "per-rotation launches k_ks_rotate + k_ks_finish (256 cts)",
                      "alg_bytes_per_launch": alg_bytes_launch, "avg_launch_ms": avg_launch * 1e3,
-                     "note": "integer-pipe bound: 2k=10 inverse NTTs of n=8192 per keyswitch after hoisting"},
+                     "int_frac": ks_int["frac"], "int": ks_int, "int_peaks_per_s": int_rates,
+                     "int_peak_source": "measured in this run: bfvgpu_int_peak_device (register-resident "
+                                        "butterfly / 64x64->128 MAC / Barrett product, full occupancy)",
+                     "note": "integer-pipe bound (int_frac): 2k=10 inverse NTTs of n=8192 per keyswitch after "
+                             "hoisting; the HBM fraction is low by construction"},
         "secondary": {"keyswitch_per_apply": {"value": plain_value, "unit": "keyswitches/s",
                                               "path": "bfvgpu_keyswitch_device (no hoisting, Switch::apply)",
                                               "avg_launch_ms": 1e3 * sum(plain_per) / len(plain_per),
@@ -1115,7 +1291,9 @@ def main():
                               "avg_launch_ms": ntt_launch_s * 1e3,
                               "achieved_gbs": ntt_bytes / ntt_launch_s / 1e9,
                               "frac_hbm": ntt_bytes / ntt_launch_s / 1e9 / hbm_peak,
-                              "round_trip_identity": ntt_ok}},
+                              "int_roofline": ntt_int,
+                              "round_trip_identity": ntt_ok},
+                      "ntt_n8192": ntt8},
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }

@@ -149,13 +149,24 @@ int32_t bfvgpu_keyswitch_rotate_device(bfvgpu_ctx *ctx, const uint64_t *cts, uin
  * scratch is a fixed 8 MiB array in the library's device image, which every GPU that
  * loads the library holds until exit.  Limit: count * 2 * k * n * 8 bytes <= 8 MiB
  * (12 ciphertexts at n = 8192 with 4+1 primes, 4 at ART-002); larger counts fail with
- * BFVGPU_E_SHAPE.  The first call for a device looks the array's address up with that
- * device current, so make it before any stream capture.  All calls share the array:
- * calls that overlap on the GPU race; it keeps the last call's contents (nothing in it
- * needs to start at zero). */
+ * BFVGPU_E_SHAPE; count == 0 is a no-op.  The first call for a device looks the array's
+ * address up with that device current, so make it before any stream capture; the address
+ * stays valid only while that device's primary context lives (no calls after a
+ * cudaDeviceReset).  All calls share the array: calls that overlap on the GPU race; it
+ * keeps the last call's contents (nothing in it needs to start at zero). */
 int32_t bfvgpu_keyswitch_device_noalloc(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,
                                         const uint64_t *key, uint32_t galois_elt, uint64_t *out,
                                         void *stream);
+/* Integer-pipe peak microbenchmark (diagnostic; no counterpart in the reference): runs one
+ * of the 64-bit modular operations the kernels are built from, from registers only, with
+ * independent chains at full occupancy -- kind 0 = NTT butterfly (Harvey lazy, Shoup
+ * twiddle of prime 0), 1 = 64x64 -> 128-bit multiply-accumulate, 2 = modular product
+ * (128-bit product + Barrett reduction by prime 0).  blocks x 256 threads; *ops receives
+ * the operations performed (blocks * 256 * 8 chains * iters); sink [blocks * 256] (device)
+ * one checksum word per thread.  Timed by the caller (CUDA events) to give this GPU's
+ * operation rates, the denominators of the integer roofline. */
+int32_t bfvgpu_int_peak_device(bfvgpu_ctx *ctx, int32_t kind, uint32_t blocks, uint32_t iters, uint64_t *sink,
+                               uint64_t *ops, void *stream);
 /* Lift + forward NTT of ring-59 weight blocks [blocks][n] -> [blocks][dk][n]. */
 int32_t bfvgpu_weights_ntt_device(bfvgpu_ctx *ctx, const uint64_t *ring, uint64_t blocks,
                                   uint64_t *out, void *stream);

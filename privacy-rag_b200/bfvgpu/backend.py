@@ -124,6 +124,14 @@ class Context:
         check(lib().bfvgpu_keyswitch_device(self._h, self._dptr(cts), count, self._dptr(key), galois_elt,
                                             self._dptr(scratch), self._dptr(out), stream), "keyswitch_device")
 
+    def int_peak_device(self, kind: int, blocks: int, iters: int, sink, stream: int | None = None) -> int:
+        """Launch the integer-pipe peak kernel of `kind` (0 butterfly, 1 multiply-accumulate,
+        2 modular product); returns the operations it performs.  sink: blocks * 256 words."""
+        ops = U64(0)
+        check(lib().bfvgpu_int_peak_device(self._h, kind, blocks, iters, self._dptr(sink), ctypes.byref(ops),
+                                           stream), "int_peak_device")
+        return int(ops.value)
+
     def keyswitch_prepared_words(self) -> int:
         return int(lib().bfvgpu_keyswitch_prepared_words(self._h))
 
