@@ -362,6 +362,17 @@ uint64_t bfvgpu_encrypt_many_scratch_words(const bfvgpu_ctx *ctx, uint64_t cts);
 int32_t bfvgpu_encrypt_many_device(bfvgpu_ctx *ctx, const uint64_t *samples, const uint64_t *pk,
                                    const uint64_t *plain, uint64_t cts, uint64_t *scratch, uint64_t *out,
                                    void *stream);
+/* Output protection of coefficient-form ciphertexts, the server's masking and
+ * re-randomisation before a hand-off (sub_plain_inplace + encrypt_zero + add_inplace,
+ * bfv_matrix.inc:215-227, bfv_token_batch.inc:271-272), device pointers:
+ *   out [count][2][dk][n] = cts - [c = 0] Delta masks + Enc(0),
+ * masks [count][n] ring-59 words (nullable: no mask), samples [count][3][k][n] (ternary u,
+ * e0, e1; nullable: no Enc(0), then pk and scratch may be NULL), pk [2][k][n] NTT form at
+ * the key level, scratch of bfvgpu_protect_scratch_words words.  out may equal cts. */
+uint64_t bfvgpu_protect_scratch_words(const bfvgpu_ctx *ctx, uint64_t count);
+int32_t bfvgpu_protect_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count, const uint64_t *masks,
+                              const uint64_t *samples, const uint64_t *pk, uint64_t *scratch, uint64_t *out,
+                              void *stream);
 int32_t bfvgpu_enc0_close(bfvgpu_enc0 *e, bfvgpu_cleanup *cleanup);
 int32_t bfvgpu_enc0_release(bfvgpu_enc0 *e);
 
@@ -393,6 +404,20 @@ uint64_t bfvgpu_packing_level_scratch_words(const bfvgpu_ctx *ctx, uint64_t coun
 int32_t bfvgpu_packing_level_device(bfvgpu_ctx *ctx, const uint64_t *in, uint64_t pairs, uint64_t slots,
                                     uint32_t level, const uint64_t *key_one, const uint64_t *key_level,
                                     uint64_t *scratch, uint64_t *out, void *stream);
+/* The return of packed token tiles, one per slot (token_packed_many's tile return,
+ * bfv_token_batch.inc:266-283, server side), device pointers: packed [slots][2][dk][n] the
+ * tiles from the packing tree, masks [slots][n] ring-59 words, samples [slots][3][k][n], pk
+ * [2][k][n] (NTT form).  out [slots][2][dk][n] = packed - [c = 0] Delta masks + Enc(0)
+ * (out may equal packed; its c1 is what the reference sends, :272) and c0_crt
+ * [slots][512][dk] = the CRT of out's c0 at packed_target(coordinate) = 32 * (the 9-bit
+ * reversal of the coordinate) for coordinates 0..511 in order, as dk little-endian 64-bit
+ * limbs of a value in [0, Q) (rns_coefficient, :273-274).  The mask words at those targets
+ * (masks[target], :274) stay with the caller.  ART-002 (n = 16384) only; slots in [1, 4];
+ * scratch of bfvgpu_token_finish_scratch_words(ctx, slots) words. */
+uint64_t bfvgpu_token_finish_scratch_words(const bfvgpu_ctx *ctx, uint64_t slots);
+int32_t bfvgpu_token_finish_device(bfvgpu_ctx *ctx, const uint64_t *packed, uint64_t slots, const uint64_t *masks,
+                                   const uint64_t *samples, const uint64_t *pk, uint64_t *scratch, uint64_t *out,
+                                   uint64_t *c0_crt, void *stream);
 int32_t bfvgpu_token_close(bfvgpu_token *t, bfvgpu_cleanup *cleanup);
 int32_t bfvgpu_token_release(bfvgpu_token *t);
 

@@ -132,6 +132,26 @@ class Context:
                                            stream), "int_peak_device")
         return int(ops.value)
 
+    def protect_scratch_words(self, count: int) -> int:
+        return int(lib().bfvgpu_protect_scratch_words(self._h, count))
+
+    def protect_device(self, cts, count: int, out, masks=None, samples=None, pk=None, scratch=None,
+                       stream: int | None = None) -> None:
+        """out = cts - Delta masks (c0) + Enc(0) from samples (bfvgpu_protect_device)."""
+        check(lib().bfvgpu_protect_device(self._h, self._dptr(cts), count, self._dptr(masks), self._dptr(samples),
+                                          self._dptr(pk), self._dptr(scratch), self._dptr(out), stream),
+              "protect_device")
+
+    def token_finish_scratch_words(self, slots: int) -> int:
+        return int(lib().bfvgpu_token_finish_scratch_words(self._h, slots))
+
+    def token_finish_device(self, packed, slots: int, masks, samples, pk, scratch, out, c0_crt,
+                            stream: int | None = None) -> None:
+        """Tile return of packed token tiles (bfvgpu_token_finish_device)."""
+        check(lib().bfvgpu_token_finish_device(self._h, self._dptr(packed), slots, self._dptr(masks),
+                                               self._dptr(samples), self._dptr(pk), self._dptr(scratch),
+                                               self._dptr(out), self._dptr(c0_crt), stream), "token_finish_device")
+
     def keyswitch_prepared_words(self) -> int:
         return int(lib().bfvgpu_keyswitch_prepared_words(self._h))
 

@@ -55,6 +55,26 @@ class TokenTile:
             self.levels_out = [t.empty((coords >> (l + 1), slots, 2, dk, n), dtype=t.int64, device=dev)
                                for l in range(self.levels)]
 
+    def finish(self, packed, masks, samples, pk):
+        """The tile return (bfv_token_batch.inc:266-283): packed [slots][2][dk][n] from run(),
+        masks [slots][n] ring-59 words, samples [slots][3][k][n] Enc(0) randomness, pk
+        [2][k][n] (NTT form).  Returns (out, c0_crt): out [slots][2][dk][n] = packed - Delta
+        masks + Enc(0) (c1 is what the reference sends) and c0_crt [slots][512][dk] the CRT of
+        c0 at packed_target(coordinate) for coordinates 0..511 (device tensors; the masks at
+        those targets stay with the caller)."""
+        if self.coords != TILE:
+            raise ValueError("E_TOKEN_BATCH_SHAPE: the tile return needs the full 512-coordinate tree")
+        t, ctx = self.torch, self.ctx
+        with t.cuda.stream(self.stream):
+            if not hasattr(self, "fscratch"):
+                dev = self.inputs.device
+                self.fscratch = t.empty(ctx.token_finish_scratch_words(self.slots), dtype=t.int64, device=dev)
+                self.fout = t.empty((self.slots, 2, ctx.dk, ctx.n), dtype=t.int64, device=dev)
+                self.fcrt = t.empty((self.slots, TILE, ctx.dk), dtype=t.int64, device=dev)
+            ctx.token_finish_device(packed, self.slots, masks, samples, pk, self.fscratch, self.fout, self.fcrt,
+                                    stream=ctx.stream())
+        return self.fout, self.fcrt
+
     def run(self, ring, local):
         ctx, s = self.ctx, self.ctx.stream()
         for c0 in range(0, self.coords, self.chunk):

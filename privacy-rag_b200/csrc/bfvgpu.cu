@@ -1735,6 +1735,57 @@ int32_t bfvgpu_encrypt_many_device(bfvgpu_ctx* ctx, const uint64_t* samples, con
   });
 }
 
+uint64_t bfvgpu_protect_scratch_words(const bfvgpu_ctx* ctx, uint64_t count) {
+  return ctx ? count * 3ull * ctx->c.k * ctx->c.n : 0;
+}
+
+int32_t bfvgpu_protect_device(bfvgpu_ctx* ctx, const uint64_t* cts, uint64_t count, const uint64_t* masks,
+                              const uint64_t* samples, const uint64_t* pk, uint64_t* scratch, uint64_t* out,
+                              void* stream) {
+  return guard([&] {
+    if (!ctx || !cts || !out) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (samples && (!pk || !scratch)) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (samples && ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    if (count * ctx->c.k > 0x7fffffffull) fail(BFVGPU_E_SHAPE, "E_BFV_PACKED_SHAPE");
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    uint64_t* u_ntt = scratch;
+    uint64_t* x = scratch ? scratch + count * (uint64_t)ctx->c.k * ctx->c.n : nullptr;
+    cuda_check(launch_protect_ct(ctx->c.P, cts, count, masks, samples, pk, u_ntt, x, out, pick(ctx, stream)),
+               "protect");
+    count_launch(samples ? 2 : 1);
+  });
+}
+
+uint64_t bfvgpu_token_finish_scratch_words(const bfvgpu_ctx* ctx, uint64_t slots) {
+  if (!ctx) return 0;
+  return slots * (3ull * ctx->c.k * ctx->c.n + 512 + 512ull * ctx->c.dk) + (slots + 1) / 2;
+}
+
+int32_t bfvgpu_token_finish_device(bfvgpu_ctx* ctx, const uint64_t* packed, uint64_t slots, const uint64_t* masks,
+                                   const uint64_t* samples, const uint64_t* pk, uint64_t* scratch, uint64_t* out,
+                                   uint64_t* c0_crt, void* stream) {
+  return guard([&] {
+    if (!ctx || !packed || !masks || !samples || !pk || !scratch || !out || !c0_crt)
+      fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    const Context& c = ctx->c;
+    if (c.n != 16384 || c.k != c.dk + 1 || c.dk > 8) fail(BFVGPU_E_CONTEXT, "E_TOKEN_CONTEXT");
+    if (slots < 1 || slots > 4) fail(BFVGPU_E_SHAPE, "E_TOKEN_BATCH_SHAPE");
+    require_device(c);
+    DeviceScope scope(c.device);
+    const cudaStream_t st = pick(ctx, stream);
+    uint64_t* u_ntt = scratch;
+    uint64_t* x = u_ntt + slots * (uint64_t)c.k * c.n;
+    uint64_t* targets = x + slots * 2ull * c.k * c.n;
+    uint64_t* selected = targets + slots * 512;
+    uint32_t* counts = reinterpret_cast<uint32_t*>(selected + slots * 512ull * c.dk);
+    cuda_check(launch_protect_ct(c.P, packed, slots, masks, samples, pk, u_ntt, x, out, st), "token finish protect");
+    cuda_check(launch_packed_targets(targets, counts, slots, st), "token finish targets");
+    cuda_check(launch_gather_targets(c.P, out, targets, counts, 512, slots, selected, c0_crt, st), "token finish CRT");
+    count_launch(4);
+  });
+}
+
 int32_t bfvgpu_enc0_close(bfvgpu_enc0* e, bfvgpu_cleanup* cleanup) {
   if (!e) return BFVGPU_E_ARGUMENT;
   const bfvgpu_cleanup c = e->h.release();

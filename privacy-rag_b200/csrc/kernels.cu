@@ -812,6 +812,38 @@ __global__ void k_packing_prepare_many(const uint64_t* in, uint64_t pairs, uint6
 
 // c0 [dk][n] += Delta-scaled plaintext coefficient (add_plain with the scaling variant),
 // for coefficients i < count (bfv_matrix.inc:40-46: encrypt_zero then add_plain_inplace).
+// Output protection of coefficient-form ciphertexts [items][2][dk][n]: out = ct + Enc(0) -
+// [c = 0] Delta mask, with Enc(0) = moddown(x) from its pre-moddown polys x [items][2][k][n]
+// (nullable) and mask [items][n] ring-59 words (nullable).  The tile return of
+// bfv_token_batch.inc:271-272 (sub_plain_inplace(mask), encrypt_zero, add_inplace) in one pass.
+__global__ void k_protect_ct(const uint64_t* ct, const uint64_t* x, const uint64_t* mask, uint64_t* out, uint64_t items,
+                             uint32_t k, uint32_t dk, int logn, const Modulus* mods, uint64_t q_mod_t,
+                             uint64_t upper_half, uint64_t t, int tlog) {
+  const uint64_t N = uint64_t(1) << logn;
+  const uint64_t total = items * 2 * dk * N;
+  for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t i = e & (N - 1);
+    const uint64_t row = e >> logn;  // (item*2 + c)*dk + p
+    const uint32_t p = (uint32_t)(row % dk);
+    const uint64_t gc = row / dk;
+    const Modulus& m = mods[p];
+    uint64_t v = ct[e];
+    if (x) {
+      const uint64_t* xr = x + gc * k * N;
+      v = add_mod(v, moddown_elem(xr[(uint64_t)p * N + i], xr[(uint64_t)(k - 1) * N + i], m, mods[k - 1]), m.q);
+    }
+    if (mask && (gc & 1) == 0)
+      v = sub_mod(v, scale_plain_coeff(mask[(gc >> 1) * N + i], q_mod_t, upper_half, t, tlog, m), m.q);
+    out[e] = v;
+  }
+}
+// The packed-tile targets of bfv_acyclic_pack.hpp:53-56 for `slots` tiles: targets
+// [slots][512] = 32 * (9-bit reversal of the coordinate), counts [slots] = 512.
+__global__ void k_packed_targets(uint64_t* targets, uint32_t* counts, uint64_t slots) {
+  const uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (e < slots * 512) targets[e] = (uint64_t)(__brev((uint32_t)(e & 511)) >> 23) * 32;
+  if (e < slots) counts[e] = 512;
+}
 __global__ void k_add_plain(uint64_t* c0, const uint64_t* plain, uint64_t count, uint32_t dk, int logn,
                             const Modulus* mods, uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog) {
   const uint64_t total = (uint64_t)dk * count;
@@ -1176,6 +1208,25 @@ cudaError_t launch_encrypt_many(const DevParams& P, const uint64_t* samples, con
   if (e != cudaSuccess) return e;
   k_add_plain_many<<<elementwise_blocks(cts * P.dk * P.n), 256, 0, st>>>(out, plain, cts, P.dk, P.logn, P.mod,
                                                                          P.q_mod_t, P.upper_half, P.t, P.tlog);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_protect_ct(const DevParams& P, const uint64_t* cts, uint64_t items, const uint64_t* masks,
+                              const uint64_t* samples, const uint64_t* pk, uint64_t* u_ntt, uint64_t* x, uint64_t* out,
+                              cudaStream_t st) {
+  if (!items) return cudaSuccess;
+  if (samples) {
+    const cudaError_t e = launch_enc0_x(P, samples, pk, u_ntt, x, items, st);
+    if (e != cudaSuccess) return e;
+  }
+  k_protect_ct<<<elementwise_blocks(items * 2 * P.dk * P.n), 256, 0, st>>>(
+      cts, samples ? x : nullptr, masks, out, items, P.k, P.dk, P.logn, P.mod, P.q_mod_t, P.upper_half, P.t, P.tlog);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_packed_targets(uint64_t* targets, uint32_t* counts, uint64_t slots, cudaStream_t st) {
+  if (!slots) return cudaSuccess;
+  k_packed_targets<<<(unsigned)((slots * 512 + 255) / 256), 256, 0, st>>>(targets, counts, slots);
   return cudaGetLastError();
 }
 

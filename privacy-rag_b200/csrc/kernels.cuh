@@ -138,6 +138,16 @@ cudaError_t launch_packing_prepare(const DevParams& P, const uint64_t* left, con
 // c0 [dk][n] += Delta * plain[i] (scaling variant) for i < count, plain < t.
 cudaError_t launch_add_plain(const DevParams& P, uint64_t* c0, const uint64_t* plain, uint64_t count,
                              cudaStream_t st);
+// Output protection of coefficient-form ciphertexts: out [items][2][dk][n] = cts + Enc(0) -
+// [c = 0] Delta masks, Enc(0) from samples [items][3][k][n] (nullable: none) and pk [2][k][n]
+// (NTT form) through the scratch u_ntt [items][k][n], x [items][2][k][n]; masks [items][n]
+// (nullable).  out may be cts.
+cudaError_t launch_protect_ct(const DevParams& P, const uint64_t* cts, uint64_t items, const uint64_t* masks,
+                              const uint64_t* samples, const uint64_t* pk, uint64_t* u_ntt, uint64_t* x, uint64_t* out,
+                              cudaStream_t st);
+// targets [slots][512] = the packed token tile's target coefficient of every coordinate,
+// counts [slots] = 512 (the gather_targets operands of a tile return).
+cudaError_t launch_packed_targets(uint64_t* targets, uint32_t* counts, uint64_t slots, cudaStream_t st);
 // a += b on [polys][n] data-prime polys.
 cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint64_t polys, cudaStream_t st);
 // Public-key encryption of cts plaintexts: samples [cts][3][k][n] (u, e0, e1), pk [2][k][n] NTT

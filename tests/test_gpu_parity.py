@@ -490,6 +490,66 @@ def test_matrix_tiles_tensor_core_vs_cuda_core(art, oracle):
         assert np.array_equal(got[t, g], oc.matrix_evaluate(cn, ring_h[g], threads=8)), (t, g)
 
 
+def test_matrix_tiles_qkv_full_shape(art, oracle):
+    """The benchmark's largest prefill call at full shape: the qkv joint projection of a
+    128-token group, 8 tiles x 64 input blocks x 128 output groups (matrix_packing of B = 16,
+    K = 1024, O = 4096), int8 weights, with the masks and Enc(0) of every output, on the
+    tcgen05 product.  Every output word equals the CUDA-core product's, and spot (tile, group)
+    pairs equal the oracle's evaluate + sub_plain + Enc(0) + add."""
+    import torch
+    hc, oc = art
+    n, k, dk = oc.n, oc.k, oc.data_k
+    tiles, I, G = 8, 64, 128
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(11)
+    q = torch.tensor(oc.primes, dtype=torch.int64, device="cuda")
+
+    def residues(shape, nprimes, lo=0, hi=None):
+        """Values in [lo, hi) (uniform residues when hi is None) reduced per prime (axis -2)."""
+        if hi is None:
+            raw = torch.randint(0, 2 ** 62, shape, dtype=torch.int64, device="cuda", generator=gen)
+        else:
+            raw = torch.randint(lo, hi, shape, dtype=torch.int64, device="cuda", generator=gen)
+        return torch.remainder(raw, q[:nprimes].view(*([1] * (len(shape) - 2)), nprimes, 1))
+
+    cts = residues((tiles, I, 2, dk, n), dk)
+    cts[0, 0, 0, 0, :64] = q[0] - 1
+    ring = torch.randint(-127, 128, (G, I, n), dtype=torch.int64, device="cuda", generator=gen) & ((1 << 59) - 1)
+    masks = torch.randint(0, 2 ** 59, (tiles, G, n), dtype=torch.int64, device="cuda", generator=gen)
+    # Enc(0) randomness as the sampler draws it: ternary u, small e0, e1, each in all k primes
+    small = lambda lo, hi: torch.randint(lo, hi, (tiles, G, 1, n), dtype=torch.int64, device="cuda",
+                                         generator=gen).expand(tiles, G, k, n)
+    samples = torch.stack([torch.remainder(small(lo, hi), q.view(1, 1, k, 1))
+                           for lo, hi in ((-1, 2), (-5, 6), (-5, 6))], dim=2).contiguous()
+    pk = residues((2, k, n), k)
+    d_in = cts.clone()
+    w = torch.empty((G, I, dk, n), dtype=torch.int64, device="cuda")
+    pk_prep = torch.empty((2, k, n, 2), dtype=torch.int64, device="cuda")
+    scratch = torch.empty(hc.matrix_tiles_scratch_words(tiles, G), dtype=torch.int64, device="cuda")
+    out_tc = torch.empty((tiles, G, 2, dk, n), dtype=torch.int64, device="cuda")
+    out_cc = torch.empty_like(out_tc)
+    hc.matrix_tiles_inputs_device(d_in, tiles * I)
+    hc.weights_ntt_device(ring, G * I, w)
+    hc.matrix_tiles_prepare_pk_device(pk, pk_prep)
+    hc.matrix_tiles_device(d_in, tiles, I, w, G, out_tc, masks=masks, samples=samples, pk_prep=pk_prep,
+                           scratch=scratch)
+    hc.set_product_path(1)
+    try:
+        hc.matrix_tiles_device(d_in, tiles, I, w, G, out_cc, masks=masks, samples=samples, pk_prep=pk_prep,
+                               scratch=scratch)
+    finally:
+        hc.set_product_path(0)
+    assert hc.check() == 0
+    assert torch.equal(out_tc, out_cc)
+    pk_h = pk.cpu().numpy().view(np.uint64)
+    for t, g in [(0, 0), (3, 63), (5, 100), (7, 127)]:
+        cn = oc.matrix_open(cts[t].cpu().numpy().view(np.uint64), threads=8)
+        e = oc.matrix_evaluate(cn, ring[g].cpu().numpy().view(np.uint64), threads=8)
+        e[0] = oc.sub_plain(e[0], masks[t, g].cpu().numpy().view(np.uint64))
+        e = oc.add(e, oc.enc0(samples[t, g].cpu().numpy().view(np.uint64), pk_h))
+        assert np.array_equal(out_tc[t, g].cpu().numpy().view(np.uint64), e), (t, g)
+
+
 # ---- resident token ----------------------------------------------------------------------------
 def test_token_weights(art, oracle):
     import bfvgpu
@@ -522,17 +582,18 @@ def test_token_weights(art, oracle):
     assert c["closed"] and c["wiped"] == c["freed"]
 
 
-def test_token_tile_batched(art, oracle):
-    """Raw token products of 8 coordinates in one batched call equal TokenWeights, one
-    coordinate at a time; the level-batched packing tree over them equals the reference's
-    binary-counter stack of pairwise merges (Switch.packing_pair, itself checked against the
-    oracle), for 2 slots."""
+@pytest.mark.parametrize("slots,coords", [(2, 8), (1, 64)])
+def test_token_tile_batched(art, oracle, slots, coords):
+    """Raw token products of `coords` coordinates in one batched call equal TokenWeights, one
+    coordinate at a time; the level-batched packing tree over them (log2 coords levels: 3, and
+    6 at 64 coordinates) equals the reference's binary-counter stack of pairwise merges
+    (Switch.packing_pair, itself checked against the oracle)."""
     import torch
     import bfvgpu
     hc, oc = art
     n, dk, k = oc.n, oc.data_k, oc.k
-    rng = np.random.default_rng(95)
-    slots, coords, bound = 2, 8, 1 << 20
+    rng = np.random.default_rng(95 + coords)
+    bound = 1 << 20
     cts = oc.uniform(96, slots * 19 * 2 * dk).reshape(slots, 19, 2, dk, n)
     tw = bfvgpu.TokenWeights(hc, cts)
     ring = (rng.integers(-bound, bound + 1, size=(coords, 19 * 8192)) & ((1 << 59) - 1)).astype(np.uint64)
@@ -551,7 +612,7 @@ def test_token_tile_batched(art, oracle):
     torch.cuda.synchronize()
     assert np.array_equal(raw.cpu().numpy().view(np.uint64), ref)
     # packing tree: level l merges pairs of 2^l-coordinate blocks with the level's two keys
-    levels = 3
+    levels = coords.bit_length() - 1
     key_one = [oc.uniform(200 + l, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n) for l in range(levels)]
     key_lev = [oc.uniform(300 + l, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n) for l in range(levels)]
     # torch allocates and frees on the context's stream, so no buffer is reused while a

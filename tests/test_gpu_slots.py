@@ -30,8 +30,10 @@ def _decode(S, tc, coeffs):
     return ev[S.slot_positions(tc.n)]
 
 
-@pytest.mark.parametrize("K,O", [(64, 128), (16, 40)])
+@pytest.mark.parametrize("K,O", [(64, 128), (16, 40), (1024, 2048)])
 def test_slot_matvec(bfv, oracle, setup, K, O):
+    """(1024, 2048) is the benchmark's config-3 shape: W 2048 x 1024 int8, baby 32 x giant 16,
+    47 keys, 31 baby-step elements in one multi-element rotation launch pair."""
     import torch
     import bfvgpu.slots as S
     hc, pc, oc, tc = setup
