@@ -562,15 +562,24 @@ def run_token_leg(torch, bfvgpu, device, args):
         ring = torch.bitwise_and(torch.randint(-bound, bound + 1, (TK.TILE, 19 * 8192), dtype=torch.int64,
                                                device="cuda", generator=g), (1 << 59) - 1)
         local = torch.randint(0, 2 ** 59, (TK.TILE, slots), dtype=torch.int64, device="cuda", generator=g)
+        mask = torch.randint(0, 2 ** 59, (slots, n), dtype=torch.int64, device="cuda", generator=g)
+        small = torch.cat([torch.randint(-1, 2, (slots, 1, n), dtype=torch.int64, device="cuda", generator=g),
+                           torch.randint(-5, 6, (slots, 2, n), dtype=torch.int64, device="cuda", generator=g)], dim=1)
+        samples = torch.remainder(small.unsqueeze(-2), q.view(k, 1)).contiguous()  # [slots][3][k][n]
+        pk = residues((2, k, n), k)
         tile = TK.TokenTile(torch, ctx, inputs, slots, keys_one, keys_lev)
-        tile.run(ring, local)
+
+        def whole_tile():
+            tile.finish(tile.run(ring, local), mask, samples, pk)
+
+        whole_tile()
         torch.cuda.synchronize()
         reps = 3
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         launches0 = bfvgpu.launch_count()
         a.record(stream)
         for _ in range(reps):
-            tile.run(ring, local)
+            whole_tile()
         b.record(stream)
         torch.cuda.synchronize()
     ms = a.elapsed_time(b) / reps
@@ -578,7 +587,7 @@ def run_token_leg(torch, bfvgpu, device, args):
            "merges": TK.TILE - 1, "keyswitches": 2 * (TK.TILE - 1),
            "raw_weight_ntts": TK.TILE * 19 * dk, "launches_per_tile": (bfvgpu.launch_count() - launches0) // reps,
            "note": "ART-002; raw products batched 64 coordinates per launch pair, packing tree as 9 batched "
-                   "levels; the tile's final mask / Enc(0) and target CRT (one ciphertext) not included"}
+                   "levels, then the tile return (mask, Enc(0), CRT of c0 at the 512 packed targets)"}
     del tile, inputs, keys_one, keys_lev, ring, local
     torch.cuda.empty_cache()
     ctx.close()

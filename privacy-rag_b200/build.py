@@ -30,8 +30,9 @@ def dependencies() -> list[str]:
     """Every file the library is compiled from: the sources, every header beside them and
     the public headers (a new header is picked up without editing this list)."""
     deps = [os.path.join(CSRC, f) for f in SOURCES]
-    for d in (CSRC, os.path.join(ROOT, "include")):
-        deps += [os.path.join(d, f) for f in sorted(os.listdir(d)) if f.endswith((".cuh", ".h", ".hpp"))]
+    deps += [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC)) if f.endswith((".cuh", ".h"))]
+    inc = os.path.join(ROOT, "include")  # the C ABI headers (the C++ adapters are header-only users)
+    deps += [os.path.join(inc, f) for f in sorted(os.listdir(inc)) if f.endswith(".h")]
     deps.append(os.path.abspath(__file__))
     return deps
 
