@@ -62,7 +62,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     with concurrent.futures.ThreadPoolExecutor(len(cmds)) as pool:
         for f in [pool.submit(subprocess.run, c, check=True) for c in cmds]:
             f.result()
-    cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-lpthread"]
     subprocess.run(cmd, check=True)
     for o in objs:
         os.remove(o)

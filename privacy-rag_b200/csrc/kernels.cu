@@ -22,12 +22,23 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include "kernels.cuh"
 #include "block_ops.cuh"
 #include "mac_tc.cuh"
 
 namespace bfvgpu {
+
+// NVTX range around each launch group (named "bfvgpu:<group>"), so a profiler timeline
+// shows which fused kernels a library call issued.  Header-only NVTX v3: without an
+// attached tool a push/pop is a check of one function pointer.
+struct LaunchRange {
+  explicit LaunchRange(const char* name) { nvtxRangePushA(name); }
+  ~LaunchRange() { nvtxRangePop(); }
+  LaunchRange(const LaunchRange&) = delete;
+  LaunchRange& operator=(const LaunchRange&) = delete;
+};
 
 // Block shape per degree, from a sweep of radix x blocks/SM x block size on B200:
 // n <= 8192: 256 threads, 3 blocks per SM (<= 80 registers); n = 16384: 512 threads,
@@ -946,6 +957,7 @@ static unsigned elementwise_blocks(uint64_t total) {
 
 cudaError_t launch_ntt(const DevParams& P, uint64_t* data, uint64_t polys, uint32_t prime_count,
                        uint32_t prime_offset, bool inverse, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:ntt");
   if (!polys) return cudaSuccess;
   BFV_DISPATCH(P.logn, {
     if (inverse)
@@ -960,6 +972,7 @@ cudaError_t launch_ntt(const DevParams& P, uint64_t* data, uint64_t polys, uint3
 
 cudaError_t launch_lift_ntt(const DevParams& P, const uint64_t* ring, uint64_t* out, uint64_t blocks,
                             cudaStream_t st) {
+  const LaunchRange range("bfvgpu:lift_ntt");
   if (!blocks) return cudaSuccess;
   BFV_DISPATCH(P.logn, {
     k_lift_ntt<L_><<<(unsigned)(blocks * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(ring, out, P.dk, P.mod,
@@ -970,6 +983,7 @@ cudaError_t launch_lift_ntt(const DevParams& P, const uint64_t* ring, uint64_t* 
 
 cudaError_t launch_mac_intt(const DevParams& P, const uint64_t* in, const uint64_t* w, uint64_t* out,
                             uint64_t inputs, uint64_t groups, const Protect& prot, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:mac_intt");
   if (!groups) return cudaSuccess;
   ProtectArgs a{prot.mask, prot.enc0_x, P.q_mod_t, P.upper_half, P.t, P.tlog};
   BFV_DISPATCH(P.logn, {
@@ -982,6 +996,7 @@ cudaError_t launch_mac_intt(const DevParams& P, const uint64_t* in, const uint64
 cudaError_t launch_gather_targets(const DevParams& P, const uint64_t* out, const uint64_t* targets,
                                   const uint32_t* counts, uint32_t max_count, uint64_t groups, uint64_t* selected,
                                   uint64_t* crt, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:gather_targets");
   if (!groups || !max_count) return cudaSuccess;
   if (P.dk > 8) return cudaErrorInvalidValue;
   dim3 grid((max_count + 127) / 128, (unsigned)groups);
@@ -1003,6 +1018,7 @@ static uint32_t inverse_mod_2n(uint32_t g, uint32_t two_n) {
 
 cudaError_t launch_keyswitch(const DevParams& P, const uint64_t* cts, const uint64_t* key, uint32_t elt,
                              uint64_t count, uint64_t* acc, uint64_t* out, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:keyswitch");
   if (!count) return cudaSuccess;
   if (P.k != P.dk + 1) return cudaErrorInvalidValue;
   const uint32_t ginv = inverse_mod_2n(elt, 2 * P.n);
@@ -1018,6 +1034,7 @@ cudaError_t launch_keyswitch(const DevParams& P, const uint64_t* cts, const uint
 
 cudaError_t launch_ks_hoist(const DevParams& P, const uint64_t* cts, uint64_t count, uint64_t* Y, uint32_t* zflag,
                             cudaStream_t st) {
+  const LaunchRange range("bfvgpu:ks_hoist");
   if (!count) return cudaSuccess;
   if (P.k != P.dk + 1) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(zflag, 0, count * sizeof(uint32_t), st);
@@ -1031,6 +1048,7 @@ cudaError_t launch_ks_hoist(const DevParams& P, const uint64_t* cts, uint64_t co
 
 cudaError_t launch_ks_keyprep(const DevParams& P, const uint64_t* keys, const uint32_t* elts, uint64_t count,
                               uint64_t* prepared, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:ks_keyprep");
   if (P.k != P.dk + 1) return cudaErrorInvalidValue;
   const uint64_t pw = (2ull * P.dk + 2) * P.k * P.n;
   const uint64_t kw = 2ull * P.dk * P.k * P.n;
@@ -1056,6 +1074,7 @@ cudaError_t launch_ks_keyprep(const DevParams& P, const uint64_t* keys, const ui
 cudaError_t launch_ks_rotate(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
                              const uint32_t* zflag, const uint64_t* prepared, uint32_t elt, uint64_t* x, uint64_t* out,
                              cudaStream_t st) {
+  const LaunchRange range("bfvgpu:ks_rotate");
   if (!count) return cudaSuccess;
   if (P.k != P.dk + 1) return cudaErrorInvalidValue;
   const uint32_t ginv = inverse_mod_2n(elt, 2 * P.n);
@@ -1071,6 +1090,7 @@ cudaError_t launch_ks_rotate(const DevParams& P, const uint64_t* cts, uint64_t c
 cudaError_t launch_ks_rotate_multi(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
                                    const uint32_t* zflag, const uint64_t* prepared, const uint32_t* elts,
                                    uint64_t elements, int paired, uint64_t* x, uint64_t* out, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:ks_rotate_multi");
   if (!count || !elements) return cudaSuccess;
   if (P.k != P.dk + 1 || (paired && elements != count)) return cudaErrorInvalidValue;
   const uint64_t pw = (2ull * P.dk + 2) * P.k * P.n;
@@ -1104,6 +1124,7 @@ cudaError_t launch_ks_rotate_multi(const DevParams& P, const uint64_t* cts, uint
 }
 
 cudaError_t launch_sum_cts(const DevParams& P, const uint64_t* in, uint64_t groups, uint64_t* acc, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:sum_cts");
   const uint64_t words = (2ull * P.dk) << P.logn;
   k_sum_cts<<<elementwise_blocks(words), 256, 0, st>>>(in, groups, acc, P.dk, P.logn, P.mod);
   return cudaGetLastError();
@@ -1111,6 +1132,7 @@ cudaError_t launch_sum_cts(const DevParams& P, const uint64_t* in, uint64_t grou
 
 cudaError_t launch_enc0_x(const DevParams& P, const uint64_t* samples, const uint64_t* pk, uint64_t* u_ntt,
                           uint64_t* x, uint64_t groups, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:enc0_x");
   if (!groups) return cudaSuccess;
   if (P.k != P.dk + 1) return cudaErrorInvalidValue;
   BFV_DISPATCH(P.logn, {
@@ -1121,6 +1143,7 @@ cudaError_t launch_enc0_x(const DevParams& P, const uint64_t* samples, const uin
 }
 
 cudaError_t launch_moddown(const DevParams& P, const uint64_t* x, uint64_t* out, uint64_t groups, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:moddown");
   if (!groups) return cudaSuccess;
   if (P.k != P.dk + 1) return cudaErrorInvalidValue;
   const uint64_t total = groups * 2 * P.dk * P.n;
@@ -1130,6 +1153,7 @@ cudaError_t launch_moddown(const DevParams& P, const uint64_t* x, uint64_t* out,
 
 cudaError_t launch_client_phase(const DevParams& P, uint64_t* data, const uint64_t* sk, uint64_t batches,
                                 cudaStream_t st) {
+  const LaunchRange range("bfvgpu:client_phase");
   if (!batches) return cudaSuccess;
   BFV_DISPATCH(P.logn, {
     k_client_phase<L_><<<(unsigned)(batches * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(data, sk, P.dk,
@@ -1140,6 +1164,7 @@ cudaError_t launch_client_phase(const DevParams& P, uint64_t* data, const uint64
 
 cudaError_t launch_check_canonical(const DevParams& P, const uint64_t* data, uint64_t polys, uint32_t prime_count,
                                    uint32_t prime_offset, uint32_t* bad, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:check_canonical");
   if (!polys) return cudaSuccess;
   k_check_canonical<<<elementwise_blocks(polys << P.logn), 256, 0, st>>>(data, polys, prime_count, prime_offset,
                                                                          P.logn, P.mod, bad);
@@ -1149,6 +1174,7 @@ cudaError_t launch_check_canonical(const DevParams& P, const uint64_t* data, uin
 cudaError_t launch_token_evaluate(const DevParams& P, const uint64_t* inputs, uint64_t slots, const uint64_t* ring,
                                   const uint64_t* scaled, uint64_t* wscratch, uint64_t* acc, uint64_t* out,
                                   cudaStream_t st) {
+  const LaunchRange range("bfvgpu:token_evaluate");
   (void)acc;
   if (P.logn != 14) return cudaErrorInvalidValue;
   constexpr int L_ = 14;
@@ -1162,6 +1188,7 @@ cudaError_t launch_token_evaluate(const DevParams& P, const uint64_t* inputs, ui
 cudaError_t launch_token_evaluate_many(const DevParams& P, const uint64_t* inputs, uint64_t slots, const uint64_t* ring,
                                        uint64_t coords, const uint64_t* local, uint64_t* scaled, uint64_t* wscratch,
                                        uint64_t* out, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:token_evaluate_many");
   if (!coords || !slots) return cudaSuccess;
   if (P.logn != 14 || coords * kTokenBlocks * P.dk > 0x7fffffffull || coords * slots * 2 * P.dk > 0x7fffffffull)
     return cudaErrorInvalidValue;
@@ -1177,6 +1204,7 @@ cudaError_t launch_token_evaluate_many(const DevParams& P, const uint64_t* input
 
 cudaError_t launch_packing_prepare_many(const DevParams& P, const uint64_t* in, uint64_t pairs, uint64_t slots,
                                         uint64_t* sum, uint64_t* diff, unsigned level, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:packing_prepare_many");
   if (!pairs || !slots) return cudaSuccess;
   const uint64_t total = pairs * slots * 2 * (uint64_t)P.dk * P.n;
   k_packing_prepare_many<<<elementwise_blocks(total), 256, 0, st>>>(in, pairs, slots, sum, diff, P.dk, P.logn,
@@ -1186,6 +1214,7 @@ cudaError_t launch_packing_prepare_many(const DevParams& P, const uint64_t* in, 
 
 cudaError_t launch_packing_prepare(const DevParams& P, const uint64_t* left, const uint64_t* right, uint64_t* sum,
                                    uint64_t* diff, unsigned level, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:packing_prepare");
   const uint64_t total = 2 * (uint64_t)P.dk * P.n;
   k_packing_prepare<<<elementwise_blocks(total), 256, 0, st>>>(left, right, sum, diff, P.dk, P.logn,
                                                               P.n >> (level + 1), P.mod);
@@ -1194,6 +1223,7 @@ cudaError_t launch_packing_prepare(const DevParams& P, const uint64_t* left, con
 
 cudaError_t launch_add_plain(const DevParams& P, uint64_t* c0, const uint64_t* plain, uint64_t count,
                              cudaStream_t st) {
+  const LaunchRange range("bfvgpu:add_plain");
   if (!count) return cudaSuccess;
   k_add_plain<<<elementwise_blocks(count * P.dk), 256, 0, st>>>(c0, plain, count, P.dk, P.logn, P.mod, P.q_mod_t,
                                                                P.upper_half, P.t, P.tlog);
@@ -1202,6 +1232,7 @@ cudaError_t launch_add_plain(const DevParams& P, uint64_t* c0, const uint64_t* p
 
 cudaError_t launch_encrypt_many(const DevParams& P, const uint64_t* samples, const uint64_t* pk, const uint64_t* plain,
                                 uint64_t cts, uint64_t* u_ntt, uint64_t* x, uint64_t* out, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:encrypt_many");
   if (!cts) return cudaSuccess;
   cudaError_t e = launch_enc0_x(P, samples, pk, u_ntt, x, cts, st);
   if (e == cudaSuccess) e = launch_moddown(P, x, out, cts, st);
@@ -1214,6 +1245,7 @@ cudaError_t launch_encrypt_many(const DevParams& P, const uint64_t* samples, con
 cudaError_t launch_protect_ct(const DevParams& P, const uint64_t* cts, uint64_t items, const uint64_t* masks,
                               const uint64_t* samples, const uint64_t* pk, uint64_t* u_ntt, uint64_t* x, uint64_t* out,
                               cudaStream_t st) {
+  const LaunchRange range("bfvgpu:protect_ct");
   if (!items) return cudaSuccess;
   if (samples) {
     const cudaError_t e = launch_enc0_x(P, samples, pk, u_ntt, x, items, st);
@@ -1225,12 +1257,14 @@ cudaError_t launch_protect_ct(const DevParams& P, const uint64_t* cts, uint64_t 
 }
 
 cudaError_t launch_packed_targets(uint64_t* targets, uint32_t* counts, uint64_t slots, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:packed_targets");
   if (!slots) return cudaSuccess;
   k_packed_targets<<<(unsigned)((slots * 512 + 255) / 256), 256, 0, st>>>(targets, counts, slots);
   return cudaGetLastError();
 }
 
 cudaError_t launch_add(const DevParams& P, uint64_t* a, const uint64_t* b, uint64_t polys, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:add");
   if (!polys) return cudaSuccess;
   k_add<<<elementwise_blocks(polys << P.logn), 256, 0, st>>>(a, b, polys, P.dk, P.logn, P.mod);
   return cudaGetLastError();
@@ -1371,6 +1405,7 @@ bool mac_tc_applies(const DevParams& P, uint64_t tiles_in_launch, uint64_t input
 
 cudaError_t launch_mac_tiles(const DevParams& P, const uint64_t* in, uint64_t tiles, uint64_t inputs,
                              const uint64_t* w, uint64_t groups, uint64_t* acc, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:mac_tiles");
   if (!tiles || !groups) return cudaSuccess;
   if (P.n < 32 || inputs > 0xffffffffull || groups > 0xffffffffull) return cudaErrorInvalidValue;
   const uint64_t in_tile = inputs * 2 * P.dk * (uint64_t)P.n, acc_tile = groups * 2 * P.dk * (uint64_t)P.n;
@@ -1420,6 +1455,7 @@ uint64_t mac_tiles_launches(uint64_t tiles) {
 
 cudaError_t launch_ntt_split(const DevParams& P, const uint64_t* data, uint64_t* out, uint64_t polys,
                              cudaStream_t st) {
+  const LaunchRange range("bfvgpu:ntt_split");
   if (!polys) return cudaSuccess;
   if (polys > 0x7fffffffull) return cudaErrorInvalidValue;
   BFV_DISPATCH(P.logn, {
@@ -1429,6 +1465,7 @@ cudaError_t launch_ntt_split(const DevParams& P, const uint64_t* data, uint64_t*
 }
 
 cudaError_t launch_pk_prep(const DevParams& P, const uint64_t* pk, ulonglong2* prep, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:pk_prep");
   const uint64_t items = 2ull * P.k * P.n;
   k_pk_prep<<<elementwise_blocks(items), 256, 0, st>>>(pk, prep, items, P.k, P.logn, P.mod);
   return cudaGetLastError();
@@ -1436,6 +1473,7 @@ cudaError_t launch_pk_prep(const DevParams& P, const uint64_t* pk, ulonglong2* p
 
 cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const ulonglong2* pk, uint64_t items,
                              uint64_t* U, uint64_t* xs, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:enc0_prep");
   if (!items) return cudaSuccess;
   if (items * P.k > 0x7fffffffull) return cudaErrorInvalidValue;
   BFV_DISPATCH(P.logn, {
@@ -1453,6 +1491,7 @@ cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const 
 
 cudaError_t launch_enc0_fin(const DevParams& P, const uint64_t* samples, const uint64_t* xs, const uint64_t* mask,
                             uint64_t items, uint64_t* E, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:enc0_fin");
   if (!items || (!samples && !mask)) return cudaSuccess;
   const uint64_t rows = items * 2 * P.dk;
   // about 16 blocks per SM in all; each walks rows (grid-stride along y)
@@ -1466,6 +1505,7 @@ cudaError_t launch_enc0_fin(const DevParams& P, const uint64_t* samples, const u
 
 cudaError_t launch_intt_protect(const DevParams& P, const uint64_t* acc, uint64_t items, const uint64_t* U,
                                 const ulonglong2* pk, const uint64_t* E, uint64_t* out, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:intt_protect");
   if (!items) return cudaSuccess;
   if (items * 2 * P.dk > 0x7fffffffull) return cudaErrorInvalidValue;
   BFV_DISPATCH(P.logn, {

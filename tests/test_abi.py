@@ -69,6 +69,23 @@ def test_host_only_context_refuses_device_work(bfv, gpu_available):
         bfv.Matrix(hc, np.zeros((1, 2, 6, 16384), dtype=np.uint64))
 
 
+@pytest.mark.parametrize("where", ["first", "last", "none"])
+def test_canonical_check_of_a_large_batch(bfv, oracle, where):
+    """A 64-ciphertext ART-002 batch (12.6 M words) is scanned by several host threads: a
+    residue >= its prime in the first or the last polynomial is found; a clean batch passes
+    validation and is refused only for the host-only context."""
+    hc = bfv.Context.art002(device=-1)
+    cts = np.zeros((64, 2, 6, 16384), dtype=np.uint64)
+    if where == "first":
+        cts[0, 0, 0, 7] = oracle.ART002_PRIMES[0]
+    elif where == "last":
+        cts[-1, -1, -1, -1] = oracle.ART002_PRIMES[5]
+    with pytest.raises(bfv.BfvGpuError) as e:
+        bfv.Matrix(hc, cts)
+    assert e.value.name == ("BFVGPU_E_DEVICE" if where == "none" else "BFVGPU_E_CANONICAL")
+    hc.close()
+
+
 def test_device_context_without_gpu_fails_loudly(bfv, gpu_available):
     if gpu_available:
         pytest.skip("a GPU is present")
