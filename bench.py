@@ -676,6 +676,10 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
           for _ in range(layers)]
     pre = L.LayerServer(torch, ctx, pk, sh_pre, 16, tiles)
     dec = L.LayerServer(torch, ctx, pk, sh_dec, 1, 1)
+    # the decode weights of every layer stay resident at fixed addresses (transformed once per
+    # pass, inside the timed region), so the decode calls can replay captured CUDA graphs
+    dec_w = [{p.name: torch.empty((p.groups, p.inputs, dk, n), dtype=torch.int64, device="cuda")
+              for p in sh_dec if p.groups} for _ in range(layers)]
 
     def call_buffers(projs, T, copies):
         return ({p.name: [residues((T, p.inputs, 2, dk, n), dk) for _ in range(copies)] for p in projs},
@@ -731,6 +735,51 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
 
     def transform(si, so, slots):
         ctx.matrix_tiles_inputs_device(si, slots, out=so, stream=sp)
+
+    # decode results travel to rank 0 in one gather per call: each group's c1 and its targets'
+    # CRT limbs side by side in a send block allocated once per projection
+    mx_dec = {p.name: dec.targets[p.name][2] for p in sh_dec}
+    dec_gg = {p.name: S.GroupGather(torch, dist, 1, f.groups, (dk * n + mx_dec[p.name] * dk,), torch.int64, "cuda",
+                                    group=pg_out) for p, f in zip(sh_dec, full_dec)} if multi else {}
+
+    def decode_call(p, layer_w, slot_k, p_next):
+        """One decode call's device work as issued eagerly or captured: the next call's output
+        protection on the side stream (into the other slot) beside this call's input transform,
+        product, protected output transform and target gather, then (N > 1) its results staged
+        into the gather's send block."""
+        dec.w_ntt = layer_w
+        join = None
+        if p_next is not None and p_next.groups and args.protect_ahead:
+            fork = torch.cuda.Event()
+            fork.record(stream)
+            aux.wait_event(fork)
+            dec.prepare_protection(p_next, masks_dec[p_next.name], samples_dec[p_next.name], 1 - slot_k,
+                                   stream=aux.cuda_stream)
+            join = torch.cuda.Event()
+            join.record(aux)
+        dec.run_projection(p, cts_dec[p.name][0], masks_dec[p.name], samples_dec[p.name], stream=sp,
+                           protected=slot_k if args.protect_ahead else None)
+        if multi:
+            rows = dec_gg[p.name].send[:, : p.groups]
+            rows[:, :, : dk * n].copy_(dec.output(p)[:, :, 1].reshape(1, p.groups, dk * n))
+            rows[:, :, dk * n:].copy_(dec.gathered(p)[1].reshape(1, p.groups, mx_dec[p.name] * dk))
+        if join is not None:
+            stream.wait_event(join)
+
+    graphs = {}
+
+    def capture_decode_graphs():
+        """One CUDA graph per (layer, projection) decode call: a call's kernels and the copies
+        into its gather block replay as one launch (the protection slot of projection i is
+        always i % 2: a decode step has an even number of calls)."""
+        for l in range(layers):
+            for i, p in enumerate(sh_dec):
+                if not p.groups:
+                    continue
+                g_ = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g_, stream=stream, capture_error_mode="thread_local"):
+                    decode_call(p, wcache[l] if wcache[l] else dec_w[l], i % 2, sh_dec[(i + 1) % 4])
+                graphs[(l, i)] = g_
 
     def run(ops, marks=None):
         calls = [i for i, op in enumerate(ops) if op[0] == "call"]
@@ -798,7 +847,7 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
             if op[0] == "wdec":
                 rings = {p.name: L.pack_weights_device(torch, w8[op[1]][p.name].long(), p, n) for p in sh_dec
                          if p.groups}
-                dec.w_ntt = {}
+                dec.w_ntt = dec_w[op[1]]
                 if rings:
                     dec.prepare_weights(rings, stream=sp)
                 wcache[op[1]] = dec.w_ntt
@@ -820,6 +869,20 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
                 works.pop(i).wait()        # this call's inputs are in place
                 if op[1] == "pre":
                     transformed = exchange[(p_local.name, pslot[i] % 3)].full
+            if op[1] == "dec" and graphs:
+                # one replay per call; its protection was prepared by the previous call's graph
+                # (the first decode call of the pass prepares its own)
+                if dpos[i] == 0 and args.protect_ahead:
+                    dec.prepare_protection(p_local, masks, samples, op[2] % 2, stream=sp)
+                graphs[(op[3], op[2])].replay()
+                stats["calls"] += 1
+                if multi:
+                    j = stats["calls"] % 2
+                    if pending[j] is not None:
+                        pending[j].wait()
+                    pending[j] = dec_gg[p_local.name].start()
+                    stats["gathered_bytes"] += dec_gg[p_local.name].send[:, : p_local.groups].numel() * 8
+                continue
             if p_local.groups and op[1] == "dec" and args.protect_ahead:
                 if i not in ready:
                     protect(i)
@@ -857,6 +920,11 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
+    if args.decode_graphs and all(p.groups for p in sh_dec):
+        for p in sh_dec:  # a replayed call reads its inputs from one buffer per projection
+            cts_dec[p.name] = cts_dec[p.name][:1]
+        capture_decode_graphs()
+        torch.cuda.synchronize()
     for key in stats:
         stats[key] = 0
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
@@ -869,6 +937,8 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
     if dist and world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total, pre_ms, dw_ms, dec_ms = (float(x) for x in t.tolist())
+    decode_graphs = len(graphs)
+    graphs.clear()
     tokens = tiles_total * 16 + decode_steps
     res = {"ms": total, "unit": "ms per pass (28 layers: 512-token prefill + 64 decode steps)",
            "tokens_per_s": tokens / (total / 1e3), "n_gpus": world, "layers": layers,
@@ -878,6 +948,7 @@ def _model_leg(torch, bfvgpu, args, dist, ctx, sp, stream):
                        "over the 4 tile groups, inputs scattered by rank 0, transformed per slice and all-gathered "
                        "(two calls ahead); decode inputs broadcast when the call starts (each depends on the "
                        "previous call); c1 + target CRT limbs gathered to rank 0 (asynchronous)",
+           "decode_graphs": decode_graphs,
            "calls_per_rank": stats["calls"], "broadcast_bytes_per_rank": stats["broadcast_bytes"],
            "gathered_bytes_per_rank": stats["gathered_bytes"],
            "prefill_mac_modmuls": layers * tiles_total * sum(p.groups * p.inputs * 2 * dk * n for p in full_pre),
@@ -958,6 +1029,8 @@ def main():
     ap.add_argument("--model-decode", type=int, default=64, help="decode steps in the config-5 leg")
     ap.add_argument("--reserved-sms", type=int, default=8,
                     help="config 5 with N > 1: SMs the persistent product kernels leave to NCCL")
+    ap.add_argument("--decode-graphs", type=int, default=1,
+                    help="config-5 decode: replay each call as a captured CUDA graph (0: issue eagerly)")
     ap.add_argument("--protect-ahead", type=int, default=1,
                     help="config-5 decode: prepare each call's Enc(0) and mask term during the previous call")
     ap.add_argument("--slots", type=int, default=1, help="0 skips the slot-packed matvec leg (config 3)")

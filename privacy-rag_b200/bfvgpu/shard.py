@@ -66,6 +66,32 @@ def gather_groups(torch, dist, local, groups: int, world: int, dst: int = 0, asy
     return finish()
 
 
+class GroupGather:
+    """gather_groups with its buffers allocated once, for calls repeated with one shape: the
+    padded send block `send` [tiles][width][...] (width = the widest shard; a rank writes its
+    groups into send[:, :g_local], e.g. from a captured CUDA graph) and, on the protocol rank,
+    one receive block per rank.  start() issues the same collective step as gather_groups;
+    result() assembles [tiles][groups][...] in global group order once it has completed."""
+
+    def __init__(self, torch, dist, tiles: int, groups: int, tail: tuple, dtype, device, dst: int = 0,
+                 group=None):
+        self.torch, self.dist, self.dst, self.group = torch, dist, dst, group
+        world = dist.get_world_size(group)
+        self.per = [group_range(groups, r, world) for r in range(world)]
+        width = max(hi - lo for lo, hi in self.per)
+        self.send = torch.zeros((tiles, width) + tuple(tail), dtype=dtype, device=device)
+        self.rank = dist.get_rank()
+        self.recv = [torch.empty_like(self.send) for _ in range(world)] if self.rank == dst else None
+
+    def start(self, async_op: bool = True):
+        return self.dist.gather(self.send, gather_list=self.recv, dst=self.dst, async_op=async_op, group=self.group)
+
+    def result(self):
+        if self.rank != self.dst:
+            return None
+        return self.torch.cat([self.recv[r][:, : hi - lo] for r, (lo, hi) in enumerate(self.per)], dim=1)
+
+
 class InputExchange:
     """One call's client ciphertexts from the protocol rank to every rank in the product's
     operand form, with the transform itself sharded: the protocol rank scatters equal slices
