@@ -169,17 +169,19 @@ def cpu_keyswitch_sample(seconds: float = 12.0):
     return done / dt, ks.cores, ks.sample_text(done, dt)
 
 
+# the files that define the transform-bearing kernels (bodies, arithmetic, launches)
+KERNEL_SOURCES = ("arith.cuh", "ntt_core.cuh", "block_ops.cuh", "kernels.cuh", "kernels.cu")
+
+
 def kernel_sources_sha16() -> str:
-    """Hash of the CUDA sources (every file of privacy-rag_b200/csrc, sorted by name): an ncu
-    figure recorded with a different hash was taken on other kernels."""
+    """Hash of the kernel sources: an ncu figure recorded with a different hash was taken on
+    other kernels."""
     import hashlib
     h = hashlib.sha256()
-    csrc = os.path.join(PKG, "csrc")
-    for f in sorted(os.listdir(csrc)):
-        if f.endswith((".cu", ".cuh", ".h")):
-            h.update(f.encode())
-            with open(os.path.join(csrc, f), "rb") as fh:
-                h.update(fh.read())
+    for f in KERNEL_SOURCES:
+        h.update(f.encode())
+        with open(os.path.join(PKG, "csrc", f), "rb") as fh:
+            h.update(fh.read())
     return h.hexdigest()[:16]
 
 
@@ -1029,6 +1031,8 @@ def main():
     ap.add_argument("--model-decode", type=int, default=64, help="decode steps in the config-5 leg")
     ap.add_argument("--reserved-sms", type=int, default=8,
                     help="config 5 with N > 1: SMs the persistent product kernels leave to NCCL")
+    ap.add_argument("--ks-pipe", type=int, default=1,
+                    help="headline: software-pipelined rotations (1) or one rotate + finish launch pair per element (0)")
     ap.add_argument("--decode-graphs", type=int, default=1,
                     help="config-5 decode: replay each call as a captured CUDA graph (0: issue eagerly)")
     ap.add_argument("--protect-ahead", type=int, default=1,
@@ -1116,11 +1120,21 @@ def main():
     torch.cuda.synchronize()
     sp = ctx.stream()
 
+    pipe_scratch = torch.empty(ctx.keyswitch_rotate_many_scratch_words(CTS), dtype=torch.int64, device="cuda")
+
     def step_hoisted(ev_pairs=None):
         """One step: prepare this rank's keys (inside the step), hoist the 256 ciphertexts,
-        then rotate every ciphertext by every element of this rank's range."""
+        then rotate every ciphertext by every element of this rank's range: software-pipelined
+        (own + 1 launches; ev_pairs[0] brackets them all) or one launch pair per element."""
         ctx.keyswitch_prepare_device(keys, elts, prepared, stream=sp)
         ctx.keyswitch_hoist_device(cts, CTS, hoisted, stream=sp)
+        if args.ks_pipe:
+            if ev_pairs is not None:
+                ev_pairs[0][0].record(stream)
+            ctx.keyswitch_rotate_many_device(cts, CTS, hoisted, prepared, elts, pipe_scratch, out, stream=sp)
+            if ev_pairs is not None:
+                ev_pairs[0][1].record(stream)
+            return
         for r in range(own):
             if ev_pairs is not None:
                 ev_pairs[r][0].record(stream)
@@ -1139,11 +1153,12 @@ def main():
             if ev_pairs is not None:
                 ev_pairs[r][1].record(stream)
 
-    def timed(step_fn, steps, warmup, clocks=False):
+    def timed(step_fn, steps, warmup, clocks=False, brackets=None):
         for _ in range(warmup):
             step_fn()
         torch.cuda.synchronize()
-        ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(own)]
+        ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+              for _ in range(own if brackets is None else brackets)]
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
@@ -1167,7 +1182,10 @@ def main():
         per = [x.elapsed_time(y) / 1e3 for x, y in ev]
         return dt, per, bfvgpu.launch_count() - l0, clk
 
-    elapsed, per_launch, launches, clk = timed(step_hoisted, args.steps, args.warmup, clocks=True)
+    elapsed, per_launch, launches, clk = timed(step_hoisted, args.steps, args.warmup, clocks=True,
+                                               brackets=1 if args.ks_pipe else None)
+    if args.ks_pipe:  # one bracket around the pipelined launches: the per-element average
+        per_launch = [per_launch[0] / own]
     hoisted_out = out[:2].clone()
     total_ks = CTS * rotations * args.steps  # the whole job, all ranks together
     value = total_ks / elapsed
@@ -1351,7 +1369,8 @@ def main():
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": ks_traffic, "peak_source": peak_kind,
                      "traffic_source": ks_traffic_note,
-                     "kernel": "per-rotation launches k_ks_rotate + k_ks_finish (256 cts)",
+                     "kernel": ("k_ks_rotate_pipe, per element (one of own + 1 pipelined launches over 256 cts)"
+                                if args.ks_pipe else "per-rotation launches k_ks_rotate + k_ks_finish (256 cts)"),
                      "alg_bytes_per_launch": alg_bytes_launch, "avg_launch_ms": avg_launch * 1e3,
                      "int_frac": ks_int["frac"], "int": ks_int, "int_peaks_per_s": int_rates,
                      "int_peak_source": "measured in this run: bfvgpu_int_peak_device (register-resident "

@@ -142,6 +142,20 @@ int32_t bfvgpu_keyswitch_rotate_device(bfvgpu_ctx *ctx, const uint64_t *cts, uin
                                        const uint64_t *hoisted, const uint64_t *prepared,
                                        uint32_t galois_elt, uint64_t *scratch, uint64_t *out,
                                        void *stream);
+/* Step 3 for many elements at once, software-pipelined: the same outputs as one
+ * bfvgpu_keyswitch_rotate_device call per element (element e's result into outs[e], a host
+ * array of `elements` device pointers [count][2][dk][n]; entries may repeat, later elements
+ * overwriting earlier ones), in elements + 1 launches instead of 2 * elements: launch r runs
+ * the special-prime product and transform of element r beside the data-prime blocks of
+ * element r - 1, which complete the keyswitch (divide-and-round by the special prime, c0,
+ * Galois permutation) in shared memory.  galois_elts (host) [elements] the elements the keys
+ * in prepared [elements][bfvgpu_keyswitch_prepared_words] were prepared for; scratch of
+ * bfvgpu_keyswitch_rotate_many_scratch_words(ctx, count) words. */
+uint64_t bfvgpu_keyswitch_rotate_many_scratch_words(const bfvgpu_ctx *ctx, uint64_t count);
+int32_t bfvgpu_keyswitch_rotate_many_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,
+                                            const uint64_t *hoisted, const uint64_t *prepared,
+                                            const uint32_t *galois_elts, uint64_t elements, uint64_t *scratch,
+                                            uint64_t *const *outs, void *stream);
 /* The same keyswitch as bfvgpu_keyswitch_device, for callers that cannot allocate
  * device memory when they need it (a worker whose device footprint is fixed and
  * audited at session start, or code that must not take cudaMalloc's implicit device

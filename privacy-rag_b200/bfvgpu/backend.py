@@ -152,6 +152,22 @@ class Context:
                                                self._dptr(samples), self._dptr(pk), self._dptr(scratch),
                                                self._dptr(out), self._dptr(c0_crt), stream), "token_finish_device")
 
+    def keyswitch_rotate_many_scratch_words(self, count: int) -> int:
+        return int(lib().bfvgpu_keyswitch_rotate_many_scratch_words(self._h, count))
+
+    def keyswitch_rotate_many_device(self, cts, count: int, hoisted, prepared, galois_elts, scratch, outs,
+                                     stream: int | None = None) -> None:
+        """The hoisted rotations of every element in galois_elts, software-pipelined; outs: one
+        device tensor (or pointer) per element, or a single one that every element overwrites."""
+        m = len(galois_elts)
+        if not isinstance(outs, (list, tuple)):
+            outs = [outs] * m
+        el = (U32 * m)(*[int(e) for e in galois_elts])
+        op = (VP * m)(*[self._dptr(o) for o in outs])
+        check(lib().bfvgpu_keyswitch_rotate_many_device(self._h, self._dptr(cts), count, self._dptr(hoisted),
+                                                        self._dptr(prepared), el, m, self._dptr(scratch), op, stream),
+              "keyswitch_rotate_many_device")
+
     def keyswitch_prepared_words(self) -> int:
         return int(lib().bfvgpu_keyswitch_prepared_words(self._h))
 

@@ -534,7 +534,7 @@ struct bfvgpu_rotations {
   std::vector<uint32_t> elts;
   uint64_t pw = 0, cap = 0;
   uint64_t* prepared = nullptr;  // [rotations][pw]
-  uint64_t *cts = nullptr, *hoisted = nullptr, *x = nullptr, *out[2] = {nullptr, nullptr};
+  uint64_t *cts = nullptr, *hoisted = nullptr, *x = nullptr, *xs = nullptr, *out[2] = {nullptr, nullptr};
   cudaStream_t copy = nullptr;
   cudaEvent_t computed[2] = {nullptr, nullptr}, copied[2] = {nullptr, nullptr};
 };
@@ -750,6 +750,34 @@ int32_t bfvgpu_keyswitch_rotate_device(bfvgpu_ctx* ctx, const uint64_t* cts, uin
                                 pick(ctx, stream)),
                "rotate");
     count_launch(2);
+  });
+}
+
+uint64_t bfvgpu_keyswitch_rotate_many_scratch_words(const bfvgpu_ctx* ctx, uint64_t count) {
+  return ctx ? count * 2ull * ctx->c.k * ctx->c.n + 2 * count * 2ull * ctx->c.n : 0;
+}
+
+int32_t bfvgpu_keyswitch_rotate_many_device(bfvgpu_ctx* ctx, const uint64_t* cts, uint64_t count,
+                                            const uint64_t* hoisted, const uint64_t* prepared,
+                                            const uint32_t* galois_elts, uint64_t elements, uint64_t* scratch,
+                                            uint64_t* const* outs, void* stream) {
+  return guard([&] {
+    if (!ctx || !cts || !hoisted || !prepared || !galois_elts || !scratch || !outs || !count)
+      fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    if (ctx->c.k != ctx->c.dk + 1) fail(BFVGPU_E_CONTEXT, "E_BFVGPU_NO_SPECIAL_PRIME");
+    for (uint64_t e = 0; e < elements; ++e) {
+      if (!(galois_elts[e] & 1) || galois_elts[e] >= 2 * ctx->c.n) fail(BFVGPU_E_ELEMENT, "E_BFVGPU_GALOIS_ELEMENT");
+      if (!outs[e]) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    }
+    require_device(ctx->c);
+    DeviceScope scope(ctx->c.device);
+    const Context& c = ctx->c;
+    const uint32_t* zflag = (const uint32_t*)(hoisted + count * c.dk * c.k * c.n);
+    uint64_t* xs = scratch + count * 2ull * c.k * c.n;
+    cuda_check(launch_ks_rotate_pipe(c.P, cts, count, hoisted, zflag, prepared, galois_elts, elements, scratch, xs,
+                                     outs, pick(ctx, stream)),
+               "rotate many");
+    count_launch(elements ? elements + 1 : 0);
   });
 }
 
@@ -1476,6 +1504,7 @@ int32_t bfvgpu_rotations_apply(bfvgpu_rotations* s, const uint64_t* cts, uint64_
         s->cts = s->h.grow(s->cts, count * ctw);
         s->hoisted = s->h.grow(s->hoisted, count * c.dk * c.k * c.n + (count + 1) / 2);
         s->x = s->h.grow(s->x, count * 2 * c.k * c.n);
+        s->xs = s->h.grow(s->xs, 2 * count * 2 * c.n);
         s->out[0] = s->h.grow(s->out[0], count * ctw);
         s->out[1] = s->h.grow(s->out[1], count * ctw);
         s->cap = count;
@@ -1484,16 +1513,22 @@ int32_t bfvgpu_rotations_apply(bfvgpu_rotations* s, const uint64_t* cts, uint64_
       const uint32_t* zflag = (const uint32_t*)(s->hoisted + count * c.dk * c.k * c.n);
       cuda_check(launch_ks_hoist(c.P, s->cts, count, s->hoisted, (uint32_t*)zflag, c.stream), "hoist");
       count_launch();
-      for (uint64_t r = 0; r < s->elts.size(); ++r) {
-        const int b = (int)(r & 1);
-        if (r >= 2) cuda_check(cudaStreamWaitEvent(c.stream, s->copied[b], 0), "wait");
-        cuda_check(launch_ks_rotate(c.P, s->cts, count, s->hoisted, zflag, s->prepared + r * s->pw, s->elts[r], s->x,
-                                    s->out[b], c.stream),
+      // pipelined rotations: launch r completes element r - 1 into out[(r - 1) & 1], whose
+      // previous contents (element r - 3) must have been copied out first; each element's
+      // copy-back overlaps the following launches on the copy stream
+      const uint64_t m = s->elts.size();
+      for (uint64_t r = 0; r <= m; ++r) {
+        const int b = (int)((r + 1) & 1);
+        if (r >= 3) cuda_check(cudaStreamWaitEvent(c.stream, s->copied[b], 0), "wait");
+        cuda_check(launch_ks_rotate_pipe_step(c.P, s->cts, count, s->hoisted, zflag, s->prepared, s->elts.data(), m, r,
+                                              s->x, s->xs, s->out[b], c.stream),
                    "rotate");
-        count_launch(2);
+        count_launch();
+        if (r == 0) continue;
         cuda_check(cudaEventRecord(s->computed[b], c.stream), "event");
         cuda_check(cudaStreamWaitEvent(s->copy, s->computed[b], 0), "wait");
-        cuda_check(cudaMemcpyAsync(out + r * count * ctw, s->out[b], count * ctw * 8, cudaMemcpyDeviceToHost, s->copy),
+        cuda_check(cudaMemcpyAsync(out + (r - 1) * count * ctw, s->out[b], count * ctw * 8, cudaMemcpyDeviceToHost,
+                                   s->copy),
                    "D2H");
         cuda_check(cudaEventRecord(s->copied[b], s->copy), "event");
       }

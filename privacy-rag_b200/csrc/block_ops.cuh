@@ -377,6 +377,56 @@ BFV_HD void op_ks_finish(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t
   }
 }
 
+// Hoisted rotations of a list of elements, software-pipelined across elements.  Launch r
+// holds two kinds of blocks, independent of each other:
+//  * blk < s_blocks = count * 2 (element r; absent in the last launch): block (ct, c) of the
+//    special prime -- the key product and inverse NTT of op_ks_rotate_into -- stored
+//    compactly into xs_w [count][2][n];
+//  * the rest (element r - 1; absent in the first launch): block (ct, c, data prime p), the
+//    same key product and inverse NTT, whose last pass leaves in the block's own shared
+//    memory the finished word moddown(x_p, x_s) (+ c0 for c = 0), with x_s read from xs_r
+//    (written by the previous launch); the block then stores its limb of out_d through the
+//    Galois permutation (out[i] = +-limb[i * g^-1 mod 2n]).
+// The outputs equal op_ks_rotate + op_ks_finish for each element; the data-prime limbs never
+// leave shared memory between the product and the finished ciphertext.  x is the zero-word
+// path's scratch [count][2][k][n] (special and data blocks use disjoint parts of it).
+template <int LOGN, class Ex>
+BFV_HD void op_ks_rotate_pipe(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t s_blocks, const uint64_t* cts,
+                              const uint64_t* Y, const uint32_t* zflag, uint64_t* x, const uint64_t* prep_s,
+                              uint32_t elt_s, uint64_t* xs_w, const uint64_t* prep_d, uint32_t elt_d, uint32_t ginv_d,
+                              const uint64_t* xs_r, uint64_t* out_d, uint32_t k, uint32_t dk, const Modulus* mods,
+                              const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv) {
+  constexpr int N = 1 << LOGN;
+  if (blk < s_blocks) {
+    const uint64_t ct = blk >> 1;
+    const uint32_t c = (uint32_t)(blk & 1);
+    uint64_t* xo = xs_w + (ct * 2 + c) * (uint64_t)N;
+    auto st = [xo](int i, uint64_t v) { xo[i] = v; };
+    op_ks_rotate_into<LOGN>(ex, s, ct, c, k - 1, cts, Y, zflag, prep_s, x, elt_s, k, dk, mods, qjp, fwd, inv, st);
+    return;
+  }
+  const uint64_t d = blk - s_blocks;
+  const uint64_t ct = d / (2ull * dk);
+  const uint32_t c = (uint32_t)((d / dk) & 1), p = (uint32_t)(d % dk);
+  const Modulus m = mods[p], ms = mods[k - 1];
+  const uint64_t* xs = xs_r + (ct * 2 + c) * (uint64_t)N;
+  const uint64_t* c0 = cts + (ct * 2 * dk + p) * (uint64_t)N;
+  auto st = [=](int i, uint64_t v) {
+    uint64_t w = moddown_elem(v, ldro(xs + i), m, ms);
+    if (c == 0) w = add_mod(w, ldro(c0 + i), m.q);
+    s[spad(i)] = w;  // the last pass writes only the words it read: in place
+  };
+  op_ks_rotate_into<LOGN>(ex, s, ct, c, p, cts, Y, zflag, prep_d, x, elt_d, k, dk, mods, qjp, fwd, inv, st);
+  uint64_t* o = out_d + ((ct * 2 + c) * dk + p) * (uint64_t)N;
+  const uint32_t mask2n = 2u * N - 1u;
+  const uint64_t q = m.q;
+  ex.run(N, [&](int i) {
+    const uint32_t src = ((uint32_t)i * ginv_d) & mask2n;
+    o[i] = src < (uint32_t)N ? s[spad((int)src)] : neg_mod(s[spad((int)src - N)], q);
+  });
+  ex.sync();
+}
+
 // ---- Enc(0) pre-moddown polys: block = (group, key-level prime p) ------------------------
 template <int LOGN, class Ex>
 BFV_HD void op_enc0_x(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* samples, const uint64_t* pk,

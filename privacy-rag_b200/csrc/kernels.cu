@@ -696,6 +696,19 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
   op_ks_finish<LOGN>(BlockExec{}, smem, blockIdx.x, x, cts, out, ginv, k, dk, mods);
 }
 
+// One launch of the pipelined rotations: the special-prime blocks of one element beside the
+// data-prime blocks (which finish the keyswitch in shared memory) of the previous one.
+template <int LOGN>
+__global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
+    k_ks_rotate_pipe(const uint64_t* cts, uint64_t s_blocks, const uint64_t* Y, const uint32_t* zflag, uint64_t* x,
+                     const uint64_t* prep_s, uint32_t elt_s, uint64_t* xs_w, const uint64_t* prep_d, uint32_t elt_d,
+                     uint32_t ginv_d, const uint64_t* xs_r, uint64_t* out_d, uint32_t k, uint32_t dk,
+                     const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_ks_rotate_pipe<LOGN>(BlockExec{}, smem, blockIdx.x, s_blocks, cts, Y, zflag, x, prep_s, elt_s, xs_w, prep_d,
+                          elt_d, ginv_d, xs_r, out_d, k, dk, mods, qjp, fwd, inv);
+}
+
 // Hoisted rotations of many (element, ciphertext) pairs in one launch pair.  paired != 0:
 // ciphertext i with element i (blocks (i, c, p); x [count][2][k][n], out [count][2][dk][n]);
 // else every element e with every ciphertext (x [m][count][2][k][n], out [m][count][2][dk][n]).
@@ -919,6 +932,7 @@ static cudaError_t configure_for() {
   chk(allow_smem(k_ks_rotate<L>, s));
   chk(allow_smem(k_ks_finish<L>, (size_t(1) << L) * 8));
   chk(allow_smem(k_ks_rotate_multi<L>, s));
+  chk(allow_smem(k_ks_rotate_pipe<L>, s));
   chk(allow_smem(k_ks_finish_multi<L>, (size_t(1) << L) * 8));
   chk(allow_smem(k_client_phase<L>, s));
   chk(allow_smem(k_enc0_prep<L>, s));
@@ -1085,6 +1099,43 @@ cudaError_t launch_ks_rotate(const DevParams& P, const uint64_t* cts, uint64_t c
                                                                                                P.k, P.dk, P.mod);
   });
   return cudaGetLastError();
+}
+
+cudaError_t launch_ks_rotate_pipe_step(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
+                                       const uint32_t* zflag, const uint64_t* prepared, const uint32_t* elts,
+                                       uint64_t elements, uint64_t r, uint64_t* x, uint64_t* xs, uint64_t* out_d,
+                                       cudaStream_t st) {
+  if (!count || r > elements) return cudaSuccess;
+  if (P.k != P.dk + 1) return cudaErrorInvalidValue;
+  const uint64_t pw = (2ull * P.dk + 2) * P.k * P.n, xsw = count * 2ull * P.n;
+  const bool special = r < elements, data = r >= 1;
+  const uint64_t s_blocks = special ? count * 2 : 0, blocks = s_blocks + (data ? count * 2 * P.dk : 0);
+  if (!blocks) return cudaSuccess;
+  const uint64_t* prep_s = special ? prepared + r * pw : nullptr;
+  const uint32_t elt_s = special ? elts[r] : 1;
+  uint64_t* xs_w = xs + (r & 1) * xsw;
+  const uint64_t* prep_d = data ? prepared + (r - 1) * pw : nullptr;
+  const uint32_t elt_d = data ? elts[r - 1] : 1, ginv_d = inverse_mod_2n(elt_d, 2u * P.n);
+  const uint64_t* xs_r = xs + ((r + 1) & 1) * xsw;  // written by launch r - 1
+  BFV_DISPATCH(P.logn, {
+    k_ks_rotate_pipe<L_><<<(unsigned)blocks, threads_for<L_>(), smem_bytes<L_>(), st>>>(
+        cts, s_blocks, Y, zflag, x, prep_s, elt_s, xs_w, prep_d, elt_d, ginv_d, xs_r, data ? out_d : nullptr, P.k,
+        P.dk, P.mod, P.qjp, P.fwd, P.inv);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ks_rotate_pipe(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
+                                  const uint32_t* zflag, const uint64_t* prepared, const uint32_t* elts,
+                                  uint64_t elements, uint64_t* x, uint64_t* xs, uint64_t* const* outs, cudaStream_t st) {
+  const LaunchRange range("bfvgpu:ks_rotate_pipe");
+  if (!count || !elements) return cudaSuccess;
+  for (uint64_t r = 0; r <= elements; ++r) {
+    const cudaError_t e =
+        launch_ks_rotate_pipe_step(P, cts, count, Y, zflag, prepared, elts, elements, r, x, xs, r ? outs[r - 1] : nullptr, st);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t launch_ks_rotate_multi(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,

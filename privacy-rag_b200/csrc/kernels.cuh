@@ -91,6 +91,21 @@ cudaError_t launch_ks_rotate(const DevParams& P, const uint64_t* cts, uint64_t c
 cudaError_t launch_ks_rotate_multi(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
                                    const uint32_t* zflag, const uint64_t* prepared, const uint32_t* elts,
                                    uint64_t elements, int paired, uint64_t* x, uint64_t* out, cudaStream_t st);
+// The hoisted rotations of `elements` elements (elts host array, prepared [elements][..]),
+// software-pipelined: elements + 1 launches, launch r holding the special-prime blocks of
+// element r and the data-prime blocks of element r - 1, which finish the keyswitch in shared
+// memory and store element r - 1's result into outs[r - 1] (host array of device pointers
+// [count][2][dk][n]; entries may repeat).  x: scratch [count][2][k][n]; xs: scratch
+// [2][count][2][n].  launch_ks_rotate_pipe_step issues launch r (0 <= r <= elements) alone,
+// element r - 1's result going to out_d: a caller that reads each result back as soon as it
+// is complete records an event after launch r.
+cudaError_t launch_ks_rotate_pipe(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
+                                  const uint32_t* zflag, const uint64_t* prepared, const uint32_t* elts,
+                                  uint64_t elements, uint64_t* x, uint64_t* xs, uint64_t* const* outs, cudaStream_t st);
+cudaError_t launch_ks_rotate_pipe_step(const DevParams& P, const uint64_t* cts, uint64_t count, const uint64_t* Y,
+                                       const uint32_t* zflag, const uint64_t* prepared, const uint32_t* elts,
+                                       uint64_t elements, uint64_t r, uint64_t* x, uint64_t* xs, uint64_t* out_d,
+                                       cudaStream_t st);
 // acc [2][dk][n] = sum of the groups ciphertexts in [groups][2][dk][n].
 cudaError_t launch_sum_cts(const DevParams& P, const uint64_t* in, uint64_t groups, uint64_t* acc, cudaStream_t st);
 

@@ -256,6 +256,49 @@ int emu_keyswitch_hoisted(int logn, uint32_t k, uint32_t dk, const uint64_t* mod
   return 0;
 }
 
+// Hoisted rotations of E elements, pipelined as launch_ks_rotate_pipe issues them: keys
+// [E][dk][2][k][n], elts [E] -> outs [E][count][2][dk][n].  Launch r runs the special-prime
+// blocks of element r and the data-prime blocks of element r - 1 over the same buffers the
+// device uses (xs parity buffers, one zero-word scratch).
+int emu_keyswitch_pipe(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd,
+                       const uint64_t* inv, const uint64_t* cts, uint64_t count, const uint64_t* keys,
+                       const uint32_t* elts, uint64_t elements, uint64_t* outs) {
+  Tabs T = tabs(k, mods16, fwd, inv);
+  const uint64_t n = 1ull << logn;
+  std::vector<uint64_t> qjp((size_t)dk * k);
+  for (uint32_t j = 0; j < dk; ++j)
+    for (uint32_t p = 0; p < k; ++p) qjp[j * k + p] = T.mods[j].q % T.mods[p].q;
+  const uint64_t pw = (2ull * dk + 2) * k * n, kw = (uint64_t)dk * 2 * k * n, ctw = 2ull * dk * n;
+  std::vector<uint64_t> Y(count * dk * k * n), prepared(elements * pw), x(count * 2 * k * n), xs(2 * count * 2 * n);
+  std::vector<uint32_t> zflag(count, 0);
+  EMU_DISPATCH(logn, {
+    std::vector<uint64_t> s(SmemWords<L_>::value);
+    for (uint64_t b = 0; b < count * dk * k; ++b)
+      op_ks_hoist<L_>(HostExec{}, s.data(), b, cts, Y.data(), zflag.data(), k, dk, T.mods.data(), T.fwd);
+    for (uint64_t e = 0; e < elements; ++e) {
+      uint64_t* pr = prepared.data() + e * pw;
+      const uint32_t ginv = inv_mod_2n(elts[e], 2 * (uint32_t)n);
+      for (uint64_t b = 0; b < k; ++b)
+        op_ks_negntt<L_>(HostExec{}, s.data(), b, pr, pw, &elts[e], k, dk, T.mods.data(), T.fwd);
+      for (uint64_t item = 0; item < k * n; ++item)
+        ks_keyperm_item(item, keys + e * kw, pr, pw, &ginv, L_, k, dk, T.mods.data(), qjp.data());
+    }
+    for (uint64_t r = 0; r <= elements; ++r) {
+      const bool special = r < elements, data = r >= 1;
+      const uint64_t s_blocks = special ? count * 2 : 0, blocks = s_blocks + (data ? count * 2 * dk : 0);
+      const uint32_t elt_d = data ? elts[r - 1] : 1;
+      for (uint64_t b = 0; b < blocks; ++b)
+        op_ks_rotate_pipe<L_>(HostExec{}, s.data(), b, s_blocks, cts, Y.data(), zflag.data(), x.data(),
+                              special ? prepared.data() + r * pw : nullptr, special ? elts[r] : 1,
+                              xs.data() + (r & 1) * count * 2 * n, data ? prepared.data() + (r - 1) * pw : nullptr,
+                              elt_d, inv_mod_2n(elt_d, 2 * (uint32_t)n), xs.data() + ((r + 1) & 1) * count * 2 * n,
+                              data ? outs + (r - 1) * count * ctw : nullptr, k, dk, T.mods.data(), qjp.data(), T.fwd,
+                              T.inv);
+    }
+  });
+  return 0;
+}
+
 // Full protected matrix evaluation for `groups` groups:
 // cts [inputs][2][dk][n] coefficient form; ring [groups][inputs][n]; mask [groups][n]
 // or null; samples [groups][3][k][n] or null (pk [2][k][n]); out [groups][2][dk][n].

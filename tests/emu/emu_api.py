@@ -8,6 +8,7 @@ SIGNATURES = {
     "emu_ntt": [INT, U32, P, P, P, P, U64, U32, U32, INT],
     "emu_keyswitch": [INT, U32, U32, P, P, P, P, U64, P, U32, P],
     "emu_keyswitch_hoisted": [INT, U32, U32, P, P, P, P, U64, P, U32, P, ctypes.POINTER(ctypes.c_uint32)],
+    "emu_keyswitch_pipe": [INT, U32, U32, P, P, P, P, U64, P, ctypes.POINTER(ctypes.c_uint32), U64, P],
     "emu_matrix": [INT, U32, U32, P, P, P, P, U64, P, U64, P, P, P, U64, U64, U64, INT, P],
     "emu_matrix_tiles": [INT, U32, U32, P, P, P, P, U64, U64, P, U64, P, P, P, U64, U64, U64, INT, P, INT],
     "emu_client_phase": [INT, U32, U32, P, P, P, P, P, U64],

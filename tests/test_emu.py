@@ -117,6 +117,28 @@ def test_hoisted_keyswitch_kernel_bodies(bfv, oracle, E, logn, elts):
             assert np.array_equal(out[c], oc.keyswitch(cts[c], key, elt)), (logn, elt, c)
 
 
+@pytest.mark.parametrize("logn,elts", [(5, [3, 63, 1, 9]), (6, [5, 127, 9]), (13, [3, 2 ** 13 + 1, 16383])])
+def test_pipelined_rotation_kernel_bodies(bfv, oracle, E, logn, elts):
+    """The software-pipelined rotations (launch r: special-prime blocks of element r beside
+    the data-prime blocks of element r - 1, which finish the keyswitch in shared memory) run
+    on the host with the device's buffers and indexing, against the reference keyswitch for
+    every element, including a ciphertext whose c1 holds zero words (the exact path)."""
+    import ctypes
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+    k, dk, n = hc.k, hc.dk, 1 << logn
+    count = 3
+    cts = oc.uniform(500 + logn, count * 2 * dk, prime_count=dk).reshape(count, 2, dk, n)
+    cts[2, 1, 1, ::4] = 0
+    keys = np.stack([oc.uniform(600 + logn + e, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n)
+                     for e in range(len(elts))])
+    outs = np.zeros((len(elts), count, 2, dk, n), dtype=np.uint64)
+    el = (ctypes.c_uint32 * len(elts))(*elts)
+    E.emu_keyswitch_pipe(logn, k, dk, p(mods), p(fwd), p(inv), p(cts), count, p(keys), el, len(elts), p(outs))
+    for e, elt in enumerate(elts):
+        for c in range(count):
+            assert np.array_equal(outs[e, c], oc.keyswitch(cts[c], keys[e], elt)), (logn, elt, c)
+
+
 @pytest.mark.parametrize("logn", [6, 14])
 def test_matrix_mask_enc0_kernel_bodies(bfv, oracle, E, logn):
     hc, oc, mods, fwd, inv = make(bfv, oracle, logn)

@@ -231,6 +231,47 @@ def test_keyswitch_hoisted_device(which, request, oracle):
         assert np.array_equal(got, exp), elt
 
 
+@pytest.mark.parametrize("which", ["cfg2", "art"])
+def test_keyswitch_rotate_many_pipelined(which, request, oracle):
+    """The software-pipelined rotations (bfvgpu_keyswitch_rotate_many_device: elements + 1
+    launches, each data-prime block finishing its keyswitch in shared memory) equal one
+    bfvgpu_keyswitch_rotate_device call per element, word for word, and the oracle; with one
+    output per element and with a single output buffer every element overwrites."""
+    import torch
+    hc, oc = request.getfixturevalue(which)
+    n, k, dk = oc.n, oc.k, oc.data_k
+    count = 6 if which == "cfg2" else 2
+    cts = oc.uniform(71, count * 2 * dk).reshape(count, 2, dk, n)
+    cts[2 % count, 1, 1, ::7] = 0  # zero c1 words: the exact path
+    elts = ([3, pow(3, 5, 2 * n), 2 * n - 1, 9, pow(3, 77, 2 * n)] if which == "cfg2"
+            else [1, 2 ** 9 + 1, 2 ** 3 + 1])
+    m = len(elts)
+    keys = np.stack([oc.uniform(80 + i, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n) for i in range(m)])
+    d_cts = torch.from_numpy(cts.view(np.int64)).cuda()
+    d_keys = torch.from_numpy(keys.view(np.int64)).cuda()
+    hoisted = torch.empty(hc.keyswitch_hoist_words(count), dtype=torch.int64, device="cuda")
+    pw = hc.keyswitch_prepared_words()
+    prepared = torch.empty(m * pw, dtype=torch.int64, device="cuda")
+    scratch = torch.empty(hc.keyswitch_rotate_many_scratch_words(count), dtype=torch.int64, device="cuda")
+    outs = [torch.full_like(d_cts, -1) for _ in range(m)]
+    shared = torch.full_like(d_cts, -1)
+    one = torch.empty_like(d_cts)
+    torch.cuda.synchronize()
+    hc.keyswitch_hoist_device(d_cts, count, hoisted)
+    hc.keyswitch_prepare_device(d_keys, elts, prepared)
+    hc.keyswitch_rotate_many_device(d_cts, count, hoisted, prepared, elts, scratch, outs)
+    hc.keyswitch_rotate_many_device(d_cts, count, hoisted, prepared, elts, scratch, shared)
+    torch.cuda.synchronize()
+    assert hc.check() == 0
+    for i, elt in enumerate(elts):
+        hc.keyswitch_rotate_device(d_cts, count, hoisted, prepared[i * pw:(i + 1) * pw], elt, scratch, one)
+        torch.cuda.synchronize()
+        assert torch.equal(outs[i], one), elt
+        got = outs[i].cpu().numpy().view(np.uint64)
+        assert np.array_equal(got, oc.keyswitch_many(cts, keys[i], [elt], threads=8)[0]), elt
+    assert torch.equal(shared, outs[-1])
+
+
 def test_rotations_object(cfg2, oracle):
     """bfvgpu.Rotations (one upload, hoisted digits, every element streamed back) equals
     Switch.apply_many per element and the oracle; a ciphertext with zero c1 words included."""
