@@ -47,7 +47,7 @@ ROTATIONS = 128
 ALG_BYTES_PER_KS = 2 * 4 * N2 * 8 * 2 + (4 * 2 * 5 * N2 * 8) // CTS  # ct in + ct out + key/256
 # The DRAM traffic of one rotation's launch pair comes from an ncu capture whose summary
 # records it with a hash of the kernel sources it was taken on (traffic_record below).
-KS_PROFILE = os.path.join(ROOT, "profiles", "keyswitch_config2_hoisted_rotate.md")
+KS_PROFILE = os.path.join(ROOT, "profiles", "keyswitch_config2_pipelined_rotations.md")
 N1 = 4096
 BITS1 = [36, 36, 37]
 NTT_POLYS = 384  # 64 cts x 2 polys x 3 limbs
@@ -1204,6 +1204,8 @@ def main():
     alg_bytes_launch = ALG_BYTES_PER_KS * CTS
     achieved = alg_bytes_launch / avg_launch / 1e9
     ks_traffic, ks_traffic_note = traffic_record(KS_PROFILE)
+    if not args.ks_pipe:
+        ks_traffic, ks_traffic_note = None, "recorded for the pipelined kernel only"
     # ---- integer roofline: this GPU's measured rates of the kernels' integer operations ----
     int_rates = measure_int_peaks(torch, ctx)
     ks_int = int_roofline(ks_pair_counts(CTS, N2, 5, 4), int_rates, avg_launch)
