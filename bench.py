@@ -355,6 +355,7 @@ def run_layer_legs(torch, bfvgpu, device, args):
     step transforms the layer's weights once and runs every tile."""
     from bfvgpu import layer as L
     ctx = bfvgpu.Context.art002(device)
+    ctx.set_limb_split(bool(args.limb_split))
     n, k, dk = ctx.n, ctx.k, ctx.dk
     sp = ctx.stream()
     stream = torch.cuda.ExternalStream(sp)
@@ -546,6 +547,7 @@ def run_token_leg(torch, bfvgpu, device, args):
     stream."""
     from bfvgpu import token as TK
     ctx = bfvgpu.Context.art002(device)
+    ctx.set_limb_split(bool(args.limb_split))
     n, k, dk = ctx.n, ctx.k, ctx.dk
     slots = 1
     q = torch.tensor(ctx.primes, dtype=torch.int64, device="cuda")
@@ -638,6 +640,7 @@ def run_model_leg(torch, bfvgpu, device, args, dist):
     client ciphertexts, masks and Enc(0) randomness synthetic and resident.  Time = device
     events on the context stream, max over ranks."""
     ctx = bfvgpu.Context.art002(device)
+    ctx.set_limb_split(bool(args.limb_split))
     sp = ctx.stream()
     stream = torch.cuda.ExternalStream(sp)
     with torch.cuda.stream(stream):  # torch's allocations and copies ordered with the kernels
@@ -1031,6 +1034,8 @@ def main():
     ap.add_argument("--model-decode", type=int, default=64, help="decode steps in the config-5 leg")
     ap.add_argument("--reserved-sms", type=int, default=8,
                     help="config 5 with N > 1: SMs the persistent product kernels leave to NCCL")
+    ap.add_argument("--limb-split", type=int, default=1,
+                    help="ART-002 legs: split each n = 16384 limb between a 2-block cluster (1) or one block (0)")
     ap.add_argument("--ks-pipe", type=int, default=1,
                     help="headline: software-pipelined rotations (1) or one rotate + finish launch pair per element (0)")
     ap.add_argument("--decode-graphs", type=int, default=1,

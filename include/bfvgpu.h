@@ -206,6 +206,12 @@ int32_t bfvgpu_ctx_set_reserved_sms(bfvgpu_ctx *ctx, int32_t sms);
  * otherwise; 1 = the TMA-staged CUDA-core product always; 2 = the CUDA-core product with
  * per-thread asynchronous-copy staging (comparison).  Results are identical. */
 int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx *ctx, int32_t path);
+/* At n = 16384, the kernels whose only shared-memory work is one transform (batched NTTs,
+ * weight lift + NTT, client-limb transform, Enc(0) preparation, protected output transform)
+ * split each limb between the two blocks of a thread-block cluster: split = 1 (default), half
+ * a limb per block, three blocks per SM, the cross level through distributed shared memory;
+ * split = 0, one block holds the whole limb (one block per SM).  Results are identical. */
+int32_t bfvgpu_ctx_set_limb_split(bfvgpu_ctx *ctx, int32_t split);
 /* Words of device scratch bfvgpu_matrix_tiles_device needs for tiles * groups outputs:
  * items * (k + 2 + 2 dk) * n with Enc(0) (enc0 != 0), items * 2 dk * n for a mask alone. */
 uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx *ctx, uint64_t tiles, uint64_t groups,

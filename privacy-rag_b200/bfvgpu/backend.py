@@ -222,6 +222,11 @@ class Context:
         """SMs the persistent product kernels leave free (for collectives running beside them)."""
         check(lib().bfvgpu_ctx_set_reserved_sms(self._h, sms), "set_reserved_sms")
 
+    def set_limb_split(self, split: bool) -> None:
+        """n = 16384 single-transform kernels: split each limb between the two blocks of a
+        cluster (True, the default) or one block per limb (False).  Results are identical."""
+        check(lib().bfvgpu_ctx_set_limb_split(self._h, int(bool(split))), "set_limb_split")
+
     def set_product_path(self, path: int) -> None:
         """0: tcgen05 product for 8-tile launches (default); 1: TMA-staged CUDA-core product only;
         2: CUDA-core product with per-thread asynchronous-copy staging."""

@@ -833,6 +833,13 @@ int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx* ctx, int32_t path) {
   });
 }
 
+int32_t bfvgpu_ctx_set_limb_split(bfvgpu_ctx* ctx, int32_t split) {
+  return guard([&] {
+    if (!ctx || split < 0 || split > 1) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    ctx->c.P.split_limbs = split;
+  });
+}
+
 uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx* ctx, uint64_t tiles, uint64_t groups, int32_t enc0) {
   if (!ctx) return 0;
   // U [items][k][n] + xs [items][2][n] (Enc(0) only) + E [items][2][dk][n]

@@ -657,6 +657,47 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
   op_intt_protect<LOGN>(BlockExec{}, smem, blockIdx.x, acc, out, U, pk, E, k, dk, mods, inv);
 }
 
+// ---- n = 16384 transforms with each limb split between the two blocks of a cluster -----------
+// For the ops whose only shared-memory work is one forward or inverse transform: a block holds
+// half a limb (68 KiB instead of 136), so three blocks share an SM instead of one, and the level
+// whose pairs straddle the halves runs through distributed shared memory (ntt_core.cuh).
+// Launched by launch_pair: cluster dimension 2, limb i = blocks 2i and 2i + 1.
+constexpr int kPairLogN = 14;
+#define BFV_PAIR_BOUNDS __launch_bounds__(threads_for<kPairLogN - 1>(), blocks_per_sm<kPairLogN - 1>())
+
+template <bool INV>
+__global__ void BFV_PAIR_BOUNDS k_ntt_pair(uint64_t* data, uint32_t prime_count, uint32_t prime_offset,
+                                           const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_ntt<kPairLogN>(ClusterPairExec{}, smem, blockIdx.x >> 1, INV, data, prime_count, prime_offset, mods, fwd, inv);
+}
+__global__ void BFV_PAIR_BOUNDS k_lift_ntt_pair(const uint64_t* ring, uint64_t* out, uint32_t dk, const Modulus* mods,
+                                                const ulonglong2* fwd) {
+  extern __shared__ uint64_t smem[];
+  op_lift_ntt<kPairLogN>(ClusterPairExec{}, smem, blockIdx.x >> 1, ring, out, dk, mods, fwd);
+}
+__global__ void BFV_PAIR_BOUNDS k_ntt_split_pair(const uint64_t* data, uint64_t* out, uint32_t dk, const Modulus* mods,
+                                                 const ulonglong2* fwd) {
+  extern __shared__ uint64_t smem[];
+  op_ntt_split<kPairLogN>(ClusterPairExec{}, smem, blockIdx.x >> 1, data, out, dk, mods, fwd);
+}
+__global__ void BFV_PAIR_BOUNDS k_enc0_prep_pair(const uint64_t* samples, uint64_t* U, uint32_t k, const Modulus* mods,
+                                                 const ulonglong2* fwd) {
+  extern __shared__ uint64_t smem[];
+  op_enc0_prep<kPairLogN>(ClusterPairExec{}, smem, blockIdx.x >> 1, samples, U, k, mods, fwd);
+}
+__global__ void BFV_PAIR_BOUNDS k_enc0_xs_pair(const uint64_t* samples, const ulonglong2* pk, const uint64_t* U,
+                                               uint64_t* xs, uint32_t k, const Modulus* mods, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_enc0_xs<kPairLogN>(ClusterPairExec{}, smem, blockIdx.x >> 1, samples, pk, U, xs, k, mods, inv);
+}
+__global__ void BFV_PAIR_BOUNDS k_intt_protect_pair(const uint64_t* acc, uint64_t* out, const uint64_t* U,
+                                                    const ulonglong2* pk, const uint64_t* E, uint32_t k, uint32_t dk,
+                                                    const Modulus* mods, const ulonglong2* inv) {
+  extern __shared__ uint64_t smem[];
+  op_intt_protect<kPairLogN>(ClusterPairExec{}, smem, blockIdx.x >> 1, acc, out, U, pk, E, k, dk, mods, inv);
+}
+
 // Galois elements of up to kKeyBatch keys and their inverses mod 2n, passed by value.
 constexpr int kKeyBatch = 256;
 struct EltBatch {
@@ -950,6 +991,14 @@ static cudaError_t configure_for() {
   chk(allow_smem(k_mac_tc<64>, tc::Smem<64>::kLaunchBytes));
   chk(allow_smem(k_intt_protect<L>, s));
   if constexpr (L == 14) {
+    const size_t half = smem_bytes<L - 1>();
+    chk(allow_smem(k_ntt_pair<false>, half));
+    chk(allow_smem(k_ntt_pair<true>, half));
+    chk(allow_smem(k_lift_ntt_pair, half));
+    chk(allow_smem(k_ntt_split_pair, half));
+    chk(allow_smem(k_enc0_prep_pair, half));
+    chk(allow_smem(k_enc0_xs_pair, half));
+    chk(allow_smem(k_intt_protect_pair, half));
     chk(allow_smem(k_token_lift_ntt<L>, s));
     chk(allow_smem(k_token_mac_intt<L>, s));
     chk(allow_smem(k_token_lift_ntt_many<L>, s));
@@ -969,10 +1018,33 @@ static unsigned elementwise_blocks(uint64_t total) {
   return (unsigned)(b < cap ? (b ? b : 1) : cap);
 }
 
+// Launch of a pair kernel over `limbs` limbs: 2 x limbs blocks in clusters of 2.
+template <class... KArgs, class... Args>
+static cudaError_t launch_pair(void (*kernel)(KArgs...), uint64_t limbs, cudaStream_t st, Args... args) {
+  if (2 * limbs > 0x7fffffffull) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * limbs));
+  cfg.blockDim = dim3(threads_for<kPairLogN - 1>());
+  cfg.dynamicSmemBytes = smem_bytes<kPairLogN - 1>();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+static bool use_pair(const DevParams& P) { return P.logn == kPairLogN && P.split_limbs; }
+
 cudaError_t launch_ntt(const DevParams& P, uint64_t* data, uint64_t polys, uint32_t prime_count,
                        uint32_t prime_offset, bool inverse, cudaStream_t st) {
   const LaunchRange range("bfvgpu:ntt");
   if (!polys) return cudaSuccess;
+  if (use_pair(P))
+    return inverse ? launch_pair(k_ntt_pair<true>, polys, st, data, prime_count, prime_offset, P.mod, P.fwd, P.inv)
+                   : launch_pair(k_ntt_pair<false>, polys, st, data, prime_count, prime_offset, P.mod, P.fwd, P.inv);
   BFV_DISPATCH(P.logn, {
     if (inverse)
       k_ntt<L_, true><<<(unsigned)polys, threads_for<L_>(), smem_bytes<L_>(), st>>>(data, prime_count, prime_offset,
@@ -988,6 +1060,7 @@ cudaError_t launch_lift_ntt(const DevParams& P, const uint64_t* ring, uint64_t* 
                             cudaStream_t st) {
   const LaunchRange range("bfvgpu:lift_ntt");
   if (!blocks) return cudaSuccess;
+  if (use_pair(P)) return launch_pair(k_lift_ntt_pair, blocks * P.dk, st, ring, out, P.dk, P.mod, P.fwd);
   BFV_DISPATCH(P.logn, {
     k_lift_ntt<L_><<<(unsigned)(blocks * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(ring, out, P.dk, P.mod,
                                                                                             P.fwd);
@@ -1509,6 +1582,7 @@ cudaError_t launch_ntt_split(const DevParams& P, const uint64_t* data, uint64_t*
   const LaunchRange range("bfvgpu:ntt_split");
   if (!polys) return cudaSuccess;
   if (polys > 0x7fffffffull) return cudaErrorInvalidValue;
+  if (use_pair(P)) return launch_pair(k_ntt_split_pair, polys, st, data, out, P.dk, P.mod, P.fwd);
   BFV_DISPATCH(P.logn, {
     k_ntt_split<L_><<<(unsigned)polys, threads_for<L_>(), smem_bytes<L_>(), st>>>(data, out, P.dk, P.mod, P.fwd);
   });
@@ -1527,6 +1601,11 @@ cudaError_t launch_enc0_prep(const DevParams& P, const uint64_t* samples, const 
   const LaunchRange range("bfvgpu:enc0_prep");
   if (!items) return cudaSuccess;
   if (items * P.k > 0x7fffffffull) return cudaErrorInvalidValue;
+  if (use_pair(P)) {
+    const cudaError_t e = launch_pair(k_enc0_prep_pair, items * P.k, st, samples, U, P.k, P.mod, P.fwd);
+    if (e != cudaSuccess) return e;
+    return launch_pair(k_enc0_xs_pair, items * 2, st, samples, pk, U, xs, P.k, P.mod, P.inv);
+  }
   BFV_DISPATCH(P.logn, {
     k_enc0_prep<L_><<<(unsigned)(items * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(samples, U, P.k, P.mod,
                                                                                          P.fwd);
@@ -1559,6 +1638,8 @@ cudaError_t launch_intt_protect(const DevParams& P, const uint64_t* acc, uint64_
   const LaunchRange range("bfvgpu:intt_protect");
   if (!items) return cudaSuccess;
   if (items * 2 * P.dk > 0x7fffffffull) return cudaErrorInvalidValue;
+  if (use_pair(P))
+    return launch_pair(k_intt_protect_pair, items * 2 * P.dk, st, acc, out, U, pk, E, P.k, P.dk, P.mod, P.inv);
   BFV_DISPATCH(P.logn, {
     k_intt_protect<L_><<<(unsigned)(items * 2 * P.dk), threads_for<L_>(), smem_bytes<L_>(), st>>>(
         acc, out, U, pk, E, P.k, P.dk, P.mod, P.inv);

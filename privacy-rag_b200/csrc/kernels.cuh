@@ -29,6 +29,8 @@ struct DevParams {
   int product_path = 0;               // 0: tcgen05 where it applies, 1: CUDA cores only (TMA-staged),
                                       // 2: CUDA cores with per-thread asynchronous-copy staging
   int reserved_sms = 0;               // SMs the persistent product kernels leave free
+  int split_limbs = 1;                // n = 16384 single-transform kernels: 1 = each limb split
+                                      // between the two blocks of a cluster, 0 = one block per limb
 };
 
 // Smallest and largest supported log2(n).

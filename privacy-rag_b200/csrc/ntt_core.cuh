@@ -22,6 +22,9 @@
 #pragma once
 #include "arith.cuh"
 
+#if defined(__CUDACC__)
+#include <cooperative_groups.h>
+#endif
 #if !defined(__CUDACC__)
 struct ulonglong2 {
   unsigned long long x, y;
@@ -82,9 +85,12 @@ BFV_HD uint64_t reduce_4q(uint64_t v, uint64_t q) {
 
 // U radix-2^R Cooley-Tukey units of the forward pass starting at level L: units u0 + j*us
 // (j < U), interleaved so that one thread has U independent butterfly chains in flight.
-template <int LOGN, int R, bool FIRST, bool LAST, int U, class Ld, class St>
+// SPLIT: the unit belongs to half `rank` of a transform of size 2^(LOGN+1) split between the
+// two blocks of a cluster (level 0 done by fwd_cross): its level L + t is the full
+// transform's level L + t + 1 and its groups start at rank * 2^(L+t).
+template <int LOGN, int R, bool FIRST, bool LAST, int U, bool SPLIT, class Ld, class St>
 BFV_HD void fwd_unit(uint64_t* s, int u0, int us, int L, const ulonglong2* tw, uint64_t q, const Ld& ld,
-                     const St& st) {
+                     const St& st, int rank) {
   constexpr int K = 1 << R;
   const int shift = LOGN - L - R;  // smallest gap of the pass is 2^shift
   int base[U], sbase[U], gl[U];
@@ -114,7 +120,9 @@ BFV_HD void fwd_unit(uint64_t* s, int u0, int us, int L, const ulonglong2* tw, u
       const int k = (jj << (hs + 1)) + kk;
 #pragma unroll
       for (int j = 0; j < U; ++j) {
-        const ulonglong2 w = tw[(1 << (L + t)) + (gl[j] << t) + jj];
+        const int ti = SPLIT ? (1 << (L + t + 1)) + (rank << (L + t)) + (gl[j] << t) + jj
+                             : (1 << (L + t)) + (gl[j] << t) + jj;
+        const ulonglong2 w = tw[ti];
         uint64_t a = x[j][k];
         if (a >= two_q) a -= two_q;
         const uint64_t b = shoup_lazy(x[j][k + (1 << hs)], w.x, w.y, q);
@@ -135,9 +143,12 @@ BFV_HD void fwd_unit(uint64_t* s, int u0, int us, int L, const ulonglong2* tw, u
 }
 
 // U radix-2^R Gentleman-Sande units of the inverse pass starting at level L.
-template <int LOGN, int R, bool FIRST, bool LAST, int U, class Ld, class St>
+// SPLIT: the unit belongs to half `rank` of a transform of size 2^(LOGN+1) split between two
+// blocks (the last level done by inv_cross): levels keep their gaps, the full transform's
+// table offsets apply and its groups at level l start at rank * 2^(LOGN-1-l).
+template <int LOGN, int R, bool FIRST, bool LAST, int U, bool SPLIT, class Ld, class St>
 BFV_HD void inv_unit(uint64_t* s, int u0, int us, int L, const ulonglong2* tw, uint64_t q, uint64_t invn,
-                     uint64_t invn_q, const Ld& ld, const St& st) {
+                     uint64_t invn_q, const Ld& ld, const St& st, int rank) {
   constexpr int K = 1 << R;
   constexpr int N = 1 << LOGN;
   int base[U], sbase[U], gg[U];
@@ -167,7 +178,9 @@ BFV_HD void inv_unit(uint64_t* s, int u0, int us, int L, const ulonglong2* tw, u
       const int k = (jj << (t + 1)) + kk;
 #pragma unroll
       for (int j = 0; j < U; ++j) {
-        const ulonglong2 w = tw[N - (N >> l) + 1 + (gg[j] << (R - t - 1)) + jj];
+        const int ti = SPLIT ? 2 * N - ((2 * N) >> l) + 1 + (rank << (LOGN - 1 - l)) + (gg[j] << (R - t - 1)) + jj
+                             : N - (N >> l) + 1 + (gg[j] << (R - t - 1)) + jj;
+        const ulonglong2 w = tw[ti];
         const uint64_t a = x[j][k], b = x[j][k + (1 << t)];
         uint64_t sum = a + b;
         if (sum >= two_q) sum -= two_q;
@@ -206,6 +219,24 @@ struct BlockExec {
     }
   }
   __device__ __forceinline__ void sync() const { __syncthreads(); }
+  static constexpr bool kSplit = false;
+};
+
+// A limb split between the two blocks of a cluster (launched with cluster dimension 2, the
+// block pair of a limb consecutive): each block holds half the limb in its shared memory
+// and reaches the other half through distributed shared memory.
+struct ClusterPairExec : BlockExec {
+  static constexpr bool kSplit = true;
+  __device__ __forceinline__ int rank() const { return (int)cooperative_groups::this_cluster().block_rank(); }
+  // block r's buffer, s being this block's own
+  __device__ __forceinline__ uint64_t* buffer(uint64_t* s, int r) const {
+    return r == rank() ? s : cooperative_groups::this_cluster().map_shared_rank(s, (unsigned)r);
+  }
+  __device__ __forceinline__ void cluster_sync() const { cooperative_groups::this_cluster().sync(); }
+  template <class F>
+  __device__ __forceinline__ void for_ranks(uint64_t* s, F&& f) const {
+    f(rank(), s);
+  }
 };
 #endif
 struct HostExec {
@@ -224,6 +255,22 @@ struct HostExec {
     }
   }
   void sync() const {}
+  static constexpr bool kSplit = false;
+};
+
+// The host form of ClusterPairExec: s holds both halves' buffers, `words` apart; every phase
+// between cluster barriers runs for block 0, then block 1 (the phases of the two blocks read
+// and write disjoint words, so running them in turn is exact).
+struct HostPairExec : HostExec {
+  int words = 0;
+  static constexpr bool kSplit = true;
+  uint64_t* buffer(uint64_t* s, int r) const { return s + (size_t)r * words; }
+  void cluster_sync() const {}
+  template <class F>
+  void for_ranks(uint64_t* s, F&& f) const {
+    f(0, s);
+    f(1, s + words);
+  }
 };
 
 // Units per thread per pass: two interleaved units at n = 16384 (one 512-thread block per SM,
@@ -233,44 +280,132 @@ struct DualUnits {
   static constexpr bool value = LOGN >= 14;
 };
 
-template <int LOGN, int MAXR, int P, class Ex, class Ld, class St>
+// SPLIT: the passes of one half of a split transform (after fwd_cross): the first pass reads
+// shared memory, the twiddles are the full transform's.
+template <int LOGN, int MAXR, int P, bool SPLIT = false, class Ex, class Ld, class St>
 BFV_HD void fwd_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t q, const Ld& ld,
-                       const St& st) {
+                       const St& st, int rank = 0) {
   using S = Schedule<LOGN, MAXR>;
   if constexpr (P < S::passes) {
     constexpr int R = S::fwd_r(P);
     constexpr int L = S::fwd_level(P);
-    constexpr bool first = P == 0, last = P == S::passes - 1;
+    constexpr bool first = P == 0 && !SPLIT, last = P == S::passes - 1;
     if constexpr (DualUnits<LOGN>::value)
       ex.run2(
-          1 << (LOGN - R), [&](int u0, int us) { fwd_unit<LOGN, R, first, last, 2>(s, u0, us, L, tw, q, ld, st); },
-          [&](int u) { fwd_unit<LOGN, R, first, last, 1>(s, u, 0, L, tw, q, ld, st); });
+          1 << (LOGN - R),
+          [&](int u0, int us) { fwd_unit<LOGN, R, first, last, 2, SPLIT>(s, u0, us, L, tw, q, ld, st, rank); },
+          [&](int u) { fwd_unit<LOGN, R, first, last, 1, SPLIT>(s, u, 0, L, tw, q, ld, st, rank); });
     else
-      ex.run(1 << (LOGN - R), [&](int u) { fwd_unit<LOGN, R, first, last, 1>(s, u, 0, L, tw, q, ld, st); });
+      ex.run(1 << (LOGN - R),
+             [&](int u) { fwd_unit<LOGN, R, first, last, 1, SPLIT>(s, u, 0, L, tw, q, ld, st, rank); });
     ex.sync();
-    fwd_passes<LOGN, MAXR, P + 1>(ex, s, tw, q, ld, st);
+    fwd_passes<LOGN, MAXR, P + 1, SPLIT>(ex, s, tw, q, ld, st, rank);
   }
 }
 
-template <int LOGN, int MAXR, int P, class Ex, class Ld, class St>
+// SPLIT: the passes of one half of a split transform (before inv_cross): the last pass keeps
+// its results in shared memory, unscaled, the twiddles are the full transform's.
+template <int LOGN, int MAXR, int P, bool SPLIT = false, class Ex, class Ld, class St>
 BFV_HD void inv_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t q, uint64_t invn,
-                       uint64_t invn_q, const Ld& ld, const St& st) {
+                       uint64_t invn_q, const Ld& ld, const St& st, int rank = 0) {
   using S = Schedule<LOGN, MAXR>;
   if constexpr (P < S::passes) {
     constexpr int R = S::inv_r(P);
     constexpr int L = S::inv_level(P);
-    constexpr bool first = P == 0, last = P == S::passes - 1;
+    constexpr bool first = P == 0, last = P == S::passes - 1 && !SPLIT;
     if constexpr (DualUnits<LOGN>::value)
       ex.run2(
           1 << (LOGN - R),
-          [&](int u0, int us) { inv_unit<LOGN, R, first, last, 2>(s, u0, us, L, tw, q, invn, invn_q, ld, st); },
-          [&](int u) { inv_unit<LOGN, R, first, last, 1>(s, u, 0, L, tw, q, invn, invn_q, ld, st); });
+          [&](int u0, int us) {
+            inv_unit<LOGN, R, first, last, 2, SPLIT>(s, u0, us, L, tw, q, invn, invn_q, ld, st, rank);
+          },
+          [&](int u) { inv_unit<LOGN, R, first, last, 1, SPLIT>(s, u, 0, L, tw, q, invn, invn_q, ld, st, rank); });
     else
       ex.run(1 << (LOGN - R),
-             [&](int u) { inv_unit<LOGN, R, first, last, 1>(s, u, 0, L, tw, q, invn, invn_q, ld, st); });
+             [&](int u) { inv_unit<LOGN, R, first, last, 1, SPLIT>(s, u, 0, L, tw, q, invn, invn_q, ld, st, rank); });
     ex.sync();
-    inv_passes<LOGN, MAXR, P + 1>(ex, s, tw, q, invn, invn_q, ld, st);
+    inv_passes<LOGN, MAXR, P + 1, SPLIT>(ex, s, tw, q, invn, invn_q, ld, st, rank);
   }
+}
+
+// ---- a limb split between two blocks ------------------------------------------------------
+// Half r (of H = n/2 words) lives in block r's shared memory.  The one level whose pairs
+// straddle the halves (forward level 0, inverse level log n - 1, gap H) runs as a "cross"
+// step: block r takes the pairs j in [r H/2, (r+1) H/2) and writes both outputs, one into its
+// own half and one into the other block's.  The two blocks' read and write sets are disjoint,
+// so a cluster barrier before and after the step is all the ordering it needs.
+template <int LOGH, class Ex>
+BFV_HD void fwd_cross(const Ex& ex, uint64_t* s0, uint64_t* s1, int rank, const ulonglong2* tw, uint64_t q) {
+  constexpr int H = 1 << LOGH;
+  const ulonglong2 w = tw[1];
+  const uint64_t two_q = 2 * q;
+  ex.run(H / 2, [&](int jj) {
+    const int sj = spad(rank * (H / 2) + jj);
+    uint64_t a = s0[sj];
+    if (a >= two_q) a -= two_q;
+    const uint64_t t = shoup_lazy(s1[sj], w.x, w.y, q);
+    s0[sj] = a + t;
+    s1[sj] = a + two_q - t;
+  });
+}
+template <int LOGH, class Ex>
+BFV_HD void inv_cross(const Ex& ex, uint64_t* s0, uint64_t* s1, int rank, const ulonglong2* tw, uint64_t q) {
+  constexpr int H = 1 << LOGH;
+  const ulonglong2 w = tw[2 * H - 1];  // the last level's single entry, n - (n >> (log n - 1)) + 1
+  const uint64_t two_q = 2 * q;
+  ex.run(H / 2, [&](int jj) {
+    const int sj = spad(rank * (H / 2) + jj);
+    const uint64_t a = s0[sj], b = s1[sj];
+    uint64_t sum = a + b;
+    if (sum >= two_q) sum -= two_q;
+    s0[sj] = sum;
+    s1[sj] = shoup_lazy(a + two_q - b, w.x, w.y, q);
+  });
+}
+
+// Forward NTT of a limb split between two blocks: stage each half through ld, the cross
+// level, then the remaining log n - 1 levels on each half (the schedule of an n/2 transform
+// with the full transform's twiddles), stored in index order through st (global indices).
+template <int LOGN, int MAXR, class Ex, class Ld, class St>
+BFV_HD void ntt_forward_split(const Ex& ex, uint64_t* s, const ulonglong2* tw, const Modulus& m, const Ld& ld,
+                              const St& st) {
+  constexpr int LOGH = LOGN - 1, H = 1 << LOGH;
+  ex.for_ranks(s, [&](int r, uint64_t* own) {
+    ex.run(H, [&](int j) { own[spad(j)] = ld(r * H + j); });
+  });
+  ex.cluster_sync();
+  ex.for_ranks(s, [&](int r, uint64_t*) { fwd_cross<LOGH>(ex, ex.buffer(s, 0), ex.buffer(s, 1), r, tw, m.q); });
+  ex.cluster_sync();
+  ex.for_ranks(s, [&](int r, uint64_t* own) {
+    auto unused = [](int) { return uint64_t(0); };
+    auto to_smem = [own](int j, uint64_t v) { own[spad(j)] = v; };
+    fwd_passes<LOGH, MAXR, 0, true>(ex, own, tw, m.q, unused, to_smem, r);
+    ex.run(H, [&](int j) { st(r * H + j, own[spad(j)]); });
+    ex.sync();
+  });
+}
+
+// Inverse NTT of a limb split between two blocks: each half staged through ld and taken
+// through the first log n - 1 levels, the cross level, then scaled by n^-1 and stored in
+// index order through st (global indices).
+template <int LOGN, int MAXR, class Ex, class Ld, class St>
+BFV_HD void ntt_inverse_split(const Ex& ex, uint64_t* s, const ulonglong2* tw, const Modulus& m, const Ld& ld,
+                              const St& st) {
+  constexpr int LOGH = LOGN - 1, H = 1 << LOGH;
+  ex.for_ranks(s, [&](int r, uint64_t* own) {
+    ex.run(H, [&](int j) { own[spad(j)] = ld(r * H + j); });
+    ex.sync();
+    auto from_smem = [own](int j) { return own[spad(j)]; };
+    auto unused = [](int, uint64_t) {};
+    inv_passes<LOGH, MAXR, 0, true>(ex, own, tw, m.q, m.invn, m.invn_q, from_smem, unused, r);
+  });
+  ex.cluster_sync();
+  ex.for_ranks(s, [&](int r, uint64_t*) { inv_cross<LOGH>(ex, ex.buffer(s, 0), ex.buffer(s, 1), r, tw, m.q); });
+  ex.cluster_sync();
+  ex.for_ranks(s, [&](int r, uint64_t* own) {
+    ex.run(H, [&](int j) { st(r * H + j, shoup(own[spad(j)], m.invn, m.invn_q, m.q)); });
+    ex.sync();
+  });
 }
 
 // Forward NTT of one limb: ld(i) gives input coefficient i (< 4q), st(i, v) receives
@@ -284,7 +419,10 @@ BFV_HD void inv_passes(const Ex& ex, uint64_t* s, const ulonglong2* tw, uint64_t
 template <int LOGN, int MAXR = 4, bool STAGE_OUT = true, class Ex, class Ld, class St>
 BFV_HD void ntt_forward(const Ex& ex, uint64_t* s, const ulonglong2* tw, const Modulus& m, const Ld& ld,
                         const St& st) {
-  if constexpr (STAGE_OUT) {
+  if constexpr (Ex::kSplit) {
+    static_assert(STAGE_OUT, "a split transform stores its output from shared memory");
+    ntt_forward_split<LOGN, MAXR>(ex, s, tw, m, ld, st);
+  } else if constexpr (STAGE_OUT) {
     auto to_smem = [s](int i, uint64_t v) { s[spad(i)] = v; };
     fwd_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, ld, to_smem);
     ex.run(1 << LOGN, [&](int i) { st(i, s[spad(i)]); });
@@ -302,7 +440,10 @@ BFV_HD void ntt_forward(const Ex& ex, uint64_t* s, const ulonglong2* tw, const M
 template <int LOGN, int MAXR = 4, bool STAGE_IN = true, class Ex, class Ld, class St>
 BFV_HD void ntt_inverse(const Ex& ex, uint64_t* s, const ulonglong2* tw, const Modulus& m, const Ld& ld,
                         const St& st) {
-  if constexpr (STAGE_IN) {
+  if constexpr (Ex::kSplit) {
+    static_assert(STAGE_IN, "a split transform stages its input into shared memory");
+    ntt_inverse_split<LOGN, MAXR>(ex, s, tw, m, ld, st);
+  } else if constexpr (STAGE_IN) {
     ex.run(1 << LOGN, [&](int i) { s[spad(i)] = ld(i); });
     ex.sync();
     auto from_smem = [s](int i) { return s[spad(i)]; };

@@ -202,6 +202,23 @@ int emu_ntt(int logn, uint32_t k, const uint64_t* mods16, const uint64_t* fwd, c
   return 0;
 }
 
+// The same batched transform with every limb split between a pair of blocks (the form the
+// n = 16384 kernels launch as 2-block clusters): both halves' buffers side by side.
+int emu_ntt_pair(int logn, uint32_t k, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv, uint64_t* data,
+                 uint64_t polys, uint32_t prime_count, uint32_t prime_offset, int inverse) {
+  Tabs T = tabs(k, mods16, fwd, inv);
+  EMU_DISPATCH(logn, {
+    if constexpr (L_ >= 6) {
+      HostPairExec ex;
+      ex.words = SmemWords<L_ - 1>::value;
+      std::vector<uint64_t> s(2 * (size_t)ex.words);
+      for (uint64_t b = 0; b < polys; ++b)
+        op_ntt<L_>(ex, s.data(), b, inverse != 0, data, prime_count, prime_offset, T.mods.data(), T.fwd, T.inv);
+    }
+  });
+  return 0;
+}
+
 // cts [count][2][dk][n], key [dk][2][k][n] -> out [count][2][dk][n]
 int emu_keyswitch(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv,
                   const uint64_t* cts, uint64_t count, const uint64_t* key, uint32_t elt, uint64_t* out) {

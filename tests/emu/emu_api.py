@@ -6,6 +6,7 @@ U64, U32, INT = ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int
 
 SIGNATURES = {
     "emu_ntt": [INT, U32, P, P, P, P, U64, U32, U32, INT],
+    "emu_ntt_pair": [INT, U32, P, P, P, P, U64, U32, U32, INT],
     "emu_keyswitch": [INT, U32, U32, P, P, P, P, U64, P, U32, P],
     "emu_keyswitch_hoisted": [INT, U32, U32, P, P, P, P, U64, P, U32, P, ctypes.POINTER(ctypes.c_uint32)],
     "emu_keyswitch_pipe": [INT, U32, U32, P, P, P, P, U64, P, ctypes.POINTER(ctypes.c_uint32), U64, P],

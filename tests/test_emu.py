@@ -80,6 +80,24 @@ def test_ntt_kernel_body(bfv, oracle, E, logn):
         assert np.array_equal(sub, exp)
 
 
+@pytest.mark.parametrize("logn", [6, 12, 13, 14])
+def test_ntt_split_between_two_blocks(bfv, oracle, E, logn):
+    """A limb split between the two blocks of a cluster (each holds half; the level whose
+    pairs straddle the halves runs as a cross step through the other block's shared memory,
+    the rest as a half-size schedule with the full transform's twiddles) transforms exactly
+    as the one-block kernel and the oracle, forward and inverse, with boundary residues."""
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+    k, n = hc.k, 1 << logn
+    data = oc.uniform(700 + logn, 2 * k, prime_count=k).reshape(2 * k, n)
+    data[0, :3] = [0, 1, oc.primes[0] - 1]
+    f = data.copy()
+    E.emu_ntt_pair(logn, k, p(mods), p(fwd), p(inv), p(f), 2 * k, k, 0, 0)
+    assert np.array_equal(f, oc.ntt(data, prime_count=k)), logn
+    back = f.copy()
+    E.emu_ntt_pair(logn, k, p(mods), p(fwd), p(inv), p(back), 2 * k, k, 0, 1)
+    assert np.array_equal(back, data), logn
+
+
 @pytest.mark.parametrize("logn,elts", [(5, [1, 3, 63]), (6, [5, 127, 9]), (13, [3, 2 ** 13 + 1, 16383]),
                                        (14, [1, 3, 1025])])
 def test_keyswitch_kernel_body(bfv, oracle, E, logn, elts):

@@ -531,6 +531,66 @@ def test_matrix_tiles_tensor_core_vs_cuda_core(art, oracle):
         assert np.array_equal(got[t, g], oc.matrix_evaluate(cn, ring_h[g], threads=8)), (t, g)
 
 
+def test_limb_split_equals_one_block_per_limb(art, oracle):
+    """At n = 16384 the single-transform kernels split each limb between the two blocks of a
+    cluster (the default).  Every kernel that takes that form -- batched forward and inverse
+    NTT, weight lift + NTT, client-limb transform, Enc(0) preparation and the protected output
+    transform of the tile product -- gives the same words as with one block per limb, and the
+    NTT equals the oracle."""
+    import torch
+    hc, oc = art
+    n, k, dk = oc.n, oc.k, oc.data_k
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(17)
+    q = torch.tensor(oc.primes, dtype=torch.int64, device="cuda")
+    res = lambda shape, m: torch.remainder(
+        torch.randint(0, 2 ** 62, shape, dtype=torch.int64, device="cuda", generator=gen), q[:m].view(m, 1))
+    data = res((5, k, n), k)
+    data[0, 0, :3] = torch.tensor([0, 1, oc.primes[0] - 1])
+    tiles, I, G = 2, 5, 3
+    cts = res((tiles, I, 2, dk, n), dk)
+    ring = torch.randint(-(1 << 20), 1 << 20, (G, I, n), dtype=torch.int64, device="cuda", generator=gen) & ((1 << 59) - 1)
+    masks = torch.randint(0, 2 ** 59, (tiles, G, n), dtype=torch.int64, device="cuda", generator=gen)
+    small = torch.cat([torch.randint(-1, 2, (tiles, G, 1, n), device="cuda", generator=gen),
+                       torch.randint(-5, 6, (tiles, G, 2, n), device="cuda", generator=gen)], dim=2)
+    samples = torch.remainder(small.unsqueeze(-2), q.view(k, 1)).contiguous()
+    pk = res((2, k, n), k)
+
+    def run():
+        f = data.clone()
+        hc.ntt_device(f, 5 * k, k)
+        b = f.clone()
+        hc.ntt_device(b, 5 * k, k, inverse=True)
+        d_in = cts.clone()
+        hc.matrix_tiles_inputs_device(d_in, tiles * I)
+        w = torch.empty((G, I, dk, n), dtype=torch.int64, device="cuda")
+        hc.weights_ntt_device(ring, G * I, w)
+        pk_prep = torch.empty((2, k, n, 2), dtype=torch.int64, device="cuda")
+        hc.matrix_tiles_prepare_pk_device(pk, pk_prep)
+        scratch = torch.empty(hc.matrix_tiles_scratch_words(tiles, G), dtype=torch.int64, device="cuda")
+        out = torch.empty((tiles, G, 2, dk, n), dtype=torch.int64, device="cuda")
+        hc.matrix_tiles_device(d_in, tiles, I, w, G, out, masks=masks, samples=samples, pk_prep=pk_prep,
+                               scratch=scratch)
+        torch.cuda.synchronize()
+        return f, b, d_in, w, out
+
+    torch.cuda.synchronize()
+    # torch's copies and the library's kernels on one stream (the context's)
+    with torch.cuda.stream(torch.cuda.ExternalStream(hc.stream())):
+        split = run()
+        hc.set_limb_split(False)
+        try:
+            whole = run()
+        finally:
+            hc.set_limb_split(True)
+    assert hc.check() == 0
+    for name, a, b in zip(("ntt", "intt", "inputs", "weights", "tiles"), split, whole):
+        assert torch.equal(a, b), name
+    assert torch.equal(split[1], data)
+    assert np.array_equal(split[0].cpu().numpy().view(np.uint64),
+                          oc.ntt(data.cpu().numpy().view(np.uint64).reshape(5 * k, n), prime_count=k).reshape(5, k, n))
+
+
 def test_matrix_tiles_qkv_full_shape(art, oracle):
     """The benchmark's largest prefill call at full shape: the qkv joint projection of a
     128-token group, 8 tiles x 64 input blocks x 128 output groups (matrix_packing of B = 16,
