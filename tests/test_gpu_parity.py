@@ -285,7 +285,12 @@ def test_rotations_object(cfg2, oracle):
     keys = np.stack([oc.uniform(80 + i, dk * 2 * k, prime_count=k).reshape(dk, 2, k, n) for i in range(len(elts))])
     rot = bfvgpu.Rotations(hc, keys, elts)
     try:
-        got = rot.apply(cts)
+        bad = cts.copy()
+        bad[count - 1, 1, dk - 1, n - 1] = oc.primes[dk - 1]  # one residue equal to its prime
+        with pytest.raises(bfvgpu.BfvGpuError) as e:
+            rot.apply(bad)  # checked on the device after the upload, before any work
+        assert e.value.name == "BFVGPU_E_CANONICAL"
+        got = rot.apply(cts)  # the object is unaffected by the rejected batch
         again = rot.apply(cts[:2])  # smaller batch on the same object
     finally:
         assert rot.close()["closed"]
