@@ -170,7 +170,7 @@ def cpu_keyswitch_sample(seconds: float = 12.0):
 
 
 # the files that define the transform-bearing kernels (bodies, arithmetic, launches)
-KERNEL_SOURCES = ("arith.cuh", "ntt_core.cuh", "block_ops.cuh", "kernels.cuh", "kernels.cu")
+KERNEL_SOURCES = ("arith.cuh", "layout.cuh", "ntt_core.cuh", "block_ops.cuh", "kernels.cuh", "kernels.cu")
 
 
 def kernel_sources_sha16() -> str:
@@ -202,14 +202,14 @@ def traffic_record(path: str):
 
 
 # ---- integer roofline -------------------------------------------------------------------------
-PEAK_KINDS = {0: "butterfly", 1: "mac", 2: "modmul"}
+PEAK_KINDS = {0: "butterfly", 1: "mac", 2: "modmul", 3: "shoup"}
 
 
 def measure_int_peaks(torch, ctx, reps: int = 5):
-    """Operations per second of the three integer operations the kernels are built from
+    """Operations per second of the integer operations the kernels are built from
     (bfvgpu_int_peak_device: butterfly, 64x64->128 multiply-accumulate, Barrett modular
-    product), each from registers at full occupancy, timed with CUDA events on the
-    context stream (3 warm-up launches, then `reps`)."""
+    product, Shoup product by a fixed operand), each from registers at full occupancy, timed
+    with CUDA events on the context stream (3 warm-up launches, then `reps`)."""
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     blocks, iters = sms * 16, 4096
     sink = torch.empty(blocks * 256, dtype=torch.int64, device="cuda")
@@ -240,20 +240,22 @@ def int_roofline(counts: dict, rates: dict, seconds: float) -> dict:
 
 
 def ks_pair_counts(cts: int, n: int, k: int, dk: int) -> dict:
-    """Algorithmic integer operations of one hoisted rotation launch pair (k_ks_rotate +
-    k_ks_finish) over `cts` ciphertexts: per (ciphertext, component, key-level prime) the key
-    inner product of dk multiply-accumulates per coefficient, its reduction and an inverse NTT
-    (n/2 log n butterflies, n scalings by n^-1); per (ciphertext, component, data prime) one
-    divide-and-round product per coefficient."""
+    """Integer operations of one element's hoisted rotation over `cts` ciphertexts, by the kind
+    the kernels execute: per (ciphertext, component, key-level prime) and coefficient the key
+    inner product of dk Shoup products (each key word carries its companion), the inverse NTT
+    (n/2 log n butterflies per limb) and its scaling by n^-1 (a Shoup product); per
+    (ciphertext, component, data prime) and coefficient the divide-and-round by the special
+    prime (a Shoup product)."""
     logn = n.bit_length() - 1
     limbs = cts * 2 * k
-    return {"butterfly": limbs * (n // 2) * logn, "mac": limbs * n * dk,
-            "modmul": limbs * n * 2 + cts * 2 * dk * n}
+    return {"butterfly": limbs * (n // 2) * logn, "mac": 0, "modmul": 0,
+            "shoup": limbs * n * dk + limbs * n + cts * 2 * dk * n}
 
 
 def ntt_counts(polys: int, n: int, inverse: bool) -> dict:
+    """Butterflies of a batch of transforms, and the inverse's scaling by n^-1 (Shoup)."""
     logn = n.bit_length() - 1
-    return {"butterfly": polys * (n // 2) * logn, "mac": 0, "modmul": polys * n if inverse else 0}
+    return {"butterfly": polys * (n // 2) * logn, "mac": 0, "modmul": 0, "shoup": polys * n if inverse else 0}
 
 
 def headline_config(world: int, rotations: int) -> dict:

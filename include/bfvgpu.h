@@ -175,7 +175,8 @@ int32_t bfvgpu_keyswitch_device_noalloc(bfvgpu_ctx *ctx, const uint64_t *cts, ui
  * of the 64-bit modular operations the kernels are built from, from registers only, with
  * independent chains at full occupancy -- kind 0 = NTT butterfly (Harvey lazy, Shoup
  * twiddle of prime 0), 1 = 64x64 -> 128-bit multiply-accumulate, 2 = modular product
- * (128-bit product + Barrett reduction by prime 0).  blocks x 256 threads; *ops receives
+ * (128-bit product + Barrett reduction by prime 0), 3 = Shoup product by a fixed operand
+ * with its companion, made canonical.  blocks x 256 threads; *ops receives
  * the operations performed (blocks * 256 * 8 chains * iters); sink [blocks * 256] (device)
  * one checksum word per thread.  Timed by the caller (CUDA events) to give this GPU's
  * operation rates, the denominators of the integer roofline. */

@@ -126,7 +126,8 @@ class Context:
 
     def int_peak_device(self, kind: int, blocks: int, iters: int, sink, stream: int | None = None) -> int:
         """Launch the integer-pipe peak kernel of `kind` (0 butterfly, 1 multiply-accumulate,
-        2 modular product); returns the operations it performs.  sink: blocks * 256 words."""
+        2 Barrett modular product, 3 Shoup product); returns the operations it performs.  sink:
+        blocks * 256 words."""
         ops = U64(0)
         check(lib().bfvgpu_int_peak_device(self._h, kind, blocks, iters, self._dptr(sink), ctypes.byref(ops),
                                            stream), "int_peak_device")

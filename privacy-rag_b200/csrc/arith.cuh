@@ -81,6 +81,16 @@ BFV_HD uint64_t mul_mod(uint64_t a, uint64_t b, const Modulus& m) {
   return reduce128(a * b, mulhi64(a, b), m);
 }
 
+// Shoup companion floor(v 2^64 / q) of v < q, by exact division: v 2^64 - r (r = v 2^64 mod q)
+// is a multiple of q, so the quotient is -r . q^-1 mod 2^64 (q odd).
+BFV_HD uint64_t shoup_companion(uint64_t v, const Modulus& m) {
+  const uint64_t r = reduce128(0, v, m);
+  uint64_t inv = m.q;  // q^-1 mod 2^64 by Newton's iteration (3 -> 96 correct bits)
+#pragma unroll
+  for (int it = 0; it < 5; ++it) inv *= 2 - m.q * inv;
+  return (uint64_t(0) - r) * inv;
+}
+
 // v mod q for v < 2^64 with the 64-bit Barrett ratio floor(2^64/q) = r1.
 BFV_HD uint64_t reduce64(uint64_t v, const Modulus& m) {
   const uint64_t r = v - mulhi64(v, m.r1) * m.q;

@@ -702,7 +702,7 @@ int32_t bfvgpu_keyswitch_device(bfvgpu_ctx* ctx, const uint64_t* cts, uint64_t c
 }
 
 uint64_t bfvgpu_keyswitch_prepared_words(const bfvgpu_ctx* ctx) {
-  return ctx ? (2ull * ctx->c.dk + 2) * ctx->c.k * ctx->c.n : 0;
+  return ctx ? ks_prepared_words(ctx->c.k, ctx->c.dk, ctx->c.n) : 0;
 }
 
 uint64_t bfvgpu_keyswitch_hoist_words(const bfvgpu_ctx* ctx, uint64_t count) {
@@ -1474,7 +1474,7 @@ int32_t bfvgpu_rotations_open(bfvgpu_ctx* ctx, const uint64_t* keys, const uint3
     auto s = std::make_unique<bfvgpu_rotations>();
     s->h.ctx = &ctx->c;
     s->elts.assign(galois_elts, galois_elts + count);
-    s->pw = (2ull * c.dk + 2) * c.k * c.n;
+    s->pw = ks_prepared_words(c.k, c.dk, c.n);
     require_device(c);
     DeviceScope scope(c.device);
     s->h.run([&] {
@@ -1613,7 +1613,7 @@ int32_t bfvgpu_slots_open(bfvgpu_ctx* ctx, const uint64_t* keys, uint32_t baby, 
     s->elts.push_back(2 * c.n - 1);
     const uint64_t nkeys = s->elts.size(), kw = (uint64_t)c.dk * 2 * c.k * c.n;
     check_canonical_host(c, keys, nkeys * c.dk * 2 * c.k, c.k, 0);
-    s->pw = (2ull * c.dk + 2) * c.k * c.n;
+    s->pw = ks_prepared_words(c.k, c.dk, c.n);
     require_device(c);
     DeviceScope scope(c.device);
     s->h.run([&] {

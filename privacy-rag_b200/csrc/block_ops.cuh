@@ -16,6 +16,7 @@
 //                      (IV1/experiments/resident_token_gpu/resident.cu:71-107)
 //   crt_target ....... rns_coefficient (IV1/native/src/bfv.cpp:138-147) in fixed-width limbs
 #pragma once
+#include "layout.cuh"
 #include "ntt_core.cuh"
 
 namespace bfvgpu {
@@ -243,8 +244,9 @@ BFV_HD void op_ks_hoist(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t*
   }
 }
 
-// Key preparation for a batch of keys, in two kernels.  The prepared layout of key r is
-// Kt [dk][2][k][n] then Ct [2][k][n] (prepared_words = (2*dk + 2)*k*n).
+// Key preparation for a batch of keys, in two kernels, into the prepared layout of
+// layout.cuh: Kt as {key word, Shoup companion} pairs (so the rotation's key product is one
+// lazy Shoup multiplication per digit), then Ct.
 // (1) block (r, p): W = NTT_p(neg_g) written to Ct[c = 0][p] of key r.
 template <int LOGN, class Ex>
 BFV_HD void op_ks_negntt(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* prepared, uint64_t prepared_words,
@@ -254,7 +256,7 @@ BFV_HD void op_ks_negntt(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* prep
   const uint32_t p = (uint32_t)(blk % k);
   const Modulus m = mods[p];
   const uint32_t elt = elts[r], mask2n = 2u * N - 1u;
-  uint64_t* w = prepared + r * prepared_words + (uint64_t)dk * 2 * k * N + (uint64_t)p * N;
+  uint64_t* w = prepared + r * prepared_words + ks_ct_offset(k, dk, N) + (uint64_t)p * N;
   auto ld = [=](int i) { return (uint64_t)((((uint32_t)i * elt) & mask2n) >= (uint32_t)N ? 1 : 0); };
   auto st = [w](int i, uint64_t v) { w[i] = v; };
   ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
@@ -271,15 +273,18 @@ BFV_HD void ks_keyperm_item(uint64_t item, const uint64_t* keys, uint64_t* prepa
   const int sl = (int)(item & (N - 1));
   const Modulus& m = mods[p];
   const uint64_t* key = keys + r * (uint64_t)dk * 2 * k * N;
-  uint64_t* Kt = prepared + r * prepared_words;
-  uint64_t* Ct = Kt + (uint64_t)dk * 2 * k * N;
+  ulonglong2* Kt = reinterpret_cast<ulonglong2*>(prepared + r * prepared_words);
+  uint64_t* Ct = prepared + r * prepared_words + ks_ct_offset(k, dk, N);
   const int from = galois_slot(sl, ginvs[r], logn);
   const uint64_t w = Ct[(uint64_t)p * N + sl];  // NTT(neg_g), overwritten below
   for (uint32_t c = 0; c < 2; ++c) {
     uint64_t sum = 0;
     for (uint32_t j = 0; j < dk; ++j) {
       const uint64_t v = key[((uint64_t)(j * 2 + c) * k + p) * N + from];
-      Kt[((uint64_t)(j * 2 + c) * k + p) * N + sl] = v;
+      ulonglong2 kv;
+      kv.x = v;
+      kv.y = shoup_companion(v, m);
+      Kt[((uint64_t)(j * 2 + c) * k + p) * N + sl] = kv;
       sum = add_mod(sum, mul_mod(v, qjp[j * k + p], m), m.q);
     }
     Ct[((uint64_t)c * k + p) * N + sl] = mul_mod(sum, w, m);
@@ -296,16 +301,25 @@ BFV_HD void op_ks_rotate_into(const Ex& ex, uint64_t* s, uint64_t ct, uint32_t c
                               const ulonglong2* fwd, const ulonglong2* inv, const St& st) {
   constexpr int N = 1 << LOGN;
   const Modulus m = mods[p];
-  const uint64_t* Kt = prepared + ((uint64_t)c * k + p) * N;  // digit j at + j*2*k*N
+  const ulonglong2* Kt = reinterpret_cast<const ulonglong2*>(prepared) + ((uint64_t)c * k + p) * N;  // digit j: + j*2*k*N
   const uint64_t kstride = 2ull * k * N;
-  const uint64_t* Ct = prepared + (uint64_t)dk * 2 * k * N + ((uint64_t)c * k + p) * N;
+  const uint64_t* Ct = prepared + ks_ct_offset(k, dk, N) + ((uint64_t)c * k + p) * N;
   if (!zflag[ct]) {
     const uint64_t* y = Y + (ct * dk * k + p) * (uint64_t)N;  // digit j at + j*k*N
     const uint64_t ystride = (uint64_t)k * N;
+    // sum_j Y_j . Kt_j - Ct as a lazy residue in [0, 2q), the inverse transform's input range:
+    // each Shoup product lies in [0, 2q) and the running sum is folded back below 2q
     auto ld = [=](int i) {
-      Acc128 acc;
-      for (uint32_t j = 0; j < dk; ++j) acc.mac(y[j * ystride + i], Kt[j * kstride + i]);
-      return sub_mod(acc.reduce(m), Ct[i], m.q);
+      const uint64_t two_q = 2 * m.q;
+      uint64_t sum = 0;
+      for (uint32_t j = 0; j < dk; ++j) {
+        const ulonglong2 kv = Kt[j * kstride + i];
+        sum += shoup_lazy(y[j * ystride + i], kv.x, kv.y, m.q);
+        if (sum >= two_q) sum -= two_q;
+      }
+      uint64_t v = sum + m.q - Ct[i];  // in (0, 3q)
+      if (v >= two_q) v -= two_q;
+      return v;
     };
     ntt_inverse<LOGN, kMaxRadix>(ex, s, inv + ((size_t)p << LOGN), m, ld, st);
     return;
@@ -325,9 +339,10 @@ BFV_HD void op_ks_rotate_into(const Ex& ex, uint64_t* s, uint64_t ct, uint32_t c
     };
     auto stj = [s](int i, uint64_t v) { s[spad(i)] = v; };
     ntt_forward<LOGN, kMaxRadix, false>(ex, s, fwd + ((size_t)p << LOGN), m, ldj, stj);
-    const uint64_t* kj = Kt + j * kstride;
+    const ulonglong2* kj = Kt + j * kstride;
     ex.run(N, [&](int i) {
-      const uint64_t v = mul_mod(s[spad(i)], kj[i], m);
+      const ulonglong2 kv = kj[i];
+      const uint64_t v = shoup(s[spad(i)], kv.x, kv.y, m.q);
       xo[i] = j ? add_mod(xo[i], v, m.q) : v;
     });
     ex.sync();
@@ -591,16 +606,6 @@ BFV_HD void op_ntt_split(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t
   auto ld = [a](int i) { return a[i]; };
   auto st = [o](int i, uint64_t v) { o[i] = split30(v); };
   ntt_forward<LOGN, kMaxRadix>(ex, s, fwd + ((size_t)p << LOGN), m, ld, st);
-}
-
-// Shoup companion floor(v 2^64 / q) of v < q, by exact division: v 2^64 - r (r = v 2^64 mod q)
-// is a multiple of q, so the quotient is -r . q^-1 mod 2^64 (q odd).
-BFV_HD uint64_t shoup_companion(uint64_t v, const Modulus& m) {
-  const uint64_t r = reduce128(0, v, m);
-  uint64_t inv = m.q;  // q^-1 mod 2^64 by Newton's iteration (3 -> 96 correct bits)
-#pragma unroll
-  for (int it = 0; it < 5; ++it) inv *= 2 - m.q * inv;
-  return (uint64_t(0) - r) * inv;
 }
 
 // Public key prepared for the layer pipeline: pk_prep[c][p][z] = {v, floor(v 2^64 / q_p)} with

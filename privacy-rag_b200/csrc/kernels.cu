@@ -1137,7 +1137,7 @@ cudaError_t launch_ks_keyprep(const DevParams& P, const uint64_t* keys, const ui
                               uint64_t* prepared, cudaStream_t st) {
   const LaunchRange range("bfvgpu:ks_keyprep");
   if (P.k != P.dk + 1) return cudaErrorInvalidValue;
-  const uint64_t pw = (2ull * P.dk + 2) * P.k * P.n;
+  const uint64_t pw = ks_prepared_words(P.k, P.dk, P.n);
   const uint64_t kw = 2ull * P.dk * P.k * P.n;
   for (uint64_t first = 0; first < count; first += kKeyBatch) {
     const uint64_t m = count - first < (uint64_t)kKeyBatch ? count - first : (uint64_t)kKeyBatch;
@@ -1180,7 +1180,7 @@ cudaError_t launch_ks_rotate_pipe_step(const DevParams& P, const uint64_t* cts, 
                                        cudaStream_t st) {
   if (!count || r > elements) return cudaSuccess;
   if (P.k != P.dk + 1) return cudaErrorInvalidValue;
-  const uint64_t pw = (2ull * P.dk + 2) * P.k * P.n, xsw = count * 2ull * P.n;
+  const uint64_t pw = ks_prepared_words(P.k, P.dk, P.n), xsw = count * 2ull * P.n;
   const bool special = r < elements, data = r >= 1;
   const uint64_t s_blocks = special ? count * 2 : 0, blocks = s_blocks + (data ? count * 2 * P.dk : 0);
   if (!blocks) return cudaSuccess;
@@ -1217,7 +1217,7 @@ cudaError_t launch_ks_rotate_multi(const DevParams& P, const uint64_t* cts, uint
   const LaunchRange range("bfvgpu:ks_rotate_multi");
   if (!count || !elements) return cudaSuccess;
   if (P.k != P.dk + 1 || (paired && elements != count)) return cudaErrorInvalidValue;
-  const uint64_t pw = (2ull * P.dk + 2) * P.k * P.n;
+  const uint64_t pw = ks_prepared_words(P.k, P.dk, P.n);
   const uint64_t ctw = 2ull * P.dk * P.n, yw = (uint64_t)P.dk * P.k * P.n, xw = 2ull * P.k * P.n;
   for (uint64_t first = 0; first < elements; first += kKeyBatch) {
     const uint64_t m = elements - first < (uint64_t)kKeyBatch ? elements - first : (uint64_t)kKeyBatch;

@@ -6,6 +6,7 @@
 #include <cstdint>
 
 #include "arith.cuh"
+#include "layout.cuh"
 
 namespace bfvgpu {
 

@@ -1,4 +1,4 @@
-// Integer-pipe peak of the three 64-bit modular operations the BFV kernels are built from.
+// Integer-pipe peak of the 64-bit modular operations the BFV kernels are built from.
 //
 // Every transform-bearing kernel of this library is bound by the SM's integer issue rate,
 // not by HBM: a 60-bit residue product is assembled from 32-bit multiply-adds.  The roofline
@@ -11,6 +11,9 @@
 //   kind 1  multiply-accumulate: 64 x 64 -> 128-bit product added to a 128-bit sum
 //           (Acc128::mac, the key inner product and ct-pt products)
 //   kind 2  modular product: 128-bit product + Barrett reduction (mul_mod)
+//   kind 3  Shoup product by a fixed operand with its precomputed companion, made canonical
+//           (twiddle-free products of the kernels: key products, n^-1 scaling,
+//           divide-and-round by the special prime)
 // The bench times each with CUDA events and reports, per hot kernel, the time these peaks
 // would need for the kernel's algorithmic operation counts divided by its measured time.
 // Operands feed back into the chain every step, so no product is loop-invariant; every
@@ -80,11 +83,17 @@ __global__ void __launch_bounds__(kPeakThreads) k_int_peak(const Modulus* mods, 
     }
 #pragma unroll
     for (int j = 0; j < kChains; ++j) b[j] = acc[j].hi;
-  } else {
+  } else if constexpr (KIND == 2) {
 #pragma unroll 2
     for (uint32_t it = 0; it < iters; ++it) {
 #pragma unroll
       for (int j = 0; j < kChains; ++j) a[j] = mul_mod(a[j], b[j], m);
+    }
+  } else {
+#pragma unroll 2
+    for (uint32_t it = 0; it < iters; ++it) {
+#pragma unroll
+      for (int j = 0; j < kChains; ++j) a[j] = shoup(a[j], w[j & 3].x, w[j & 3].y, q);
     }
   }
   uint64_t h = 0;
@@ -104,7 +113,7 @@ int32_t int_peak(bfvgpu_ctx* ctx, int32_t kind, uint32_t blocks, uint32_t iters,
   cudaStream_t ctx_stream = nullptr;
   const DevParams* P = internal_params(ctx, &device, &ctx_stream);
   if (!P || !sink || !ops || blocks == 0) return fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
-  if (kind < 0 || kind > 2) return fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_PEAK_KIND");
+  if (kind < 0 || kind > 3) return fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_PEAK_KIND");
   if (device < 0) return fail(BFVGPU_E_DEVICE, "E_BFVGPU_HOST_ONLY_CONTEXT");
   if (P->n < 8) return fail(BFVGPU_E_CONTEXT, "E_BFVGPU_PEAK_DEGREE");
   *ops = (uint64_t)blocks * kPeakThreads * kChains * iters;
@@ -117,8 +126,10 @@ int32_t int_peak(bfvgpu_ctx* ctx, int32_t kind, uint32_t blocks, uint32_t iters,
     k_int_peak<0><<<blocks, kPeakThreads, 0, st>>>(P->mod, P->fwd, iters, sink);
   else if (kind == 1)
     k_int_peak<1><<<blocks, kPeakThreads, 0, st>>>(P->mod, P->fwd, iters, sink);
-  else
+  else if (kind == 2)
     k_int_peak<2><<<blocks, kPeakThreads, 0, st>>>(P->mod, P->fwd, iters, sink);
+  else
+    k_int_peak<3><<<blocks, kPeakThreads, 0, st>>>(P->mod, P->fwd, iters, sink);
   const cudaError_t e = cudaGetLastError();
   if (previous >= 0 && previous != device) cudaSetDevice(previous);
   if (e != cudaSuccess) return fail(BFVGPU_E_CUDA, std::string("E_BFVGPU_CUDA: int peak: ") + cudaGetErrorString(e));

@@ -250,7 +250,7 @@ int emu_keyswitch_hoisted(int logn, uint32_t k, uint32_t dk, const uint64_t* mod
   std::vector<uint64_t> qjp((size_t)dk * k);
   for (uint32_t j = 0; j < dk; ++j)
     for (uint32_t p = 0; p < k; ++p) qjp[j * k + p] = T.mods[j].q % T.mods[p].q;
-  std::vector<uint64_t> Y(count * dk * k * n), prepared((2ull * dk + 2) * k * n), x(count * 2 * k * n);
+  std::vector<uint64_t> Y(count * dk * k * n), prepared(ks_prepared_words(k, dk, n)), x(count * 2 * k * n);
   std::vector<uint32_t> zflag(count, 0);
   const uint32_t ginv = inv_mod_2n(elt, 2 * (uint32_t)n);
   EMU_DISPATCH(logn, {
@@ -285,7 +285,7 @@ int emu_keyswitch_pipe(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16
   std::vector<uint64_t> qjp((size_t)dk * k);
   for (uint32_t j = 0; j < dk; ++j)
     for (uint32_t p = 0; p < k; ++p) qjp[j * k + p] = T.mods[j].q % T.mods[p].q;
-  const uint64_t pw = (2ull * dk + 2) * k * n, kw = (uint64_t)dk * 2 * k * n, ctw = 2ull * dk * n;
+  const uint64_t pw = ks_prepared_words(k, dk, n), kw = (uint64_t)dk * 2 * k * n, ctw = 2ull * dk * n;
   std::vector<uint64_t> Y(count * dk * k * n), prepared(elements * pw), x(count * 2 * k * n), xs(2 * count * 2 * n);
   std::vector<uint32_t> zflag(count, 0);
   EMU_DISPATCH(logn, {

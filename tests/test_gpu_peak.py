@@ -44,10 +44,14 @@ def _expected(kind: int, iters: int, q: int, tw) -> list[int]:
                     acc[j] = (acc[j] + a[j] * b[j]) & ((1 << 128) - 1)
                     a[j] = acc[j] & M64
             b = [v >> 64 for v in acc]
-        else:
+        elif kind == 2:
             for _ in range(iters):
                 for j in range(CHAINS):
                     a[j] = a[j] * b[j] % q
+        else:
+            for _ in range(iters):
+                for j in range(CHAINS):
+                    a[j] = a[j] * tw[j & 3][0] % q
         h = 0
         for j in range(CHAINS):
             h ^= (a[j] * 0x9E3779B97F4A7C15 + b[j]) & M64
@@ -55,7 +59,7 @@ def _expected(kind: int, iters: int, q: int, tw) -> list[int]:
     return out
 
 
-@pytest.mark.parametrize("kind", [0, 1, 2])
+@pytest.mark.parametrize("kind", [0, 1, 2, 3])
 def test_int_peak_checksums(bfv, oracle, kind):
     import torch
     if not torch.cuda.is_available():
