@@ -1040,8 +1040,8 @@ def main():
                     help="ART-002 legs: split each n = 16384 limb between a 2-block cluster (1) or one block (0)")
     ap.add_argument("--ks-pipe", type=int, default=1,
                     help="headline: software-pipelined rotations (1) or one rotate + finish launch pair per element (0)")
-    ap.add_argument("--decode-graphs", type=int, default=1,
-                    help="config-5 decode: replay each call as a captured CUDA graph (0: issue eagerly)")
+    ap.add_argument("--decode-graphs", type=int, default=0,
+                    help="config-5 decode: replay each call as a captured CUDA graph (measured no faster at 1 and 2 GPUs)")
     ap.add_argument("--protect-ahead", type=int, default=1,
                     help="config-5 decode: prepare each call's Enc(0) and mask term during the previous call")
     ap.add_argument("--slots", type=int, default=1, help="0 skips the slot-packed matvec leg (config 3)")
