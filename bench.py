@@ -202,14 +202,16 @@ def traffic_record(path: str):
 
 
 # ---- integer roofline -------------------------------------------------------------------------
-PEAK_KINDS = {0: "butterfly", 1: "mac", 2: "modmul", 3: "shoup"}
+PEAK_KINDS = {0: "butterfly", 1: "mac", 2: "modmul", 3: "shoup", 4: "butterfly_f64", 5: "mulmod_f64"}
 
 
 def measure_int_peaks(torch, ctx, reps: int = 5):
     """Operations per second of the integer operations the kernels are built from
     (bfvgpu_int_peak_device: butterfly, 64x64->128 multiply-accumulate, Barrett modular
-    product, Shoup product by a fixed operand), each from registers at full occupancy, timed
-    with CUDA events on the context stream (3 warm-up launches, then `reps`)."""
+    product, Shoup product by a fixed operand; and on the FP64 pipe the butterfly and the
+    product by a fixed operand for primes < 2^50), each from registers at full occupancy, timed
+    with CUDA events on the context stream (3 warm-up launches, then `reps`).  `ctx`'s first
+    prime is below 2^50 (config 2)."""
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     blocks, iters = sms * 16, 4096
     sink = torch.empty(blocks * 256, dtype=torch.int64, device="cuda")
@@ -239,23 +241,37 @@ def int_roofline(counts: dict, rates: dict, seconds: float) -> dict:
             "measured_ms": seconds * 1e3, "frac": at_peak / seconds}
 
 
-def ks_pair_counts(cts: int, n: int, k: int, dk: int) -> dict:
-    """Integer operations of one element's hoisted rotation over `cts` ciphertexts, by the kind
-    the kernels execute: per (ciphertext, component, key-level prime) and coefficient the key
-    inner product of dk Shoup products (each key word carries its companion), the inverse NTT
-    (n/2 log n butterflies per limb) and its scaling by n^-1 (a Shoup product); per
+def _zero_counts() -> dict:
+    return {key: 0 for key in PEAK_KINDS.values()}
+
+
+def ks_pair_counts(cts: int, n: int, k: int, dk: int, fp64: bool) -> dict:
+    """Modular operations of one element's hoisted rotation over `cts` ciphertexts, by the kind
+    and pipe the kernels execute: per (ciphertext, component, key-level prime) and coefficient
+    the key inner product of dk products by a fixed operand (each key word carries its
+    companion), the inverse NTT (n/2 log n butterflies per limb) and its scaling by n^-1; per
     (ciphertext, component, data prime) and coefficient the divide-and-round by the special
-    prime (a Shoup product)."""
+    prime (a product by a fixed operand).  With fp64 the data primes (< 2^50) run these on the
+    FP64 pipe and the special prime on the integer pipe."""
     logn = n.bit_length() - 1
-    limbs = cts * 2 * k
-    return {"butterfly": limbs * (n // 2) * logn, "mac": 0, "modmul": 0,
-            "shoup": limbs * n * dk + limbs * n + cts * 2 * dk * n}
+    data, special = cts * 2 * dk, cts * 2 * (k - dk)
+    c = _zero_counts()
+    bf, prod = ("butterfly_f64", "mulmod_f64") if fp64 else ("butterfly", "shoup")
+    c["butterfly"] += special * (n // 2) * logn
+    c["shoup"] += special * n * dk + special * n
+    c[bf] += data * (n // 2) * logn
+    c[prod] += data * n * dk + data * n + data * n
+    return c
 
 
-def ntt_counts(polys: int, n: int, inverse: bool) -> dict:
-    """Butterflies of a batch of transforms, and the inverse's scaling by n^-1 (Shoup)."""
+def ntt_counts(polys: int, n: int, inverse: bool, fp64: bool) -> dict:
+    """Butterflies of a batch of transforms, and the inverse's scaling by n^-1 (a product by a
+    fixed operand), on the pipe the kernels use."""
     logn = n.bit_length() - 1
-    return {"butterfly": polys * (n // 2) * logn, "mac": 0, "modmul": 0, "shoup": polys * n if inverse else 0}
+    c = _zero_counts()
+    c["butterfly_f64" if fp64 else "butterfly"] = polys * (n // 2) * logn
+    c["mulmod_f64" if fp64 else "shoup"] = polys * n if inverse else 0
+    return c
 
 
 def headline_config(world: int, rotations: int) -> dict:
@@ -450,6 +466,7 @@ def run_slots_leg(torch, bfvgpu, device, args):
     import bfvgpu.slots as S
     primes = bfvgpu.find_primes(N2, BITS2)
     ctx = bfvgpu.Context(N2, primes, 4, 1, T2, device=device)
+    ctx.set_fp64(bool(args.fp64))
     pc = bfvgpu.Context(N2, [T2], 1, 0, 2, device=device)
     lay = S.SlotLayout(N2, 1024, 2048, T2)
     baby, giant = lay.steps
@@ -1038,6 +1055,8 @@ def main():
                     help="config 5 with N > 1: SMs the persistent product kernels leave to NCCL")
     ap.add_argument("--limb-split", type=int, default=1,
                     help="ART-002 legs: split each n = 16384 limb between a 2-block cluster (1) or one block (0)")
+    ap.add_argument("--fp64", type=int, default=1,
+                    help="configs 1-3: primes below 2^50 compute on the FP64 pipe (1) or the integer pipe (0)")
     ap.add_argument("--ks-pipe", type=int, default=1,
                     help="headline: software-pipelined rotations (1) or one rotate + finish launch pair per element (0)")
     ap.add_argument("--decode-graphs", type=int, default=0,
@@ -1097,6 +1116,8 @@ def main():
 
     primes2 = bfvgpu.find_primes(N2, BITS2)
     ctx = bfvgpu.Context(N2, primes2, 4, 1, T2, device=local)
+    fp64 = bool(args.fp64)
+    ctx.set_fp64(fp64)
     stream = torch.cuda.ExternalStream(ctx.stream())
     g = torch.Generator(device="cuda")
     g.manual_seed(1234)  # the same job on every rank: each rank takes a range of its rotations
@@ -1215,7 +1236,7 @@ def main():
         ks_traffic, ks_traffic_note = None, "recorded for the pipelined kernel only"
     # ---- integer roofline: this GPU's measured rates of the kernels' integer operations ----
     int_rates = measure_int_peaks(torch, ctx)
-    ks_int = int_roofline(ks_pair_counts(CTS, N2, 5, 4), int_rates, avg_launch)
+    ks_int = int_roofline(ks_pair_counts(CTS, N2, 5, 4, fp64), int_rates, avg_launch)
 
     # ---- secondary: ct-pt matvec (config 3) and one decoder layer (config 4), ART-002 ----
     layer_res = run_layer_legs(torch, bfvgpu, local, args) if args.layer else None
@@ -1226,6 +1247,7 @@ def main():
     # ---- secondary: NTT round trips (config 1) ----
     primes1 = bfvgpu.find_primes(N1, BITS1)
     ctx1 = bfvgpu.Context(N1, primes1, 3, 0, T2, device=local)
+    ctx1.set_fp64(fp64)
     s1 = torch.cuda.ExternalStream(ctx1.stream())
     reps = max(1, args.ntt_reps)
     ntt_data = uniform((NTT_POLYS // 3, 3, N1), primes1).contiguous()
@@ -1248,7 +1270,7 @@ def main():
     ntt_launch_s = ntt_dt / (2 * reps)
     ntt_bytes = NTT_POLYS * N1 * 8 * 2
     ntt_ok = bool(torch.equal(big[0], ntt_data))
-    ntt_cnt = {key: (ntt_counts(NTT_POLYS, N1, False)[key] + ntt_counts(NTT_POLYS, N1, True)[key]) / 2
+    ntt_cnt = {key: (ntt_counts(NTT_POLYS, N1, False, fp64)[key] + ntt_counts(NTT_POLYS, N1, True, fp64)[key]) / 2
                for key in PEAK_KINDS.values()}
     ntt_int = int_roofline(ntt_cnt, int_rates, ntt_launch_s)
 
@@ -1273,7 +1295,7 @@ def main():
     torch.cuda.synchronize()
     dt8 = a8.elapsed_time(b8) / 1e3
     launch8 = dt8 / (2 * reps8)
-    cnt8 = {key: (ntt_counts(polys8, N2, False)[key] + ntt_counts(polys8, N2, True)[key]) / 2
+    cnt8 = {key: (ntt_counts(polys8, N2, False, fp64)[key] + ntt_counts(polys8, N2, True, fp64)[key]) / 2
             for key in PEAK_KINDS.values()}
     ntt8 = {"value": reps8 * 2 * polys8 / dt8, "unit": "NTTs/s",
             "config": "n=8192, config-2 data primes (4 x 50-bit), 2048 limb-polys fwd+inv per round trip",
@@ -1382,10 +1404,14 @@ def main():
                                 if args.ks_pipe else "per-rotation launches k_ks_rotate + k_ks_finish (256 cts)"),
                      "alg_bytes_per_launch": alg_bytes_launch, "avg_launch_ms": avg_launch * 1e3,
                      "int_frac": ks_int["frac"], "int": ks_int, "int_peaks_per_s": int_rates,
+                     "arithmetic": ("FP64 pipe for the 50-bit data primes, integer pipe for the 60-bit special "
+                                    "prime" if fp64 else "integer pipe for every prime"),
                      "int_peak_source": "measured in this run: bfvgpu_int_peak_device (register-resident "
-                                        "butterfly / 64x64->128 MAC / Barrett product, full occupancy)",
-                     "note": "integer-pipe bound (int_frac): 2k=10 inverse NTTs of n=8192 per keyswitch after "
-                             "hoisting; the HBM fraction is low by construction"},
+                                        "butterfly / 64x64->128 MAC / Barrett / Shoup product on the integer "
+                                        "pipe, butterfly / fixed-operand product on the FP64 pipe; full occupancy)",
+                     "note": "arithmetic-pipe bound (int_frac, time at the measured per-pipe rates over the "
+                             "measured time): 2k=10 inverse NTTs of n=8192 per keyswitch after hoisting; the HBM "
+                             "fraction is low by construction"},
         "secondary": {"keyswitch_per_apply": {"value": plain_value, "unit": "keyswitches/s",
                                               "path": "bfvgpu_keyswitch_device (no hoisting, Switch::apply)",
                                               "avg_launch_ms": 1e3 * sum(plain_per) / len(plain_per),

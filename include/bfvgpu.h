@@ -176,8 +176,10 @@ int32_t bfvgpu_keyswitch_device_noalloc(bfvgpu_ctx *ctx, const uint64_t *cts, ui
  * independent chains at full occupancy -- kind 0 = NTT butterfly (Harvey lazy, Shoup
  * twiddle of prime 0), 1 = 64x64 -> 128-bit multiply-accumulate, 2 = modular product
  * (128-bit product + Barrett reduction by prime 0), 3 = Shoup product by a fixed operand
- * with its companion, made canonical.  blocks x 256 threads; *ops receives
- * the operations performed (blocks * 256 * 8 chains * iters); sink [blocks * 256] (device)
+ * with its companion, made canonical; on the FP64 pipe (prime 0 below 2^50, else
+ * BFVGPU_E_CONTEXT): 4 = NTT butterfly (two per step, one centred reduction per step),
+ * 5 = product by a fixed operand.  blocks x 256 threads; *ops receives the operations
+ * performed (blocks * 256 * 8 chains * iters, twice that for kind 4); sink [blocks * 256] (device)
  * one checksum word per thread.  Timed by the caller (CUDA events) to give this GPU's
  * operation rates, the denominators of the integer roofline. */
 int32_t bfvgpu_int_peak_device(bfvgpu_ctx *ctx, int32_t kind, uint32_t blocks, uint32_t iters, uint64_t *sink,
@@ -213,6 +215,13 @@ int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx *ctx, int32_t path);
  * a limb per block, three blocks per SM, the cross level through distributed shared memory;
  * split = 0, one block holds the whole limb (one block per SM).  Results are identical. */
 int32_t bfvgpu_ctx_set_limb_split(bfvgpu_ctx *ctx, int32_t split);
+/* Arithmetic of the primes below 2^50 (configs with 36- to 50-bit primes): on = 1 (default),
+ * the transforms and products that have an FP64 form (batched NTTs, Galois keyswitch
+ * rotations and their key preparation) compute on the FP64 pipe with exact integer-valued
+ * doubles; on = 0, everything computes on the integer pipe.  Results are identical.
+ * Prepared keys are laid out for the mode they were prepared in, so the mode is fixed once
+ * the context has prepared keys: changing it then fails with BFVGPU_E_STATE. */
+int32_t bfvgpu_ctx_set_fp64(bfvgpu_ctx *ctx, int32_t on);
 /* Words of device scratch bfvgpu_matrix_tiles_device needs for tiles * groups outputs:
  * items * (k + 2 + 2 dk) * n with Enc(0) (enc0 != 0), items * 2 dk * n for a mask alone. */
 uint64_t bfvgpu_matrix_tiles_scratch_words(const bfvgpu_ctx *ctx, uint64_t tiles, uint64_t groups,

@@ -72,6 +72,7 @@ _SIGNATURES = {
     "bfvgpu_keyswitch_device_noalloc": (I32, [VP, VP, U64, VP, U32, VP, VP]),
     "bfvgpu_int_peak_device": (I32, [VP, I32, U32, U32, VP, U64P, VP]),
     "bfvgpu_ctx_set_limb_split": (I32, [VP, I32]),
+    "bfvgpu_ctx_set_fp64": (I32, [VP, I32]),
     "bfvgpu_keyswitch_rotate_many_scratch_words": (U64, [VP, U64]),
     "bfvgpu_keyswitch_rotate_many_device": (I32, [VP, VP, U64, VP, VP, U32P, U64, VP, ctypes.POINTER(VP), VP]),
     "bfvgpu_protect_scratch_words": (U64, [VP, U64]),

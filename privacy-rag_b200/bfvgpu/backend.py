@@ -125,9 +125,10 @@ class Context:
                                             self._dptr(scratch), self._dptr(out), stream), "keyswitch_device")
 
     def int_peak_device(self, kind: int, blocks: int, iters: int, sink, stream: int | None = None) -> int:
-        """Launch the integer-pipe peak kernel of `kind` (0 butterfly, 1 multiply-accumulate,
-        2 Barrett modular product, 3 Shoup product); returns the operations it performs.  sink:
-        blocks * 256 words."""
+        """Launch the peak kernel of `kind` (integer pipe: 0 butterfly, 1 multiply-accumulate,
+        2 Barrett modular product, 3 Shoup product; FP64 pipe, prime 0 < 2^50: 4 butterfly,
+        5 product by a fixed operand); returns the operations it performs.  sink: blocks * 256
+        words."""
         ops = U64(0)
         check(lib().bfvgpu_int_peak_device(self._h, kind, blocks, iters, self._dptr(sink), ctypes.byref(ops),
                                            stream), "int_peak_device")
@@ -227,6 +228,12 @@ class Context:
         """n = 16384 single-transform kernels: split each limb between the two blocks of a
         cluster (True, the default) or one block per limb (False).  Results are identical."""
         check(lib().bfvgpu_ctx_set_limb_split(self._h, int(bool(split))), "set_limb_split")
+
+    def set_fp64(self, on: bool) -> None:
+        """Primes below 2^50: compute the transforms and rotations that have an FP64 form on
+        the FP64 pipe (True, the default) or on the integer pipe (False).  Results are
+        identical; fixed once the context has prepared keys (BFVGPU_E_STATE)."""
+        check(lib().bfvgpu_ctx_set_fp64(self._h, int(bool(on))), "set_fp64")
 
     def set_product_path(self, path: int) -> None:
         """0: tcgen05 product for 8-tile launches (default); 1: TMA-staged CUDA-core product only;

@@ -36,7 +36,12 @@ struct Modulus {
   uint64_t inv_special, inv_special_q;  // q_special^-1 mod q (data primes), Shoup pair
   uint64_t half_special_mod;            // floor(q_special/2) mod q
   uint64_t delta, delta_q;              // floor(Q/t) mod q (data primes), Shoup pair
-  uint64_t pad[6];
+  // FP64-pipe constants (f64mod.cuh), set for primes below 2^50 when the context computes on
+  // that pipe (f64 != 0); doubles are centred residues with their quotients fl(v / q)
+  uint64_t f64;
+  double f64_qinv;                      // fl(1/q)
+  double f64_invn, f64_invn_q;          // n^-1
+  double f64_inv_special, f64_inv_special_q;  // q_special^-1 (data primes)
 };
 static_assert(sizeof(Modulus) == 128, "Modulus is one 128-byte line");
 

@@ -22,6 +22,7 @@
 #include "bfvgpu.h"
 #include "ctx_internal.h"
 #include "kernels.cuh"
+#include "ntt_core.cuh"
 
 using u128 = unsigned __int128;
 
@@ -148,8 +149,14 @@ struct Context {
   int logn = 0;
   uint64_t t = 0;
   std::vector<uint64_t> q;
-  std::vector<Modulus> mods;
+  std::vector<Modulus> mods;           // integer-pipe records (f64 = 0)
+  std::vector<Modulus> mods_f64;       // the same with the FP64 constants of primes < 2^50
   std::vector<uint64_t> fwd_h, inv_h;  // [k][n][2]
+  std::vector<double> fwd64_h, inv64_h;  // [k][n][2]
+  bool use_f64 = true;                 // primes < 2^50 compute on the FP64 pipe
+  const Modulus* dmod_int = nullptr;   // device copies of mods / mods_f64
+  const Modulus* dmod_f64 = nullptr;
+  uint64_t keys_prepared = 0;          // key preparations issued (fixes the arithmetic mode)
   cudaStream_t stream = nullptr;
   cudaStream_t aux = nullptr;                     // side stream for independent work of one call
   cudaEvent_t fork = nullptr, join = nullptr;     // ordering between a caller's stream and aux
@@ -260,6 +267,19 @@ static void build_context(Context& c, uint32_t n, const uint64_t* primes, uint32
       pw = mulmod_h(pw, psi_inv, qp);
     }
   }
+  // FP64-pipe constants and twiddles (used for the primes below 2^50)
+  c.mods_f64 = c.mods;
+  c.fwd64_h.assign((size_t)c.k * n * 2, 0.0);
+  c.inv64_h.assign((size_t)c.k * n * 2, 0.0);
+  for (uint32_t p = 0; p < c.k; ++p) {
+    f64_fill_modulus(c.mods_f64[p]);
+    if (!c.mods_f64[p].f64) continue;
+    const size_t at = (size_t)p * n;
+    f64_twiddles(reinterpret_cast<const ulonglong2*>(c.fwd_h.data()) + at, c.q[p], n,
+                 reinterpret_cast<double2*>(c.fwd64_h.data()) + at);
+    f64_twiddles(reinterpret_cast<const ulonglong2*>(c.inv_h.data()) + at, c.q[p], n,
+                 reinterpret_cast<double2*>(c.inv64_h.data()) + at);
+  }
   // q_j mod q_p
   std::vector<uint64_t> qjp((size_t)dk * c.k);
   for (uint32_t j = 0; j < dk; ++j)
@@ -314,7 +334,7 @@ static void build_context(Context& c, uint32_t n, const uint64_t* primes, uint32
   const size_t qjp_bytes = qjp.size() * 8, part_bytes = part.size() * 8, cinv_bytes = cinv.size() * 8,
                q_bytes = dk * 8;
   auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
-  const size_t total = up(mod_bytes) + 2 * up(tab_bytes) + up(qjp_bytes) + up(part_bytes) + up(cinv_bytes) +
+  const size_t total = 2 * up(mod_bytes) + 4 * up(tab_bytes) + up(qjp_bytes) + up(part_bytes) + up(cinv_bytes) +
                        up(q_bytes) + up(kErrBytes);
   cuda_check(cudaMalloc(&c.dmem, total), "cudaMalloc(tables)");
   char* base = (char*)c.dmem;
@@ -325,9 +345,13 @@ static void build_context(Context& c, uint32_t n, const uint64_t* primes, uint32
     off += up(bytes);
     return dst;
   };
-  c.P.mod = (const Modulus*)place(c.mods.data(), mod_bytes);
+  c.dmod_int = (const Modulus*)place(c.mods.data(), mod_bytes);
+  c.dmod_f64 = (const Modulus*)place(c.mods_f64.data(), mod_bytes);
+  c.P.mod = c.use_f64 ? c.dmod_f64 : c.dmod_int;
   c.P.fwd = (const ulonglong2*)place(c.fwd_h.data(), tab_bytes);
   c.P.inv = (const ulonglong2*)place(c.inv_h.data(), tab_bytes);
+  c.P.fwd64 = (const double2*)place(c.fwd64_h.data(), tab_bytes);
+  c.P.inv64 = (const double2*)place(c.inv64_h.data(), tab_bytes);
   c.P.qjp = (const uint64_t*)place(qjp.data(), qjp_bytes);
   c.P.crt_part = (const uint64_t*)place(part.data(), part_bytes);
   c.P.crt_inv = (const uint64_t*)place(cinv.data(), cinv_bytes);
@@ -655,7 +679,7 @@ int32_t bfvgpu_ctx_tables(const bfvgpu_ctx* ctx, uint32_t prime, uint64_t* fwd, 
 int32_t bfvgpu_ctx_moduli(const bfvgpu_ctx* ctx, uint32_t prime, uint64_t* out) {
   return guard([&] {
     if (!ctx || !out || prime >= ctx->c.k) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
-    std::memcpy(out, &ctx->c.mods[prime], sizeof(Modulus));
+    std::memcpy(out, ctx->c.use_f64 ? &ctx->c.mods_f64[prime] : &ctx->c.mods[prime], sizeof(Modulus));
   });
 }
 
@@ -718,6 +742,7 @@ int32_t bfvgpu_keyswitch_prepare_device(bfvgpu_ctx* ctx, const uint64_t* keys, c
       if (!(galois_elts[r] & 1) || galois_elts[r] >= 2 * ctx->c.n) fail(BFVGPU_E_ELEMENT, "E_BFVGPU_GALOIS_ELEMENT");
     require_device(ctx->c);
     DeviceScope scope(ctx->c.device);
+    ++ctx->c.keys_prepared;
     cuda_check(launch_ks_keyprep(ctx->c.P, keys, galois_elts, count, prepared, pick(ctx, stream)), "keyprep");
     count_launch(2 * ((count + 255) / 256));
   });
@@ -831,6 +856,16 @@ int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx* ctx, int32_t path) {
   return guard([&] {
     if (!ctx || path < 0 || path > 2) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
     ctx->c.P.product_path = path;
+  });
+}
+
+int32_t bfvgpu_ctx_set_fp64(bfvgpu_ctx* ctx, int32_t on) {
+  return guard([&] {
+    if (!ctx || on < 0 || on > 1) fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
+    Context& c = ctx->c;
+    if ((on != 0) != c.use_f64 && c.keys_prepared) fail(BFVGPU_E_STATE, "E_BFVGPU_ARITH_STATE");
+    c.use_f64 = on != 0;
+    if (c.device >= 0) c.P.mod = c.use_f64 ? c.dmod_f64 : c.dmod_int;
   });
 }
 
@@ -1484,6 +1519,7 @@ int32_t bfvgpu_rotations_open(bfvgpu_ctx* ctx, const uint64_t* keys, const uint3
       for (uint64_t first = 0; first < count; first += kBatch) {
         const uint64_t m = count - first < kBatch ? count - first : kBatch;
         s->h.h2d(tmp, keys + first * kw, m * kw);
+        ++ctx->c.keys_prepared;
         cuda_check(launch_ks_keyprep(c.P, tmp, s->elts.data() + first, m, s->prepared + first * s->pw, c.stream),
                    "keyprep");
         count_launch(2);
@@ -1624,6 +1660,7 @@ int32_t bfvgpu_slots_open(bfvgpu_ctx* ctx, const uint64_t* keys, uint32_t baby, 
       for (uint64_t first = 0; first < nkeys; first += kBatch) {
         const uint64_t m = nkeys - first < kBatch ? nkeys - first : kBatch;
         s->h.h2d(tmp, keys + first * kw, m * kw);
+        ++ctx->c.keys_prepared;
         cuda_check(launch_ks_keyprep(c.P, tmp, s->elts.data() + first, m, s->prepared + first * s->pw, c.stream),
                    "keyprep");
         count_launch(2);
@@ -2029,4 +2066,5 @@ const DevParams* internal_params(const bfvgpu_ctx* ctx, int* device, cudaStream_
 }
 void internal_set_error(const std::string& what) { g_last_error = what; }
 void internal_count_launch(uint64_t n) { count_launch(n); }
+uint64_t internal_first_prime(const bfvgpu_ctx* ctx) { return ctx && !ctx->c.q.empty() ? ctx->c.q[0] : 0; }
 }  // namespace bfvgpu

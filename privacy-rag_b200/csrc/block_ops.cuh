@@ -35,6 +35,32 @@ BFV_HD uint64_t ldro(const uint64_t* p) {
   return *p;
 #endif
 }
+BFV_HD ulonglong2 ldro_pair(const ulonglong2* p) {
+#if defined(__CUDA_ARCH__)
+  return __ldg(p);
+#else
+  return *p;
+#endif
+}
+BFV_HD double2 ldro2(const double2* p) {
+#if defined(__CUDA_ARCH__)
+  return __ldg(p);
+#else
+  return *p;
+#endif
+}
+
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2,
+// issued by one thread of the block; the block's demand loads of that range then hit L2
+// instead of waiting a DRAM round trip each.  No effect on the host.
+BFV_HD void block_prefetch_l2(const void* p, uint32_t bytes) {
+#if defined(__CUDA_ARCH__)
+  if (threadIdx.x == 0) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+#else
+  (void)p;
+  (void)bytes;
+#endif
+}
 
 
 // Divide-and-round by the special prime q_s (last prime) of one coefficient:
@@ -54,12 +80,26 @@ struct ProtectArgs {
 };
 
 // ---- batched transform: block = one poly -----------------------------------------------
+// Primes whose record has f64 set transform on the FP64 pipe (one limb per block only).
 template <int LOGN, class Ex>
 BFV_HD void op_ntt(const Ex& ex, uint64_t* s, uint64_t blk, bool inverse, uint64_t* data, uint32_t prime_count,
-                   uint32_t prime_offset, const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv) {
+                   uint32_t prime_offset, const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv,
+                   const double2* fwd64, const double2* inv64) {
   const uint32_t p = prime_offset + (uint32_t)(blk % prime_count);
   const Modulus m = mods[p];
   uint64_t* a = data + (blk << LOGN);
+  if constexpr (!Ex::kSplit) {
+    if (m.f64) {
+      const F64Prime fp = f64_prime(m);
+      auto ldf = [a](int i) { return u64_to_f64(a[i]); };
+      auto stf = [a, fp](int i, double v) { a[i] = canon_f64(v, fp.q, fp.qinv); };
+      if (inverse)
+        ntt_inverse_f64<LOGN, kMaxRadix>(ex, s, inv64 + ((size_t)p << LOGN), m, ldf, stf);
+      else
+        ntt_forward_f64<LOGN, kMaxRadix>(ex, s, fwd64 + ((size_t)p << LOGN), m, ldf, stf);
+      return;
+    }
+  }
   auto ld = [a](int i) { return a[i]; };
   auto st = [a](int i, uint64_t v) { a[i] = v; };
   if (inverse)
@@ -246,7 +286,8 @@ BFV_HD void op_ks_hoist(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t*
 
 // Key preparation for a batch of keys, in two kernels, into the prepared layout of
 // layout.cuh: Kt as {key word, Shoup companion} pairs (so the rotation's key product is one
-// lazy Shoup multiplication per digit), then Ct.
+// lazy Shoup multiplication per digit) -- for a prime whose record has f64 set, as the bit
+// patterns of {centred key word, fl(word / q)}, the operand pair of mulmod_f64 -- then Ct.
 // (1) block (r, p): W = NTT_p(neg_g) written to Ct[c = 0][p] of key r.
 template <int LOGN, class Ex>
 BFV_HD void op_ks_negntt(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t* prepared, uint64_t prepared_words,
@@ -282,8 +323,19 @@ BFV_HD void ks_keyperm_item(uint64_t item, const uint64_t* keys, uint64_t* prepa
     for (uint32_t j = 0; j < dk; ++j) {
       const uint64_t v = key[((uint64_t)(j * 2 + c) * k + p) * N + from];
       ulonglong2 kv;
-      kv.x = v;
-      kv.y = shoup_companion(v, m);
+      if (m.f64) {
+        const double vc = centred_f64(v, m.q);
+#if defined(__CUDA_ARCH__)
+        const double vq = __ddiv_rn(vc, u64_to_f64(m.q));
+#else
+        const double vq = vc / (double)m.q;
+#endif
+        kv.x = f64_bits(vc);
+        kv.y = f64_bits(vq);
+      } else {
+        kv.x = v;
+        kv.y = shoup_companion(v, m);
+      }
       Kt[((uint64_t)(j * 2 + c) * k + p) * N + sl] = kv;
       sum = add_mod(sum, mul_mod(v, qjp[j * k + p], m), m.q);
     }
@@ -291,22 +343,183 @@ BFV_HD void ks_keyperm_item(uint64_t item, const uint64_t* keys, uint64_t* prepa
   }
 }
 
-// One rotation for (ct, c, p): st(i, v) receives INTT(A_c)[i].  Ciphertexts flagged in
-// zflag take the exact path: A_c accumulated from fresh pre-negated digit transforms in
-// the global scratch x [ct][2][k][n], then transformed.
-template <int LOGN, class Ex, class St>
+// The FP64 form of op_ks_rotate_into for one prime below 2^50 (Kd: its {centred key word,
+// quotient} pairs).  Hoisted: sum_j Y_j . Kt_j - Ct as a representative (at most 0.75 q per
+// product; folded every four digits so it stays below 4q) staged into shared memory, then the
+// FP64 inverse transform.  Zero-word ciphertexts: per digit the FP64 forward transform of the
+// pre-negated digit, its product with Kt_j accumulated canonically in x, then the inverse.
+template <int LOGN, class Ex, class StF>
+BFV_HD void op_ks_rotate_into_f64(const Ex& ex, uint64_t* s, uint64_t ct, uint32_t c, uint32_t p, const uint64_t* cts,
+                                  const uint64_t* Y, const uint32_t* zflag, const double2* Kd, uint64_t kstride,
+                                  const uint64_t* Ct, uint64_t* x, uint32_t elt, uint32_t k, uint32_t dk,
+                                  const Modulus* mods, const uint64_t* qjp, const double2* fwd64,
+                                  const double2* inv64, const StF& stf) {
+  constexpr int N = 1 << LOGN;
+  const Modulus m = mods[p];
+  const F64Prime fp = f64_prime(m);
+  const double2* tinv = inv64 + ((size_t)p << LOGN);
+  double* d = reinterpret_cast<double*>(s);
+  if (!zflag[ct]) {
+    const uint64_t* y = Y + (ct * dk * k + p) * (uint64_t)N;  // digit j at + j*k*N
+    const uint64_t ystride = (uint64_t)k * N;
+    // Stage the transform's input with every operand load issued well before the products
+    // that consume it: the loads (digits, key pairs, correction) are the latency this step
+    // waits on, and occupancy is capped by registers.  dk = 4: four coefficients (i + r n/4)
+    // per call in two interleaved streams, the next coefficient's loads in flight during each
+    // product.  Otherwise two coefficients (i, i + n/2) per call.
+    if (dk == 4) {
+      struct Ops {
+        uint64_t ct, y[4];
+        double2 k[4];
+      };
+      auto load = [&](int i, Ops& o) {
+        o.ct = ldro(Ct + i);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          o.y[j] = ldro(y + j * ystride + i);
+          o.k[j] = ldro2(Kd + j * kstride + i);
+        }
+      };
+      auto finish = [&](int i, const Ops& o) {
+        double sum = -u64_to_f64(o.ct);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sum = f64_add(sum, mulmod_f64(u64_to_f64(o.y[j]), o.k[j].x, o.k[j].y, fp.q));
+        d[spad(i)] = sum;
+      };
+      ex.run(N / 4, [&](int u) {
+        Ops a, b;
+        load(u, a);
+        load(u + N / 4, b);
+        finish(u, a);
+        load(u + N / 2, a);
+        finish(u + N / 4, b);
+        load(u + 3 * N / 4, b);
+        finish(u + N / 2, a);
+        finish(u + 3 * N / 4, b);
+      });
+    } else {
+      ex.run(N / 2, [&](int i0) {
+        const int i1 = i0 + N / 2;
+        double s0 = -u64_to_f64(ldro(Ct + i0)), s1 = -u64_to_f64(ldro(Ct + i1));
+        for (uint32_t j = 0; j < dk; ++j) {
+          const double2 a = ldro2(Kd + j * kstride + i0), b = ldro2(Kd + j * kstride + i1);
+          s0 = f64_add(s0, mulmod_f64(u64_to_f64(ldro(y + j * ystride + i0)), a.x, a.y, fp.q));
+          s1 = f64_add(s1, mulmod_f64(u64_to_f64(ldro(y + j * ystride + i1)), b.x, b.y, fp.q));
+          if ((j & 3) == 3 && j + 1 < dk) {
+            s0 = reduce_f64(s0, fp.q, fp.qinv);
+            s1 = reduce_f64(s1, fp.q, fp.qinv);
+          }
+        }
+        d[spad(i0)] = s0;
+        d[spad(i1)] = s1;
+      });
+    }
+    ex.sync();
+    auto from_smem = [d](int i) { return d[spad(i)]; };
+    ntt_inverse_f64<LOGN, kMaxRadix, false>(ex, s, tinv, m, from_smem, stf);
+    return;
+  }
+  uint64_t* xo = x + ((ct * 2 + c) * k + p) * (uint64_t)N;
+  const uint64_t* c1 = cts + (ct * 2 * dk + dk) * (uint64_t)N;
+  const uint32_t mask2n = 2u * N - 1u;
+  for (uint32_t j = 0; j < dk; ++j) {
+    const uint64_t* src = c1 + (uint64_t)j * N;
+    const uint64_t adj = qjp[j * k + p];
+    const bool reduce = mods[j].q > m.q;
+    auto ldj = [=](int i) {
+      const uint64_t xv = src[i];
+      uint64_t yv = reduce ? reduce64(xv, m) : xv;
+      if (xv && (((uint32_t)i * elt) & mask2n) >= (uint32_t)N) yv = sub_mod(yv, adj, m.q);
+      return u64_to_f64(yv);
+    };
+    auto stj = [d](int i, double v) { d[spad(i)] = v; };
+    ntt_forward_f64<LOGN, kMaxRadix, false>(ex, s, fwd64 + ((size_t)p << LOGN), m, ldj, stj);
+    const double2* kj = Kd + j * kstride;
+    ex.run(N, [&](int i) {
+      const double2 kv = kj[i];
+      const uint64_t v = canon_f64(mulmod_f64(d[spad(i)], kv.x, kv.y, fp.q), fp.q, fp.qinv);
+      xo[i] = j ? add_mod(xo[i], v, m.q) : v;
+    });
+    ex.sync();
+  }
+  auto ldx = [xo](int i) { return u64_to_f64(xo[i]); };
+  ntt_inverse_f64<LOGN, kMaxRadix>(ex, s, tinv, m, ldx, stf);
+}
+
+// One rotation for (ct, c, p): st(i, v) receives INTT(A_c)[i] (canonical); for a prime whose
+// record has f64 set the transforms and products run on the FP64 pipe and stf(i, v) receives
+// it instead, as a representative |v| <= 0.75 q.  Ciphertexts flagged in zflag take the
+// exact path: A_c accumulated from fresh pre-negated digit transforms in the global scratch
+// x [ct][2][k][n], then transformed.
+template <int LOGN, class Ex, class St, class StF>
 BFV_HD void op_ks_rotate_into(const Ex& ex, uint64_t* s, uint64_t ct, uint32_t c, uint32_t p, const uint64_t* cts,
                               const uint64_t* Y, const uint32_t* zflag, const uint64_t* prepared, uint64_t* x,
                               uint32_t elt, uint32_t k, uint32_t dk, const Modulus* mods, const uint64_t* qjp,
-                              const ulonglong2* fwd, const ulonglong2* inv, const St& st) {
+                              const ulonglong2* fwd, const ulonglong2* inv, const double2* fwd64,
+                              const double2* inv64, const St& st, const StF& stf) {
   constexpr int N = 1 << LOGN;
   const Modulus m = mods[p];
   const ulonglong2* Kt = reinterpret_cast<const ulonglong2*>(prepared) + ((uint64_t)c * k + p) * N;  // digit j: + j*2*k*N
   const uint64_t kstride = 2ull * k * N;
   const uint64_t* Ct = prepared + ks_ct_offset(k, dk, N) + ((uint64_t)c * k + p) * N;
-  if (!zflag[ct]) {
+  const bool hoisted = !zflag[ct];
+  // the block's hoisted digits stream from DRAM once per element: start them all into L2
+  if (hoisted)
+    for (uint32_t j = 0; j < dk; ++j) block_prefetch_l2(Y + ((ct * dk + j) * k + p) * (uint64_t)N, N * 8);
+  if constexpr (!Ex::kSplit) {
+    if (m.f64) {
+      op_ks_rotate_into_f64<LOGN>(ex, s, ct, c, p, cts, Y, zflag, reinterpret_cast<const double2*>(Kt), kstride, Ct,
+                                  x, elt, k, dk, mods, qjp, fwd64, inv64, stf);
+      return;
+    }
+  }
+  if (hoisted) {
     const uint64_t* y = Y + (ct * dk * k + p) * (uint64_t)N;  // digit j at + j*k*N
     const uint64_t ystride = (uint64_t)k * N;
+    if (dk == 4) {
+      // as in the FP64 form: four coefficients per call in two interleaved streams, each
+      // coefficient's operand loads in flight during the previous one's products; the sum
+      // is a lazy residue in [0, 2q), the inverse transform's input range
+      struct Ops {
+        uint64_t ct, y[4];
+        ulonglong2 k[4];
+      };
+      auto load = [&](int i, Ops& o) {
+        o.ct = ldro(Ct + i);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          o.y[j] = ldro(y + j * ystride + i);
+          o.k[j] = ldro_pair(Kt + j * kstride + i);
+        }
+      };
+      const uint64_t q = m.q, two_q = 2 * m.q;
+      auto finish = [&](int i, const Ops& o) {
+        uint64_t sum = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sum += shoup_lazy(o.y[j], o.k[j].x, o.k[j].y, q);
+          if (sum >= two_q) sum -= two_q;
+        }
+        uint64_t v = sum + q - o.ct;
+        if (v >= two_q) v -= two_q;
+        s[spad(i)] = v;
+      };
+      ex.run(N / 4, [&](int u) {
+        Ops a, b;
+        load(u, a);
+        load(u + N / 4, b);
+        finish(u, a);
+        load(u + N / 2, a);
+        finish(u + N / 4, b);
+        load(u + 3 * N / 4, b);
+        finish(u + N / 2, a);
+        finish(u + 3 * N / 4, b);
+      });
+      ex.sync();
+      auto from_smem = [s](int i) { return s[spad(i)]; };
+      ntt_inverse<LOGN, kMaxRadix, false>(ex, s, inv + ((size_t)p << LOGN), m, from_smem, st);
+      return;
+    }
     // sum_j Y_j . Kt_j - Ct as a lazy residue in [0, 2q), the inverse transform's input range:
     // each Shoup product lies in [0, 2q) and the running sum is folded back below 2q
     auto ld = [=](int i) {
@@ -356,12 +569,15 @@ template <int LOGN, class Ex>
 BFV_HD void op_ks_rotate(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t* cts, const uint64_t* Y,
                          const uint32_t* zflag, const uint64_t* prepared, uint64_t* x, uint32_t elt, uint32_t k,
                          uint32_t dk, const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd,
-                         const ulonglong2* inv) {
+                         const ulonglong2* inv, const double2* fwd64, const double2* inv64) {
   const uint64_t ct = blk / (2 * k);
   const uint32_t cp = (uint32_t)(blk % (2 * k)), c = cp / k, p = cp % k;
   uint64_t* xo = x + ((ct * 2 + c) * k + p) * ((uint64_t)1 << LOGN);
   auto st = [xo](int i, uint64_t v) { xo[i] = v; };
-  op_ks_rotate_into<LOGN>(ex, s, ct, c, p, cts, Y, zflag, prepared, x, elt, k, dk, mods, qjp, fwd, inv, st);
+  const F64Prime fp = f64_prime(mods[p]);
+  auto stf = [xo, fp](int i, double v) { xo[i] = canon_f64(v, fp.q, fp.qinv); };
+  op_ks_rotate_into<LOGN>(ex, s, ct, c, p, cts, Y, zflag, prepared, x, elt, k, dk, mods, qjp, fwd, inv, fwd64, inv64,
+                          st, stf);
 }
 
 // out [ct][2][dk][n] = sigma_g(moddown(x_c) + [c=0] c0).  Block (ct, data prime p); the
@@ -410,14 +626,18 @@ BFV_HD void op_ks_rotate_pipe(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t 
                               const uint64_t* Y, const uint32_t* zflag, uint64_t* x, const uint64_t* prep_s,
                               uint32_t elt_s, uint64_t* xs_w, const uint64_t* prep_d, uint32_t elt_d, uint32_t ginv_d,
                               const uint64_t* xs_r, uint64_t* out_d, uint32_t k, uint32_t dk, const Modulus* mods,
-                              const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv) {
+                              const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv, const double2* fwd64,
+                              const double2* inv64) {
   constexpr int N = 1 << LOGN;
   if (blk < s_blocks) {
     const uint64_t ct = blk >> 1;
     const uint32_t c = (uint32_t)(blk & 1);
     uint64_t* xo = xs_w + (ct * 2 + c) * (uint64_t)N;
     auto st = [xo](int i, uint64_t v) { xo[i] = v; };
-    op_ks_rotate_into<LOGN>(ex, s, ct, c, k - 1, cts, Y, zflag, prep_s, x, elt_s, k, dk, mods, qjp, fwd, inv, st);
+    const F64Prime fs = f64_prime(mods[k - 1]);
+    auto stf = [xo, fs](int i, double v) { xo[i] = canon_f64(v, fs.q, fs.qinv); };
+    op_ks_rotate_into<LOGN>(ex, s, ct, c, k - 1, cts, Y, zflag, prep_s, x, elt_s, k, dk, mods, qjp, fwd, inv, fwd64,
+                            inv64, st, stf);
     return;
   }
   const uint64_t d = blk - s_blocks;
@@ -426,12 +646,29 @@ BFV_HD void op_ks_rotate_pipe(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t 
   const Modulus m = mods[p], ms = mods[k - 1];
   const uint64_t* xs = xs_r + (ct * 2 + c) * (uint64_t)N;
   const uint64_t* c0 = cts + (ct * 2 * dk + p) * (uint64_t)N;
+  block_prefetch_l2(xs, N * 8);  // the finish's operands, read in the transform's last pass
+  if (c == 0) block_prefetch_l2(c0, N * 8);
   auto st = [=](int i, uint64_t v) {
     uint64_t w = moddown_elem(v, ldro(xs + i), m, ms);
     if (c == 0) w = add_mod(w, ldro(c0 + i), m.q);
     s[spad(i)] = w;  // the last pass writes only the words it read: in place
   };
-  op_ks_rotate_into<LOGN>(ex, s, ct, c, p, cts, Y, zflag, prep_d, x, elt_d, k, dk, mods, qjp, fwd, inv, st);
+  // FP64 form of the same finish: (v - corr) . q_s^-1 (+ c0), corr from the special-prime limb
+  // on the integer pipe (|v - corr| < 1.75 q, the sum with c0 below 1.75 q), made canonical
+  const F64Prime fp = f64_prime(m);
+  const uint64_t qs = ms.q, qp = m.q, r1 = m.r1;  // reduce64 needs q and the 64-bit ratio only
+  const double half_s = u64_to_f64(m.half_special_mod), isp = m.f64_inv_special, isp_q = m.f64_inv_special_q;
+  auto stf = [=](int i, double v) {
+    const uint64_t last = add_mod(ldro(xs + i), qs >> 1, qs);
+    uint64_t lastp = last - mulhi64(last, r1) * qp;
+    if (lastp >= qp) lastp -= qp;
+    const double corr = f64_sub(u64_to_f64(lastp), half_s);
+    double w = mulmod_f64(f64_sub(v, corr), isp, isp_q, fp.q);
+    if (c == 0) w = f64_add(w, u64_to_f64(ldro(c0 + i)));
+    s[spad(i)] = canon_f64(w, fp.q, fp.qinv);  // in place, as above
+  };
+  op_ks_rotate_into<LOGN>(ex, s, ct, c, p, cts, Y, zflag, prep_d, x, elt_d, k, dk, mods, qjp, fwd, inv, fwd64, inv64,
+                          st, stf);
   uint64_t* o = out_d + ((ct * 2 + c) * dk + p) * (uint64_t)N;
   const uint32_t mask2n = 2u * N - 1u;
   const uint64_t q = m.q;

@@ -16,4 +16,6 @@ const DevParams* internal_params(const bfvgpu_ctx* ctx, int* device, cudaStream_
 void internal_set_error(const std::string& what);
 // Adds to the process-wide launch counter of bfvgpu_launch_count().
 void internal_count_launch(uint64_t n);
+// The context's first prime (0 for a null context).
+uint64_t internal_first_prime(const bfvgpu_ctx* ctx);
 }  // namespace bfvgpu

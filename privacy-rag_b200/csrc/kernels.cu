@@ -62,9 +62,9 @@ constexpr size_t smem_bytes() {
 template <int LOGN, bool INV>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_ntt(uint64_t* data, uint32_t prime_count, uint32_t prime_offset, const Modulus* mods, const ulonglong2* fwd,
-          const ulonglong2* inv) {
+          const ulonglong2* inv, const double2* fwd64, const double2* inv64) {
   extern __shared__ uint64_t smem[];
-  op_ntt<LOGN>(BlockExec{}, smem, blockIdx.x, INV, data, prime_count, prime_offset, mods, fwd, inv);
+  op_ntt<LOGN>(BlockExec{}, smem, blockIdx.x, INV, data, prime_count, prime_offset, mods, fwd, inv, fwd64, inv64);
 }
 
 template <int LOGN>
@@ -669,7 +669,8 @@ template <bool INV>
 __global__ void BFV_PAIR_BOUNDS k_ntt_pair(uint64_t* data, uint32_t prime_count, uint32_t prime_offset,
                                            const Modulus* mods, const ulonglong2* fwd, const ulonglong2* inv) {
   extern __shared__ uint64_t smem[];
-  op_ntt<kPairLogN>(ClusterPairExec{}, smem, blockIdx.x >> 1, INV, data, prime_count, prime_offset, mods, fwd, inv);
+  op_ntt<kPairLogN>(ClusterPairExec{}, smem, blockIdx.x >> 1, INV, data, prime_count, prime_offset, mods, fwd, inv,
+                    nullptr, nullptr);
 }
 __global__ void BFV_PAIR_BOUNDS k_lift_ntt_pair(const uint64_t* ring, uint64_t* out, uint32_t dk, const Modulus* mods,
                                                 const ulonglong2* fwd) {
@@ -724,9 +725,10 @@ template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_ks_rotate(const uint64_t* cts, const uint64_t* Y, const uint32_t* zflag, const uint64_t* prepared, uint64_t* x,
                 uint32_t elt, uint32_t k, uint32_t dk, const Modulus* mods, const uint64_t* qjp,
-                const ulonglong2* fwd, const ulonglong2* inv) {
+                const ulonglong2* fwd, const ulonglong2* inv, const double2* fwd64, const double2* inv64) {
   extern __shared__ uint64_t smem[];
-  op_ks_rotate<LOGN>(BlockExec{}, smem, blockIdx.x, cts, Y, zflag, prepared, x, elt, k, dk, mods, qjp, fwd, inv);
+  op_ks_rotate<LOGN>(BlockExec{}, smem, blockIdx.x, cts, Y, zflag, prepared, x, elt, k, dk, mods, qjp, fwd, inv, fwd64,
+                     inv64);
 }
 
 template <int LOGN>
@@ -744,10 +746,11 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_ks_rotate_pipe(const uint64_t* cts, uint64_t s_blocks, const uint64_t* Y, const uint32_t* zflag, uint64_t* x,
                      const uint64_t* prep_s, uint32_t elt_s, uint64_t* xs_w, const uint64_t* prep_d, uint32_t elt_d,
                      uint32_t ginv_d, const uint64_t* xs_r, uint64_t* out_d, uint32_t k, uint32_t dk,
-                     const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv) {
+                     const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv,
+                     const double2* fwd64, const double2* inv64) {
   extern __shared__ uint64_t smem[];
   op_ks_rotate_pipe<LOGN>(BlockExec{}, smem, blockIdx.x, s_blocks, cts, Y, zflag, x, prep_s, elt_s, xs_w, prep_d,
-                          elt_d, ginv_d, xs_r, out_d, k, dk, mods, qjp, fwd, inv);
+                          elt_d, ginv_d, xs_r, out_d, k, dk, mods, qjp, fwd, inv, fwd64, inv64);
 }
 
 // Hoisted rotations of many (element, ciphertext) pairs in one launch pair.  paired != 0:
@@ -759,13 +762,13 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_ks_rotate_multi(const uint64_t* cts, uint64_t count, const uint64_t* Y, const uint32_t* zflag,
                       const uint64_t* prepared, uint64_t prepared_words, EltBatch eb, int paired, uint64_t* x,
                       uint32_t k, uint32_t dk, const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd,
-                      const ulonglong2* inv) {
+                      const ulonglong2* inv, const double2* fwd64, const double2* inv64) {
   extern __shared__ uint64_t smem[];
   const uint64_t per = paired ? 2ull * k : count * 2 * k;
   const uint64_t e = blockIdx.x / per, blk = paired ? blockIdx.x : blockIdx.x % per;
   uint64_t* xe = paired ? x : x + ((e * count * 2 * k) << LOGN);
   op_ks_rotate<LOGN>(BlockExec{}, smem, blk, cts, Y, zflag, prepared + e * prepared_words, xe, eb.elt[e], k, dk, mods,
-                     qjp, fwd, inv);
+                     qjp, fwd, inv, fwd64, inv64);
 }
 
 template <int LOGN>
@@ -1048,10 +1051,10 @@ cudaError_t launch_ntt(const DevParams& P, uint64_t* data, uint64_t polys, uint3
   BFV_DISPATCH(P.logn, {
     if (inverse)
       k_ntt<L_, true><<<(unsigned)polys, threads_for<L_>(), smem_bytes<L_>(), st>>>(data, prime_count, prime_offset,
-                                                                                 P.mod, P.fwd, P.inv);
+                                                                                 P.mod, P.fwd, P.inv, P.fwd64, P.inv64);
     else
       k_ntt<L_, false><<<(unsigned)polys, threads_for<L_>(), smem_bytes<L_>(), st>>>(data, prime_count, prime_offset,
-                                                                                  P.mod, P.fwd, P.inv);
+                                                                                  P.mod, P.fwd, P.inv, P.fwd64, P.inv64);
   });
   return cudaGetLastError();
 }
@@ -1167,7 +1170,7 @@ cudaError_t launch_ks_rotate(const DevParams& P, const uint64_t* cts, uint64_t c
   const uint32_t ginv = inverse_mod_2n(elt, 2 * P.n);
   BFV_DISPATCH(P.logn, {
     k_ks_rotate<L_><<<(unsigned)(count * 2 * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(
-        cts, Y, zflag, prepared, x, elt, P.k, P.dk, P.mod, P.qjp, P.fwd, P.inv);
+        cts, Y, zflag, prepared, x, elt, P.k, P.dk, P.mod, P.qjp, P.fwd, P.inv, P.fwd64, P.inv64);
     k_ks_finish<L_><<<(unsigned)(count * P.dk), threads_for<L_>(), (size_t(1) << L_) * 8, st>>>(x, cts, out, ginv,
                                                                                                P.k, P.dk, P.mod);
   });
@@ -1193,7 +1196,7 @@ cudaError_t launch_ks_rotate_pipe_step(const DevParams& P, const uint64_t* cts, 
   BFV_DISPATCH(P.logn, {
     k_ks_rotate_pipe<L_><<<(unsigned)blocks, threads_for<L_>(), smem_bytes<L_>(), st>>>(
         cts, s_blocks, Y, zflag, x, prep_s, elt_s, xs_w, prep_d, elt_d, ginv_d, xs_r, data ? out_d : nullptr, P.k,
-        P.dk, P.mod, P.qjp, P.fwd, P.inv);
+        P.dk, P.mod, P.qjp, P.fwd, P.inv, P.fwd64, P.inv64);
   });
   return cudaGetLastError();
 }
@@ -1237,7 +1240,8 @@ cudaError_t launch_ks_rotate_multi(const DevParams& P, const uint64_t* cts, uint
     if (rot_blocks > 0x7fffffffull) return cudaErrorInvalidValue;
     BFV_DISPATCH(P.logn, {
       k_ks_rotate_multi<L_><<<(unsigned)rot_blocks, threads_for<L_>(), smem_bytes<L_>(), st>>>(
-          cp, cn, yp, zp, prepared + first * pw, pw, eb, paired, xp, P.k, P.dk, P.mod, P.qjp, P.fwd, P.inv);
+          cp, cn, yp, zp, prepared + first * pw, pw, eb, paired, xp, P.k, P.dk, P.mod, P.qjp, P.fwd, P.inv,
+          P.fwd64, P.inv64);
       k_ks_finish_multi<L_><<<(unsigned)fin_blocks, threads_for<L_>(), (size_t(1) << L_) * 8, st>>>(
           xp, cp, cn, op, eb, paired, P.k, P.dk, P.mod);
     });

@@ -22,6 +22,8 @@ struct DevParams {
   const Modulus* mod = nullptr;       // [k]
   const ulonglong2* fwd = nullptr;    // [k][n]
   const ulonglong2* inv = nullptr;    // [k][n]
+  const double2* fwd64 = nullptr;     // [k][n] FP64 twiddles {w_c, fl(w_c / q)} of fwd / inv, used by
+  const double2* inv64 = nullptr;     // the primes whose record has f64 set (f64mod.cuh)
   const uint64_t* qjp = nullptr;      // [dk][k]: q_j mod q_p
   const uint64_t* crt_part = nullptr; // [dk][dk] limbs of Q/q_j
   const uint64_t* crt_inv = nullptr;  // [dk][2] Shoup pair of (Q/q_j)^-1 mod q_j

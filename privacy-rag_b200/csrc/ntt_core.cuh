@@ -21,6 +21,7 @@
 // index arithmetic also runs on the host (tests/emu) against the CPU oracle.
 #pragma once
 #include "arith.cuh"
+#include "f64mod.cuh"
 
 #if defined(__CUDACC__)
 #include <cooperative_groups.h>
@@ -28,6 +29,9 @@
 #if !defined(__CUDACC__)
 struct ulonglong2 {
   unsigned long long x, y;
+};
+struct double2 {
+  double x, y;
 };
 #endif
 
@@ -450,6 +454,178 @@ BFV_HD void ntt_inverse(const Ex& ex, uint64_t* s, const ulonglong2* tw, const M
     inv_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, m.invn, m.invn_q, from_smem, st);
   } else {
     inv_passes<LOGN, MAXR, 0>(ex, s, tw, m.q, m.invn, m.invn_q, ld, st);
+  }
+}
+
+// ---- the same transforms on the FP64 pipe (primes below 2^50, f64mod.cuh) -----------------
+// Shared memory holds integer-valued doubles (centred representatives) in place of words;
+// twiddle tables hold {w_c, fl(w_c / q)} with w_c the centred twiddle (f64_twiddles), at the
+// integer tables' indices.  Bounds (q < 2^50): a product is at most 0.75 q whatever its input
+// (below 2^52).  Forward: each pass first reduces its level-0 upper inputs to |v| <= (q+1)/2
+// (the lower inputs only enter products), so after a radix-2^R pass |v| <= (0.5 + 0.75 R) q + 1,
+// below 4q for R <= 4.  Inverse: each pass reduces all its inputs to |v| <= (q+1)/2; a level at
+// most doubles the sums, so after a radix-8 pass |v| <= 4q + 4 < 2^52 and every product input
+// stays in range.  All sums stay below 2^53, so every operation is exact and the canonical
+// results equal the integer transforms' word for word.
+struct F64Prime {
+  double q, qinv;
+};
+BFV_HD F64Prime f64_prime(const Modulus& m) { return F64Prime{u64_to_f64(m.q), m.f64_qinv}; }
+
+// Twiddle load on the read-only path (no kernel writes the tables), which lets the compiler
+// issue it ahead of the shared-memory stores of the previous unit.
+BFV_HD double2 ldg_tw(const double2* p) {
+#if defined(__CUDA_ARCH__)
+  return __ldg(p);
+#else
+  return *p;
+#endif
+}
+
+// Host setup: the FP64 twiddle table {w_c, fl(w_c / q)} of an integer table {w, w'} (n entries).
+inline void f64_twiddles(const ulonglong2* tw, uint64_t q, size_t n, double2* out) {
+  const double qd = (double)q;
+  for (size_t i = 0; i < n; ++i) {
+    out[i].x = centred_f64(tw[i].x, q);
+    out[i].y = out[i].x / qd;
+  }
+}
+
+template <int LOGN, int R, bool FIRST, bool LAST, class Ld, class St>
+BFV_HD void fwd_unit_f64(double* s, int u, int L, const double2* tw, F64Prime fp, const Ld& ld, const St& st) {
+  constexpr int K = 1 << R;
+  const int shift = LOGN - L - R;
+  const int o = u & ((1 << shift) - 1), gl = u >> shift;
+  const int base = (gl << (LOGN - L)) + o, sbase = spad(base);
+  double x[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    if constexpr (FIRST)
+      x[k] = ld(base + (k << shift));
+    else
+      x[k] = s[spad_unit(base, sbase, k << shift)];
+  }
+#pragma unroll
+  for (int t = 0; t < R; ++t) {
+    const int hs = R - t - 1;
+#pragma unroll
+    for (int pr = 0; pr < K / 2; ++pr) {
+      const int jj = pr >> hs, kk = pr & ((1 << hs) - 1);
+      const int k = (jj << (hs + 1)) + kk;
+      const double2 w = ldg_tw(tw + (1 << (L + t)) + (gl << t) + jj);
+      double a = x[k];
+      if (t == 0) a = reduce_f64(a, fp.q, fp.qinv);
+      const double b = mulmod_f64(x[k + (1 << hs)], w.x, w.y, fp.q);
+      x[k] = f64_add(a, b);
+      x[k + (1 << hs)] = f64_sub(a, b);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    if constexpr (LAST)
+      st(base + (k << shift), x[k]);
+    else
+      s[spad_unit(base, sbase, k << shift)] = x[k];
+  }
+}
+
+template <int LOGN, int R, bool FIRST, bool LAST, class Ld, class St>
+BFV_HD void inv_unit_f64(double* s, int u, int L, const double2* tw, F64Prime fp, double invn, double invn_q,
+                         const Ld& ld, const St& st) {
+  static_assert(R <= 3, "inverse FP64 passes are at most radix 8 (sums grow 2x per level)");
+  constexpr int K = 1 << R;
+  constexpr int N = 1 << LOGN;
+  const int o = u & ((1 << L) - 1), gg = u >> L;
+  const int base = (gg << (L + R)) + o, sbase = spad(base);
+  double x[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const double v = FIRST ? ld(base + (k << L)) : s[spad_unit(base, sbase, k << L)];
+    x[k] = reduce_f64(v, fp.q, fp.qinv);
+  }
+#pragma unroll
+  for (int t = 0; t < R; ++t) {
+    const int l = L + t;
+#pragma unroll
+    for (int pr = 0; pr < K / 2; ++pr) {
+      const int jj = pr >> t, kk = pr & ((1 << t) - 1);
+      const int k = (jj << (t + 1)) + kk;
+      const double2 w = ldg_tw(tw + N - (N >> l) + 1 + (gg << (R - t - 1)) + jj);
+      const double a = x[k], b = x[k + (1 << t)];
+      x[k] = f64_add(a, b);
+      x[k + (1 << t)] = mulmod_f64(f64_sub(a, b), w.x, w.y, fp.q);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    if constexpr (LAST)
+      st(base + (k << L), mulmod_f64(x[k], invn, invn_q, fp.q));
+    else
+      s[spad_unit(base, sbase, k << L)] = x[k];
+  }
+}
+
+template <int LOGN, int MAXR, int P, class Ex, class Ld, class St>
+BFV_HD void fwd_passes_f64(const Ex& ex, double* s, const double2* tw, F64Prime fp, const Ld& ld, const St& st) {
+  using S = Schedule<LOGN, MAXR>;
+  if constexpr (P < S::passes) {
+    constexpr int R = S::fwd_r(P);
+    constexpr int L = S::fwd_level(P);
+    ex.run(1 << (LOGN - R), [&](int u) { fwd_unit_f64<LOGN, R, P == 0, P == S::passes - 1>(s, u, L, tw, fp, ld, st); });
+    ex.sync();
+    fwd_passes_f64<LOGN, MAXR, P + 1>(ex, s, tw, fp, ld, st);
+  }
+}
+template <int LOGN, int MAXR, int P, class Ex, class Ld, class St>
+BFV_HD void inv_passes_f64(const Ex& ex, double* s, const double2* tw, F64Prime fp, double invn, double invn_q,
+                           const Ld& ld, const St& st) {
+  using S = Schedule<LOGN, MAXR>;
+  if constexpr (P < S::passes) {
+    constexpr int R = S::inv_r(P);
+    constexpr int L = S::inv_level(P);
+    ex.run(1 << (LOGN - R),
+           [&](int u) { inv_unit_f64<LOGN, R, P == 0, P == S::passes - 1>(s, u, L, tw, fp, invn, invn_q, ld, st); });
+    ex.sync();
+    inv_passes_f64<LOGN, MAXR, P + 1>(ex, s, tw, fp, invn, invn_q, ld, st);
+  }
+}
+
+// Forward NTT of one limb on the FP64 pipe: ld(i) gives input coefficient i as a double with
+// |v| < 2^52 (any representative), st(i, v) receives NTT slot i as a representative with
+// |v| < 4q (canon_f64 makes it canonical).  STAGE_OUT as for ntt_forward.  Ends with a
+// block-wide barrier.  s: the block's shared words, reused as doubles.
+template <int LOGN, int MAXR = 3, bool STAGE_OUT = true, class Ex, class Ld, class St>
+BFV_HD void ntt_forward_f64(const Ex& ex, uint64_t* s, const double2* tw, const Modulus& m, const Ld& ld,
+                            const St& st) {
+  static_assert(!Ex::kSplit, "FP64 transforms run one limb per block");
+  double* d = reinterpret_cast<double*>(s);
+  const F64Prime fp = f64_prime(m);
+  if constexpr (STAGE_OUT) {
+    auto to_smem = [d](int i, double v) { d[spad(i)] = v; };
+    fwd_passes_f64<LOGN, MAXR, 0>(ex, d, tw, fp, ld, to_smem);
+    ex.run(1 << LOGN, [&](int i) { st(i, d[spad(i)]); });
+    ex.sync();
+  } else {
+    fwd_passes_f64<LOGN, MAXR, 0>(ex, d, tw, fp, ld, st);
+  }
+}
+
+// Inverse NTT of one limb on the FP64 pipe: ld(i) gives NTT slot i as a double with
+// |v| < 2^52, st(i, v) receives coefficient i times n^-1 as a representative with
+// |v| <= 0.75 q.  STAGE_IN as for ntt_inverse.  Ends with a block-wide barrier.
+template <int LOGN, int MAXR = 3, bool STAGE_IN = true, class Ex, class Ld, class St>
+BFV_HD void ntt_inverse_f64(const Ex& ex, uint64_t* s, const double2* tw, const Modulus& m, const Ld& ld,
+                            const St& st) {
+  static_assert(!Ex::kSplit, "FP64 transforms run one limb per block");
+  double* d = reinterpret_cast<double*>(s);
+  const F64Prime fp = f64_prime(m);
+  if constexpr (STAGE_IN) {
+    ex.run(1 << LOGN, [&](int i) { d[spad(i)] = ld(i); });
+    ex.sync();
+    auto from_smem = [d](int i) { return d[spad(i)]; };
+    inv_passes_f64<LOGN, MAXR, 0>(ex, d, tw, fp, m.f64_invn, m.f64_invn_q, from_smem, st);
+  } else {
+    inv_passes_f64<LOGN, MAXR, 0>(ex, d, tw, fp, m.f64_invn, m.f64_invn_q, ld, st);
   }
 }
 

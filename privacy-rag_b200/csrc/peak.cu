@@ -14,6 +14,10 @@
 //   kind 3  Shoup product by a fixed operand with its precomputed companion, made canonical
 //           (twiddle-free products of the kernels: key products, n^-1 scaling,
 //           divide-and-round by the special prime)
+//   kind 4  NTT butterfly on the FP64 pipe (f64mod.cuh, primes < 2^50): two Cooley-Tukey
+//           butterflies per step with one centred reduction, the mix of a radix-8 pass
+//           (a product, an add and a subtract per butterfly, one reduction per two)
+//   kind 5  product by a fixed operand on the FP64 pipe (mulmod_f64)
 // The bench times each with CUDA events and reports, per hot kernel, the time these peaks
 // would need for the kernel's algorithmic operation counts divided by its measured time.
 // Operands feed back into the chain every step, so no product is loop-invariant; every
@@ -27,6 +31,7 @@
 
 #include "bfvgpu.h"
 #include "ctx_internal.h"
+#include "f64mod.cuh"
 #include "kernels.cuh"
 #include "ntt_core.cuh"
 
@@ -89,11 +94,50 @@ __global__ void __launch_bounds__(kPeakThreads) k_int_peak(const Modulus* mods, 
 #pragma unroll
       for (int j = 0; j < kChains; ++j) a[j] = mul_mod(a[j], b[j], m);
     }
-  } else {
+  } else if constexpr (KIND == 3) {
 #pragma unroll 2
     for (uint32_t it = 0; it < iters; ++it) {
 #pragma unroll
       for (int j = 0; j < kChains; ++j) a[j] = shoup(a[j], w[j & 3].x, w[j & 3].y, q);
+    }
+  } else {
+    const double qd = (double)q, qinv = __ddiv_rn(1.0, qd);
+    double wc[4], wq[4], fa[kChains], fb[kChains];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      wc[k] = centred_f64(w[k].x, q);
+      wq[k] = __ddiv_rn(wc[k], qd);
+    }
+#pragma unroll
+    for (int j = 0; j < kChains; ++j) {
+      fa[j] = u64_to_f64(a[j]);
+      fb[j] = u64_to_f64(b[j]);
+    }
+    if constexpr (KIND == 4) {
+      // |a| <= q/2 after the reduction, then |a|, |b| <= 1.25 q and 2 q: inside mulmod's range
+#pragma unroll 2
+      for (uint32_t it = 0; it < iters; ++it) {
+#pragma unroll
+        for (int j = 0; j < kChains; ++j) {
+          const double x = reduce_f64(fa[j], qd, qinv);
+          const double t = mulmod_f64(fb[j], wc[j & 3], wq[j & 3], qd);
+          const double x1 = f64_add(x, t), y1 = f64_sub(x, t);
+          const double t2 = mulmod_f64(y1, wc[j & 3], wq[j & 3], qd);
+          fa[j] = f64_add(x1, t2);
+          fb[j] = f64_sub(x1, t2);
+        }
+      }
+    } else {
+#pragma unroll 2
+      for (uint32_t it = 0; it < iters; ++it) {
+#pragma unroll
+        for (int j = 0; j < kChains; ++j) fa[j] = mulmod_f64(fa[j], wc[j & 3], wq[j & 3], qd);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kChains; ++j) {
+      a[j] = canon_f64(fa[j], qd, qinv);
+      b[j] = canon_f64(fb[j], qd, qinv);
     }
   }
   uint64_t h = 0;
@@ -113,10 +157,11 @@ int32_t int_peak(bfvgpu_ctx* ctx, int32_t kind, uint32_t blocks, uint32_t iters,
   cudaStream_t ctx_stream = nullptr;
   const DevParams* P = internal_params(ctx, &device, &ctx_stream);
   if (!P || !sink || !ops || blocks == 0) return fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_ARGUMENT");
-  if (kind < 0 || kind > 3) return fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_PEAK_KIND");
+  if (kind < 0 || kind > 5) return fail(BFVGPU_E_ARGUMENT, "E_BFVGPU_PEAK_KIND");
   if (device < 0) return fail(BFVGPU_E_DEVICE, "E_BFVGPU_HOST_ONLY_CONTEXT");
   if (P->n < 8) return fail(BFVGPU_E_CONTEXT, "E_BFVGPU_PEAK_DEGREE");
-  *ops = (uint64_t)blocks * kPeakThreads * kChains * iters;
+  if (kind >= 4 && internal_first_prime(ctx) >= kF64MaxPrime) return fail(BFVGPU_E_CONTEXT, "E_BFVGPU_PEAK_PRIME");
+  *ops = (uint64_t)blocks * kPeakThreads * kChains * iters * (kind == 4 ? 2 : 1);
   int previous = -1;
   if (cudaGetDevice(&previous) != cudaSuccess) previous = -1;
   if (previous != device && cudaSetDevice(device) != cudaSuccess)
@@ -128,8 +173,12 @@ int32_t int_peak(bfvgpu_ctx* ctx, int32_t kind, uint32_t blocks, uint32_t iters,
     k_int_peak<1><<<blocks, kPeakThreads, 0, st>>>(P->mod, P->fwd, iters, sink);
   else if (kind == 2)
     k_int_peak<2><<<blocks, kPeakThreads, 0, st>>>(P->mod, P->fwd, iters, sink);
-  else
+  else if (kind == 3)
     k_int_peak<3><<<blocks, kPeakThreads, 0, st>>>(P->mod, P->fwd, iters, sink);
+  else if (kind == 4)
+    k_int_peak<4><<<blocks, kPeakThreads, 0, st>>>(P->mod, P->fwd, iters, sink);
+  else
+    k_int_peak<5><<<blocks, kPeakThreads, 0, st>>>(P->mod, P->fwd, iters, sink);
   const cudaError_t e = cudaGetLastError();
   if (previous >= 0 && previous != device) cudaSetDevice(previous);
   if (e != cudaSuccess) return fail(BFVGPU_E_CUDA, std::string("E_BFVGPU_CUDA: int peak: ") + cudaGetErrorString(e));

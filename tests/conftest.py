@@ -47,9 +47,9 @@ def emu(built_lib):
     here = os.path.join(ROOT, "tests", "emu")
     out = os.path.join(here, "libemu.so")
     src = os.path.join(here, "emu.cpp")
-    deps = [src] + [os.path.join(PKG, "csrc", f) for f in ("arith.cuh", "layout.cuh", "ntt_core.cuh", "block_ops.cuh")]
+    deps = [src] + [os.path.join(PKG, "csrc", f) for f in ("arith.cuh", "f64mod.cuh", "layout.cuh", "ntt_core.cuh", "block_ops.cuh")]
     if not os.path.exists(out) or any(os.path.getmtime(d) > os.path.getmtime(out) for d in deps):
-        subprocess.run(["/usr/bin/g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-x", "c++",
+        subprocess.run(["/usr/bin/g++", "-O2", "-std=c++17", "-ffp-contract=off", "-shared", "-fPIC", "-x", "c++",
                         "-I", os.path.join(PKG, "csrc"), src, "-o", out], check=True)
     return ctypes.CDLL(out)
 

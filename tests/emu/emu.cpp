@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "block_ops.cuh"
+#include "f64mod.cuh"
 #include "mac_tc.cuh"
 
 using namespace bfvgpu;
@@ -21,13 +22,26 @@ struct Tabs {
   std::vector<Modulus> mods;
   const ulonglong2* fwd;
   const ulonglong2* inv;
+  std::vector<double2> fwd64_v, inv64_v;  // FP64 twiddles of the primes with f64 set
+  const double2* fwd64 = nullptr;
+  const double2* inv64 = nullptr;
 };
-Tabs tabs(uint32_t k, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv) {
+Tabs tabs(uint32_t k, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv, int logn) {
   Tabs t;
   t.mods.resize(k);
   std::memcpy(t.mods.data(), mods16, k * sizeof(Modulus));
   t.fwd = reinterpret_cast<const ulonglong2*>(fwd);
   t.inv = reinterpret_cast<const ulonglong2*>(inv);
+  const size_t n = size_t(1) << logn;
+  t.fwd64_v.assign(k * n, double2{0.0, 0.0});
+  t.inv64_v.assign(k * n, double2{0.0, 0.0});
+  for (uint32_t p = 0; p < k; ++p) {
+    if (!t.mods[p].f64) continue;
+    f64_twiddles(t.fwd + p * n, t.mods[p].q, n, t.fwd64_v.data() + p * n);
+    f64_twiddles(t.inv + p * n, t.mods[p].q, n, t.inv64_v.data() + p * n);
+  }
+  t.fwd64 = t.fwd64_v.data();
+  t.inv64 = t.inv64_v.data();
   return t;
 }
 uint32_t inv_mod_2n(uint32_t g, uint32_t two_n) {
@@ -193,11 +207,12 @@ extern "C" {
 
 int emu_ntt(int logn, uint32_t k, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv, uint64_t* data,
             uint64_t polys, uint32_t prime_count, uint32_t prime_offset, int inverse) {
-  Tabs T = tabs(k, mods16, fwd, inv);
+  Tabs T = tabs(k, mods16, fwd, inv, logn);
   EMU_DISPATCH(logn, {
     std::vector<uint64_t> s(SmemWords<L_>::value);
     for (uint64_t b = 0; b < polys; ++b)
-      op_ntt<L_>(HostExec{}, s.data(), b, inverse != 0, data, prime_count, prime_offset, T.mods.data(), T.fwd, T.inv);
+      op_ntt<L_>(HostExec{}, s.data(), b, inverse != 0, data, prime_count, prime_offset, T.mods.data(), T.fwd, T.inv,
+                 T.fwd64, T.inv64);
   });
   return 0;
 }
@@ -206,14 +221,15 @@ int emu_ntt(int logn, uint32_t k, const uint64_t* mods16, const uint64_t* fwd, c
 // n = 16384 kernels launch as 2-block clusters): both halves' buffers side by side.
 int emu_ntt_pair(int logn, uint32_t k, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv, uint64_t* data,
                  uint64_t polys, uint32_t prime_count, uint32_t prime_offset, int inverse) {
-  Tabs T = tabs(k, mods16, fwd, inv);
+  Tabs T = tabs(k, mods16, fwd, inv, logn);
   EMU_DISPATCH(logn, {
     if constexpr (L_ >= 6) {
       HostPairExec ex;
       ex.words = SmemWords<L_ - 1>::value;
       std::vector<uint64_t> s(2 * (size_t)ex.words);
       for (uint64_t b = 0; b < polys; ++b)
-        op_ntt<L_>(ex, s.data(), b, inverse != 0, data, prime_count, prime_offset, T.mods.data(), T.fwd, T.inv);
+        op_ntt<L_>(ex, s.data(), b, inverse != 0, data, prime_count, prime_offset, T.mods.data(), T.fwd, T.inv,
+                   T.fwd64, T.inv64);
     }
   });
   return 0;
@@ -222,7 +238,7 @@ int emu_ntt_pair(int logn, uint32_t k, const uint64_t* mods16, const uint64_t* f
 // cts [count][2][dk][n], key [dk][2][k][n] -> out [count][2][dk][n]
 int emu_keyswitch(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv,
                   const uint64_t* cts, uint64_t count, const uint64_t* key, uint32_t elt, uint64_t* out) {
-  Tabs T = tabs(k, mods16, fwd, inv);
+  Tabs T = tabs(k, mods16, fwd, inv, logn);
   const uint64_t n = 1ull << logn;
   std::vector<uint64_t> qjp((size_t)dk * k);
   for (uint32_t j = 0; j < dk; ++j)
@@ -245,7 +261,7 @@ int emu_keyswitch(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, con
 int emu_keyswitch_hoisted(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd,
                           const uint64_t* inv, const uint64_t* cts, uint64_t count, const uint64_t* key, uint32_t elt,
                           uint64_t* out, uint32_t* zflag_out) {
-  Tabs T = tabs(k, mods16, fwd, inv);
+  Tabs T = tabs(k, mods16, fwd, inv, logn);
   const uint64_t n = 1ull << logn;
   std::vector<uint64_t> qjp((size_t)dk * k);
   for (uint32_t j = 0; j < dk; ++j)
@@ -264,7 +280,7 @@ int emu_keyswitch_hoisted(int logn, uint32_t k, uint32_t dk, const uint64_t* mod
       ks_keyperm_item(item, key, prepared.data(), pw, &ginv, L_, k, dk, T.mods.data(), qjp.data());
     for (uint64_t b = 0; b < count * 2 * k; ++b)
       op_ks_rotate<L_>(HostExec{}, s.data(), b, cts, Y.data(), zflag.data(), prepared.data(), x.data(), elt, k, dk,
-                       T.mods.data(), qjp.data(), T.fwd, T.inv);
+                       T.mods.data(), qjp.data(), T.fwd, T.inv, T.fwd64, T.inv64);
     std::vector<uint64_t> s2(n);
     for (uint64_t b = 0; b < count * dk; ++b)
       op_ks_finish<L_>(HostExec{}, s2.data(), b, x.data(), cts, out, ginv, k, dk, T.mods.data());
@@ -280,7 +296,7 @@ int emu_keyswitch_hoisted(int logn, uint32_t k, uint32_t dk, const uint64_t* mod
 int emu_keyswitch_pipe(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd,
                        const uint64_t* inv, const uint64_t* cts, uint64_t count, const uint64_t* keys,
                        const uint32_t* elts, uint64_t elements, uint64_t* outs) {
-  Tabs T = tabs(k, mods16, fwd, inv);
+  Tabs T = tabs(k, mods16, fwd, inv, logn);
   const uint64_t n = 1ull << logn;
   std::vector<uint64_t> qjp((size_t)dk * k);
   for (uint32_t j = 0; j < dk; ++j)
@@ -310,7 +326,7 @@ int emu_keyswitch_pipe(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16
                               xs.data() + (r & 1) * count * 2 * n, data ? prepared.data() + (r - 1) * pw : nullptr,
                               elt_d, inv_mod_2n(elt_d, 2 * (uint32_t)n), xs.data() + ((r + 1) & 1) * count * 2 * n,
                               data ? outs + (r - 1) * count * ctw : nullptr, k, dk, T.mods.data(), qjp.data(), T.fwd,
-                              T.inv);
+                              T.inv, T.fwd64, T.inv64);
     }
   });
   return 0;
@@ -323,7 +339,7 @@ int emu_matrix(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const 
                const uint64_t* cts, uint64_t inputs, const uint64_t* ring, uint64_t groups, const uint64_t* mask,
                const uint64_t* samples, const uint64_t* pk, uint64_t q_mod_t, uint64_t upper_half, uint64_t t,
                int tlog, uint64_t* out) {
-  Tabs T = tabs(k, mods16, fwd, inv);
+  Tabs T = tabs(k, mods16, fwd, inv, logn);
   const uint64_t n = 1ull << logn;
   std::vector<uint64_t> in(cts, cts + inputs * 2 * dk * n);
   std::vector<uint64_t> w(groups * inputs * dk * n);
@@ -331,7 +347,7 @@ int emu_matrix(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const 
   EMU_DISPATCH(logn, {
     std::vector<uint64_t> s(SmemWords<L_>::value);
     for (uint64_t b = 0; b < inputs * 2 * dk; ++b)
-      op_ntt<L_>(HostExec{}, s.data(), b, false, in.data(), dk, 0, T.mods.data(), T.fwd, T.inv);
+      op_ntt<L_>(HostExec{}, s.data(), b, false, in.data(), dk, 0, T.mods.data(), T.fwd, T.inv, T.fwd64, T.inv64);
     for (uint64_t b = 0; b < groups * inputs * dk; ++b)
       op_lift_ntt<L_>(HostExec{}, s.data(), b, ring, w.data(), dk, T.mods.data(), T.fwd);
     ProtectArgs prot{mask, nullptr, q_mod_t, upper_half, t, tlog};
@@ -355,7 +371,7 @@ int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, 
                      const uint64_t* inv, const uint64_t* cts, uint64_t tiles, uint64_t inputs, const uint64_t* ring,
                      uint64_t groups, const uint64_t* masks, const uint64_t* samples, const uint64_t* pk,
                      uint64_t q_mod_t, uint64_t upper_half, uint64_t t, int tlog, uint64_t* out, int path) {
-  Tabs T = tabs(k, mods16, fwd, inv);
+  Tabs T = tabs(k, mods16, fwd, inv, logn);
   const uint64_t n = 1ull << logn;
   const uint64_t items = tiles * groups;
   std::vector<uint64_t> in(cts, cts + tiles * inputs * 2 * dk * n);
@@ -411,7 +427,7 @@ int emu_matrix_tiles(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, 
 // data [batches][dk][n] in place, sk [dk][n] NTT form.
 int emu_client_phase(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd,
                      const uint64_t* inv, uint64_t* data, const uint64_t* sk, uint64_t batches) {
-  Tabs T = tabs(k, mods16, fwd, inv);
+  Tabs T = tabs(k, mods16, fwd, inv, logn);
   EMU_DISPATCH(logn, {
     std::vector<uint64_t> s(SmemWords<L_>::value);
     for (uint64_t b = 0; b < batches * dk; ++b)
@@ -432,7 +448,7 @@ int emu_crt(uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* res
 // Token product: cts_ntt [19][slots][2][dk][n] NTT form, ring [19][8192], scaled [slots][dk].
 int emu_token(uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* fwd, const uint64_t* inv,
               const uint64_t* cts_ntt, uint64_t slots, const uint64_t* ring, const uint64_t* scaled, uint64_t* out) {
-  Tabs T = tabs(k, mods16, fwd, inv);
+  Tabs T = tabs(k, mods16, fwd, inv, 14);
   constexpr int L_ = 14;
   const uint64_t n = 1ull << L_;
   std::vector<uint64_t> w(19 * dk * n), s(SmemWords<L_>::value);
@@ -445,3 +461,23 @@ int emu_token(uint32_t k, uint32_t dk, const uint64_t* mods16, const uint64_t* f
 }
 
 }  // extern "C"
+
+// FP64-pipe modular arithmetic (f64mod.cuh) on arrays: r[i] = mulmod_f64(y[i], w[i]) (signed
+// representatives) and c[i] = canon_f64 of it; red[i] = reduce_f64(y[i]).
+extern "C" int emu_f64_mulmod(const int64_t* y, const int64_t* w, uint64_t count, uint64_t q, int64_t* r,
+                              uint64_t* c, int64_t* red) {
+  const double qd = (double)q, qinv = 1.0 / qd;
+  for (uint64_t i = 0; i < count; ++i) {
+    const double wd = (double)w[i], wq = wd / qd;
+    const double v = mulmod_f64((double)y[i], wd, wq, qd);
+    r[i] = (int64_t)v;
+    c[i] = canon_f64(v, qd, qinv);
+    red[i] = (int64_t)reduce_f64((double)y[i], qd, qinv);
+  }
+  return 0;
+}
+// u64_to_f64 / f64_to_u64 round trip of values below 2^52.
+extern "C" int emu_f64_convert(const uint64_t* x, uint64_t count, uint64_t* out) {
+  for (uint64_t i = 0; i < count; ++i) out[i] = f64_to_u64(u64_to_f64(x[i]));
+  return 0;
+}

@@ -15,6 +15,8 @@ SIGNATURES = {
     "emu_client_phase": [INT, U32, U32, P, P, P, P, P, U64],
     "emu_crt": [U32, U32, P, P, U64, P, P, P, P],
     "emu_token": [U32, U32, P, P, P, P, U64, P, P, P],
+    "emu_f64_mulmod": [P, P, U64, U64, P, P, P],
+    "emu_f64_convert": [P, U64, P],
 }
 
 

@@ -28,11 +28,14 @@ SETS = {
 }
 
 
-def make(bfv, oracle, logn):
+def make(bfv, oracle, logn, fp64=True):
+    """Host-only context, oracle and the kernels' constants.  fp64=False: the integer-pipe
+    records (the FP64 path is taken for primes below 2^50 only when f64 is set)."""
     primes_fn, dk, t = SETS[logn]
     primes = primes_fn(oracle)
     n = 1 << logn
     hc = bfv.Context(n, primes, dk, len(primes) - dk, t, device=-1)
+    hc.set_fp64(fp64)
     oc = oracle.Ctx(n, primes, data_k=dk, t=t)
     mods = np.ascontiguousarray(hc.moduli())
     fwd = np.ascontiguousarray(np.stack([hc.tables(i)[0] for i in range(hc.k)]))
@@ -58,9 +61,15 @@ def test_tables_match_oracle(bfv, oracle, logn):
         assert int(mods[i, 8]) == oc.delta[i]
 
 
-@pytest.mark.parametrize("logn", [5, 6, 12, 13, 14])
-def test_ntt_kernel_body(bfv, oracle, E, logn):
-    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+# (logn, fp64): the FP64 path applies to the 36/37-bit (n = 4096) and 50-bit (n = 8192)
+# data primes; the integer path is kept covered at those degrees with fp64 off
+ARITH = [(5, True), (6, True), (12, True), (12, False), (13, True), (13, False), (14, True)]
+
+
+@pytest.mark.parametrize("logn,fp64", ARITH)
+def test_ntt_kernel_body(bfv, oracle, E, logn, fp64):
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn, fp64)
+    assert bool(int(mods[0, 10])) == (fp64 and oc.primes[0] < 2 ** 50)
     k = hc.k
     data = oc.uniform(logn, 2 * k, prime_count=k)
     n = 1 << logn
@@ -98,10 +107,11 @@ def test_ntt_split_between_two_blocks(bfv, oracle, E, logn):
     assert np.array_equal(back, data), logn
 
 
-@pytest.mark.parametrize("logn,elts", [(5, [1, 3, 63]), (6, [5, 127, 9]), (13, [3, 2 ** 13 + 1, 16383]),
-                                       (14, [1, 3, 1025])])
-def test_keyswitch_kernel_body(bfv, oracle, E, logn, elts):
-    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+@pytest.mark.parametrize("logn,elts,fp64", [(5, [1, 3, 63], True), (6, [5, 127, 9], True),
+                                            (13, [3, 2 ** 13 + 1, 16383], True), (13, [3, 16383], False),
+                                            (14, [1, 3, 1025], True)])
+def test_keyswitch_kernel_body(bfv, oracle, E, logn, elts, fp64):
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn, fp64)
     k, dk, n = hc.k, hc.dk, 1 << logn
     count = 2
     cts = oc.uniform(100 + logn, count * 2 * dk, prime_count=dk).reshape(count, 2, dk, n)
@@ -114,13 +124,14 @@ def test_keyswitch_kernel_body(bfv, oracle, E, logn, elts):
             assert np.array_equal(out[c], oc.keyswitch(cts[c], key, elt)), (logn, elt, c)
 
 
-@pytest.mark.parametrize("logn,elts", [(5, [1, 3, 63]), (6, [5, 127, 9]), (13, [3, 2 ** 13 + 1, 16383]),
-                                       (14, [3, 1025])])
-def test_hoisted_keyswitch_kernel_bodies(bfv, oracle, E, logn, elts):
+@pytest.mark.parametrize("logn,elts,fp64", [(5, [1, 3, 63], True), (6, [5, 127, 9], True),
+                                            (13, [3, 2 ** 13 + 1, 16383], True), (13, [2 ** 13 + 1], False),
+                                            (14, [3, 1025], True)])
+def test_hoisted_keyswitch_kernel_bodies(bfv, oracle, E, logn, elts, fp64):
     """Hoist + key preparation + rotate + finish equals the reference keyswitch; the
     ciphertext with zero c1 words is flagged and takes the exact path."""
     import ctypes
-    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn, fp64)
     k, dk, n = hc.k, hc.dk, 1 << logn
     count = 3
     cts = oc.uniform(300 + logn, count * 2 * dk, prime_count=dk).reshape(count, 2, dk, n)
@@ -135,14 +146,15 @@ def test_hoisted_keyswitch_kernel_bodies(bfv, oracle, E, logn, elts):
             assert np.array_equal(out[c], oc.keyswitch(cts[c], key, elt)), (logn, elt, c)
 
 
-@pytest.mark.parametrize("logn,elts", [(5, [3, 63, 1, 9]), (6, [5, 127, 9]), (13, [3, 2 ** 13 + 1, 16383])])
-def test_pipelined_rotation_kernel_bodies(bfv, oracle, E, logn, elts):
+@pytest.mark.parametrize("logn,elts,fp64", [(5, [3, 63, 1, 9], True), (6, [5, 127, 9], True),
+                                            (13, [3, 2 ** 13 + 1, 16383], True), (13, [3, 16383], False)])
+def test_pipelined_rotation_kernel_bodies(bfv, oracle, E, logn, elts, fp64):
     """The software-pipelined rotations (launch r: special-prime blocks of element r beside
     the data-prime blocks of element r - 1, which finish the keyswitch in shared memory) run
     on the host with the device's buffers and indexing, against the reference keyswitch for
     every element, including a ciphertext whose c1 holds zero words (the exact path)."""
     import ctypes
-    hc, oc, mods, fwd, inv = make(bfv, oracle, logn)
+    hc, oc, mods, fwd, inv = make(bfv, oracle, logn, fp64)
     k, dk, n = hc.k, hc.dk, 1 << logn
     count = 3
     cts = oc.uniform(500 + logn, count * 2 * dk, prime_count=dk).reshape(count, 2, dk, n)

@@ -4,7 +4,8 @@ The bench divides each hot kernel's algorithmic operation count by these kernels
 rates, so a peak kernel whose loop the compiler shortened would inflate every integer
 fraction.  Here one block runs a few iterations of each kind and every thread's checksum is
 recomputed on the host from the same start values, twiddles and prime: the kernel must have
-performed exactly blocks x 256 x 8 x iters operations of its kind.
+performed exactly blocks x 256 x 8 x iters operations of its kind (kinds 4 and 5 run on
+the FP64 pipe and end with canonical residues, so only the residues are compared there).
 """
 from __future__ import annotations
 
@@ -48,6 +49,17 @@ def _expected(kind: int, iters: int, q: int, tw) -> list[int]:
             for _ in range(iters):
                 for j in range(CHAINS):
                     a[j] = a[j] * b[j] % q
+        elif kind == 3:
+            for _ in range(iters):
+                for j in range(CHAINS):
+                    a[j] = a[j] * tw[j & 3][0] % q
+        elif kind == 4:  # residues only: the FP64 path's representatives are made canonical
+            for _ in range(iters):
+                for j in range(CHAINS):
+                    w = tw[j & 3][0]
+                    for _ in range(2):
+                        t = b[j] * w % q
+                        a[j], b[j] = (a[j] + t) % q, (a[j] - t) % q
         else:
             for _ in range(iters):
                 for j in range(CHAINS):
@@ -59,7 +71,7 @@ def _expected(kind: int, iters: int, q: int, tw) -> list[int]:
     return out
 
 
-@pytest.mark.parametrize("kind", [0, 1, 2, 3])
+@pytest.mark.parametrize("kind", [0, 1, 2, 3, 4, 5])
 def test_int_peak_checksums(bfv, oracle, kind):
     import torch
     if not torch.cuda.is_available():
@@ -74,6 +86,6 @@ def test_int_peak_checksums(bfv, oracle, kind):
     sink = torch.zeros(THREADS, dtype=torch.int64, device="cuda")
     ops = ctx.int_peak_device(kind, 1, iters, sink)
     torch.cuda.synchronize()
-    assert ops == THREADS * CHAINS * iters
+    assert ops == THREADS * CHAINS * iters * (2 if kind == 4 else 1)
     got = sink.cpu().numpy().view(np.uint64).tolist()
     assert got == _expected(kind, iters, primes[0], tw)
