@@ -170,7 +170,7 @@ def cpu_keyswitch_sample(seconds: float = 12.0):
 
 
 # the files that define the transform-bearing kernels (bodies, arithmetic, launches)
-KERNEL_SOURCES = ("arith.cuh", "layout.cuh", "ntt_core.cuh", "block_ops.cuh", "kernels.cuh", "kernels.cu")
+KERNEL_SOURCES = ("arith.cuh", "f64mod.cuh", "layout.cuh", "ntt_core.cuh", "block_ops.cuh", "kernels.cuh", "kernels.cu")
 
 
 def kernel_sources_sha16() -> str:
