@@ -621,17 +621,35 @@ BFV_HD void op_ks_finish(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t
 // The outputs equal op_ks_rotate + op_ks_finish for each element; the data-prime limbs never
 // leave shared memory between the product and the finished ciphertext.  x is the zero-word
 // path's scratch [count][2][k][n] (special and data blocks use disjoint parts of it).
+// Block order of one pipelined launch (order: bit 0 = it holds special-prime blocks, bit 1 =
+// data-prime blocks, bit 2 = ciphertexts in reverse).  The blocks of one ciphertext -- its two
+// special-prime blocks, then its 2 dk data-prime blocks -- are consecutive, and consecutive
+// launches walk the ciphertexts in opposite directions, so a launch starts on the ciphertexts
+// whose hoisted digits and special-prime limbs the previous launch touched last (in L2).
+BFV_HD void pipe_block(uint64_t blk, uint64_t count, uint32_t order, uint32_t dk, bool* special, uint64_t* ct,
+                       uint32_t* c, uint32_t* p) {
+  const uint64_t sp = (order & 1) ? 2 : 0, per = sp + ((order & 2) ? 2ull * dk : 0);
+  const uint64_t i = blk / per, w = blk % per;
+  *ct = (order & 4) ? count - 1 - i : i;
+  *special = w < sp;
+  const uint64_t d = w - (*special ? 0 : sp);
+  *c = *special ? (uint32_t)w : (uint32_t)(d / dk);
+  *p = *special ? 0 : (uint32_t)(d % dk);
+}
+
 template <int LOGN, class Ex>
-BFV_HD void op_ks_rotate_pipe(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t s_blocks, const uint64_t* cts,
+BFV_HD void op_ks_rotate_pipe(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t count, uint32_t order, const uint64_t* cts,
                               const uint64_t* Y, const uint32_t* zflag, uint64_t* x, const uint64_t* prep_s,
                               uint32_t elt_s, uint64_t* xs_w, const uint64_t* prep_d, uint32_t elt_d, uint32_t ginv_d,
                               const uint64_t* xs_r, uint64_t* out_d, uint32_t k, uint32_t dk, const Modulus* mods,
                               const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv, const double2* fwd64,
                               const double2* inv64) {
   constexpr int N = 1 << LOGN;
-  if (blk < s_blocks) {
-    const uint64_t ct = blk >> 1;
-    const uint32_t c = (uint32_t)(blk & 1);
+  bool special_block;
+  uint64_t ct;
+  uint32_t c, p;
+  pipe_block(blk, count, order, dk, &special_block, &ct, &c, &p);
+  if (special_block) {
     uint64_t* xo = xs_w + (ct * 2 + c) * (uint64_t)N;
     auto st = [xo](int i, uint64_t v) { xo[i] = v; };
     const F64Prime fs = f64_prime(mods[k - 1]);
@@ -640,9 +658,6 @@ BFV_HD void op_ks_rotate_pipe(const Ex& ex, uint64_t* s, uint64_t blk, uint64_t 
                             inv64, st, stf);
     return;
   }
-  const uint64_t d = blk - s_blocks;
-  const uint64_t ct = d / (2ull * dk);
-  const uint32_t c = (uint32_t)((d / dk) & 1), p = (uint32_t)(d % dk);
   const Modulus m = mods[p], ms = mods[k - 1];
   const uint64_t* xs = xs_r + (ct * 2 + c) * (uint64_t)N;
   const uint64_t* c0 = cts + (ct * 2 * dk + p) * (uint64_t)N;

@@ -743,13 +743,13 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
 // data-prime blocks (which finish the keyswitch in shared memory) of the previous one.
 template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
-    k_ks_rotate_pipe(const uint64_t* cts, uint64_t s_blocks, const uint64_t* Y, const uint32_t* zflag, uint64_t* x,
-                     const uint64_t* prep_s, uint32_t elt_s, uint64_t* xs_w, const uint64_t* prep_d, uint32_t elt_d,
+    k_ks_rotate_pipe(const uint64_t* cts, uint64_t count, uint32_t order, const uint64_t* Y, const uint32_t* zflag,
+                     uint64_t* x, const uint64_t* prep_s, uint32_t elt_s, uint64_t* xs_w, const uint64_t* prep_d, uint32_t elt_d,
                      uint32_t ginv_d, const uint64_t* xs_r, uint64_t* out_d, uint32_t k, uint32_t dk,
                      const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv,
                      const double2* fwd64, const double2* inv64) {
   extern __shared__ uint64_t smem[];
-  op_ks_rotate_pipe<LOGN>(BlockExec{}, smem, blockIdx.x, s_blocks, cts, Y, zflag, x, prep_s, elt_s, xs_w, prep_d,
+  op_ks_rotate_pipe<LOGN>(BlockExec{}, smem, blockIdx.x, count, order, cts, Y, zflag, x, prep_s, elt_s, xs_w, prep_d,
                           elt_d, ginv_d, xs_r, out_d, k, dk, mods, qjp, fwd, inv, fwd64, inv64);
 }
 
@@ -1185,7 +1185,8 @@ cudaError_t launch_ks_rotate_pipe_step(const DevParams& P, const uint64_t* cts, 
   if (P.k != P.dk + 1) return cudaErrorInvalidValue;
   const uint64_t pw = ks_prepared_words(P.k, P.dk, P.n), xsw = count * 2ull * P.n;
   const bool special = r < elements, data = r >= 1;
-  const uint64_t s_blocks = special ? count * 2 : 0, blocks = s_blocks + (data ? count * 2 * P.dk : 0);
+  const uint64_t blocks = (special ? count * 2 : 0) + (data ? count * 2 * P.dk : 0);
+  const uint32_t order = (special ? 1u : 0u) | (data ? 2u : 0u) | ((r & 1) ? 4u : 0u);
   if (!blocks) return cudaSuccess;
   const uint64_t* prep_s = special ? prepared + r * pw : nullptr;
   const uint32_t elt_s = special ? elts[r] : 1;
@@ -1195,7 +1196,7 @@ cudaError_t launch_ks_rotate_pipe_step(const DevParams& P, const uint64_t* cts, 
   const uint64_t* xs_r = xs + ((r + 1) & 1) * xsw;  // written by launch r - 1
   BFV_DISPATCH(P.logn, {
     k_ks_rotate_pipe<L_><<<(unsigned)blocks, threads_for<L_>(), smem_bytes<L_>(), st>>>(
-        cts, s_blocks, Y, zflag, x, prep_s, elt_s, xs_w, prep_d, elt_d, ginv_d, xs_r, data ? out_d : nullptr, P.k,
+        cts, count, order, Y, zflag, x, prep_s, elt_s, xs_w, prep_d, elt_d, ginv_d, xs_r, data ? out_d : nullptr, P.k,
         P.dk, P.mod, P.qjp, P.fwd, P.inv, P.fwd64, P.inv64);
   });
   return cudaGetLastError();

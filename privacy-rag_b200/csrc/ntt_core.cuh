@@ -491,19 +491,29 @@ inline void f64_twiddles(const ulonglong2* tw, uint64_t q, size_t n, double2* ou
   }
 }
 
-template <int LOGN, int R, bool FIRST, bool LAST, class Ld, class St>
-BFV_HD void fwd_unit_f64(double* s, int u, int L, const double2* tw, F64Prime fp, const Ld& ld, const St& st) {
+// U interleaved units per thread (u0 + j us), so that one thread has U independent chains of
+// butterflies -- and of twiddle loads -- in flight.
+template <int LOGN, int R, bool FIRST, bool LAST, int U, class Ld, class St>
+BFV_HD void fwd_unit_f64(double* s, int u0, int us, int L, const double2* tw, F64Prime fp, const Ld& ld,
+                         const St& st) {
   constexpr int K = 1 << R;
   const int shift = LOGN - L - R;
-  const int o = u & ((1 << shift) - 1), gl = u >> shift;
-  const int base = (gl << (LOGN - L)) + o, sbase = spad(base);
-  double x[K];
+  int base[U], sbase[U], gl[U];
+  double x[U][K];
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    if constexpr (FIRST)
-      x[k] = ld(base + (k << shift));
-    else
-      x[k] = s[spad_unit(base, sbase, k << shift)];
+  for (int j = 0; j < U; ++j) {
+    const int u = u0 + j * us;
+    const int o = u & ((1 << shift) - 1);
+    gl[j] = u >> shift;
+    base[j] = (gl[j] << (LOGN - L)) + o;
+    sbase[j] = spad(base[j]);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if constexpr (FIRST)
+        x[j][k] = ld(base[j] + (k << shift));
+      else
+        x[j][k] = s[spad_unit(base[j], sbase[j], k << shift)];
+    }
   }
 #pragma unroll
   for (int t = 0; t < R; ++t) {
@@ -512,36 +522,48 @@ BFV_HD void fwd_unit_f64(double* s, int u, int L, const double2* tw, F64Prime fp
     for (int pr = 0; pr < K / 2; ++pr) {
       const int jj = pr >> hs, kk = pr & ((1 << hs) - 1);
       const int k = (jj << (hs + 1)) + kk;
-      const double2 w = ldg_tw(tw + (1 << (L + t)) + (gl << t) + jj);
-      double a = x[k];
-      if (t == 0) a = reduce_f64(a, fp.q, fp.qinv);
-      const double b = mulmod_f64(x[k + (1 << hs)], w.x, w.y, fp.q);
-      x[k] = f64_add(a, b);
-      x[k + (1 << hs)] = f64_sub(a, b);
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const double2 w = ldg_tw(tw + (1 << (L + t)) + (gl[j] << t) + jj);
+        double a = x[j][k];
+        if (t == 0) a = reduce_f64(a, fp.q, fp.qinv);
+        const double b = mulmod_f64(x[j][k + (1 << hs)], w.x, w.y, fp.q);
+        x[j][k] = f64_add(a, b);
+        x[j][k + (1 << hs)] = f64_sub(a, b);
+      }
     }
   }
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    if constexpr (LAST)
-      st(base + (k << shift), x[k]);
-    else
-      s[spad_unit(base, sbase, k << shift)] = x[k];
-  }
+  for (int j = 0; j < U; ++j)
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if constexpr (LAST)
+        st(base[j] + (k << shift), x[j][k]);
+      else
+        s[spad_unit(base[j], sbase[j], k << shift)] = x[j][k];
+    }
 }
 
-template <int LOGN, int R, bool FIRST, bool LAST, class Ld, class St>
-BFV_HD void inv_unit_f64(double* s, int u, int L, const double2* tw, F64Prime fp, double invn, double invn_q,
-                         const Ld& ld, const St& st) {
+template <int LOGN, int R, bool FIRST, bool LAST, int U, class Ld, class St>
+BFV_HD void inv_unit_f64(double* s, int u0, int us, int L, const double2* tw, F64Prime fp, double invn,
+                         double invn_q, const Ld& ld, const St& st) {
   static_assert(R <= 3, "inverse FP64 passes are at most radix 8 (sums grow 2x per level)");
   constexpr int K = 1 << R;
   constexpr int N = 1 << LOGN;
-  const int o = u & ((1 << L) - 1), gg = u >> L;
-  const int base = (gg << (L + R)) + o, sbase = spad(base);
-  double x[K];
+  int base[U], sbase[U], gg[U];
+  double x[U][K];
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const double v = FIRST ? ld(base + (k << L)) : s[spad_unit(base, sbase, k << L)];
-    x[k] = reduce_f64(v, fp.q, fp.qinv);
+  for (int j = 0; j < U; ++j) {
+    const int u = u0 + j * us;
+    const int o = u & ((1 << L) - 1);
+    gg[j] = u >> L;
+    base[j] = (gg[j] << (L + R)) + o;
+    sbase[j] = spad(base[j]);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const double v = FIRST ? ld(base[j] + (k << L)) : s[spad_unit(base[j], sbase[j], k << L)];
+      x[j][k] = reduce_f64(v, fp.q, fp.qinv);
+    }
   }
 #pragma unroll
   for (int t = 0; t < R; ++t) {
@@ -550,20 +572,34 @@ BFV_HD void inv_unit_f64(double* s, int u, int L, const double2* tw, F64Prime fp
     for (int pr = 0; pr < K / 2; ++pr) {
       const int jj = pr >> t, kk = pr & ((1 << t) - 1);
       const int k = (jj << (t + 1)) + kk;
-      const double2 w = ldg_tw(tw + N - (N >> l) + 1 + (gg << (R - t - 1)) + jj);
-      const double a = x[k], b = x[k + (1 << t)];
-      x[k] = f64_add(a, b);
-      x[k + (1 << t)] = mulmod_f64(f64_sub(a, b), w.x, w.y, fp.q);
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const double2 w = ldg_tw(tw + N - (N >> l) + 1 + (gg[j] << (R - t - 1)) + jj);
+        const double a = x[j][k], b = x[j][k + (1 << t)];
+        x[j][k] = f64_add(a, b);
+        x[j][k + (1 << t)] = mulmod_f64(f64_sub(a, b), w.x, w.y, fp.q);
+      }
     }
   }
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    if constexpr (LAST)
-      st(base + (k << L), mulmod_f64(x[k], invn, invn_q, fp.q));
-    else
-      s[spad_unit(base, sbase, k << L)] = x[k];
-  }
+  for (int j = 0; j < U; ++j)
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if constexpr (LAST)
+        st(base[j] + (k << L), mulmod_f64(x[j][k], invn, invn_q, fp.q));
+      else
+        s[spad_unit(base[j], sbase[j], k << L)] = x[j][k];
+    }
 }
+
+// Units per thread per pass of the FP64 transforms: two interleaved units (the FP64 unit
+// holds its 8 values in 16 registers, so two fit under the 80-register cap of three blocks
+// per SM), which doubles the loads and butterfly chains each thread has in flight; the last
+// pass, whose storer carries the callers' epilogues, keeps one unit.
+template <int LOGN>
+struct DualUnitsF64 {
+  static constexpr bool value = LOGN >= 12;
+};
 
 template <int LOGN, int MAXR, int P, class Ex, class Ld, class St>
 BFV_HD void fwd_passes_f64(const Ex& ex, double* s, const double2* tw, F64Prime fp, const Ld& ld, const St& st) {
@@ -571,7 +607,14 @@ BFV_HD void fwd_passes_f64(const Ex& ex, double* s, const double2* tw, F64Prime 
   if constexpr (P < S::passes) {
     constexpr int R = S::fwd_r(P);
     constexpr int L = S::fwd_level(P);
-    ex.run(1 << (LOGN - R), [&](int u) { fwd_unit_f64<LOGN, R, P == 0, P == S::passes - 1>(s, u, L, tw, fp, ld, st); });
+    constexpr bool first = P == 0, last = P == S::passes - 1;
+    if constexpr (DualUnitsF64<LOGN>::value && !last)
+      ex.run2(
+          1 << (LOGN - R),
+          [&](int u0, int us) { fwd_unit_f64<LOGN, R, first, last, 2>(s, u0, us, L, tw, fp, ld, st); },
+          [&](int u) { fwd_unit_f64<LOGN, R, first, last, 1>(s, u, 0, L, tw, fp, ld, st); });
+    else
+      ex.run(1 << (LOGN - R), [&](int u) { fwd_unit_f64<LOGN, R, first, last, 1>(s, u, 0, L, tw, fp, ld, st); });
     ex.sync();
     fwd_passes_f64<LOGN, MAXR, P + 1>(ex, s, tw, fp, ld, st);
   }
@@ -583,8 +626,17 @@ BFV_HD void inv_passes_f64(const Ex& ex, double* s, const double2* tw, F64Prime 
   if constexpr (P < S::passes) {
     constexpr int R = S::inv_r(P);
     constexpr int L = S::inv_level(P);
-    ex.run(1 << (LOGN - R),
-           [&](int u) { inv_unit_f64<LOGN, R, P == 0, P == S::passes - 1>(s, u, L, tw, fp, invn, invn_q, ld, st); });
+    constexpr bool first = P == 0, last = P == S::passes - 1;
+    if constexpr (DualUnitsF64<LOGN>::value && !last)
+      ex.run2(
+          1 << (LOGN - R),
+          [&](int u0, int us) {
+            inv_unit_f64<LOGN, R, first, last, 2>(s, u0, us, L, tw, fp, invn, invn_q, ld, st);
+          },
+          [&](int u) { inv_unit_f64<LOGN, R, first, last, 1>(s, u, 0, L, tw, fp, invn, invn_q, ld, st); });
+    else
+      ex.run(1 << (LOGN - R),
+             [&](int u) { inv_unit_f64<LOGN, R, first, last, 1>(s, u, 0, L, tw, fp, invn, invn_q, ld, st); });
     ex.sync();
     inv_passes_f64<LOGN, MAXR, P + 1>(ex, s, tw, fp, invn, invn_q, ld, st);
   }

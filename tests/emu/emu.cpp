@@ -318,10 +318,11 @@ int emu_keyswitch_pipe(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16
     }
     for (uint64_t r = 0; r <= elements; ++r) {
       const bool special = r < elements, data = r >= 1;
-      const uint64_t s_blocks = special ? count * 2 : 0, blocks = s_blocks + (data ? count * 2 * dk : 0);
+      const uint64_t blocks = (special ? count * 2 : 0) + (data ? count * 2 * dk : 0);
+      const uint32_t order = (special ? 1u : 0u) | (data ? 2u : 0u) | ((r & 1) ? 4u : 0u);
       const uint32_t elt_d = data ? elts[r - 1] : 1;
       for (uint64_t b = 0; b < blocks; ++b)
-        op_ks_rotate_pipe<L_>(HostExec{}, s.data(), b, s_blocks, cts, Y.data(), zflag.data(), x.data(),
+        op_ks_rotate_pipe<L_>(HostExec{}, s.data(), b, count, order, cts, Y.data(), zflag.data(), x.data(),
                               special ? prepared.data() + r * pw : nullptr, special ? elts[r] : 1,
                               xs.data() + (r & 1) * count * 2 * n, data ? prepared.data() + (r - 1) * pw : nullptr,
                               elt_d, inv_mod_2n(elt_d, 2 * (uint32_t)n), xs.data() + ((r + 1) & 1) * count * 2 * n,
