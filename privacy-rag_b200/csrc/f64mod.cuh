@@ -101,6 +101,17 @@ BFV_HD double mulmod_f64(double y, double w, double wq, double q) {
   return f64_add(f64_fma(-k, q, h), l);
 }
 
+// y w mod q for an operand without a precomputed quotient (Barrett's form: the quotient from
+// fl(1/q)), for |y| <= (q + 1)/2 and 0 <= w < q: |y w| < q^2 / 2, so |l| <= |y w| 2^-53 and
+// |h fl(1/q) - y w / q| <= q 2^-53 <= 1/8; with the rounding, |k - y w / q| <= 5/8 and
+// |r| <= 0.75 q.
+BFV_HD double mulmod_f64_barrett(double y, double w, double q, double qinv) {
+  const double h = f64_mul(y, w);
+  const double l = f64_fma(y, w, -h);
+  const double k = f64_sub(f64_fma(h, qinv, kF64Round), kF64Round);
+  return f64_add(f64_fma(-k, q, h), l);
+}
+
 // v mod q as a centred representative, |r| <= (q + 1) / 2 (|v| < 2^52, qinv = fl(1/q)).
 BFV_HD double reduce_f64(double v, double q, double qinv) {
   const double k = f64_sub(f64_fma(v, qinv, kF64Round), kF64Round);

@@ -85,9 +85,10 @@ __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
 template <int LOGN>
 __global__ void __launch_bounds__(threads_for<LOGN>(), blocks_per_sm<LOGN>())
     k_ks_main(const uint64_t* cts, const uint64_t* key, uint64_t* acc, uint32_t elt, uint32_t k, uint32_t dk,
-              const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv) {
+              const Modulus* mods, const uint64_t* qjp, const ulonglong2* fwd, const ulonglong2* inv,
+              const double2* fwd64, const double2* inv64) {
   extern __shared__ uint64_t smem[];
-  op_ks_main<LOGN>(BlockExec{}, smem, blockIdx.x, cts, key, acc, elt, k, dk, mods, qjp, fwd, inv);
+  op_ks_main<LOGN>(BlockExec{}, smem, blockIdx.x, cts, key, acc, elt, k, dk, mods, qjp, fwd, inv, fwd64, inv64);
 }
 
 template <int LOGN>
@@ -1115,7 +1116,7 @@ cudaError_t launch_keyswitch(const DevParams& P, const uint64_t* cts, const uint
   BFV_DISPATCH(P.logn, {
     k_ks_main<L_><<<(unsigned)(count * P.k), threads_for<L_>(), smem_bytes<L_>(), st>>>(cts, key, acc, elt, P.k,
                                                                                         P.dk, P.mod, P.qjp, P.fwd,
-                                                                                        P.inv);
+                                                                                        P.inv, P.fwd64, P.inv64);
     k_ks_moddown<L_><<<(unsigned)(count * P.dk), threads_for<L_>(), (size_t(1) << L_) * 8, st>>>(acc, cts, out, ginv,
                                                                                                  P.k, P.dk, P.mod);
   });
@@ -1186,7 +1187,7 @@ cudaError_t launch_ks_rotate_pipe_step(const DevParams& P, const uint64_t* cts, 
   const uint64_t pw = ks_prepared_words(P.k, P.dk, P.n), xsw = count * 2ull * P.n;
   const bool special = r < elements, data = r >= 1;
   const uint64_t blocks = (special ? count * 2 : 0) + (data ? count * 2 * P.dk : 0);
-  const uint32_t order = (special ? 1u : 0u) | (data ? 2u : 0u) | ((r & 1) ? 4u : 0u);
+  const uint32_t order = special ? 1u : 0u;
   if (!blocks) return cudaSuccess;
   const uint64_t* prep_s = special ? prepared + r * pw : nullptr;
   const uint32_t elt_s = special ? elts[r] : 1;

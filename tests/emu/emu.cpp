@@ -249,7 +249,7 @@ int emu_keyswitch(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16, con
     std::vector<uint64_t> s(SmemWords<L_>::value);
     for (uint64_t b = 0; b < count * k; ++b)
       op_ks_main<L_>(HostExec{}, s.data(), b, cts, key, acc.data(), elt, k, dk, T.mods.data(), qjp.data(), T.fwd,
-                     T.inv);
+                     T.inv, T.fwd64, T.inv64);
     std::vector<uint64_t> s2(n);
     for (uint64_t b = 0; b < count * dk; ++b)
       op_ks_moddown<L_>(HostExec{}, s2.data(), b, acc.data(), cts, out, ginv, k, dk, T.mods.data());
@@ -319,7 +319,7 @@ int emu_keyswitch_pipe(int logn, uint32_t k, uint32_t dk, const uint64_t* mods16
     for (uint64_t r = 0; r <= elements; ++r) {
       const bool special = r < elements, data = r >= 1;
       const uint64_t blocks = (special ? count * 2 : 0) + (data ? count * 2 * dk : 0);
-      const uint32_t order = (special ? 1u : 0u) | (data ? 2u : 0u) | ((r & 1) ? 4u : 0u);
+      const uint32_t order = special ? 1u : 0u;
       const uint32_t elt_d = data ? elts[r - 1] : 1;
       for (uint64_t b = 0; b < blocks; ++b)
         op_ks_rotate_pipe<L_>(HostExec{}, s.data(), b, count, order, cts, Y.data(), zflag.data(), x.data(),
@@ -475,6 +475,12 @@ extern "C" int emu_f64_mulmod(const int64_t* y, const int64_t* w, uint64_t count
     c[i] = canon_f64(v, qd, qinv);
     red[i] = (int64_t)reduce_f64((double)y[i], qd, qinv);
   }
+  return 0;
+}
+// Barrett-form products: r[i] = mulmod_f64_barrett(y[i], w[i]) for |y| <= (q+1)/2, 0 <= w < q.
+extern "C" int emu_f64_mulmod_barrett(const int64_t* y, const uint64_t* w, uint64_t count, uint64_t q, int64_t* r) {
+  const double qd = (double)q, qinv = 1.0 / qd;
+  for (uint64_t i = 0; i < count; ++i) r[i] = (int64_t)mulmod_f64_barrett((double)y[i], (double)w[i], qd, qinv);
   return 0;
 }
 // u64_to_f64 / f64_to_u64 round trip of values below 2^52.

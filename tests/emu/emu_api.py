@@ -17,6 +17,7 @@ SIGNATURES = {
     "emu_token": [U32, U32, P, P, P, P, U64, P, P, P],
     "emu_f64_mulmod": [P, P, U64, U64, P, P, P],
     "emu_f64_convert": [P, U64, P],
+    "emu_f64_mulmod_barrett": [P, P, U64, U64, P],
 }
 
 

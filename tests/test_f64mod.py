@@ -3,7 +3,9 @@ the host build of the same header (IEEE double operations with std::fma, no cont
 
 mulmod_f64(y, w) must return a representative of y*w mod q with |r| <= 0.75 q for every
 |y| < 2^52 and centred |w| <= q/2, q < 2^50; reduce_f64(v) one with |r| <= (q + 1)/2;
-canon_f64 the canonical residue.  (The NTT passes rely on the (q + 1)/2 bound: eight
+canon_f64 the canonical residue; mulmod_f64_barrett(y, w) (quotient from fl(1/q), for key
+words that carry no quotient) a representative with |r| <= 0.75 q for |y| <= (q + 1)/2 and
+0 <= w < q.  (The NTT passes rely on the (q + 1)/2 bound: eight
 reduced values summed stay below 4q + 4 < 2^52.)  The cases include the range limits
 (|y| = 2^52 - 1, |w| = floor(q/2), q just below 2^50) and random values for several moduli.
 """
@@ -59,6 +61,23 @@ def test_mulmod_reduce_exact(E, q):
         rd = int(red[i])
         assert rd % q == ys[i] % q
         assert 2 * abs(rd) <= q + 1
+
+
+@pytest.mark.parametrize("q", [(1 << 50) - 27, 1125899906826241, (1 << 49) + 1, 68719403009, 97])
+def test_mulmod_barrett_exact(E, q):
+    rng = np.random.default_rng((q & 0xFFFF) + 1)
+    hy = (q + 1) // 2
+    ys = [0, 1, -1, hy, -hy, hy - 1, -(hy - 1)] * 4
+    ws = [0] * 7 + [1] * 7 + [q - 1] * 7 + [q // 2] * 7
+    ys += [int(v) for v in rng.integers(-hy, hy + 1, size=20000, dtype=np.int64)]
+    ws += [int(v) for v in rng.integers(0, q, size=20000, dtype=np.uint64)]
+    y = np.array(ys, dtype=np.int64)
+    w = np.array(ws, dtype=np.uint64)
+    r = np.zeros(len(ys), dtype=np.int64)
+    assert E.emu_f64_mulmod_barrett(p(y.view(np.uint64)), p(w), len(ys), q, p(r.view(np.uint64))) == 0
+    for yi, wi, ri in zip(ys, ws, r.tolist()):
+        assert ri % q == yi * wi % q, (yi, wi)
+        assert 4 * abs(ri) <= 3 * q
 
 
 def test_convert_round_trip(E):
