@@ -216,8 +216,8 @@ int32_t bfvgpu_ctx_set_product_path(bfvgpu_ctx *ctx, int32_t path);
  * split = 0, one block holds the whole limb (one block per SM).  Results are identical. */
 int32_t bfvgpu_ctx_set_limb_split(bfvgpu_ctx *ctx, int32_t split);
 /* Arithmetic of the primes below 2^50 (configs with 36- to 50-bit primes): on = 1 (default),
- * the transforms and products that have an FP64 form (batched NTTs, Galois keyswitch
- * rotations and their key preparation) compute on the FP64 pipe with exact integer-valued
+ * the transforms and products that have an FP64 form (batched NTTs, the per-apply Galois
+ * keyswitch, the hoisted rotations and their key preparation) compute on the FP64 pipe with exact integer-valued
  * doubles; on = 0, everything computes on the integer pipe.  Results are identical.
  * Prepared keys are laid out for the mode they were prepared in, so the mode is fixed once
  * the context has prepared keys: changing it then fails with BFVGPU_E_STATE. */

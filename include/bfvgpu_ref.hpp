@@ -76,6 +76,9 @@ class Context {
   size_t n() const { return n_; }
   size_t k() const { return k_; }    // primes at the key level
   size_t dk() const { return dk_; }  // data primes
+  // Primes below 2^50 on the FP64 pipe (default) or the integer pipe; set before keys are
+  // prepared (bfvgpu_ctx_set_fp64).
+  void set_fp64(bool on) { check(bfvgpu_ctx_set_fp64(h_, on ? 1 : 0)); }
 
  private:
   Context(bfvgpu_ctx* h, size_t n, size_t k, size_t dk) : h_(h), n_(n), k_(k), dk_(dk) {}

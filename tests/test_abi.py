@@ -60,6 +60,29 @@ def test_host_context_validation(bfv, oracle):
     hc.close()
 
 
+def test_fp64_mode_switch_on_host(bfv, oracle):
+    """bfvgpu_ctx_set_fp64: the prime records carry the FP64 flag and constants for primes
+    below 2^50 only when the mode is on; the 60-bit special prime never; bad values rejected."""
+    import ctypes
+    import numpy as np
+    primes = oracle.coeff_modulus(8192, [50, 50, 50, 50, 60])
+    hc = bfv.Context(8192, primes, 4, 1, 65537, device=-1)
+    m = np.asarray(hc.moduli())
+    assert list(m[:, 10]) == [1, 1, 1, 1, 0]
+    qinv = m[:4, 11].copy().view(np.float64)
+    assert all(abs(float(v) * q - 1.0) < 1e-15 for v, q in zip(qinv, primes[:4]))
+    hc.set_fp64(False)
+    assert not np.asarray(hc.moduli())[:, 10].any()
+    hc.set_fp64(True)
+    assert list(np.asarray(hc.moduli())[:, 10]) == [1, 1, 1, 1, 0]
+    from bfvgpu._lib import lib
+    assert lib().bfvgpu_ctx_set_fp64(hc.handle, 2) != 0
+    art = bfv.Context.art002(device=-1)
+    assert not np.asarray(art.moduli())[:, 10].any()
+    hc.close()
+    art.close()
+
+
 def test_host_only_context_refuses_device_work(bfv, gpu_available):
     hc = bfv.Context.art002(device=-1)
     with pytest.raises(bfv.BfvGpuError) as e:
