@@ -674,10 +674,8 @@ BFV_HD void op_ks_finish(const Ex& ex, uint64_t* s, uint64_t blk, const uint64_t
 // Block order of one pipelined launch (order bit 0: the launch holds special-prime blocks):
 // the special-prime blocks (ciphertext, component) first -- they are the longest, so they
 // start in the first wave -- then the data-prime blocks (ciphertext, component, prime).
-// Measured slower: ordering the blocks by ciphertext, alternate launches in reverse so that a
-// launch starts on the digits the previous one read last (0.367 against 0.350 ms), and
-// alternating one special-prime block with two data-prime blocks over the first waves so
-// that the integer and FP64 pipes overlap on each SM (0.373 ms).
+// (Ordering the blocks by ciphertext, alternate launches in reverse so that a launch starts
+// on the digits the previous one read last, measured slower: 0.367 against 0.350 ms.)
 BFV_HD void pipe_block(uint64_t blk, uint64_t count, uint32_t order, uint32_t dk, bool* special, uint64_t* ct,
                        uint32_t* c, uint32_t* p) {
   const uint64_t s_blocks = (order & 1) ? 2 * count : 0;
