@@ -114,7 +114,9 @@ int32_t bfvgpu_ntt_device(bfvgpu_ctx *ctx, uint64_t *data, uint64_t polys, uint3
                           uint32_t prime_offset, int32_t inverse, void *stream);
 /* Galois automorphism + keyswitch of count ciphertexts [count][2][dk][n] with one key
  * [dk][2][k][n]; scratch holds bfvgpu_keyswitch_scratch_words(ctx, count) words;
- * out [count][2][dk][n].  Switch::apply for a whole batch (switch.cu:142-154). */
+ * out [count][2][dk][n].  Switch::apply for a whole batch (switch.cu:142-154).  Ciphertext
+ * and key words must be canonical residues (below their primes), as SEAL produces them: the
+ * device entry points assume it (the host objects, Switch and Rotations, check it). */
 uint64_t bfvgpu_keyswitch_scratch_words(const bfvgpu_ctx *ctx, uint64_t count);
 int32_t bfvgpu_keyswitch_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t count,
                                 const uint64_t *key, uint32_t galois_elt, uint64_t *scratch,
@@ -131,7 +133,9 @@ int32_t bfvgpu_keyswitch_device(bfvgpu_ctx *ctx, const uint64_t *cts, uint64_t c
  *  3. rotate (per element): out [count][2][dk][n] from hoisted + prepared; scratch holds
  *     count * 2 * k * n words.  galois_elt must be the element the key was prepared for.
  * Per element this runs 2k inverse NTTs per ciphertext instead of dk*k forward + 2k
- * inverse (switch.cu:146-149 runs both per apply). */
+ * inverse (switch.cu:146-149 runs both per apply).  Keys and ciphertexts canonical, as for
+ * bfvgpu_keyswitch_device; prepared keys are laid out for the context's arithmetic mode
+ * (bfvgpu_ctx_set_fp64) at the time of preparation. */
 uint64_t bfvgpu_keyswitch_prepared_words(const bfvgpu_ctx *ctx);
 uint64_t bfvgpu_keyswitch_hoist_words(const bfvgpu_ctx *ctx, uint64_t count);
 int32_t bfvgpu_keyswitch_prepare_device(bfvgpu_ctx *ctx, const uint64_t *keys, const uint32_t *galois_elts,
